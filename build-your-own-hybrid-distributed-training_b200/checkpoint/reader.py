@@ -1,0 +1,302 @@
+"""Loading (and resharding) checkpoints; inspection.
+
+``load_checkpoint`` validates the manifest, refuses topology changes the
+format cannot express (a different tensor-parallel width, or a different
+independent sequence-parallel width), then fills every local parameter --
+FSDP flat shards interval by interval, unsharded models tensor by tensor --
+and the optimizer state in the same global coordinates, so a checkpoint
+written at one data-parallel / shard width loads at another, bit for bit.
+RNG state is restored only on ranks that saved one.  Semantics of
+``src/hybrid_training/checkpoint/reader.py:174-663``.
+"""
+
+from __future__ import annotations
+
+import json
+import sys
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any
+
+import torch
+
+from ..config import ExperimentConfig
+from ..distributed.context import DistributedContext
+from ..errors import CheckpointError, CheckpointTopologyError, IncompleteCheckpointError, format_error
+from ..logging import get_logger
+from ..optim.sharded_optimizer import ShardedOptimizer
+from ..parallel.hybrid import HybridModel
+from ..training.state import TrainingState
+from ..utils.reproducibility import restore_rng_state, rng_state_from_serialisable
+from ..utils.tensors import ShardRange
+from .format import MANIFEST_FILENAME, METADATA_FILENAME, resolve_inside, shard_filename, validate_format_version
+from .manifest import CheckpointManifest
+from .reshard import ShardFileCache, read_tensor_range
+
+__all__ = ["LoadedCheckpoint", "inspect_checkpoint", "load_checkpoint", "read_metadata"]
+
+_LOG = get_logger(__name__)
+_RNG = "rng::"
+
+
+@dataclass
+class LoadedCheckpoint:
+    path: Path
+    manifest: CheckpointManifest
+    metadata: dict[str, Any]
+    state: TrainingState
+    scheduler_state: dict[str, Any] = field(default_factory=dict)
+    scaler_state: dict[str, Any] = field(default_factory=dict)
+    seconds: float = 0.0
+    tensors_loaded: int = 0
+    files_read: tuple[str, ...] = ()
+    rng_restored: bool = False
+
+    @property
+    def step(self) -> int:
+        return self.state.step
+
+    def __repr__(self) -> str:
+        return (f"LoadedCheckpoint(path={self.path.name!r}, step={self.step}, tensors={self.tensors_loaded}, "
+                f"files={len(self.files_read)}, {self.seconds:.3f}s)")
+
+
+def read_metadata(directory: str | Path) -> dict[str, Any]:
+    path = Path(directory) / METADATA_FILENAME
+    if not path.is_file():
+        raise IncompleteCheckpointError(format_error("checkpoint.read_metadata", "metadata.json is missing", expected=str(path),
+                                                     observed="absent", resolution="the checkpoint is incomplete"))
+    try:
+        data = json.loads(path.read_text(encoding="utf-8"))
+    except json.JSONDecodeError as exc:
+        raise CheckpointError(format_error("checkpoint.read_metadata", "metadata.json is not valid JSON", expected="a JSON object",
+                                           observed=str(exc), resolution="the file is corrupt")) from exc
+    if not isinstance(data, dict):
+        raise CheckpointError(format_error("checkpoint.read_metadata", "metadata.json is not a JSON object", expected="object",
+                                           observed=type(data).__name__, resolution="the file is corrupt"))
+    return data
+
+
+def _validate_topology_transition(manifest: CheckpointManifest, context: DistributedContext) -> None:
+    sizes = dict(manifest.topology.get("sizes", {}))
+    saved_t, now_t = int(sizes.get("tensor", 1)), context.topology.size("tensor")
+    if saved_t != now_t:
+        raise CheckpointTopologyError(format_error(
+            "checkpoint.load", "the tensor-parallel width differs from the checkpoint's; tensor-parallel slices are a "
+            "decomposition of each matrix (a row-parallel slice is a set of strided columns), not a byte range",
+            rank=context.rank, world_size=context.world_size, expected=f"tensor_parallel_size == {saved_t}", observed=now_t,
+            resolution="resume at the original tensor-parallel width; export a full state dict to change it"))
+    saved_s, now_s = int(sizes.get("sequence", 1)), context.topology.size("sequence")
+    if saved_s != now_s:
+        raise CheckpointTopologyError(format_error(
+            "checkpoint.load", "the standalone sequence-parallel width differs from the checkpoint's", rank=context.rank,
+            world_size=context.world_size, expected=f"sequence_parallel_size == {saved_s}", observed=now_s,
+            resolution="resume with the original sequence-parallel size"))
+
+
+def _check_shape(record: Any, shape: tuple[int, ...], key: str, context: DistributedContext) -> None:
+    if tuple(record.global_shape) != tuple(shape):
+        raise CheckpointError(format_error("checkpoint.load", f"tensor {key!r} has a different shape in the checkpoint",
+                                           rank=context.rank, world_size=context.world_size, expected=tuple(shape),
+                                           observed=tuple(record.global_shape),
+                                           resolution="resume with the model definition that produced the checkpoint"))
+
+
+def _missing(key: str, manifest: CheckpointManifest, context: DistributedContext) -> str:
+    avail = sorted(manifest.tensors_by_category("model"))
+    return format_error("checkpoint.load", f"the checkpoint does not contain tensor {key!r} that the model needs", rank=context.rank,
+                        world_size=context.world_size, expected=key, observed=avail[:8] + (["..."] if len(avail) > 8 else []),
+                        resolution="resume with the model definition that produced the checkpoint, or pass strict=False")
+
+
+def load_checkpoint(directory: str | Path, *, model: HybridModel, context: DistributedContext,
+                    optimizer: ShardedOptimizer | None = None, config: ExperimentConfig | None = None, verify_checksums: bool = True,
+                    load_optimizer: bool = True, load_rng: bool = True, strict: bool = True) -> LoadedCheckpoint:
+    start = time.perf_counter()
+    path = Path(directory)
+    manifest = CheckpointManifest.read(path / MANIFEST_FILENAME)
+    validate_format_version(manifest.format_version)
+    manifest.validate()
+    _validate_topology_transition(manifest, context)
+    metadata = read_metadata(path)
+    if config is not None:
+        _warn_on_config_drift(metadata.get("config"), config)
+    cache = ShardFileCache(path, manifest, verify_checksums=verify_checksums)
+    info_of = model.parameter_parallel_info()
+    loaded = _load_model_tensors(model, manifest, cache, info_of, context, strict)
+    if load_optimizer and optimizer is not None:
+        _load_optimizer_state(model, optimizer, manifest, cache, info_of, metadata, context, strict)
+    rng = False
+    if load_rng and metadata.get("rng", {}).get("saved"):
+        rng = _restore_rng(path, manifest, metadata, cache, context)
+    state = TrainingState.from_dict(metadata.get("training_state", {}))
+    result = LoadedCheckpoint(path, manifest, metadata, state, dict(metadata.get("scheduler", {})), dict(metadata.get("scaler", {})),
+                              time.perf_counter() - start, loaded, cache.loaded_files, rng)
+    cache.clear()
+    _LOG.info("resumed from %s at step %d", path.name, state.step)
+    return result
+
+
+def _load_model_tensors(model: HybridModel, manifest: CheckpointManifest, cache: ShardFileCache, info_of: dict[str, Any],
+                        context: DistributedContext, strict: bool) -> int:
+    loaded = 0
+    if model.fsdp is not None:
+        for flat_param, layout in model.fsdp.optimizer_parameter_layout():
+            dst = flat_param.data
+            for item in layout:
+                info = info_of.get(item.name)
+                key = info.storage_key if info else item.name
+                record = manifest.tensors.get(key)
+                if record is None:
+                    if strict:
+                        raise IncompleteCheckpointError(_missing(key, manifest, context))
+                    _LOG.warning("checkpoint has no tensor %r; keeping the current value", key)
+                    continue
+                _check_shape(record, item.global_shape, key, context)
+                values = read_tensor_range(record, ShardRange(item.parameter_offset, item.length), cache, dtype=dst.dtype)
+                dst[item.local_offset:item.local_offset + item.length].copy_(values)
+                loaded += 1
+    else:
+        full: dict[str, torch.Tensor] = {}
+        for name, piece in model.sharded_state_dict().items():
+            info = info_of.get(name)
+            key = info.storage_key if info else name
+            record = manifest.tensors.get(key)
+            if record is None:
+                if strict:
+                    raise IncompleteCheckpointError(_missing(key, manifest, context))
+                _LOG.warning("checkpoint has no tensor %r; keeping the current value", key)
+                continue
+            _check_shape(record, piece.global_shape, key, context)
+            full[name] = read_tensor_range(record, ShardRange(0, record.numel), cache, dtype=piece.data.dtype).view(piece.global_shape)
+            loaded += 1
+        model.load_full_state_dict(full)
+    buffers = model.buffers_state_dict()
+    restored = {}
+    for name, buf in buffers.items():
+        record = manifest.tensors.get(name)
+        if record is not None:
+            restored[name] = read_tensor_range(record, ShardRange(0, record.numel), cache, dtype=buf.dtype).view(record.global_shape)
+            loaded += 1
+    if restored:
+        model.load_full_state_dict(restored)
+    return loaded
+
+
+def _load_optimizer_state(model: HybridModel, optimizer: ShardedOptimizer, manifest: CheckpointManifest, cache: ShardFileCache,
+                          info_of: dict[str, Any], metadata: dict[str, Any], context: DistributedContext, strict: bool) -> None:
+    layouts = model.optimizer_parameter_layout()
+    scalars = dict(metadata.get("optimizer_scalars", {}))
+    names = {r.state_name for r in manifest.tensors_by_category("optimizer").values()} - {""}
+    if not names and not scalars:
+        _LOG.warning("checkpoint holds no optimizer state; the optimizer starts fresh")
+        return
+    rebuilt: dict[int, dict[str, Any]] = {}
+    for index, param in enumerate(optimizer.parameters):
+        entry: dict[str, Any] = {}
+        for state_name in sorted(names):
+            buf = torch.zeros(param.numel(), dtype=param.dtype)
+            found = False
+            for item in layouts[index]:
+                info = info_of.get(item.name)
+                base = info.storage_key if info else item.name
+                record = manifest.tensors.get(f"{base}::{state_name}")
+                if record is None:
+                    continue
+                found = True
+                buf[item.local_offset:item.local_offset + item.length] = read_tensor_range(
+                    record, ShardRange(item.parameter_offset, item.length), cache, dtype=param.dtype)
+            if found:
+                entry[state_name] = buf.view(param.shape)
+            elif strict:
+                raise IncompleteCheckpointError(format_error("checkpoint.load_optimizer", f"optimizer state {state_name!r} is missing "
+                                                             f"for parameter {index}", rank=context.rank, world_size=context.world_size,
+                                                             expected=f"state entries for parameter {index}", observed="none",
+                                                             resolution="the checkpoint was written with save_optimizer=False"))
+        for name, value in scalars.items():
+            entry[name] = torch.tensor(value) if isinstance(value, (int, float)) else value
+        if entry:
+            rebuilt[index] = entry
+    groups = [{k: v for k, v in g.items() if k != "params"} for g in optimizer.inner.state_dict()["param_groups"]]
+    optimizer.load_state_dict({"param_groups": groups, "state": rebuilt, "num_parameters": len(optimizer.parameters)})
+
+
+def _restore_rng(path: Path, manifest: CheckpointManifest, metadata: dict[str, Any], cache: ShardFileCache,
+                 context: DistributedContext) -> bool:
+    ranks = set(metadata.get("rng", {}).get("ranks", []))
+    if context.rank not in ranks:
+        _LOG.warning("the checkpoint holds RNG state for %d rank(s) but this run has %d; rank %d keeps its fresh RNG", len(ranks),
+                     context.world_size, context.rank)
+        return False
+    name = shard_filename(context.rank)
+    if name not in manifest.files:
+        return False
+    resolve_inside(path, name)
+    tensors = {k[len(_RNG):]: v for k, v in cache.get(name).items() if k.startswith(_RNG)}
+    if not tensors:
+        return False
+    restore_rng_state(rng_state_from_serialisable({"tensors": tensors, "meta": metadata.get("rng", {}).get("meta", {})}))
+    return True
+
+
+def _warn_on_config_drift(saved: Any, current: ExperimentConfig) -> None:
+    if not isinstance(saved, dict):
+        return
+    diffs: list[str] = []
+
+    def norm(v: Any) -> Any:
+        if isinstance(v, (tuple, list)):
+            return [norm(x) for x in v]
+        if isinstance(v, dict):
+            return {k: norm(x) for k, x in v.items()}
+        return v
+
+    def walk(a: Any, b: Any, prefix: str) -> None:
+        if isinstance(a, dict) and isinstance(b, dict):
+            for k in sorted(set(a) | set(b)):
+                walk(a.get(k), b.get(k), f"{prefix}.{k}" if prefix else k)
+        elif a != b:
+            diffs.append(f"{prefix}: {a!r} -> {b!r}")
+
+    walk(norm(saved), norm(current.to_dict()), "")
+    if diffs:
+        _LOG.warning("configuration differs from the checkpoint (%d field(s)); resuming anyway:\n  %s", len(diffs), "\n  ".join(diffs[:12]))
+
+
+def inspect_checkpoint(directory: str | Path, *, verify: bool = True) -> dict[str, Any]:
+    """JSON-safe summary of a checkpoint (optionally verifying every file's size and SHA-256)."""
+    path = Path(directory)
+    manifest = CheckpointManifest.read(path / MANIFEST_FILENAME)
+    validate_format_version(manifest.format_version)
+    manifest.validate()
+    metadata = read_metadata(path)
+    verification: dict[str, Any] = {"performed": verify}
+    if verify:
+        from .reshard import verify_files
+
+        verify_files(path, manifest)
+        verification["files_verified"] = len(manifest.referenced_files())
+    counts: dict[str, int] = {}
+    elements: dict[str, int] = {}
+    for r in manifest.tensors.values():
+        counts[r.category] = counts.get(r.category, 0) + 1
+        elements[r.category] = elements.get(r.category, 0) + r.numel
+    return {"path": str(path), "format_version": manifest.format_version, "created_by": manifest.created_by, "step": manifest.step,
+            "writer_world_size": manifest.writer_world_size, "topology": manifest.topology, "complete": manifest.complete,
+            "tensor_counts": counts, "element_counts": elements, "files": len(manifest.files),
+            "total_bytes": sum(f.bytes for f in manifest.files.values()), "training_state": metadata.get("training_state", {}),
+            "verification": verification}
+
+
+def _console_main() -> int:
+    if len(sys.argv) < 2:
+        print("usage: hybrid-inspect-checkpoint <checkpoint-directory>", file=sys.stderr)
+        return 2
+    try:
+        summary = inspect_checkpoint(sys.argv[1])
+    except CheckpointError as exc:
+        print(f"error: {exc}", file=sys.stderr)
+        return 1
+    print(json.dumps(summary, indent=2, sort_keys=True))
+    return 0

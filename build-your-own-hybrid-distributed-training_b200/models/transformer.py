@@ -1,0 +1,321 @@
+"""Decoder-only transformer covering GPT-2 and Llama shapes, built from parallel layers.
+
+The module tree and parameter names follow the reference's ``TinyTransformer``
+(``src/hybrid_training/models/transformer.py:98-658``): ``token_embedding``,
+``position_embedding``, ``blocks.{i}.{input_norm, attention, post_attention_norm,
+feed_forward}``, ``final_norm``, ``output_projection``; pre-norm residual
+blocks; causal attention; the tensor-parallel plan (vocab-parallel embedding,
+column/row layers, sequence parallelism with padding of uneven lengths).
+
+What changes, B200-first:
+
+* q/k/v are **one** column-parallel GEMM (``attention.qkv``) and attention
+  reads the packed result directly with a flash kernel (no ``S x S`` scores);
+* the residual stream is fp32 and each ``residual + branch`` is fused into the
+  following norm (:func:`hybrid_training.ops.add_norm`); branches compute in
+  the compute dtype (bf16 under mixed precision) from fp32 master weights;
+* GELU is fused into the fc1 GEMM epilogue;
+* Llama features: RMSNorm, rotary embeddings, SwiGLU, grouped-query attention,
+  no biases;
+* with ``targets`` the model returns the mean cross-entropy computed by the
+  fused head + vocab-parallel CE op instead of materialising (and, under TP,
+  all-gathering) the full logits; without ``targets`` it returns logits
+  exactly as the reference does.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import ops
+from ..autograd.collectives import reduce_from_group
+from ..config import ModelConfig
+from ..distributed.groups import GroupHandle
+from ..errors import ConfigurationError, UnsupportedFeatureError, format_error
+from ..parallel.sequence_parallel import (
+    SEQUENCE_DIM,
+    SequenceParallelLayerNorm,
+    SequenceParallelRMSNorm,
+    SequenceShardInfo,
+    gather_sequence,
+    local_sequence_slice,
+    pad_sequence_dimension,
+    scatter_sequence,
+    unpad_sequence_dimension,
+)
+from ..parallel.tensor_parallel import (
+    ColumnParallelLinear,
+    QKVParallelLinear,
+    RowParallelLinear,
+    TensorParallelFeedForward,
+    VocabParallelEmbedding,
+    init_linear_parameters,
+)
+from ..utils.reproducibility import derive_seed, temporary_seed
+
+__all__ = ["ParallelPlan", "TensorParallelAttention", "TinyTransformer", "TransformerBlock", "build_reference_linear"]
+
+
+@dataclass(frozen=True)
+class ParallelPlan:
+    """Which groups the layers of one rank use."""
+
+    tensor_group: GroupHandle
+    sequence_group: GroupHandle
+    sequence_parallel: bool = False
+    vocab_parallel: bool = True
+
+    @classmethod
+    def single_process(cls) -> ParallelPlan:
+        trivial = GroupHandle.trivial("tensor")
+        return cls(tensor_group=trivial, sequence_group=trivial, sequence_parallel=False)
+
+    def __post_init__(self) -> None:
+        if self.sequence_parallel and self.sequence_group.size == 1:
+            raise ConfigurationError(format_error("models.ParallelPlan", "sequence_parallel requested but the sequence group has one member",
+                                                  expected="sequence_group.size > 1", observed=self.sequence_group.size,
+                                                  resolution="pass a real sequence-parallel group or disable the flag"))
+        if self.sequence_parallel and self.sequence_group.ranks != self.tensor_group.ranks and self.tensor_group.size > 1:
+            raise UnsupportedFeatureError(format_error(
+                "models.ParallelPlan", "sequence parallelism over a group other than the tensor group (independent mode) "
+                "combined with tensor parallelism would give attention only the local sequence chunk",
+                expected="sequence group == tensor group, or tensor_parallel_size == 1",
+                observed=f"sequence {self.sequence_group.ranks} vs tensor {self.tensor_group.ranks}",
+                resolution="use sequence_parallel_mode='tensor_group'"))
+
+
+def _make_norm(config: ModelConfig, plan: ParallelPlan, device: torch.device | None, dtype: torch.dtype | None) -> nn.Module:
+    cls = SequenceParallelRMSNorm if config.norm == "rmsnorm" else SequenceParallelLayerNorm
+    return cls(config.hidden_size, eps=config.layer_norm_eps, group=plan.tensor_group, sequence_parallel=plan.sequence_parallel,
+               device=device, dtype=dtype)
+
+
+class TensorParallelAttention(nn.Module):
+    """Causal (grouped-query) self-attention, heads split over the tensor group."""
+
+    def __init__(self, hidden_size: int, num_heads: int, plan: ParallelPlan, *, num_kv_heads: int | None = None,
+                 dropout: float = 0.0, bias: bool = True, causal: bool = True, init_seed: int = 0,
+                 device: torch.device | None = None, dtype: torch.dtype | None = None, rope_theta: float | None = None,
+                 init_std: float | None = None) -> None:
+        super().__init__()
+        t = plan.tensor_group.size
+        kv = num_kv_heads or num_heads
+        if num_heads % t or kv % t:
+            raise ConfigurationError(format_error(
+                "models.TensorParallelAttention", "attention heads must divide evenly across the tensor-parallel group",
+                rank=plan.tensor_group.global_rank, expected=f"num_heads % {t} == 0 and num_kv_heads % {t} == 0",
+                observed=(num_heads, kv), resolution="choose head counts that are multiples of the tensor-parallel size"))
+        self.hidden_size, self.num_heads, self.num_kv_heads = hidden_size, num_heads, kv
+        self.head_dim = hidden_size // num_heads
+        self.heads_per_partition, self.kv_heads_per_partition = num_heads // t, kv // t
+        self.causal, self.dropout, self.plan, self.rope_theta = causal, dropout, plan, rope_theta
+        self.qkv = QKVParallelLinear(hidden_size, num_heads, kv, self.head_dim, plan.tensor_group, bias=bias,
+                                     sequence_parallel=plan.sequence_parallel, init_seed=init_seed, device=device, dtype=dtype,
+                                     init_std=init_std)
+        self.output = RowParallelLinear(num_heads * self.head_dim, hidden_size, plan.tensor_group, bias=bias, input_is_parallel=True,
+                                        sequence_parallel=plan.sequence_parallel, init_seed=derive_seed(init_seed, "attn-o"),
+                                        device=device, dtype=dtype, init_std=init_std)
+        self._rope_cache: dict[tuple[int, str], tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def _rope(self, seq: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+        key = (seq, str(device))
+        if key not in self._rope_cache:
+            self._rope_cache[key] = ops.rope_tables(seq, self.head_dim, float(self.rope_theta), device)
+        return self._rope_cache[key]
+
+    def forward(self, x: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+        qkv = self.qkv(x)
+        h, hkv, d = self.heads_per_partition, self.kv_heads_per_partition, self.head_dim
+        if self.rope_theta is not None:
+            cos, sin = self._rope(qkv.shape[1], qkv.device)
+            qkv = ops.apply_rope(qkv, cos, sin, h, hkv, d)
+        if attention_mask is not None or (self.dropout > 0.0 and self.training):
+            context = _explicit_attention(qkv, h, hkv, d, self.causal, attention_mask, self.dropout if self.training else 0.0)
+        else:
+            context = ops.attention(qkv, h, hkv, d, causal=self.causal)
+        return self.output(context)
+
+
+def _explicit_attention(qkv: torch.Tensor, h: int, hkv: int, d: int, causal: bool, mask: torch.Tensor | None,
+                        dropout: float) -> torch.Tensor:
+    """Materialised-score attention, only for additive masks or attention dropout (CPU reference semantics)."""
+    if qkv.is_cuda:
+        raise UnsupportedFeatureError(format_error(
+            "models.attention", "explicit attention masks and attention dropout are not implemented by the flash kernel",
+            expected="attention_mask=None and dropout=0 on CUDA", observed="mask or dropout given",
+            resolution="rely on causal masking and disable attention dropout"))
+    b, s, _ = qkv.shape
+    q = qkv[..., : h * d].reshape(b, s, h, d).transpose(1, 2).float()
+    k = qkv[..., h * d:(h + hkv) * d].reshape(b, s, hkv, d).transpose(1, 2).float().repeat_interleave(h // hkv, 1)
+    v = qkv[..., (h + hkv) * d:].reshape(b, s, hkv, d).transpose(1, 2).float().repeat_interleave(h // hkv, 1)
+    scores = q @ k.transpose(-1, -2) / d**0.5
+    if causal:
+        scores = scores.masked_fill(torch.ones(s, s, dtype=torch.bool, device=qkv.device).triu(1), float("-inf"))
+    if mask is not None:
+        scores = scores + mask
+    w = torch.softmax(scores, dim=-1)
+    if dropout > 0:
+        w = F.dropout(w, p=dropout)
+    return (w @ v).transpose(1, 2).reshape(b, s, h * d).to(qkv.dtype)
+
+
+class TransformerBlock(nn.Module):
+    """Pre-norm block: ``x + attn(norm(x))`` then ``+ ffn(norm(.))``."""
+
+    def __init__(self, config: ModelConfig, plan: ParallelPlan, *, layer_index: int = 0, init_seed: int = 0,
+                 device: torch.device | None = None, dtype: torch.dtype | None = None,
+                 compute_dtype: torch.dtype | None = None) -> None:
+        super().__init__()
+        seed = derive_seed(init_seed, "block", layer_index)
+        self.compute_dtype = compute_dtype
+        self.input_norm = _make_norm(config, plan, device, dtype)
+        self.attention = TensorParallelAttention(
+            config.hidden_size, config.num_heads, plan, num_kv_heads=config.resolved_num_kv_heads, dropout=config.dropout,
+            bias=config.bias, causal=True, init_seed=derive_seed(seed, "attn"), device=device, dtype=dtype,
+            rope_theta=config.rope_theta if config.position_embedding == "rope" else None)
+        self.post_attention_norm = _make_norm(config, plan, device, dtype)
+        self.feed_forward = TensorParallelFeedForward(config.hidden_size, config.resolved_ffn_hidden_size, plan.tensor_group,
+                                                      activation=config.activation, bias=config.bias,
+                                                      sequence_parallel=plan.sequence_parallel, init_seed=derive_seed(seed, "ffn"),
+                                                      device=device, dtype=dtype)
+        self.dropout = config.dropout
+
+    def _drop(self, x: torch.Tensor) -> torch.Tensor:
+        return F.dropout(x, p=self.dropout) if self.dropout > 0.0 and self.training else x
+
+    def forward_fused(self, residual: torch.Tensor, delta: torch.Tensor | None,
+                      attention_mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(residual, pending delta)`` in, ``(residual, pending delta)`` out; the adds run inside the norms."""
+        if delta is None:
+            h = self.input_norm(residual, out_dtype=self.compute_dtype)
+        else:
+            residual, h = self.input_norm(residual, delta, out_dtype=self.compute_dtype)
+        a = self._drop(self.attention(h, attention_mask))
+        residual, h = self.post_attention_norm(residual, a, out_dtype=self.compute_dtype)
+        return residual, self._drop(self.feed_forward(h))
+
+    def forward(self, x: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+        residual, delta = self.forward_fused(x, None, attention_mask)
+        return residual + delta.to(residual.dtype)
+
+
+class TinyTransformer(nn.Module):
+    """The decoder model; see the module docstring."""
+
+    def __init__(self, config: ModelConfig, plan: ParallelPlan | None = None, *, seed: int = 0, device: torch.device | None = None,
+                 dtype: torch.dtype | None = None, compute_dtype: torch.dtype | None = None) -> None:
+        super().__init__()
+        if config.kind != "transformer":
+            raise ConfigurationError(format_error("models.TinyTransformer", "model kind must be 'transformer'", expected="transformer",
+                                                  observed=config.kind, resolution="set ModelConfig.kind='transformer'"))
+        self.config = config
+        self.plan = plan if plan is not None else ParallelPlan.single_process()
+        tp = self.plan.tensor_group
+        if config.tie_word_embeddings and self.plan.vocab_parallel and tp.size > 1:
+            raise UnsupportedFeatureError(format_error(
+                "models.TinyTransformer", "tied embeddings with a vocabulary-parallel embedding are not supported: the "
+                "embedding is split by vocabulary rows while the head needs the same matrix split by output features",
+                expected="tie_word_embeddings=False, or vocab_parallel=False", observed="both enabled",
+                resolution="untie the weights, or disable vocabulary partitioning"))
+        self.compute_dtype = compute_dtype
+        vocab_group = tp if self.plan.vocab_parallel else GroupHandle.trivial("tensor")
+        self.token_embedding = VocabParallelEmbedding(config.vocab_size, config.hidden_size, vocab_group,
+                                                      init_seed=derive_seed(seed, "token-embedding"), device=device, dtype=dtype)
+        self.position_embedding: nn.Embedding | None = None
+        if config.position_embedding == "learned":
+            with temporary_seed(derive_seed(seed, "position-embedding")):
+                table = torch.empty(config.max_sequence_length, config.hidden_size, device=device, dtype=dtype)
+                nn.init.normal_(table, mean=0.0, std=0.02)
+            self.position_embedding = nn.Embedding(config.max_sequence_length, config.hidden_size, device=device, dtype=dtype)
+            with torch.no_grad():
+                self.position_embedding.weight.copy_(table)
+        self.blocks = nn.ModuleList([
+            TransformerBlock(config, self.plan, layer_index=i, init_seed=derive_seed(seed, "blocks"), device=device, dtype=dtype,
+                             compute_dtype=compute_dtype) for i in range(config.num_layers)])
+        self.final_norm = _make_norm(config, self.plan, device, dtype)
+        self.output_projection = ColumnParallelLinear(config.hidden_size, config.vocab_size, tp, bias=False, gather_output=True,
+                                                      sequence_parallel=False, init_seed=derive_seed(seed, "output-projection"),
+                                                      device=device, dtype=dtype)
+        if config.tie_word_embeddings:
+            self.output_projection.weight = self.token_embedding.weight
+        self.dropout = config.dropout
+
+    def _embed(self, token_ids: torch.Tensor) -> torch.Tensor:
+        emb = self.token_embedding
+        pos = self.position_embedding.weight if self.position_embedding is not None else None
+        if emb.group.size == 1:
+            return emb.local_lookup(token_ids, pos)
+        out = reduce_from_group(emb.local_lookup(token_ids), emb.group)
+        return out if pos is None else out + pos[: token_ids.shape[1]][None].to(out.dtype)
+
+    def forward(self, token_ids: torch.Tensor, attention_mask: torch.Tensor | None = None, *,
+                targets: torch.Tensor | None = None) -> torch.Tensor:
+        """Logits ``[B, S, V]``; or, with ``targets``, the mean next-token cross-entropy."""
+        b, s = token_ids.shape
+        if s > self.config.max_sequence_length:
+            raise ConfigurationError(format_error("models.TinyTransformer.forward", "sequence longer than the model supports",
+                                                  expected=f"<= {self.config.max_sequence_length}", observed=s,
+                                                  resolution="raise ModelConfig.max_sequence_length or shorten the input"))
+        hidden = self._embed(token_ids)
+        if self.dropout > 0.0 and self.training:
+            hidden = F.dropout(hidden, p=self.dropout)
+        info: SequenceShardInfo | None = None
+        sp_group = self.plan.sequence_group
+        if self.plan.sequence_parallel:
+            hidden, info = pad_sequence_dimension(hidden, sp_group.size, dim=SEQUENCE_DIM)
+            if attention_mask is not None and info.requires_padding:
+                raise UnsupportedFeatureError(format_error(
+                    "models.TinyTransformer.forward", "an explicit attention mask with sequence padding is not supported",
+                    expected="a sequence length divisible by the sequence-parallel size",
+                    observed=f"length {s}, group {sp_group.size}", resolution="pad the batch or drop the explicit mask"))
+            hidden = scatter_sequence(hidden, sp_group, dim=SEQUENCE_DIM)
+        residual, delta = hidden, None
+        for block in self.blocks:
+            residual, delta = block.forward_fused(residual, delta, attention_mask)
+        if delta is None:
+            h = self.final_norm(residual, out_dtype=self.compute_dtype)
+        else:
+            _, h = self.final_norm(residual, delta, out_dtype=self.compute_dtype)
+        if self.plan.sequence_parallel:
+            h = gather_sequence(h, sp_group, dim=SEQUENCE_DIM)
+            h = unpad_sequence_dimension(h, info, dim=SEQUENCE_DIM)
+        if targets is not None:
+            head = self.output_projection
+            group = head.group if head.group.size > 1 else None
+            start = head.group.local_rank * head.output_features_per_partition
+            return ops.lm_head_cross_entropy(h, head.weight, targets, group=group, vocab_start=start,
+                                             vocab_size=self.config.vocab_size)
+        return self.output_projection(h)
+
+    def local_positions(self, sequence_length: int) -> tuple[int, int]:
+        if not self.plan.sequence_parallel:
+            return 0, sequence_length
+        return local_sequence_slice(sequence_length, self.plan.sequence_group)
+
+    def num_parameters(self) -> int:
+        return sum(p.numel() for p in self.parameters())
+
+    def __repr__(self) -> str:
+        c = self.config
+        sp = self.plan.sequence_group.size if self.plan.sequence_parallel else 1
+        return (f"TinyTransformer(layers={c.num_layers}, hidden={c.hidden_size}, heads={c.num_heads}/{c.resolved_num_kv_heads}, "
+                f"vocab={c.vocab_size}, norm={c.norm}, pos={c.position_embedding}, act={c.activation}, "
+                f"tp={self.plan.tensor_group.size}, sp={sp})")
+
+
+def build_reference_linear(in_features: int, out_features: int, *, bias: bool = True, init_seed: int = 0,
+                           device: torch.device | None = None, dtype: torch.dtype | None = None) -> nn.Linear:
+    """An ``nn.Linear`` initialised exactly like a width-1 column/row-parallel layer with the same seed."""
+    linear = nn.Linear(in_features, out_features, bias=bias, device=device, dtype=dtype)
+    with temporary_seed(derive_seed(init_seed, "tensor-parallel-init")), torch.no_grad():
+        w = torch.empty(out_features, in_features, device=device, dtype=dtype)
+        b = torch.empty(out_features, device=device, dtype=dtype) if bias else None
+        init_linear_parameters(w, b, in_features=in_features)
+        linear.weight.copy_(w)
+        if b is not None:
+            linear.bias.copy_(b)
+    return linear

@@ -1,0 +1,435 @@
+"""Bucketed data parallelism with gradient views and an in-kernel NVLink all-reduce.
+
+Semantics kept from ``src/hybrid_training/parallel/ddp.py:266-837``:
+
+* parameters are bucketed in **reverse registration order** (the order their
+  gradients become ready), a new bucket starts at the byte cap or a
+  dtype/device change;
+* the (name, shape, dtype) list and the bucket layout are checked to be
+  identical on every rank, and parameters/buffers are broadcast from the group
+  source at construction;
+* a bucket is reduced (``AVG`` = pre-divide + sum) as soon as all its
+  gradients have arrived, but buckets are **launched strictly in index order**
+  so every rank issues the same collective sequence; out-of-order readiness is
+  counted;
+* ``no_sync()`` accumulates without communication; ``find_unused_parameters``
+  zero-fills the slots of parameters that got no gradient (otherwise that is
+  an error, because the bucket could never complete);
+* after synchronisation ``param.grad`` is a view into its bucket.
+
+B200-native differences:
+
+* all buckets are slices of **one flat fp32 gradient buffer**, and every
+  parameter's ``main_grad`` is a view into it *from the first step*: the
+  native wgrad GEMM writes gradients straight into the bucket (overwriting on
+  the first micro-batch, accumulating after), so there is no copy into the
+  bucket and no separate gradient tensor;
+* on CUDA with a symmetric (peer-mapped) workspace for the group, the flat
+  buffer lives in peer memory and each bucket is reduced by
+  ``ops.comm.bucket_all_reduce`` -- a two-shot all-reduce that reads the peers'
+  slices over NVLink, scales by ``1/G`` in the same pass and writes the result
+  back to every rank -- issued on a communication stream that overlaps the
+  rest of the backward pass; otherwise NCCL all-reduce (pre-multiplied sum)
+  is used.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterator, Sequence
+from contextlib import contextmanager
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+import torch.nn as nn
+
+from ..config import DDPConfig
+from ..distributed.collectives import (
+    AsyncWork,
+    CommunicationRecorder,
+    ReduceOp,
+    all_reduce,
+    assert_metadata_consistent,
+    assert_tensor_consistent,
+    broadcast,
+)
+from ..distributed.groups import GroupHandle
+from ..errors import ShardingError, format_error
+from ..logging import get_logger
+
+__all__ = ["BucketLayout", "DDPStatistics", "DistributedDataParallel", "GradientBucket"]
+
+_LOG = get_logger(__name__)
+_MIB = 1 << 20
+_ALIGN = 64  # elements: every bucket starts on a 256-byte boundary
+
+
+@dataclass(frozen=True)
+class BucketLayout:
+    index: int
+    parameter_names: tuple[str, ...]
+    offsets: tuple[int, ...]
+    numels: tuple[int, ...]
+    total_numel: int
+    dtype_str: str
+    device_str: str
+
+    def as_dict(self) -> dict[str, Any]:
+        return {"index": self.index, "parameter_names": list(self.parameter_names), "offsets": list(self.offsets),
+                "numels": list(self.numels), "total_numel": self.total_numel, "dtype": self.dtype_str}
+
+
+class GradientBucket:
+    """One contiguous slice of the flat gradient buffer and its readiness bookkeeping."""
+
+    __slots__ = ("buffer", "launched", "layout", "parameters", "pending", "ready", "start", "work")
+
+    def __init__(self, layout: BucketLayout, parameters: Sequence[nn.Parameter], buffer: torch.Tensor, start: int) -> None:
+        self.layout = layout
+        self.parameters = tuple(parameters)
+        self.buffer = buffer
+        self.start = start
+        self.pending = len(parameters)
+        self.ready = False
+        self.launched = False
+        self.work: AsyncWork | None = None
+
+    @property
+    def is_allocated(self) -> bool:
+        return True
+
+    def view_for(self, position: int) -> torch.Tensor:
+        off, n = self.layout.offsets[position], self.layout.numels[position]
+        return self.buffer[off:off + n].view(self.parameters[position].shape)
+
+    def reset(self) -> None:
+        self.pending = len(self.parameters)
+        self.ready = self.launched = False
+        self.work = None
+
+    def num_bytes(self) -> int:
+        return self.layout.total_numel * self.buffer.element_size()
+
+    def __repr__(self) -> str:
+        return f"GradientBucket(index={self.layout.index}, params={len(self.parameters)}, numel={self.layout.total_numel}, pending={self.pending})"
+
+
+@dataclass
+class DDPStatistics:
+    steps: int = 0
+    buckets_reduced: int = 0
+    bytes_reduced: int = 0
+    unused_parameters: tuple[str, ...] = ()
+    out_of_order_buckets: int = 0
+
+    def as_dict(self) -> dict[str, Any]:
+        return {"steps": self.steps, "buckets_reduced": self.buckets_reduced, "bytes_reduced": self.bytes_reduced,
+                "unused_parameters": list(self.unused_parameters), "out_of_order_buckets": self.out_of_order_buckets}
+
+
+class _FusedLaunch:
+    """Completion handle for an in-kernel bucket all-reduce issued on the comm stream."""
+
+    def __init__(self, event: torch.cuda.Event, status: Any) -> None:
+        self.event = event
+        self.status = status
+
+    def wait(self) -> None:
+        torch.cuda.current_stream().wait_event(self.event)
+
+
+class DistributedDataParallel(nn.Module):
+    """Replicates ``module`` over ``group`` and averages gradients bucket by bucket."""
+
+    def __init__(self, module: nn.Module, group: GroupHandle, config: DDPConfig | None = None, *,
+                 recorder: CommunicationRecorder | None = None, workspace: Any = None) -> None:
+        super().__init__()
+        self.module = module
+        self._group = group
+        self._config = config or DDPConfig()
+        self._recorder = recorder
+        self._named_parameters: list[tuple[str, nn.Parameter]] = []
+        seen: set[int] = set()
+        for name, p in module.named_parameters():
+            if p.requires_grad and id(p) not in seen:
+                seen.add(id(p))
+                self._named_parameters.append((name, p))
+        if not self._named_parameters:
+            raise ShardingError(format_error("ddp.__init__", "the module has no trainable parameters to synchronise",
+                                             rank=group.global_rank, expected=">= 1 parameter with requires_grad=True",
+                                             observed=0, resolution="wrap a module that has trainable parameters"))
+        self._name_of = {id(p): n for n, p in self._named_parameters}
+        self._buckets: list[GradientBucket] = []
+        self._bucket_of: dict[int, tuple[GradientBucket, int]] = {}
+        self._handles: list[Any] = []
+        self._require_backward_grad_sync = True
+        self._backward_in_progress = False
+        self._next_bucket = 0
+        self._statistics = DDPStatistics()
+        self._workspace = workspace if (self._config.fused_allreduce and not group.is_trivial) else None
+        self._comm_stream: torch.cuda.Stream | None = None
+        if self._config.check_parameter_consistency:
+            signature = [(n, tuple(p.shape), str(p.dtype)) for n, p in self._named_parameters]
+            assert_metadata_consistent(signature, group, name="the (name, shape, dtype) list of trainable parameters",
+                                       operation="ddp.verify_parameter_structure")
+        self._broadcast_initial_state()
+        self._build_buckets()
+        self._register_hooks()
+        _LOG.info("DDP ready over %r (size %d): %d parameters in %d buckets (%s all-reduce)", group.name, group.size,
+                  len(self._named_parameters), len(self._buckets), "in-kernel" if self._workspace is not None else "NCCL")
+
+    # -- construction -------------------------------------------------------------------------
+    def _broadcast_initial_state(self) -> None:
+        src = self._config.source_rank_in_group
+        for _, p in self._named_parameters:
+            broadcast(p.data, self._group, source_local_rank=src, recorder=self._recorder).wait()
+        for _, b in self.module.named_buffers():
+            if b is not None and b.numel():
+                broadcast(b.data, self._group, source_local_rank=src, recorder=self._recorder).wait()
+
+    def _build_buckets(self) -> None:
+        cap = int(self._config.bucket_cap_mb * _MIB)
+        groups: list[list[tuple[str, nn.Parameter]]] = []
+        current: list[tuple[str, nn.Parameter]] = []
+        size = 0
+        key = None
+        for name, p in reversed(self._named_parameters):
+            k = (p.dtype, p.device)
+            nbytes = p.numel() * p.element_size()
+            if current and (k != key or size + nbytes > cap):
+                groups.append(current)
+                current, size = [], 0
+            key = k
+            current.append((name, p))
+            size += nbytes
+        if current:
+            groups.append(current)
+        # Gradients are reduced in fp32 (or the parameter dtype when wider).
+        starts, total = [], 0
+        for members in groups:
+            starts.append(total)
+            n = sum(p.numel() for _, p in members)
+            total += -(-n // _ALIGN) * _ALIGN
+        device = self._named_parameters[0][1].device
+        grad_dtype = torch.float32 if self._named_parameters[0][1].dtype in (torch.float16, torch.bfloat16, torch.float32) else self._named_parameters[0][1].dtype
+        if self._workspace is not None and device.type == "cuda":
+            flat = self._workspace.allocate(total, grad_dtype)
+        else:
+            flat = torch.zeros(total, dtype=grad_dtype, device=device)
+        self._flat_grad = flat
+        for index, (members, start) in enumerate(zip(groups, starts)):
+            offsets, numels, off = [], [], 0
+            for _, p in members:
+                offsets.append(off)
+                numels.append(p.numel())
+                off += p.numel()
+            layout = BucketLayout(index, tuple(n for n, _ in members), tuple(offsets), tuple(numels), off,
+                                  str(members[0][1].dtype), str(members[0][1].device))
+            bucket = GradientBucket(layout, [p for _, p in members], flat[start:start + off], start)
+            self._buckets.append(bucket)
+            for pos, (_, p) in enumerate(members):
+                self._bucket_of[id(p)] = (bucket, pos)
+                p.main_grad = bucket.view_for(pos)
+                p.main_grad_fresh = True
+        if self._config.check_parameter_consistency:
+            assert_metadata_consistent([b.layout.as_dict() for b in self._buckets], self._group,
+                                       name="the gradient bucket layout", operation="ddp.verify_bucket_layout")
+
+    def _register_hooks(self) -> None:
+        for _, p in self._named_parameters:
+            p.grad_ready_hook = self._on_grad_ready
+            self._handles.append(p.register_post_accumulate_grad_hook(self._on_autograd_grad))
+
+    # -- backward-time bookkeeping ------------------------------------------------------------------
+    def _on_autograd_grad(self, param: torch.Tensor) -> None:
+        """Gradient produced by plain autograd (CPU ops, or ops without fused delivery)."""
+        if param.grad is None:
+            return
+        from ..ops.grads import deliver_grad
+
+        grad = param.grad
+        param.grad = None
+        deliver_grad(param, value=grad.detach().to(param.main_grad.dtype))
+
+    def _on_grad_ready(self, param: torch.Tensor) -> None:
+        self._backward_in_progress = True
+        if not self._require_backward_grad_sync:
+            return
+        entry = self._bucket_of.get(id(param))
+        if entry is None:
+            return
+        bucket, _ = entry
+        if bucket.pending == 0:
+            raise ShardingError(format_error(
+                "ddp.on_grad_ready", "a gradient arrived for a bucket already reduced this iteration; backward() ran twice "
+                "without a synchronisation boundary", rank=self._group.global_rank,
+                expected="one backward() per finish_gradient_synchronization()", observed=f"bucket {bucket.layout.index}",
+                resolution="call finish_gradient_synchronization() after each backward(), or use no_sync()"))
+        bucket.pending -= 1
+        if bucket.pending == 0:
+            bucket.ready = True
+            if bucket.layout.index != self._next_bucket:
+                self._statistics.out_of_order_buckets += 1
+            if self._config.async_reduction:
+                self._launch_ready_buckets()
+
+    def _launch_ready_buckets(self) -> None:
+        while self._next_bucket < len(self._buckets) and self._buckets[self._next_bucket].ready:
+            self._launch(self._buckets[self._next_bucket])
+            self._next_bucket += 1
+
+    def _launch(self, bucket: GradientBucket) -> None:
+        average = self._config.average_gradients
+        if self._workspace is not None and bucket.buffer.is_cuda:
+            from ..ops.comm import bucket_all_reduce
+
+            if self._comm_stream is None:
+                self._comm_stream = torch.cuda.Stream(device=bucket.buffer.device)
+            self._comm_stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self._comm_stream):
+                status = bucket_all_reduce(self._workspace, self._flat_grad, bucket.start, bucket.layout.total_numel,
+                                           1.0 / self._group.size if average else 1.0)
+                event = torch.cuda.Event()
+                event.record(self._comm_stream)
+            bucket.work = _FusedLaunch(event, status)  # type: ignore[assignment]
+            if self._recorder is not None:
+                self._recorder.record("all_reduce", self._group.name, num_bytes=bucket.num_bytes())
+        else:
+            bucket.work = all_reduce(bucket.buffer, self._group, op=ReduceOp.AVG if average else ReduceOp.SUM,
+                                     async_op=self._config.async_reduction, recorder=self._recorder)
+        bucket.launched = True
+        self._statistics.buckets_reduced += 1
+        self._statistics.bytes_reduced += bucket.num_bytes()
+
+    def finish_gradient_synchronization(self) -> None:
+        """Wait for every bucket and expose the averaged gradients as ``param.grad`` views."""
+        if not self._backward_in_progress:
+            return
+        if not self._require_backward_grad_sync:
+            self._backward_in_progress = False
+            return
+        missing: list[str] = []
+        for bucket in self._buckets:
+            if bucket.pending == 0:
+                continue
+            for pos, p in enumerate(bucket.parameters):
+                if getattr(p, "main_grad_fresh", False):
+                    missing.append(self._name_of.get(id(p), f"<param#{pos}>"))
+                    if self._config.find_unused_parameters:
+                        bucket.view_for(pos).zero_()
+                        p.main_grad_fresh = False
+                        bucket.pending -= 1
+            if bucket.pending == 0:
+                bucket.ready = True
+        if missing and not self._config.find_unused_parameters:
+            raise ShardingError(format_error(
+                "ddp.finish_gradient_synchronization", "some parameters received no gradient, so their buckets can never "
+                "become ready and the all-reduce would never be issued", rank=self._group.global_rank,
+                world_size=self._group.size, expected="every trainable parameter to receive a gradient",
+                observed=f"{len(missing)} without gradients: {missing[:8]}",
+                resolution="set DDPConfig(find_unused_parameters=True), or stop marking unused parameters trainable"))
+        self._statistics.unused_parameters = tuple(missing)
+        self._launch_ready_buckets()
+        for bucket in self._buckets:
+            if not bucket.launched:
+                raise ShardingError(format_error("ddp.finish_gradient_synchronization",
+                                                 f"bucket {bucket.layout.index} never became ready", rank=self._group.global_rank,
+                                                 expected="all buckets ready", observed=f"{bucket.pending} parameters pending",
+                                                 resolution="this indicates a bug in the bucket bookkeeping"))
+        for bucket in self._buckets:
+            if bucket.work is not None:
+                bucket.work.wait()
+        if self._workspace is not None:
+            self._workspace.check_status()
+        for bucket in self._buckets:
+            for pos, p in enumerate(bucket.parameters):
+                p.grad = bucket.view_for(pos).to(p.dtype) if p.dtype != bucket.buffer.dtype else bucket.view_for(pos)
+            bucket.reset()
+        self._next_bucket = 0
+        self._backward_in_progress = False
+        self._statistics.steps += 1
+
+    # -- forward / context managers ----------------------------------------------------------------
+    def forward(self, *args: Any, **kwargs: Any) -> Any:
+        if self._backward_in_progress and self._require_backward_grad_sync:
+            raise ShardingError(format_error(
+                "ddp.forward", "a previous backward pass has not been synchronised; stepping now would use gradients "
+                "that were never averaged", rank=self._group.global_rank,
+                expected="finish_gradient_synchronization() after every backward()", observed="pending bucket reductions",
+                resolution="call finish_gradient_synchronization() before the next forward"))
+        if self._config.broadcast_buffers and self.training:
+            src = self._config.source_rank_in_group
+            for _, b in self.module.named_buffers():
+                if b.numel():
+                    broadcast(b.data, self._group, source_local_rank=src, recorder=self._recorder).wait()
+        return self.module(*args, **kwargs)
+
+    @contextmanager
+    def no_sync(self) -> Iterator[None]:
+        previous = self._require_backward_grad_sync
+        self._require_backward_grad_sync = False
+        try:
+            yield
+        finally:
+            self._require_backward_grad_sync = previous
+
+    # -- introspection / teardown ------------------------------------------------------------------
+    @property
+    def group(self) -> GroupHandle:
+        return self._group
+
+    @property
+    def config(self) -> DDPConfig:
+        return self._config
+
+    @property
+    def statistics(self) -> DDPStatistics:
+        return self._statistics
+
+    @property
+    def flat_gradient_buffer(self) -> torch.Tensor:
+        return self._flat_grad
+
+    def bucket_layouts(self) -> tuple[BucketLayout, ...]:
+        return tuple(b.layout for b in self._buckets)
+
+    def communication_summary(self) -> str:
+        if self._recorder is None:
+            return "communication recording is disabled (pass recorder= to enable it)"
+        return self._recorder.summary()
+
+    def parameters_and_names(self) -> tuple[tuple[str, nn.Parameter], ...]:
+        return tuple(self._named_parameters)
+
+    def verify_replica_consistency(self, *, atol: float = 0.0) -> None:
+        for name, p in self._named_parameters:
+            assert_tensor_consistent(p.data, self._group, name=f"parameter {name!r}", atol=atol,
+                                     operation="ddp.verify_replica_consistency")
+
+    def drain_pending_reductions(self) -> int:
+        """Wait for in-flight reductions and reset bookkeeping (safe teardown after an exception)."""
+        drained = 0
+        for bucket in self._buckets:
+            if bucket.work is not None:
+                bucket.work.wait()
+                drained += 1
+            bucket.reset()
+        self._next_bucket = 0
+        self._backward_in_progress = False
+        return drained
+
+    def teardown(self) -> None:
+        self.drain_pending_reductions()
+        for h in self._handles:
+            h.remove()
+        self._handles.clear()
+        for _, p in self._named_parameters:
+            for attr in ("grad_ready_hook", "main_grad"):
+                if hasattr(p, attr):
+                    delattr(p, attr)
+        self._bucket_of.clear()
+        self._buckets.clear()
+
+    def __repr__(self) -> str:
+        return (f"DistributedDataParallel(group={self._group.name!r}, size={self._group.size}, buckets={len(self._buckets)}, "
+                f"params={len(self._named_parameters)})")

@@ -1,0 +1,329 @@
+"""Composition of all strategies over the 4-D grid, and the rendered parallel plan.
+
+Same rules as ``src/hybrid_training/parallel/hybrid.py:120-848``:
+
+* ``shard > 1`` wraps the model in FSDP over the shard group, with the data
+  group as the replica group (HSDP) when ``data_parallel > 1``;
+* otherwise ``data_parallel > 1`` wraps it in DDP;
+* tensor / sequence parallelism live inside the model's layers;
+* metrics are averaged over ``dp_shard``; the gradient norm is reduced over
+  ``world`` with per-parameter multiplicity weights;
+* tensor-parallel slices are stored under ``name#tp{K}of{N}``.
+
+One ordering differs: the sequence-parallel partial gradients are summed
+*after* DDP's bucket all-reduce, on the synchronised bucket views (both are
+linear, so the order does not change the result; doing it afterwards means the
+SP sum acts on the buffer that the optimizer will read).  Under FSDP the SP sum
+happens inside each unit before its reduce-scatter.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterator
+from contextlib import AbstractContextManager, contextmanager, nullcontext
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+import torch.nn as nn
+
+from ..config import ExperimentConfig
+from ..distributed.collectives import CommunicationRecorder, ReduceOp, assert_tensor_consistent, sum_scalar
+from ..distributed.context import DistributedContext
+from ..distributed.groups import GroupHandle
+from ..errors import ConfigurationError, ShardingError, format_error
+from ..logging import get_logger
+from .ddp import DistributedDataParallel
+from .fsdp import FullyShardedDataParallel, PieceLayout, ShardedTensorPiece
+from .tensor_parallel import all_reduce_sequence_parallel_gradients
+
+__all__ = ["HybridModel", "ParallelismDescription", "ParameterParallelInfo", "build_model", "build_parallel_model",
+           "describe_parallel_plan"]
+
+_LOG = get_logger(__name__)
+
+
+@dataclass(frozen=True)
+class ParameterParallelInfo:
+    name: str
+    shape: tuple[int, ...]
+    partition_dim: int | None
+    tensor_parallel_size: int
+    tensor_parallel_rank: int
+
+    @property
+    def storage_key(self) -> str:
+        """Checkpoint key: the name, plus ``#tp{rank}of{size}`` for tensor-parallel slices."""
+        if self.tensor_parallel_size <= 1:
+            return self.name
+        return f"{self.name}#tp{self.tensor_parallel_rank}of{self.tensor_parallel_size}"
+
+    def as_dict(self) -> dict[str, Any]:
+        return {"name": self.name, "shape": list(self.shape), "partition_dim": self.partition_dim,
+                "tensor_parallel_size": self.tensor_parallel_size, "tensor_parallel_rank": self.tensor_parallel_rank}
+
+
+@dataclass
+class ParallelismDescription:
+    strategy: str
+    replicated_parameters: list[str] = field(default_factory=list)
+    sharded_parameters: list[str] = field(default_factory=list)
+    sharded_activations: list[str] = field(default_factory=list)
+    gradient_reductions: list[tuple[str, str]] = field(default_factory=list)
+    metric_group: str = "dp_shard"
+    notes: list[str] = field(default_factory=list)
+
+    def render(self) -> str:
+        lines = [
+            f"parallel strategy: {self.strategy}",
+            f"  parameters replicated over : {self.replicated_parameters or ['-']}",
+            f"  parameters sharded over    : {self.sharded_parameters or ['-']}",
+            f"  activations sharded over   : {self.sharded_activations or ['-']}",
+            "  gradient reduction order   :",
+        ]
+        lines += [f"      {i}. {op} over {g!r}" for i, (op, g) in enumerate(self.gradient_reductions, start=1)]
+        lines.append(f"  metrics reduced over       : {self.metric_group!r}")
+        lines += [f"  note: {n}" for n in self.notes]
+        return "\n".join(lines)
+
+
+def build_model(config: ExperimentConfig, context: DistributedContext, *, device: torch.device | None = None) -> nn.Module:
+    """Instantiate the configured model with this rank's tensor/sequence-parallel plan."""
+    from ..models.mlp import MLP
+    from ..models.transformer import ParallelPlan, TinyTransformer
+
+    device = device if device is not None else context.device
+    tensor = context.group("tensor")
+    sequence = context.group("sequence_effective")
+    sp = config.topology.sequence_parallel_enabled
+    if config.model.kind == "transformer":
+        plan = ParallelPlan(tensor_group=tensor, sequence_group=sequence, sequence_parallel=sp, vocab_parallel=tensor.size > 1)
+        return TinyTransformer(config.model, plan, seed=config.training.seed, device=device,
+                               compute_dtype=config.mixed_precision.compute_dtype)
+    if sp:
+        raise ConfigurationError(format_error("hybrid.build_model", "the MLP has no sequence dimension to split",
+                                              rank=context.rank, world_size=context.world_size,
+                                              expected="model.kind='transformer' for sequence parallelism",
+                                              observed=config.model.kind, resolution="use the transformer or disable SP"))
+    return MLP(config.model, seed=config.training.seed, tensor_parallel_group=tensor if tensor.size > 1 else None, device=device)
+
+
+def describe_parallel_plan(config: ExperimentConfig, context: DistributedContext) -> ParallelismDescription:
+    """Human-readable account of who holds what and which reductions run in which order."""
+    topo = context.topology
+    shard, replica, tensor = topo.size("shard"), topo.size("data_parallel"), topo.size("tensor")
+    labels = (["fsdp"] if shard > 1 else []) + (["ddp" if shard == 1 else "replicate"] if replica > 1 else [])
+    labels += (["tensor"] if tensor > 1 else []) + (["sequence"] if topo.sequence_parallel_enabled else [])
+    d = ParallelismDescription(strategy="+".join(labels) if labels else "single-process")
+    if tensor > 1:
+        d.sharded_parameters.append("tensor")
+        d.replicated_parameters.append("data_parallel")
+    if shard > 1:
+        d.sharded_parameters.append("shard")
+    if replica > 1 and "data_parallel" not in d.replicated_parameters:
+        d.replicated_parameters.append("data_parallel")
+    if topo.sequence_parallel_enabled:
+        d.sharded_activations.append(topo.sequence_group_name)
+    if tensor > 1:
+        d.gradient_reductions.append(("all-reduce of activation gradients (inside the layers, not of the weights)", "tensor"))
+    if shard > 1:
+        d.gradient_reductions.append(("reduce-scatter of flat gradients", "shard"))
+        if replica > 1:
+            d.gradient_reductions.append(("all-reduce of the sharded gradient", "data_parallel"))
+    elif replica > 1:
+        d.gradient_reductions.append(("bucketed all-reduce of gradients", "data_parallel"))
+    if topo.sequence_parallel_enabled and shard == 1:
+        d.gradient_reductions.append(("all-reduce of sequence-parallel partial gradients (norms, row biases)",
+                                      topo.sequence_group_name))
+    if tensor > 1:
+        d.notes.append("ranks in the same tensor group must receive identical input batches")
+    if shard > 1 and replica > 1:
+        d.notes.append("hybrid sharding: memory scales with 1/shard_size only; the replica dimension buys communication "
+                       "locality, not memory")
+    if shard > 1:
+        if config.fsdp.reshard_after_forward:
+            d.notes.append("reshard_after_forward=True: one extra all-gather per unit per step, in exchange for not holding "
+                           "the full parameters between forward and backward")
+        else:
+            d.notes.append("reshard_after_forward=False: gathered parameters stay resident until backward, saving one "
+                           "all-gather per unit")
+        if config.fsdp.auto_wrap_min_num_params == 0:
+            d.notes.append("the whole module is one FSDP unit, so the transient all-gather buffer is the size of the entire "
+                           "model; set fsdp.auto_wrap_min_num_params to split it")
+    elif replica > 1:
+        d.notes.append(f"DDP bucket cap {config.ddp.bucket_cap_mb} MiB, async_reduction={config.ddp.async_reduction}, "
+                       f"fused_allreduce={config.ddp.fused_allreduce}")
+    if config.training.gradient_accumulation_steps > 1:
+        n = config.training.gradient_accumulation_steps
+        d.notes.append(f"{n} micro-batches per optimizer step: the first {n - 1} run inside no_sync(), so the step costs one "
+                       f"gradient reduction rather than {n}")
+    return d
+
+
+def _unique_named_parameters(model: nn.Module) -> dict[str, nn.Parameter]:
+    seen: set[int] = set()
+    out: dict[str, nn.Parameter] = {}
+    for name, p in model.named_parameters():
+        if id(p) not in seen:
+            seen.add(id(p))
+            out[name] = p
+    return out
+
+
+class HybridModel(nn.Module):
+    """The model wrapped for the grid: FSDP / DDP / plain, plus SP gradient handling and state views."""
+
+    def __init__(self, model: nn.Module, config: ExperimentConfig, context: DistributedContext, *,
+                 recorder: CommunicationRecorder | None = None) -> None:
+        super().__init__()
+        self._config, self._context, self._recorder = config, context, recorder
+        self._description = describe_parallel_plan(config, context)
+        shard, replica = context.group("shard"), context.group("data_parallel")
+        sp = config.topology.sequence_parallel_enabled
+        self._sp_group: GroupHandle | None = context.group("sequence_effective") if sp else None
+        self._fsdp: FullyShardedDataParallel | None = None
+        self._ddp: DistributedDataParallel | None = None
+        if shard.size > 1:
+            self._fsdp = FullyShardedDataParallel(model, shard, config.fsdp, replica_group=replica if replica.size > 1 else None,
+                                                  mixed_precision=config.mixed_precision, device=context.device,
+                                                  recorder=recorder, sequence_group=self._sp_group)
+            self.wrapped: nn.Module = self._fsdp
+        elif replica.size > 1:
+            workspace = None
+            if config.ddp.fused_allreduce and context.device.type == "cuda":
+                workspace = context.symmetric_workspace("data_parallel")
+            self._ddp = DistributedDataParallel(model, replica, config.ddp, recorder=recorder, workspace=workspace)
+            self.wrapped = self._ddp
+        else:
+            self.wrapped = model
+        self._inner_model = model
+        _LOG.info("hybrid model ready\n%s", self._description.render())
+
+    def forward(self, *args: Any, **kwargs: Any) -> Any:
+        return self.wrapped(*args, **kwargs)
+
+    def no_sync(self) -> AbstractContextManager[None]:
+        if self._ddp is not None:
+            return self._ddp.no_sync()
+        if self._fsdp is not None:
+            return self._fsdp.no_sync()
+        return nullcontext()
+
+    def finish_backward(self) -> None:
+        """Complete every gradient reduction for the step (DDP wait, SP partial sums, FSDP free)."""
+        if self._ddp is not None:
+            self._ddp.finish_gradient_synchronization()
+        if self._sp_group is not None and self._fsdp is None:
+            all_reduce_sequence_parallel_gradients(self._inner_model, self._sp_group, recorder=self._recorder)
+        if self._fsdp is not None:
+            self._fsdp.finish_backward()
+
+    def optimizer_parameters(self) -> list[nn.Parameter]:
+        return [p for p in self.wrapped.parameters() if p.requires_grad]
+
+    metric_group = property(lambda self: self._context.group("dp_shard"))
+    norm_group = property(lambda self: self._context.group("world"))
+    data_group = property(lambda self: self._context.group("dp_shard"))
+    description = property(lambda self: self._description)
+    fsdp = property(lambda self: self._fsdp)
+    ddp = property(lambda self: self._ddp)
+    inner_model = property(lambda self: self._inner_model)
+
+    def reduce_metric(self, value: float | torch.Tensor, *, average: bool = True) -> float:
+        return sum_scalar(value, self.metric_group, device=self._context.device,
+                          op=ReduceOp.AVG if average else ReduceOp.SUM, recorder=self._recorder)
+
+    def validate_input_replication(self, batch: torch.Tensor) -> None:
+        group = self._context.group("tensor_sequence")
+        if group.size > 1:
+            data = batch.detach().double() if batch.is_floating_point() else batch.detach()
+            assert_tensor_consistent(data, group, name="the input batch", operation="hybrid.validate_input_replication")
+
+    def parameter_parallel_info(self) -> dict[str, ParameterParallelInfo]:
+        tensor = self._context.group("tensor")
+        if self._fsdp is not None:
+            described = self._fsdp.original_named_parameters()
+        else:
+            described = {n: (tuple(p.shape), p) for n, p in _unique_named_parameters(self._inner_model).items()}
+        out = {}
+        for name, (shape, p) in described.items():
+            replicated = bool(getattr(p, "is_tensor_parallel_replicated", True))
+            dim = None if replicated else int(getattr(p, "tensor_parallel_partition_dim", 0))
+            out[name] = ParameterParallelInfo(name, shape, dim, tensor.size, tensor.local_rank)
+        return out
+
+    def optimizer_parameter_layout(self) -> list[list[PieceLayout]]:
+        params = self.optimizer_parameters()
+        if self._fsdp is not None:
+            pairs = self._fsdp.optimizer_parameter_layout()
+            if [id(p) for p, _ in pairs] != [id(p) for p in params]:
+                raise ShardingError(format_error("hybrid.optimizer_parameter_layout",
+                                                 "the FSDP flat-parameter order does not match the optimizer's parameters",
+                                                 rank=self._context.rank, expected=len(params), observed=len(pairs),
+                                                 resolution="build the optimizer from model.optimizer_parameters()"))
+            return [layout for _, layout in pairs]
+        by_id = {id(p): (n, tuple(p.shape)) for n, p in _unique_named_parameters(self._inner_model).items()}
+        out = []
+        for p in params:
+            entry = by_id.get(id(p))
+            if entry is None:
+                raise ShardingError(format_error("hybrid.optimizer_parameter_layout",
+                                                 "an optimizer parameter does not belong to the wrapped model", rank=self._context.rank,
+                                                 expected="a parameter of the wrapped model", observed=f"tensor {tuple(p.shape)}",
+                                                 resolution="build the optimizer from model.optimizer_parameters()"))
+            out.append([PieceLayout(entry[0], entry[1], 0, p.numel(), 0)])
+        return out
+
+    def sharded_state_dict(self) -> dict[str, ShardedTensorPiece]:
+        if self._fsdp is not None:
+            return self._fsdp.sharded_state_dict()
+        return {n: ShardedTensorPiece(n, tuple(p.shape), 0, p.detach().reshape(-1).clone())
+                for n, p in _unique_named_parameters(self._inner_model).items()}
+
+    def buffers_state_dict(self) -> dict[str, torch.Tensor]:
+        if self._fsdp is not None:
+            return {n: b.detach().clone() for n, b in self._fsdp.original_named_buffers()}
+        return {n: b.detach().clone() for n, b in self._inner_model.named_buffers()}
+
+    def full_state_dict(self) -> dict[str, torch.Tensor]:
+        if self._fsdp is not None:
+            return self._fsdp.full_state_dict()
+        out = {n: p.detach().clone() for n, p in _unique_named_parameters(self._inner_model).items()}
+        out.update(self.buffers_state_dict())
+        return out
+
+    def load_full_state_dict(self, state_dict: dict[str, torch.Tensor]) -> None:
+        if self._fsdp is not None:
+            self._fsdp.load_full_state_dict(state_dict)
+            return
+        with torch.no_grad():
+            for n, p in _unique_named_parameters(self._inner_model).items():
+                if n in state_dict:
+                    p.data.copy_(state_dict[n].to(device=p.device, dtype=p.dtype))
+            for n, b in self._inner_model.named_buffers():
+                if n in state_dict:
+                    b.data.copy_(state_dict[n].to(b.dtype))
+
+    @contextmanager
+    def summon_full_params(self) -> Iterator[None]:
+        if self._fsdp is None:
+            yield
+            return
+        with self._fsdp.summon_full_params():
+            yield
+
+    def memory_summary(self) -> dict[str, int]:
+        if self._fsdp is not None:
+            return self._fsdp.memory_summary()
+        params = list(self._inner_model.parameters())
+        pb = sum(p.numel() * p.element_size() for p in params)
+        gb = sum(p.grad.numel() * p.grad.element_size() for p in params if p.grad is not None)
+        return {"shard_bytes": pb, "full_bytes": pb, "grad_shard_bytes": gb, "padding_bytes": 0, "units": 0}
+
+    def __repr__(self) -> str:
+        return f"HybridModel({self._description.strategy}, wrapped={type(self.wrapped).__name__})"
+
+
+def build_parallel_model(config: ExperimentConfig, context: DistributedContext, *, recorder: CommunicationRecorder | None = None,
+                         device: torch.device | None = None) -> HybridModel:
+    return HybridModel(build_model(config, context, device=device), config, context, recorder=recorder)
