@@ -1,0 +1,131 @@
+"""Runner behind ``bench.py --impl native``: the GPT-2-124M DDP step through the public engine API.
+
+``run`` builds the experiment with :class:`TrainingEngine` (one process per GPU,
+NCCL process groups, DDP over the data-parallel group with the in-kernel
+bucket all-reduce, bf16 compute with fp32 master weights, fused AdamW, CUDA
+graph step) and returns device-timed and end-to-end step times (max over
+ranks), the bytes crossing the host/device boundary per step, and the number
+of native kernel launches per timed region.
+"""
+
+from __future__ import annotations
+
+import os
+from collections.abc import Callable
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from .config import (
+    DataConfig,
+    DDPConfig,
+    ExperimentConfig,
+    MixedPrecisionConfig,
+    ModelConfig,
+    OptimizerConfig,
+    TopologyConfig,
+    TrainingConfig,
+)
+from .distributed.context import init_distributed
+from .training.data import Batch
+from .training.engine import TrainingEngine
+
+__all__ = ["count_native_launches", "run"]
+
+
+def count_native_launches(fn: Callable[[], Any]) -> int:
+    """Number of kernels from this package's native module launched by ``fn()`` (profiled, untimed)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return sum(1 for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA and "ht::" in e.name)
+
+
+def _max_over_ranks(ms: float) -> float:
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed(fn: Callable[[], None]) -> float:
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    fn()
+    stop.record()
+    torch.cuda.synchronize()
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+    return _max_over_ranks(start.elapsed_time(stop))
+
+
+def experiment(world: int, *, micro_batch: int, seq: int, samples: int, use_graph: bool) -> ExperimentConfig:
+    return ExperimentConfig(
+        name="bench-gpt2-124m-ddp",
+        backend="nccl",
+        device="cuda",
+        timeout_seconds=600.0,
+        topology=TopologyConfig(data_parallel_size=world),
+        model=ModelConfig.gpt2_124m(),
+        data=DataConfig(micro_batch_size=micro_batch, sequence_length=seq, num_train_samples=samples, num_eval_samples=0,
+                        token_distribution="uniform", shuffle=False),
+        optimizer=OptimizerConfig(learning_rate=6e-4, weight_decay=0.1, betas=(0.9, 0.95)),
+        training=TrainingConfig(max_steps=1_000_000, log_every_steps=0, deterministic=False, cuda_graph=use_graph),
+        ddp=DDPConfig(bucket_cap_mb=25.0),
+        mixed_precision=MixedPrecisionConfig(enabled=True, param_dtype="bfloat16"),
+    )
+
+
+def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool = True,
+        clock_start: Callable[[], None] | None = None, clock_stop: Callable[[], dict] | None = None) -> dict:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    cfg = experiment(world, micro_batch=micro_batch, seq=seq, samples=micro_batch * world * (2 * steps + warmup + 8),
+                     use_graph=use_graph)
+    ctx = init_distributed(cfg)
+    engine = TrainingEngine(cfg, ctx)
+    stream = engine.batch_stream(host=True)
+    dev = ctx.device
+
+    def step(batch: Batch, read: bool) -> Any:
+        return engine.train_step(iter([batch]), read_metrics=read)
+
+    launches_per_step = 0
+    for i in range(warmup):
+        b = next(stream)
+        if i == 0 and ctx.rank == 0 and os.environ.get("HT_COUNT_LAUNCHES", "1") != "0":
+            launches_per_step = count_native_launches(lambda: step(b, True))
+        else:
+            step(b, True)
+    # device-resident batches for the device-timed loop
+    dev_batches = [next(stream).to(dev) for _ in range(steps)]
+    host_batches = [next(stream) for _ in range(steps)]
+    torch.cuda.synchronize()
+
+    def device_loop() -> None:
+        for b in dev_batches:
+            step(b, False)
+
+    if clock_start is not None:
+        clock_start()
+    device_ms = _timed(device_loop)
+    clocks = clock_stop() if clock_stop is not None else {}
+    losses: list[float] = []
+
+    def e2e_loop() -> None:
+        for b in host_batches:
+            losses.append(step(b, True).loss)
+
+    e2e_ms = _timed(e2e_loop)
+    h2d = host_batches[0].inputs.numel() * host_batches[0].inputs.element_size() + \
+        host_batches[0].targets.numel() * host_batches[0].targets.element_size()
+    engine.close()
+    ctx.shutdown()
+    return {"device_ms": device_ms, "e2e_ms": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+            "gpu_launches": launches_per_step * steps, "clocks": clocks, "loss": losses[-1] if losses else None,
+            "exposed_comm_ms_per_step": None}

@@ -32,7 +32,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops
-from ..autograd.collectives import reduce_from_group
+from ..autograd.collectives import copy_to_group, gather_from_sequence_parallel_region
 from ..config import ModelConfig
 from ..distributed.groups import GroupHandle
 from ..errors import ConfigurationError, UnsupportedFeatureError, format_error
@@ -53,11 +53,20 @@ from ..parallel.tensor_parallel import (
     RowParallelLinear,
     TensorParallelFeedForward,
     VocabParallelEmbedding,
+    VocabParallelHead,
     init_linear_parameters,
 )
 from ..utils.reproducibility import derive_seed, temporary_seed
 
-__all__ = ["ParallelPlan", "TensorParallelAttention", "TinyTransformer", "TransformerBlock", "build_reference_linear"]
+__all__ = ["LearnedPositionEmbedding", "ParallelPlan", "TensorParallelAttention", "TinyTransformer", "TransformerBlock",
+           "build_reference_linear"]
+
+
+class LearnedPositionEmbedding(nn.Embedding):
+    """Learned absolute positions; ``forward(x)`` returns ``x + rows[:S]`` (never a view of the table)."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:  # type: ignore[override]
+        return x + self.weight[: x.shape[1]][None].to(x.dtype)
 
 
 @dataclass(frozen=True)
@@ -225,32 +234,37 @@ class TinyTransformer(nn.Module):
         vocab_group = tp if self.plan.vocab_parallel else GroupHandle.trivial("tensor")
         self.token_embedding = VocabParallelEmbedding(config.vocab_size, config.hidden_size, vocab_group,
                                                       init_seed=derive_seed(seed, "token-embedding"), device=device, dtype=dtype)
-        self.position_embedding: nn.Embedding | None = None
+        self.position_embedding: LearnedPositionEmbedding | None = None
         if config.position_embedding == "learned":
             with temporary_seed(derive_seed(seed, "position-embedding")):
                 table = torch.empty(config.max_sequence_length, config.hidden_size, device=device, dtype=dtype)
                 nn.init.normal_(table, mean=0.0, std=0.02)
-            self.position_embedding = nn.Embedding(config.max_sequence_length, config.hidden_size, device=device, dtype=dtype)
+            self.position_embedding = LearnedPositionEmbedding(config.max_sequence_length, config.hidden_size, device=device,
+                                                               dtype=dtype)
             with torch.no_grad():
                 self.position_embedding.weight.copy_(table)
         self.blocks = nn.ModuleList([
             TransformerBlock(config, self.plan, layer_index=i, init_seed=derive_seed(seed, "blocks"), device=device, dtype=dtype,
                              compute_dtype=compute_dtype) for i in range(config.num_layers)])
         self.final_norm = _make_norm(config, self.plan, device, dtype)
-        self.output_projection = ColumnParallelLinear(config.hidden_size, config.vocab_size, tp, bias=False, gather_output=True,
-                                                      sequence_parallel=False, init_seed=derive_seed(seed, "output-projection"),
-                                                      device=device, dtype=dtype)
+        self.output_projection = VocabParallelHead(config.hidden_size, config.vocab_size, tp, bias=False, gather_output=True,
+                                                   sequence_parallel=False, init_seed=derive_seed(seed, "output-projection"),
+                                                   device=device, dtype=dtype)
         if config.tie_word_embeddings:
             self.output_projection.weight = self.token_embedding.weight
         self.dropout = config.dropout
 
     def _embed(self, token_ids: torch.Tensor) -> torch.Tensor:
-        emb = self.token_embedding
-        pos = self.position_embedding.weight if self.position_embedding is not None else None
-        if emb.group.size == 1:
-            return emb.local_lookup(token_ids, pos)
-        out = reduce_from_group(emb.local_lookup(token_ids), emb.group)
-        return out if pos is None else out + pos[: token_ids.shape[1]][None].to(out.dtype)
+        from ..parallel.fsdp import FullyShardedDataParallel
+
+        emb, pos = self.token_embedding, self.position_embedding
+        # Sub-modules are always *called*, never read from, so an FSDP unit wrapping one of them has
+        # its parameters gathered.  The position rows are fused into the gather kernel when they
+        # belong to this module's own unit and the vocabulary is not split.
+        if pos is not None and not isinstance(pos, FullyShardedDataParallel) and emb.group.size == 1:
+            return emb(token_ids, pos.weight)
+        out = emb(token_ids)
+        return out if pos is None else pos(out)
 
     def forward(self, token_ids: torch.Tensor, attention_mask: torch.Tensor | None = None, *,
                 targets: torch.Tensor | None = None) -> torch.Tensor:
@@ -280,16 +294,17 @@ class TinyTransformer(nn.Module):
             h = self.final_norm(residual, out_dtype=self.compute_dtype)
         else:
             _, h = self.final_norm(residual, delta, out_dtype=self.compute_dtype)
+        head = self.output_projection
+        vocab_split = targets is not None and head.group.size > 1
         if self.plan.sequence_parallel:
-            h = gather_sequence(h, sp_group, dim=SEQUENCE_DIM)
+            # With a vocab-split loss every rank's head produces a partial gradient for the whole
+            # sequence, so the gather's adjoint must sum over ranks (reduce-scatter), not slice.
+            gather = gather_from_sequence_parallel_region if vocab_split else gather_sequence
+            h = gather(h, sp_group, dim=SEQUENCE_DIM)
             h = unpad_sequence_dimension(h, info, dim=SEQUENCE_DIM)
-        if targets is not None:
-            head = self.output_projection
-            group = head.group if head.group.size > 1 else None
-            start = head.group.local_rank * head.output_features_per_partition
-            return ops.lm_head_cross_entropy(h, head.weight, targets, group=group, vocab_start=start,
-                                             vocab_size=self.config.vocab_size)
-        return self.output_projection(h)
+        elif vocab_split:
+            h = copy_to_group(h, head.group)
+        return head(h) if targets is None else head(h, targets=targets)
 
     def local_positions(self, sequence_length: int) -> tuple[int, int]:
         if not self.plan.sequence_parallel:

@@ -86,9 +86,8 @@ class _AttentionFunction(torch.autograd.Function):
         h, hkv, d, causal = ctx.dims
         b, s, _ = qkv.shape
         dqkv = torch.empty_like(qkv)
-        dq_acc = torch.zeros(b, s, h * d, dtype=torch.float32, device=qkv.device)
         delta = torch.empty(b, h, s, dtype=torch.float32, device=qkv.device)
-        extension().attention_backward(qkv, out, dout.contiguous(), lse, delta, dq_acc, dqkv, h, hkv, d, bool(causal),
+        extension().attention_backward(qkv, out, dout.contiguous(), lse, delta, dqkv, h, hkv, d, bool(causal),
                                        1.0 / math.sqrt(d))
         return dqkv, None, None, None, None
 

@@ -1,0 +1,59 @@
+// Python bindings of the native sm_100a kernels (module hybrid_training.ops._C).
+#include <torch/extension.h>
+
+namespace ht {
+void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
+          c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta);
+at::Tensor gemm_error_word(at::Tensor like);
+void norm_forward(at::Tensor res, c10::optional<at::Tensor> delta, at::Tensor w, c10::optional<at::Tensor> b, at::Tensor r_out,
+                  at::Tensor y, at::Tensor mean, at::Tensor rstd, double eps, bool rms);
+void norm_backward(c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dr, at::Tensor r, at::Tensor w, at::Tensor mean,
+                   at::Tensor rstd, at::Tensor dres, c10::optional<at::Tensor> ddelta, at::Tensor part_w,
+                   c10::optional<at::Tensor> part_b, bool rms);
+int64_t norm_backward_blocks(int64_t rows);
+void sum_rows(at::Tensor part, at::Tensor out, double beta);
+void gelu_backward(at::Tensor g, at::Tensor pre, at::Tensor out);
+void swiglu_forward(at::Tensor h, at::Tensor out);
+void swiglu_backward(at::Tensor h, at::Tensor g, at::Tensor dh);
+void column_sum(at::Tensor x, at::Tensor out);
+void embedding_forward(at::Tensor ids, at::Tensor table, c10::optional<at::Tensor> pos, at::Tensor out, int64_t vocab_start);
+void embedding_backward(at::Tensor ids, at::Tensor grad, at::Tensor dtable, int64_t vocab_start);
+void sum_batch_into(at::Tensor grad, at::Tensor out, double beta);
+void rope_(at::Tensor x, at::Tensor cosv, at::Tensor sinv, int64_t heads, int64_t hd, bool inverse);
+void cross_entropy_fused(at::Tensor logits, at::Tensor targets, at::Tensor grad, at::Tensor loss, int64_t vocab_start, double scale);
+void cross_entropy_stats(at::Tensor logits, at::Tensor targets, at::Tensor stats, int64_t vocab_start);
+void cross_entropy_combine(at::Tensor gathered, at::Tensor lse, at::Tensor loss, int64_t world, double scale);
+void cross_entropy_grad(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor grad, int64_t vocab_start, double scale);
+void adamw_flat(at::Tensor param, at::Tensor grad, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> copy, at::Tensor hyper,
+                double beta1, double beta2, double eps, double wd);
+void grad_sumsq(at::Tensor g, c10::optional<at::Tensor> w, at::Tensor out, double scale);
+void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
+void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv,
+                        int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
+}  // namespace ht
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "hybrid_training native kernels (sm_100a)";
+  m.def("gemm", &ht::gemm, "tcgen05 GEMM with fused epilogue");
+  m.def("gemm_error_word", &ht::gemm_error_word, "device error word written by timed-out GEMM waits");
+  m.def("norm_forward", &ht::norm_forward);
+  m.def("norm_backward", &ht::norm_backward);
+  m.def("norm_backward_blocks", &ht::norm_backward_blocks);
+  m.def("sum_rows", &ht::sum_rows);
+  m.def("gelu_backward", &ht::gelu_backward);
+  m.def("swiglu_forward", &ht::swiglu_forward);
+  m.def("swiglu_backward", &ht::swiglu_backward);
+  m.def("column_sum", &ht::column_sum);
+  m.def("embedding_forward", &ht::embedding_forward);
+  m.def("embedding_backward", &ht::embedding_backward);
+  m.def("sum_batch_into", &ht::sum_batch_into);
+  m.def("rope_", &ht::rope_);
+  m.def("cross_entropy_fused", &ht::cross_entropy_fused);
+  m.def("cross_entropy_stats", &ht::cross_entropy_stats);
+  m.def("cross_entropy_combine", &ht::cross_entropy_combine);
+  m.def("cross_entropy_grad", &ht::cross_entropy_grad);
+  m.def("adamw_flat", &ht::adamw_flat);
+  m.def("grad_sumsq", &ht::grad_sumsq);
+  m.def("attention_forward", &ht::attention_forward);
+  m.def("attention_backward", &ht::attention_backward);
+}

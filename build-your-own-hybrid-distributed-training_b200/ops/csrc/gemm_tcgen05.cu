@@ -1,0 +1,427 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-generation tensor cores.
+//
+//   D[M,N] = epilogue(alpha * A . B^T + bias) (+ beta * D)
+//
+// Data path: TMA (cp.async.bulk.tensor, 128-byte swizzle) moves A/B tiles into a 4-stage
+// shared-memory ring; one thread issues tcgen05.mma (M=128, N=256, K=16) into a
+// double-buffered fp32 accumulator in tensor memory; four epilogue warps read it back with
+// tcgen05.ld, apply the fused epilogue and store to global memory while the tensor cores
+// already work on the next tile.  One CTA per SM loops over output tiles (grouped along M for
+// L2 reuse).
+//
+// Operands may be K-major or MN-major (the instruction descriptor's transpose bits), which
+// covers the forward (A=X, B=W), data-gradient (B=W read MN-major) and weight-gradient (both
+// MN-major) products of a linear layer without any transpose in memory.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner,
+// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. tile rows).
+// Every wait is bounded; on timeout an error code is written to `err` and the CTA unwinds,
+// still freeing its tensor memory.
+
+#include "common.cuh"
+
+namespace ht {
+namespace tcg {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;   // 16 KiB
+constexpr int B_BYTES = BN * BK * 2;   // 32 KiB
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 2 * BN;      // double-buffered accumulator (512 columns)
+constexpr int GROUP_M = 8;
+constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024;
+
+enum Epilogue : int { kPlain = 0, kGelu = 1, kGeluBwd = 2 };
+
+struct EpiParams {
+  void* d;
+  long long ldd;
+  int d_fp32;
+  const float* bias_f32;
+  const __nv_bfloat16* bias_bf16;
+  __nv_bfloat16* aux;
+  long long ldaux;
+  const float* alpha;
+  float beta;
+  int epi;
+  int vec_ok;  // D (and aux) rows are 16-byte aligned: vector stores allowed
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = GROUP_M * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * GROUP_M;
+  const int gm = min(GROUP_M, num_m - first_m);
+  const int r = tile - group * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__device__ __forceinline__ void store_chunk(const EpiParams& ep, int row, int col0, int N, float alpha, float* v) {
+  const bool full = col0 + 32 <= N;
+  const bool vec = full && ep.vec_ok;
+  // bias + alpha
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float x = v[i] * alpha;
+    const int c = col0 + i;
+    if (ep.bias_f32 != nullptr && (full || c < N)) x += ep.bias_f32[c];
+    if (ep.bias_bf16 != nullptr && (full || c < N)) x += bf2f(ep.bias_bf16[c]);
+    v[i] = x;
+  }
+  if (ep.epi == kGelu) {
+    __nv_bfloat16* aux = ep.aux + (long long)row * ep.ldaux + col0;
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __align__(16) __nv_bfloat16 pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pk[j] = f2bf(v[q * 8 + j]);
+        *reinterpret_cast<uint4*>(aux + q * 8) = *reinterpret_cast<uint4*>(pk);
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) aux[i] = f2bf(v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+  } else if (ep.epi == kGeluBwd) {
+    const __nv_bfloat16* aux = ep.aux + (long long)row * ep.ldaux + col0;
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 raw = *reinterpret_cast<const uint4*>(aux + q * 8);
+        const __nv_bfloat16* pk = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[q * 8 + j] *= gelu_tanh_grad(bf2f(pk[j]));
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) v[i] *= gelu_tanh_grad(bf2f(aux[i]));
+    }
+  }
+  if (ep.d_fp32) {
+    float* d = reinterpret_cast<float*>(ep.d) + (long long)row * ep.ldd + col0;
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 o = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+        if (ep.beta != 0.f) {
+          const float4 old = *reinterpret_cast<const float4*>(d + q * 4);
+          o.x += ep.beta * old.x;
+          o.y += ep.beta * old.y;
+          o.z += ep.beta * old.z;
+          o.w += ep.beta * old.w;
+        }
+        *reinterpret_cast<float4*>(d + q * 4) = o;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) d[i] = v[i] + (ep.beta != 0.f ? ep.beta * d[i] : 0.f);
+    }
+  } else {
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ep.d) + (long long)row * ep.ldd + col0;
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __align__(16) __nv_bfloat16 pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pk[j] = f2bf(v[q * 8 + j] + (ep.beta != 0.f ? ep.beta * bf2f(d[q * 8 + j]) : 0.f));
+        *reinterpret_cast<uint4*>(d + q * 8) = *reinterpret_cast<uint4*>(pk);
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) d[i] = f2bf(v[i] + (ep.beta != 0.f ? ep.beta * bf2f(d[i]) : 0.f));
+    }
+  }
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, int M, int N, int K,
+                EpiParams ep, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ uint32_t tmem_base_slot;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4);
+    }
+    fence_barrier_init();
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int m0 = mb * BM, n0 = nb * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, 1)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
+          if (A_MN) {
+            tma_load_2d(a_dst, &tma_a, &full_bar[stage], m0, k0);
+            tma_load_2d(a_dst + BK * 128, &tma_a, &full_bar[stage], m0 + 64, k0);
+          } else {
+            tma_load_2d(a_dst, &tma_a, &full_bar[stage], k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], n0 + 64 * j, k0);
+          } else {
+            tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, n0);
+          }
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, err, 2)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, err, 3)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a_addr + k * 2048, BK * 128, 1024)
+                                        : umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, BK * 128, 1024)
+                                        : umma_desc_sw128(b_addr + k * 32, 16, 1024);
+            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(&tfull_bar[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const float alpha = ep.alpha != nullptr ? *ep.alpha : 1.f;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 4)) break;
+      tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      const int nchunks = min(BN / 32, (N - nb * BN + 31) / 32);
+      for (int c = 0; c < nchunks; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * 32, v);
+        if (c == nchunks - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        }
+        if (row < M) store_chunk(ep, row, nb * BN + c * 32, N, alpha, v);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Host side: tensor maps and launch.
+// ------------------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    HT_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    HT_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr, "cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 map over a row-major matrix with `rows` rows of `cols` elements (row stride `ld`).
+static CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  HT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r, " (rows=", rows, " cols=", cols,
+           " ld=", ld, ")");
+  return map;
+}
+
+int* error_word(const at::Device& dev) {
+  // Intentionally leaked: a static tensor destroyed after the CUDA context would fault at exit.
+  static at::Tensor* words = new at::Tensor[64];
+  const int idx = dev.index();
+  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().dtype(at::kInt).device(dev));
+  return words[idx].data_ptr<int>();
+}
+
+static void check_operand(const at::Tensor& t, const char* name) {
+  HT_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be a CUDA bf16 tensor");
+  HT_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit inner stride");
+  HT_CHECK((t.stride(0) * 2) % 16 == 0, name, " row stride must be a multiple of 16 bytes");
+  HT_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+template <bool A_MN, bool B_MN>
+static void launch(const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K, const EpiParams& ep, int* err,
+                   cudaStream_t s) {
+  auto kernel = gemm_kernel<A_MN, B_MN>;
+  static bool configured = false;
+  if (!configured) {
+    HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    configured = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms());
+  kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, M, N, K, ep, err);
+  HT_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace tcg
+
+void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
+          c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta) {
+  using namespace tcg;
+  check_operand(a, "A");
+  check_operand(b, "B");
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int64_t M = a_mn_major ? a.size(1) : a.size(0);
+  const int64_t K = a_mn_major ? a.size(0) : a.size(1);
+  const int64_t N = b_mn_major ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn_major ? b.size(0) : b.size(1);
+  HT_CHECK(K == Kb, "GEMM reduction sizes differ: ", K, " vs ", Kb);
+  HT_CHECK(d.dim() == 2 && d.size(0) == M && d.size(1) == N && d.stride(1) == 1, "D must be [M, N] with unit inner stride");
+  HT_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "D must be bf16 or fp32");
+  const bool d32 = d.scalar_type() == at::kFloat;
+  if (M == 0 || N == 0) return;
+  EpiParams ep{};
+  ep.d = d.data_ptr();
+  ep.ldd = d.stride(0);
+  ep.d_fp32 = d32 ? 1 : 0;
+  ep.beta = static_cast<float>(beta);
+  ep.epi = static_cast<int>(epilogue);
+  ep.vec_ok = ((d.stride(0) * d.element_size()) % 16 == 0 && reinterpret_cast<uintptr_t>(d.data_ptr()) % 16 == 0) ? 1 : 0;
+  if (bias.has_value() && bias->defined()) {
+    HT_CHECK(bias->is_contiguous() && bias->numel() == N, "bias must be a contiguous [N] tensor");
+    if (bias->scalar_type() == at::kFloat) ep.bias_f32 = bias->data_ptr<float>();
+    else if (bias->scalar_type() == at::kBFloat16) ep.bias_bf16 = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+    else HT_CHECK(false, "bias must be fp32 or bf16");
+  }
+  if (epilogue != kPlain) {
+    HT_CHECK(aux.has_value() && aux->defined() && aux->scalar_type() == at::kBFloat16 && aux->size(0) == M &&
+                 aux->size(1) == N && aux->stride(1) == 1,
+             "GELU epilogues need a bf16 [M, N] aux tensor");
+    ep.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+    ep.ldaux = aux->stride(0);
+    if ((aux->stride(0) * 2) % 16 != 0 || reinterpret_cast<uintptr_t>(aux->data_ptr()) % 16 != 0) ep.vec_ok = 0;
+  }
+  if (alpha.has_value() && alpha->defined()) {
+    HT_CHECK(alpha->scalar_type() == at::kFloat && alpha->numel() == 1 && alpha->is_cuda(), "alpha must be one fp32 device value");
+    ep.alpha = alpha->data_ptr<float>();
+  }
+  if (K == 0) {
+    HT_CHECK(false, "GEMM with K == 0 is not supported");
+  }
+  const CUtensorMap ma = a_mn_major ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64)
+                                    : make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
+  const CUtensorMap mb = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64)
+                                    : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
+  int* err = error_word(a.device());
+  cudaStream_t s = stream();
+  if (!a_mn_major && !b_mn_major) launch<false, false>(ma, mb, M, N, K, ep, err, s);
+  else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, M, N, K, ep, err, s);
+  else if (a_mn_major && b_mn_major) launch<true, true>(ma, mb, M, N, K, ep, err, s);
+  else launch<true, false>(ma, mb, M, N, K, ep, err, s);
+}
+
+at::Tensor gemm_error_word(at::Tensor like) { return at::from_blob(tcg::error_word(like.device()), {4}, like.options().dtype(at::kInt)); }
+
+}  // namespace ht

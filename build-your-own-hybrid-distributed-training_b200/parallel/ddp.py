@@ -252,9 +252,9 @@ class DistributedDataParallel(nn.Module):
         deliver_grad(param, value=grad.detach().to(param.main_grad.dtype))
 
     def _on_grad_ready(self, param: torch.Tensor) -> None:
-        self._backward_in_progress = True
         if not self._require_backward_grad_sync:
             return
+        self._backward_in_progress = True
         entry = self._bucket_of.get(id(param))
         if entry is None:
             return

@@ -480,7 +480,10 @@ class FullyShardedDataParallel(nn.Module):
                 continue
             child = self._auto_wrap(child)
             managed, _ = _collect_managed_parameters(child)
-            if sum(p.numel() for _, p in managed) >= threshold:
+            # Containers (ModuleList / ModuleDict) are iterated by their owners, so they are never
+            # units themselves; their children are.
+            container = isinstance(child, (nn.ModuleList, nn.ModuleDict))
+            if not container and sum(p.numel() for _, p in managed) >= threshold:
                 child = FullyShardedDataParallel(child, self._shard_group, dataclasses.replace(self._config, auto_wrap_min_num_params=0),
                                                  replica_group=self._replica_group, mixed_precision=self._mixed_precision,
                                                  device=self._device, recorder=self._recorder, sync_module_states=False,

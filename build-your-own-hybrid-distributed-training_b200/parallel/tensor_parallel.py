@@ -57,6 +57,7 @@ __all__ = [
     "TensorParallelFeedForward",
     "TensorParallelMLPBlock",
     "VocabParallelEmbedding",
+    "VocabParallelHead",
     "all_reduce_sequence_parallel_gradients",
     "init_linear_parameters",
     "mark_sequence_parallel_partial",
@@ -306,6 +307,17 @@ class QKVParallelLinear(ColumnParallelLinear):
         if self.bias is not None:
             _mark_partitioned(self.bias, group, partition_dim=0)
 
+    def canonical(self, gathered: torch.Tensor) -> torch.Tensor:
+        """Reorder a rank-major gathered tensor ``[q_0 k_0 v_0 | q_1 ...]`` (dim 0) into ``[q; k; v]``."""
+        t = self.group.size
+        q, kv = self.num_heads * self.head_dim // t, self.num_kv_heads * self.head_dim // t
+        parts = [p.split([q, kv, kv], dim=0) for p in gathered.chunk(t, dim=0)]
+        return torch.cat([p[0] for p in parts] + [p[1] for p in parts] + [p[2] for p in parts], dim=0)
+
+    def full_weight(self) -> torch.Tensor:
+        """The full ``[(H + 2 Hkv) * D, hidden]`` projection in the canonical ``[q; k; v]`` order."""
+        return self.canonical(all_gather_along_dim(self.weight.detach(), self.group, 0))
+
     def extra_repr(self) -> str:
         return (f"hidden={self.in_features}, heads={self.num_heads}, kv_heads={self.num_kv_heads}, head_dim={self.head_dim}, "
                 f"tp_size={self.group.size}, bias={self.bias is not None}, sequence_parallel={self.sequence_parallel}")
@@ -331,9 +343,15 @@ class VocabParallelEmbedding(nn.Module):
         """This shard's contribution (zeros for foreign ids), before any reduction."""
         return ops.embedding(token_ids, self.weight, positions, vocab_start=self.vocab_start)
 
-    def forward(self, token_ids: torch.Tensor) -> torch.Tensor:
-        out = self.local_lookup(token_ids)
-        return out if self.group.size == 1 else reduce_from_group(out, self.group)
+    def forward(self, token_ids: torch.Tensor, positions: torch.Tensor | None = None, *, reduce: bool = True) -> torch.Tensor:
+        """Embedded tokens (fp32 on CUDA).  ``positions`` (rows ``[:S]`` added) is only allowed at width 1,
+        where it fuses the position add into the gather; ``reduce=False`` returns this shard's partial sum."""
+        if positions is not None and self.group.size > 1:
+            raise TensorParallelError(format_error("tensor_parallel.VocabParallelEmbedding", "positions can only be fused at width 1",
+                                                   rank=self.group.global_rank, expected=1, observed=self.group.size,
+                                                   resolution="add the position rows after the reduction"))
+        out = self.local_lookup(token_ids, positions)
+        return out if (self.group.size == 1 or not reduce) else reduce_from_group(out, self.group)
 
     def full_weight(self) -> torch.Tensor:
         return all_gather_along_dim(self.weight.detach(), self.group, 0)
@@ -457,3 +475,22 @@ def all_reduce_sequence_parallel_gradients(module: nn.Module, group: GroupHandle
         g.detach().copy_(flat[offset:offset + n].view(g.shape))
         offset += n
     return len(targets)
+
+
+class VocabParallelHead(ColumnParallelLinear):
+    """Output projection split by vocabulary rows; with ``targets`` it returns the fused mean cross-entropy.
+
+    Without targets it is the reference's column-parallel head (full logits via
+    ``gather_output``).  With targets the logits never leave the rank: the head GEMM
+    feeds :func:`hybrid_training.ops.lm_head_cross_entropy`, which exchanges three
+    floats per token over the tensor group.  The input must already carry the
+    adjoint that sums the per-rank partial input gradients (``copy_to_group`` or the
+    sequence-parallel gather), which the model inserts.
+    """
+
+    def forward(self, x: torch.Tensor, targets: torch.Tensor | None = None) -> torch.Tensor:
+        if targets is None:
+            return super().forward(x)
+        group = self.group if self.group.size > 1 else None
+        start = self.group.local_rank * self.output_features_per_partition
+        return ops.lm_head_cross_entropy(x, self.weight, targets, group=group, vocab_start=start, vocab_size=self.out_features)

@@ -119,6 +119,7 @@ class TrainingEngine:
         self._graph: torch.cuda.CUDAGraph | None = None
         self._graph_io: dict[str, Any] = {}
         self._eager_steps = 0
+        self._graph_done: torch.cuda.Event | None = None
         self.last_loss_tensor: torch.Tensor | None = None
         self.last_grad_norm_tensor: torch.Tensor | None = None
         reset_peak_memory(ctx.device)
@@ -145,7 +146,8 @@ class TrainingEngine:
                 rank=self.context.rank, world_size=self.context.world_size, expected=f">= {need} micro-batches per epoch",
                 observed=len(self.train_loader), resolution="raise data.num_train_samples or lower gradient_accumulation_steps"))
 
-    def _batch_stream(self, *, host: bool = False) -> Any:
+    def batch_stream(self, *, host: bool = False) -> Any:
+        """Endless stream of this rank's micro-batches (on the device, or pinned host memory with ``host``)."""
         while True:
             epoch = self.state.epoch
             source = self.train_loader.iter_host(epoch) if host else self.train_loader.iter_epoch(epoch)
@@ -160,7 +162,7 @@ class TrainingEngine:
     # -- the loop ---------------------------------------------------------------------------------------------
     def train(self, max_steps: int | None = None) -> TrainingState:
         target = self.config.training.max_steps if max_steps is None else max_steps
-        batches = self._batch_stream(host=self._use_graph())
+        batches = self.batch_stream(host=self._use_graph())
         while self.state.step < target:
             m = self.train_step(batches)
             self.history.append(m)
@@ -222,6 +224,10 @@ class TrainingEngine:
         micro = [next(batches) for _ in range(n)]
         samples = sum(b.size for b in micro)
         inner = self.optimizer.inner
+        if self._graph_done is not None:
+            # The captured step reads the optimizer's pinned hyper-parameter buffer; do not
+            # overwrite it before the previous replay has consumed it.
+            self._graph_done.synchronize()
         if isinstance(inner, FusedAdamW) and inner.flat_parameters.is_cuda and not self.scaler.enabled:
             inner.prepare_step()
         if self._use_graph():
@@ -272,12 +278,16 @@ class TrainingEngine:
             io["loss"], io["norm"] = loss, norm
             self._graph = graph
         self._graph.replay()
+        if self._graph_done is None:
+            self._graph_done = torch.cuda.Event()
+        self._graph_done.record()
         return self._graph_io["loss"], self._graph_io["norm"]
 
     def release_graph(self) -> None:
         """Drop the captured graph (required before destroying process groups it uses)."""
         self._graph = None
         self._graph_io.clear()
+        self._graph_done = None
 
     # -- evaluation / checkpoints --------------------------------------------------------------------------------------------
     @torch.no_grad()

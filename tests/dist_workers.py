@@ -1,0 +1,203 @@
+"""Module-level worker functions for multi-process (Gloo/CPU) tests.
+
+Each worker runs inside a rank spawned by ``launch_workers`` and returns
+plain Python / CPU tensors for the parent to compare against a single-process
+reference computed with the same seeds.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from pathlib import Path
+from typing import Any
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from hybrid_training.config import (
+    CheckpointConfig,
+    DataConfig,
+    DDPConfig,
+    ExperimentConfig,
+    FSDPConfig,
+    ModelConfig,
+    OptimizerConfig,
+    TopologyConfig,
+    TrainingConfig,
+)
+from hybrid_training.distributed import CommunicationRecorder, init_distributed
+from hybrid_training.models import MLP
+from hybrid_training.parallel import DistributedDataParallel, FullyShardedDataParallel
+from hybrid_training.training import TrainingEngine
+
+MLP_CFG = ModelConfig(kind="mlp", input_size=16, hidden_size=32, num_layers=2, output_size=1, activation="relu")
+
+
+def mlp_batch(step: int, rank: int, per_rank: int = 8) -> tuple[torch.Tensor, torch.Tensor]:
+    g = torch.Generator().manual_seed(1000 * step + rank)
+    return torch.randn(per_rank, 16, generator=g), torch.randn(per_rank, 1, generator=g)
+
+
+def single_process_mlp(world: int, steps: int, lr: float = 1e-3) -> dict[str, Any]:
+    """The reference run: one process sees the concatenation of every rank's batch."""
+    model = MLP(MLP_CFG, seed=0)
+    opt = torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=0.0)
+    grads = None
+    for step in range(steps):
+        xs, ys = zip(*(mlp_batch(step, r) for r in range(world)))
+        x, y = torch.cat(xs), torch.cat(ys)
+        opt.zero_grad()
+        F.mse_loss(model(x), y).backward()
+        if step == 0:
+            grads = {n: p.grad.clone() for n, p in model.named_parameters()}
+        opt.step()
+    return {"params": {n: p.detach().clone() for n, p in model.named_parameters()}, "grads0": grads}
+
+
+def ddp_mlp_worker(rank: int, world: int, steps: int, bucket_mb: float) -> dict[str, Any]:
+    ctx = init_distributed(TopologyConfig(data_parallel_size=world), backend="gloo", device="cpu")
+    try:
+        model = MLP(MLP_CFG, seed=0)
+        recorder = CommunicationRecorder()
+        ddp = DistributedDataParallel(model, ctx.group("data_parallel"), DDPConfig(bucket_cap_mb=bucket_mb), recorder=recorder)
+        from hybrid_training.optim import FusedAdamW
+
+        opt = FusedAdamW(ddp.parameters(), lr=1e-3, weight_decay=0.0)
+        grads0 = None
+        for step in range(steps):
+            x, y = mlp_batch(step, rank)
+            F.mse_loss(ddp(x), y).backward()
+            ddp.finish_gradient_synchronization()
+            if step == 0:
+                grads0 = {n: p.grad.clone() for n, p in model.named_parameters()}
+            opt.step()
+            opt.zero_grad()
+        return {"params": {n: p.detach().clone() for n, p in model.named_parameters()}, "grads0": grads0,
+                "buckets": len(ddp.bucket_layouts()), "calls": recorder.total().calls,
+                "stats": ddp.statistics.as_dict()}
+    finally:
+        ctx.shutdown()
+
+
+def ddp_no_sync_worker(rank: int, world: int) -> dict[str, Any]:
+    """Two accumulated micro-batches under no_sync equal one batch of twice the size."""
+    ctx = init_distributed(TopologyConfig(data_parallel_size=world), backend="gloo", device="cpu")
+    try:
+        model = MLP(MLP_CFG, seed=0)
+        ddp = DistributedDataParallel(model, ctx.group("data_parallel"), DDPConfig(bucket_cap_mb=0.01))
+        x, y = mlp_batch(0, rank, per_rank=8)
+        with ddp.no_sync():
+            (F.mse_loss(ddp(x[:4]), y[:4]) / 2).backward()
+        (F.mse_loss(ddp(x[4:]), y[4:]) / 2).backward()
+        ddp.finish_gradient_synchronization()
+        return {n: p.grad.clone() for n, p in model.named_parameters()}
+    finally:
+        ctx.shutdown()
+
+
+def ddp_unused_worker(rank: int, world: int, find_unused: bool) -> str:
+    ctx = init_distributed(TopologyConfig(data_parallel_size=world), backend="gloo", device="cpu")
+    try:
+        model = nn.ModuleDict({"used": nn.Linear(4, 4), "unused": nn.Linear(4, 4)})
+
+        class Wrapper(nn.Module):
+            def __init__(self) -> None:
+                super().__init__()
+                self.m = model
+
+            def forward(self, x: torch.Tensor) -> torch.Tensor:
+                return self.m["used"](x)
+
+        ddp = DistributedDataParallel(Wrapper(), ctx.group("data_parallel"), DDPConfig(find_unused_parameters=find_unused))
+        ddp(torch.randn(2, 4)).sum().backward()
+        try:
+            ddp.finish_gradient_synchronization()
+        except Exception as exc:  # noqa: BLE001
+            return f"error:{type(exc).__name__}"
+        return "ok:" + ",".join(ddp.statistics.unused_parameters)
+    finally:
+        ctx.shutdown()
+
+
+def fsdp_mlp_worker(rank: int, world: int, steps: int) -> dict[str, Any]:
+    ctx = init_distributed(TopologyConfig(shard_parallel_size=world), backend="gloo", device="cpu")
+    try:
+        model = MLP(MLP_CFG, seed=0)
+        fsdp = FullyShardedDataParallel(model, ctx.group("shard"))
+        from hybrid_training.optim import FusedAdamW
+
+        opt = FusedAdamW([fsdp.handle.flat_param], lr=1e-3, weight_decay=0.0)
+        for step in range(steps):
+            x, y = mlp_batch(step, rank)
+            F.mse_loss(fsdp(x), y).backward()
+            fsdp.finish_backward()
+            opt.step()
+            opt.zero_grad()
+        full = fsdp.full_state_dict()
+        return {"full": full, "shard": fsdp.handle.shard_numel, "padding": fsdp.handle.padding,
+                "full_bytes": fsdp.memory_summary()["full_bytes"]}
+    finally:
+        ctx.shutdown()
+
+
+def _tiny_transformer(kind: str = "gpt2") -> ModelConfig:
+    if kind == "llama":
+        return ModelConfig.llama_1b3(hidden_size=32, num_layers=2, num_heads=4, num_kv_heads=2, ffn_hidden_size=48,
+                                     vocab_size=64, max_sequence_length=16)
+    return ModelConfig(kind="transformer", hidden_size=32, num_layers=2, num_heads=4, vocab_size=64, max_sequence_length=16)
+
+
+def transformer_forward_worker(rank: int, world: int, tp: int, sp: bool, kind: str) -> dict[str, Any]:
+    """Loss, logits and a few gradients of the transformer at TP width ``tp`` (optionally with SP)."""
+    topo = TopologyConfig(tensor_parallel_size=tp, data_parallel_size=world // tp,
+                          sequence_parallel_mode="tensor_group" if sp else "disabled")
+    cfg = ExperimentConfig(backend="gloo", device="cpu", topology=topo, model=_tiny_transformer(kind),
+                           tensor_parallel=dataclasses.replace(ExperimentConfig().tensor_parallel, sequence_parallel=sp))
+    ctx = init_distributed(cfg)
+    try:
+        from hybrid_training.parallel import build_model
+
+        model = build_model(cfg, ctx)
+        g = torch.Generator().manual_seed(7)
+        tokens = torch.randint(0, 64, (2, 17), generator=g)
+        logits = model(tokens[:, :-1])
+        loss = model(tokens[:, :-1], targets=tokens[:, 1:])
+        loss.backward()
+        if sp:
+            from hybrid_training.parallel import all_reduce_sequence_parallel_gradients
+
+            all_reduce_sequence_parallel_gradients(model, ctx.group("tensor"))
+        grads = {}
+        for name, p in model.named_parameters():
+            if p.grad is not None and ("input_norm.weight" in name or "qkv.weight" in name):
+                full = p.grad
+                if getattr(p, "tensor_parallel_partition_dim", None) is not None and tp > 1:
+                    from hybrid_training.autograd import all_gather_along_dim
+
+                    full = all_gather_along_dim(p.grad.contiguous(), ctx.group("tensor"), p.tensor_parallel_partition_dim)
+                    if "qkv" in name:
+                        owner = model.get_submodule(name.rsplit(".", 1)[0])
+                        full = owner.canonical(full)
+                grads[name] = full.clone()
+        return {"loss": float(loss.detach()), "logits": logits.detach().clone(), "grads": grads}
+    finally:
+        ctx.shutdown()
+
+
+def engine_worker(rank: int, world: int, overrides: dict[str, Any], steps: int, ckpt: str | None, resume: str | None) -> dict[str, Any]:
+    cfg = ExperimentConfig.from_dict(overrides)
+    ctx = init_distributed(cfg)
+    try:
+        engine = TrainingEngine(cfg, ctx)
+        if resume:
+            engine.load_checkpoint(resume)
+        engine.train(max_steps=steps)
+        path = str(engine.save_checkpoint(ckpt)) if ckpt else None
+        full = engine.model.full_state_dict()
+        out = {"losses": [m.loss for m in engine.history], "path": path,
+               "full": {k: v.detach().clone() for k, v in full.items()}, "step": engine.state.step}
+        engine.close()
+        return out
+    finally:
+        ctx.shutdown()

@@ -1,0 +1,179 @@
+"""Numerics of every native sm_100a kernel against a plain fp32 PyTorch statement of the same op.
+
+Shapes include ragged sizes (not multiples of the tile) to exercise TMA
+out-of-bounds fill and the epilogue masks.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    import hybrid_training.ops as ops
+
+    ops.extension()  # fail loudly if the native module is missing
+    return ops
+
+
+def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.detach().float().cpu(), b.detach().float().cpu()
+    return float((a - b).norm() / (b.norm() + 1e-12))
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 512, 192), (200, 300, 100), (1, 33, 64), (1000, 257, 770)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm_matches_fp32(m: int, n: int, k: int, a_mn: bool, b_mn: bool) -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    a = torch.randn((k, m) if a_mn else (m, k), device=dev).bfloat16()
+    b = torch.randn((k, n) if b_mn else (n, k), device=dev).bfloat16()
+    if (a.stride(0) * 2) % 16 or (b.stride(0) * 2) % 16:
+        pytest.skip("TMA needs 16-byte aligned operand rows")
+    d = ops.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn, out_dtype=torch.float32)
+    ref, _ = ops.reference_gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn)
+    assert _rel(d, ref) < 1e-5, _rel(d, ref)
+
+
+def test_gemm_epilogues() -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    m, n, k = 384, 520, 256
+    a = torch.randn(m, k, device=dev).bfloat16()
+    b = (torch.randn(n, k, device=dev) * 0.05).bfloat16()
+    bias = torch.randn(n, device=dev)
+    pre = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    y = ops.gemm(a, b, bias=bias, aux=pre, epilogue=ops.EPI_GELU)
+    ref, ref_pre = ops.reference_gemm(a, b, bias=bias, epilogue=ops.EPI_GELU)
+    assert _rel(y, ref) < 1e-2 and _rel(pre, ref_pre) < 1e-2
+    g = torch.randn(m, n, device=dev).bfloat16()
+    w = torch.randn(n, n, device=dev).bfloat16()
+    dx = ops.gemm(g, w, b_mn_major=True, aux=pre, epilogue=ops.EPI_GELU_BWD)
+    ref_dx, _ = ops.reference_gemm(g, w, b_mn_major=True, aux=pre, epilogue=ops.EPI_GELU_BWD)
+    assert _rel(dx, ref_dx) < 1e-2
+    # fp32 accumulation with beta and a device-side alpha
+    c = torch.randn(n, k, device=dev)
+    alpha = torch.tensor([0.5], device=dev)
+    out = c.clone()
+    ops.gemm(g, a, out=out, a_mn_major=True, b_mn_major=True, beta=1.0, alpha=alpha)
+    ref_acc, _ = ops.reference_gemm(g, a, a_mn_major=True, b_mn_major=True, c=c, beta=1.0, alpha=alpha)
+    assert _rel(out, ref_acc) < 1e-5
+
+
+def test_gemm_padded_output_rows() -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    a = torch.randn(64, 128, device=dev).bfloat16()
+    b = torch.randn(1003, 128, device=dev).bfloat16()
+    store = torch.zeros(64, 1024, device=dev, dtype=torch.bfloat16)
+    ops.gemm(a, b, out=store[:, :1003])
+    ref, _ = ops.reference_gemm(a, b)
+    assert _rel(store[:, :1003], ref) < 1e-2
+    assert float(store[:, 1003:].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("rms", [False, True])
+@pytest.mark.parametrize("d", [768, 100, 2048])
+def test_add_norm_forward_backward(rms: bool, d: int) -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    rows = 37
+    res = torch.randn(rows, d, device=dev, requires_grad=True)
+    delta = torch.randn(rows, d, device=dev).bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(d, device=dev)).requires_grad_(True)
+    b = None if rms else (0.1 * torch.randn(d, device=dev)).requires_grad_(True)
+    r, y = ops.add_norm(res, delta, w, b, eps=1e-5, rms=rms, out_dtype=torch.bfloat16)
+    res_c, delta_c = res.detach().cpu().requires_grad_(True), delta.detach().float().cpu().requires_grad_(True)
+    w_c = w.detach().cpu().requires_grad_(True)
+    b_c = None if b is None else b.detach().cpu().requires_grad_(True)
+    r_ref, y_ref = ops.add_norm(res_c, delta_c, w_c, b_c, eps=1e-5, rms=rms, out_dtype=torch.float32)
+    assert _rel(r, r_ref) < 1e-6 and _rel(y, y_ref) < 1e-2
+    gy = torch.randn(rows, d)
+    gr = torch.randn(rows, d)
+    torch.autograd.backward([r, y], [gr.to(dev), gy.to(dev).bfloat16()])
+    torch.autograd.backward([r_ref, y_ref], [gr, gy.bfloat16().float()])
+    assert _rel(res.grad, res_c.grad) < 1e-2
+    assert _rel(delta.grad, delta_c.grad) < 2e-2
+    assert _rel(w.grad, w_c.grad) < 1e-2
+    if b is not None:
+        assert _rel(b.grad, b_c.grad) < 1e-2
+
+
+@pytest.mark.parametrize("d,h,hkv,s", [(64, 4, 4, 128), (64, 4, 2, 100), (128, 4, 1, 192), (128, 2, 2, 64)])
+def test_attention_forward_backward(d: int, h: int, hkv: int, s: int) -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    bsz = 2
+    qkv = (torch.randn(bsz, s, (h + 2 * hkv) * d, device=dev) * 0.5).bfloat16().requires_grad_(True)
+    out = ops.attention(qkv, h, hkv, d)
+    ref_in = qkv.detach().float().cpu().requires_grad_(True)
+    ref = ops.reference_attention(ref_in, h, hkv, d)
+    assert _rel(out, ref) < 2e-2, _rel(out, ref)
+    g = torch.randn_like(ref)
+    out.backward(g.to(dev).bfloat16())
+    ref.backward(g.bfloat16().float())
+    assert _rel(qkv.grad, ref_in.grad) < 3e-2, _rel(qkv.grad, ref_in.grad)
+
+
+def test_head_cross_entropy_matches_torch() -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    rows, d, v = 300, 128, 1003
+    h = torch.randn(rows, d, device=dev).bfloat16().requires_grad_(True)
+    w = (torch.randn(v, d, device=dev) * 0.05).requires_grad_(True)
+    t = torch.randint(0, v, (rows,), device=dev)
+    loss = ops.lm_head_cross_entropy(h, w, t)
+    hr, wr = h.detach().float().cpu().requires_grad_(True), w.detach().cpu().requires_grad_(True)
+    ref = F.cross_entropy(hr @ wr.bfloat16().float().t(), t.cpu())
+    assert abs(float(loss) - float(ref)) < 2e-2
+    (loss * 2.0).backward()
+    (ref * 2.0).backward()
+    assert _rel(h.grad, hr.grad) < 3e-2 and _rel(w.grad, wr.grad) < 3e-2
+
+
+def test_adamw_flat_matches_reference() -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    n = 4096 + 64
+    p, g = torch.randn(n, device=dev), torch.randn(n, device=dev)
+    m, v = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+    copy = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    pr, mr, vr = p.cpu().clone(), m.cpu().clone(), v.cpu().clone()
+    for step in (1, 2, 3):
+        hyper = torch.tensor([1e-2, float(step), 0.5, 0.0], device=dev)
+        ops.adamw_flat(p, g, m, v, copy, hyper, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1)
+        ops.reference_adamw(pr, g.cpu(), mr, vr, lr=1e-2, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, step=step,
+                            grad_scale=0.5)
+    assert torch.allclose(p.cpu(), pr, atol=1e-5) and torch.allclose(copy.float().cpu(), pr, atol=1e-2)
+
+
+def test_embedding_swiglu_rope() -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    ids = torch.randint(0, 50, (3, 17), device=dev)
+    table = torch.randn(40, 24, device=dev, requires_grad=True)
+    pos = torch.randn(32, 24, device=dev, requires_grad=True)
+    out = ops.embedding(ids, table, pos, vocab_start=10)
+    ref = ops.embedding(ids.cpu(), table.detach().cpu().requires_grad_(True), pos.detach().cpu().requires_grad_(True), vocab_start=10)
+    assert torch.allclose(out.cpu(), ref, atol=1e-6)
+    out.sum().backward()
+    assert table.grad is not None and pos.grad is not None
+    h = torch.randn(5, 7, 64, device=dev).bfloat16().requires_grad_(True)
+    y = ops.swiglu(h)
+    hr = h.detach().float().cpu().requires_grad_(True)
+    yr = ops.swiglu(hr)
+    assert _rel(y, yr) < 1e-2
+    y.float().sum().backward()
+    yr.sum().backward()
+    assert _rel(h.grad, hr.grad) < 2e-2
+    cos, sin = ops.rope_tables(16, 64, 10000.0, dev)
+    qkv = torch.randn(2, 16, (2 + 2) * 64, device=dev).bfloat16()
+    rot = ops.apply_rope(qkv, cos, sin, 2, 1, 64)
+    rot_ref = ops.apply_rope(qkv.float().cpu(), cos.cpu(), sin.cpu(), 2, 1, 64)
+    assert _rel(rot, rot_ref) < 1e-2
