@@ -30,6 +30,9 @@ void grad_sumsq(at::Tensor g, c10::optional<at::Tensor> w, at::Tensor out, doubl
 void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
 void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv,
                         int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
+void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
+                       int64_t start, int64_t numel, double scale, int64_t rank, int64_t slot_base, int64_t max_blocks,
+                       at::Tensor status, double timeout_s);
 }  // namespace ht
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -56,4 +59,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_sumsq", &ht::grad_sumsq);
   m.def("attention_forward", &ht::attention_forward);
   m.def("attention_backward", &ht::attention_backward);
+  m.def("bucket_all_reduce", &ht::bucket_all_reduce, "in-kernel NVLink all-reduce of one DDP bucket");
 }

@@ -339,7 +339,7 @@ class DistributedDataParallel(nn.Module):
         for bucket in self._buckets:
             if bucket.work is not None:
                 bucket.work.wait()
-        if self._workspace is not None:
+        if self._workspace is not None and not torch.cuda.is_current_stream_capturing():
             self._workspace.check_status()
         for bucket in self._buckets:
             for pos, p in enumerate(bucket.parameters):

@@ -132,7 +132,9 @@ def _fused_comm(group: GroupHandle, x: torch.Tensor) -> Any:
         return None
     from ..distributed.context import current_context, is_context_active
 
-    if not is_context_active() or not getattr(current_context(), "fused_tensor_collectives", False):
+    from ..ops.comm import HAS_FUSED_TENSOR_PARALLEL
+
+    if not HAS_FUSED_TENSOR_PARALLEL or not is_context_active() or not getattr(current_context(), "fused_tensor_collectives", False):
         return None
     return current_context().symmetric_workspace(group.name)
 

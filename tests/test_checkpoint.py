@@ -1,0 +1,159 @@
+"""Checkpoint format, integrity checks, resume and resharding across world sizes (CPU/Gloo)."""
+
+from __future__ import annotations
+
+import json
+import shutil
+from pathlib import Path
+
+import pytest
+import torch
+
+from hybrid_training.checkpoint import (
+    CheckpointManifest,
+    ShardRecord,
+    TensorRecord,
+    checkpoint_directory_name,
+    find_latest_checkpoint,
+    inspect_checkpoint,
+    prune_checkpoints,
+    shard_filename,
+    validate_shard_filename,
+)
+from hybrid_training.checkpoint.format import resolve_inside, staging_directory_name
+from hybrid_training.distributed import launch_workers
+from hybrid_training.errors import CheckpointCorruptionError, CheckpointError, IncompleteCheckpointError
+
+from . import dist_workers as W
+
+
+def test_names_and_path_safety(tmp_path: Path) -> None:
+    assert checkpoint_directory_name(7) == "checkpoint-step-000007"
+    assert shard_filename(3) == "rank-00003.pt"
+    assert staging_directory_name("checkpoint-step-000007", "abc").startswith(".staging-checkpoint-step-000007-")
+    for bad in ("../etc/passwd", "rank-1.pt", "x.pt"):
+        with pytest.raises(CheckpointError):
+            validate_shard_filename(bad)
+    (tmp_path / "out").mkdir()
+    with pytest.raises(CheckpointError):
+        resolve_inside(tmp_path / "out", "../escape")
+
+
+def _record(key: str, numel: int, shards: list[tuple[int, int]]) -> TensorRecord:
+    r = TensorRecord(key=key, name=key, global_shape=(numel,), dtype="torch.float32")
+    for i, (off, n) in enumerate(shards):
+        r.shards.append(ShardRecord(rank=i, file=shard_filename(i), offset=off, length=n, key=f"model::{key}@{off}"))
+    return r
+
+
+def test_manifest_validation() -> None:
+    _record("a", 10, [(0, 5), (5, 5)]).validate()
+    with pytest.raises(CheckpointCorruptionError):
+        _record("a", 10, [(0, 6), (5, 5)]).validate()
+    with pytest.raises(IncompleteCheckpointError):
+        _record("a", 10, [(0, 4), (5, 5)]).validate()
+    m = CheckpointManifest()
+    m.tensors["a"] = _record("a", 10, [(0, 10)])
+    with pytest.raises(IncompleteCheckpointError):
+        m.validate()  # not marked complete
+    m.complete = True
+    with pytest.raises(IncompleteCheckpointError):
+        m.validate()  # no integrity record for the file
+    assert CheckpointManifest.from_dict(json.loads(m.to_json())).tensors["a"].numel == 10
+
+
+def _cfg(world: int, shard: int, dp: int = 1, tp: int = 1, steps: int = 4) -> dict:
+    return {"backend": "gloo", "device": "cpu",
+            "topology": {"shard_parallel_size": shard, "data_parallel_size": dp, "tensor_parallel_size": tp},
+            "model": {"kind": "transformer", "hidden_size": 32, "num_layers": 2, "num_heads": 4, "vocab_size": 64,
+                      "max_sequence_length": 16},
+            "data": {"micro_batch_size": 8 // (world // tp), "sequence_length": 16, "num_train_samples": 256,
+                     "num_eval_samples": 0, "shuffle": False},
+            "optimizer": {"learning_rate": 0.003}, "fsdp": {"auto_wrap_min_num_params": 1000},
+            "training": {"max_steps": steps, "log_every_steps": 0}}
+
+
+@pytest.mark.distributed
+def test_save_fsdp4_reload_fsdp2_and_ddp2_bitwise(tmp_path: Path) -> None:
+    saved = launch_workers(W.engine_worker, 4, args=(_cfg(4, 4), 3, str(tmp_path), None), timeout_seconds=600)
+    path = saved[0].value["path"]
+    assert path and Path(path, "manifest.json").is_file()
+    full_before = saved[0].value["full"]
+    info = inspect_checkpoint(path)
+    assert info["complete"] and info["writer_world_size"] == 4 and info["verification"]["files_verified"] == 4
+    for shard, dp in ((2, 1), (1, 2)):
+        reloaded = launch_workers(W.engine_worker, 2, args=(_cfg(2, shard, dp), 3, None, path), timeout_seconds=600)
+        for name, t in full_before.items():
+            assert torch.equal(reloaded[0].value["full"][name], t), (shard, dp, name)
+
+
+@pytest.mark.distributed
+def test_resume_reproduces_uninterrupted_run(tmp_path: Path) -> None:
+    straight = launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 4, None, None), timeout_seconds=600)
+    first = launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 2, str(tmp_path), None), timeout_seconds=600)
+    resumed = launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 4, None, first[0].value["path"]), timeout_seconds=600)
+    assert resumed[0].value["losses"] == straight[0].value["losses"][2:]
+    for name, t in straight[0].value["full"].items():
+        assert torch.equal(resumed[0].value["full"][name], t), name
+
+
+@pytest.mark.distributed
+def test_hybrid_dp2_tp2_saves_and_restores_at_dp1_tp2_bitwise(tmp_path: Path) -> None:
+    """The benchmark's reshard rule at small scale: DP2 x TP2 -> DP1 x TP2 (tensor width unchanged)."""
+    saved = launch_workers(W.engine_worker, 4, args=(_cfg(4, 1, dp=2, tp=2), 2, str(tmp_path), None), timeout_seconds=600)
+    restored = launch_workers(W.engine_worker, 2, args=(_cfg(2, 1, dp=1, tp=2), 2, None, saved[0].value["path"]),
+                              timeout_seconds=600)
+    for rank in range(2):
+        for name, t in saved[rank].value["full"].items():
+            assert torch.equal(restored[rank].value["full"][name], t), (rank, name)
+
+
+@pytest.mark.distributed
+def test_corruption_and_topology_errors_are_detected(tmp_path: Path) -> None:
+    saved = launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 1, str(tmp_path / "c"), None), timeout_seconds=600)
+    path = Path(saved[0].value["path"])
+
+    def variant(name: str) -> Path:
+        dst = tmp_path / name / path.name
+        shutil.copytree(path, dst)
+        return dst
+
+    flipped = variant("flip")
+    blob = bytearray((flipped / "rank-00001.pt").read_bytes())
+    blob[-20] ^= 0xFF
+    (flipped / "rank-00001.pt").write_bytes(bytes(blob))
+    with pytest.raises(CheckpointCorruptionError):
+        inspect_checkpoint(flipped)
+    truncated = variant("trunc")
+    data = (truncated / "rank-00000.pt").read_bytes()
+    (truncated / "rank-00000.pt").write_bytes(data[:-10])
+    with pytest.raises(CheckpointCorruptionError):
+        inspect_checkpoint(truncated)
+    missing = variant("missing")
+    (missing / "rank-00001.pt").unlink()
+    with pytest.raises(IncompleteCheckpointError):
+        inspect_checkpoint(missing)
+    nomanifest = variant("nomanifest")
+    (nomanifest / "manifest.json").unlink()
+    with pytest.raises(IncompleteCheckpointError):
+        inspect_checkpoint(nomanifest)
+    edited = variant("edited")
+    m = json.loads((edited / "manifest.json").read_text())
+    m["complete"] = False
+    (edited / "manifest.json").write_text(json.dumps(m))
+    with pytest.raises(IncompleteCheckpointError):
+        inspect_checkpoint(edited)
+    tp_cfg = _cfg(2, 1, tp=2)
+    results = launch_workers(W.engine_worker, 2, args=(tp_cfg, 1, None, str(path)), timeout_seconds=600, raise_on_failure=False)
+    assert all("CheckpointTopologyError" in (r.traceback_text or "") for r in results)
+
+
+def test_prune_and_find_latest(tmp_path: Path) -> None:
+    for step in (1, 5, 3):
+        d = tmp_path / checkpoint_directory_name(step)
+        d.mkdir()
+        (d / "manifest.json").write_text("{}")
+    (tmp_path / checkpoint_directory_name(9)).mkdir()  # unpublished: no manifest
+    assert find_latest_checkpoint(tmp_path).name == checkpoint_directory_name(5)
+    removed = prune_checkpoints(tmp_path, keep_last=2)
+    assert sorted(p.name for p in removed) == [checkpoint_directory_name(1), checkpoint_directory_name(3)]
