@@ -45,6 +45,27 @@ def _sources() -> list[str]:
     return sorted(glob.glob(str(_CSRC / "*.cu")) + glob.glob(str(_CSRC / "*.cpp")))
 
 
+def _libstdcxx_link_flags() -> list[str]:
+    """Link the C++ runtime that this Python process already uses, as a shared library.
+
+    When the toolchain's ``libstdc++.so`` link is missing, ``g++ -shared`` silently falls back to
+    ``libstdc++.a``.  A second, static copy of the C++ runtime inside the extension then formats
+    error messages through locale data that the process's own copy initialised, and crashes.  The
+    mapped ``libstdc++.so.6`` of this process (torch loads it) is passed to the linker by path.
+    """
+    import torch  # noqa: F401  (maps the C++ runtime)
+
+    try:
+        with open("/proc/self/maps") as maps:
+            for line in maps:
+                path = line.split()[-1]
+                if "libstdc++.so" in path and os.path.exists(path):
+                    return [path]
+    except OSError:
+        pass
+    return []
+
+
 def build_extension(verbose: bool = False, jobs: int | None = None) -> Path:
     """Compile all sources (ninja, incremental) and place ``_C*.so`` next to this file."""
     from torch.utils import cpp_extension
@@ -60,7 +81,7 @@ def build_extension(verbose: bool = False, jobs: int | None = None) -> Path:
         build_directory=str(_BUILD_DIR),
         extra_cflags=["-O3", "-std=c++17", f"-I{_CSRC}"],
         extra_cuda_cflags=cuda_flags,
-        extra_ldflags=[],
+        extra_ldflags=_libstdcxx_link_flags(),
         verbose=verbose,
         is_python_module=True,
         with_cuda=True,

@@ -27,6 +27,18 @@ constexpr long long kSpinLimit = 1ll << 22;
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
 
+// Makes the device's primary context current on the calling thread.  Torch's device guard skips
+// cudaSetDevice when the thread's current device index already matches, which leaves a fresh
+// thread (the autograd engine's worker, for one) without a current context; driver-API calls such
+// as cuTensorMapEncodeTiled then fail there.  Done once per thread and device.
+inline void bind_context(int dev) {
+  thread_local uint64_t bound = 0;
+  if (dev >= 0 && dev < 64 && !(bound & (1ull << dev))) {
+    TORCH_CHECK(cudaSetDevice(dev) == cudaSuccess, "cudaSetDevice failed");
+    bound |= 1ull << dev;
+  }
+}
+
 inline int num_sms() {
   static int cached[64] = {0};
   int dev = 0;

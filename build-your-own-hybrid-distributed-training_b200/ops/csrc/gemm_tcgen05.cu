@@ -373,6 +373,7 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   check_operand(a, "A");
   check_operand(b, "B");
   const c10::cuda::CUDAGuard guard(a.device());
+  bind_context(a.device().index());
   const int64_t M = a_mn_major ? a.size(1) : a.size(0);
   const int64_t K = a_mn_major ? a.size(0) : a.size(1);
   const int64_t N = b_mn_major ? b.size(1) : b.size(0);
