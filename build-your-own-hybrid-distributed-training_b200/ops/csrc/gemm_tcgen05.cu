@@ -4,17 +4,20 @@
 //
 // Data path: TMA (cp.async.bulk.tensor, 128-byte swizzle) moves A/B tiles into a 4-stage
 // shared-memory ring; one thread issues tcgen05.mma (M=128, N=256, K=16) into a
-// double-buffered fp32 accumulator in tensor memory; four epilogue warps read it back with
-// tcgen05.ld, apply the fused epilogue and store to global memory while the tensor cores
-// already work on the next tile.  One CTA per SM loops over output tiles (grouped along M for
-// L2 reuse).
+// double-buffered fp32 accumulator in tensor memory; eight epilogue warps read it back with
+// tcgen05.ld, apply the fused epilogue in registers, stage 32-row x 128-byte pieces in swizzled
+// shared memory and write them with TMA bulk-tensor stores (or TMA fp32 reduce-add for the
+// `beta = 1` gradient accumulation), while the tensor cores already work on the next tile.
+// Outputs whose rows are not 16-byte aligned fall back to per-thread stores.  One CTA per SM
+// loops over output tiles (grouped along M for L2 reuse).
 //
 // Operands may be K-major or MN-major (the instruction descriptor's transpose bits), which
 // covers the forward (A=X, B=W), data-gradient (B=W read MN-major) and weight-gradient (both
 // MN-major) products of a linear layer without any transpose in memory.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner,
-// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. tile rows).
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner,
+// warps 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. tile rows; warps 2..5 take
+// the even 128-byte column chunks of the tile and warps 6..9 the odd ones).
 // Every wait is bounded; on timeout an error code is written to `err` and the CTA unwinds,
 // still freeing its tensor memory.
 
@@ -29,10 +32,13 @@ constexpr int BK = 64;
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;   // 16 KiB
 constexpr int B_BYTES = BN * BK * 2;   // 32 KiB
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;      // double-buffered accumulator (512 columns)
 constexpr int GROUP_M = 8;
-constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024;
+constexpr int EPI_STAGE_BYTES = 32 * 128;  // one 32-row x 128-byte output piece per epilogue warp
+constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * EPI_STAGE_BYTES + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA exceeded");
 
 enum Epilogue : int { kPlain = 0, kGelu = 1, kGeluBwd = 2 };
 
@@ -47,7 +53,10 @@ struct EpiParams {
   const float* alpha;
   float beta;
   int epi;
-  int vec_ok;  // D (and aux) rows are 16-byte aligned: vector stores allowed
+  int vec_ok;      // D (and aux) rows are 16-byte aligned: vector stores allowed
+  int tma_d;       // write D through the output tensor map
+  int tma_aux;     // write the GELU pre-activation through the aux tensor map
+  int reduce_add;  // D (fp32) += result through TMA reduce-add (beta == 1)
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -139,15 +148,149 @@ __device__ __forceinline__ void store_chunk(const EpiParams& ep, int row, int co
   }
 }
 
+// Writes one thread's row of a 128-byte output piece into a 32-row staging tile laid out with the
+// 128-byte swizzle the output tensor map expects (16-byte unit j of row r sits at unit j ^ (r % 8)).
+__device__ __forceinline__ void stage_row(uint8_t* tile, int r, const uint4* units) {
+  uint8_t* row = tile + r * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = units[j];
+}
+
+__device__ __forceinline__ void pack_bf16x64(const float* v, uint4* units) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[j * 8 + 2 * q], v[j * 8 + 2 * q + 1]);
+    units[j] = *reinterpret_cast<const uint4*>(h);
+  }
+}
+
+// Epilogue of one 128-byte column piece (CW = 64 bf16 or 32 fp32 output columns) of one row,
+// through the staging tile and a TMA store.  `v` holds the raw accumulator values.
+template <int CW>
+__device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
+                                                   uint8_t* tile, int lane, int row, int M, int col0, int N, int tile_row0,
+                                                   float alpha, float* v) {
+  const bool full = col0 + CW <= N;
+#pragma unroll
+  for (int i = 0; i < CW; ++i) {
+    float x = v[i] * alpha;
+    const int c = col0 + i;
+    if (ep.bias_f32 != nullptr) x += (full || c < N) ? __ldg(ep.bias_f32 + c) : 0.f;
+    if (ep.bias_bf16 != nullptr) x += (full || c < N) ? bf2f(ep.bias_bf16[c]) : 0.f;
+    v[i] = x;
+  }
+  uint4 units[8];
+  if (ep.epi == kGeluBwd) {
+    const __nv_bfloat16* aux = ep.aux + (long long)row * ep.ldaux + col0;
+    if (row < M && full) {
+#pragma unroll
+      for (int q = 0; q < CW / 8; ++q) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(aux + q * 8);
+        const __nv_bfloat16* pk = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[q * 8 + j] *= gelu_tanh_grad(bf2f(pk[j]));
+      }
+    } else if (row < M) {
+#pragma unroll
+      for (int i = 0; i < CW; ++i) v[i] *= (col0 + i < N) ? gelu_tanh_grad(bf2f(aux[i])) : 0.f;
+    }
+  }
+  if (ep.tma_aux) {  // GELU forward: store the pre-activation first (bf16 only, CW == 64)
+    if (CW == 64) {
+      pack_bf16x64(v, units);
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+      stage_row(tile, lane, units);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(map_aux, tile, col0, tile_row0);
+        bulk_commit();
+      }
+    }
+  }
+  if (ep.epi == kGelu) {
+#pragma unroll
+    for (int i = 0; i < CW; ++i) v[i] = gelu_tanh(v[i]);
+  }
+  if (CW == 64) {
+    pack_bf16x64(v, units);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) units[j] = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                                     __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+  }
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+  stage_row(tile, lane, units);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (ep.reduce_add) tma_reduce_add_2d(map_d, tile, col0, tile_row0);
+    else tma_store_2d(map_d, tile, col0, tile_row0);
+    bulk_commit();
+  }
+}
+
+// All output tiles of one epilogue warp.  CW = output columns per 128-byte piece.
+template <int CW>
+__device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
+                                              uint8_t* tile, uint32_t tmem_base, uint64_t* tfull_bar, uint64_t* tempty_bar,
+                                              int M, int N, int num_m, int num_n, int num_tiles, int warp, int lane, int* err) {
+  const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
+  const int row_in_tile = quarter * 32 + lane;
+  const float alpha = ep.alpha != nullptr ? *ep.alpha : 1.f;
+  constexpr int PIECES = BN / CW;
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  for (int tile_id = blockIdx.x; tile_id < num_tiles; tile_id += gridDim.x) {
+    int mb, nb;
+    tile_coords(tile_id, num_m, num_n, mb, nb);
+    if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 4)) break;
+    tc_fence_after();
+    const int row = mb * BM + row_in_tile;
+#pragma unroll 1
+    for (int c = half; c < PIECES; c += 2) {
+      const int col0 = nb * BN + c * CW;
+      if (col0 >= N) break;
+      float v[CW];
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * CW;
+#pragma unroll
+      for (int s = 0; s < CW / 32; ++s) tmem_ld_32x32b_x32(taddr + 32 * s, v + 32 * s);
+      if (ep.tma_d) {
+        epilogue_piece_tma<CW>(ep, map_d, map_aux, tile, lane, row, M, col0, N, mb * BM + quarter * 32, alpha, v);
+      } else if (row < M) {
+#pragma unroll
+        for (int s = 0; s < CW / 32; ++s)
+          if (col0 + 32 * s < N) store_chunk(ep, row, col0 + 32 * s, N, alpha, v + 32 * s);
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    if (++acc == 2) {
+      acc = 0;
+      acc_phase ^= 1u;
+    }
+  }
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, int M, int N, int K,
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
                 EpiParams ep, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sEpi = smem + STAGES * (A_BYTES + B_BYTES);  // 1024-byte aligned staging tiles
 
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -169,11 +312,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 4);
+      mbar_init(&tempty_bar[b], EPI_WARPS);
     }
     fence_barrier_init();
     prefetch_tensormap(&tma_a);
     prefetch_tensormap(&tma_b);
+    if (ep.tma_d) prefetch_tensormap(&tma_d);
+    if (ep.tma_aux) prefetch_tensormap(&tma_aux);
   }
   if (warp == 1) tmem_alloc(&tmem_base_slot, TMEM_COLS);
   tc_fence_before();
@@ -267,33 +412,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------- epilogue ----------------
-    const int quarter = warp & 3;
-    const int row_in_tile = quarter * 32 + lane;
-    const float alpha = ep.alpha != nullptr ? *ep.alpha : 1.f;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 4)) break;
-      tc_fence_after();
-      const int row = mb * BM + row_in_tile;
-      const int nchunks = min(BN / 32, (N - nb * BN + 31) / 32);
-      for (int c = 0; c < nchunks; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * 32, v);
-        if (c == nchunks - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-        }
-        if (row < M) store_chunk(ep, row, nb * BN + c * 32, N, alpha, v);
-      }
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
-    }
+    uint8_t* tile = sEpi + (warp - 2) * EPI_STAGE_BYTES;
+    if (ep.d_fp32)
+      epilogue_loop<32>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err);
+    else
+      epilogue_loop<64>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err);
   }
   tc_fence_before();
   __syncthreads();
@@ -335,6 +458,22 @@ static CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_
   return map;
 }
 
+// 2-D map over a row-major output (bf16 or fp32) for the epilogue's 32-row x 128-byte stores.
+static CUtensorMap make_out_map(void* base, int64_t rows, int64_t cols, int64_t ld, bool fp32) {
+  CUtensorMap map;
+  const int esize = fp32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esize), 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  HT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output) failed with code ", (int)r, " (rows=", rows,
+           " cols=", cols, " ld=", ld, ")");
+  return map;
+}
+
 int* error_word(const at::Device& dev) {
   // Intentionally leaked: a static tensor destroyed after the CUDA context would fault at exit.
   static at::Tensor* words = new at::Tensor[64];
@@ -351,8 +490,8 @@ static void check_operand(const at::Tensor& t, const char* name) {
 }
 
 template <bool A_MN, bool B_MN>
-static void launch(const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K, const EpiParams& ep, int* err,
-                   cudaStream_t s) {
+static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
+                   int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
   auto kernel = gemm_kernel<A_MN, B_MN>;
   static bool configured = false;
   if (!configured) {
@@ -361,7 +500,7 @@ static void launch(const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, i
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, num_sms());
-  kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, M, N, K, ep, err);
+  kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, md, maux, M, N, K, ep, err);
   HT_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -415,12 +554,23 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
                                     : make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
   const CUtensorMap mb = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64)
                                     : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
+  // TMA output path: aligned rows, and a store or an fp32 accumulate (beta = 1); the GELU
+  // pre-activation is written through its own map when D is bf16.
+  CUtensorMap md{}, maux{};
+  const bool tma_out = ep.vec_ok && (beta == 0.0 || (beta == 1.0 && d32)) && !(epilogue == kGelu && d32);
+  if (tma_out) {
+    md = make_out_map(d.data_ptr(), M, N, d.stride(0), d32);
+    if (epilogue == kGelu) maux = make_out_map(aux->data_ptr(), M, N, aux->stride(0), false);
+    ep.tma_d = 1;
+    ep.tma_aux = epilogue == kGelu ? 1 : 0;
+    ep.reduce_add = beta == 1.0 ? 1 : 0;
+  }
   int* err = error_word(a.device());
   cudaStream_t s = stream();
-  if (!a_mn_major && !b_mn_major) launch<false, false>(ma, mb, M, N, K, ep, err, s);
-  else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, M, N, K, ep, err, s);
-  else if (a_mn_major && b_mn_major) launch<true, true>(ma, mb, M, N, K, ep, err, s);
-  else launch<true, false>(ma, mb, M, N, K, ep, err, s);
+  if (!a_mn_major && !b_mn_major) launch<false, false>(ma, mb, md, maux, M, N, K, ep, err, s);
+  else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, md, maux, M, N, K, ep, err, s);
+  else if (a_mn_major && b_mn_major) launch<true, true>(ma, mb, md, maux, M, N, K, ep, err, s);
+  else launch<true, false>(ma, mb, md, maux, M, N, K, ep, err, s);
 }
 
 at::Tensor gemm_error_word(at::Tensor like) { return at::from_blob(tcg::error_word(like.device()), {4}, like.options().dtype(at::kInt)); }
