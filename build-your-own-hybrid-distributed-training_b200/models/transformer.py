@@ -252,6 +252,9 @@ class TinyTransformer(nn.Module):
                                                    device=device, dtype=dtype)
         if config.tie_word_embeddings:
             self.output_projection.weight = self.token_embedding.weight
+            # The native backward of the head and of the embedding each write into the shared
+            # weight's main_grad; the weight is complete after both.
+            self.token_embedding.weight.native_grad_uses = 2
         self.dropout = config.dropout
 
     def _embed(self, token_ids: torch.Tensor) -> torch.Tensor:

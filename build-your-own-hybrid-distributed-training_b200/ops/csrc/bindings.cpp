@@ -15,7 +15,7 @@ void sum_rows(at::Tensor part, at::Tensor out, double beta);
 void gelu_backward(at::Tensor g, at::Tensor pre, at::Tensor out);
 void swiglu_forward(at::Tensor h, at::Tensor out);
 void swiglu_backward(at::Tensor h, at::Tensor g, at::Tensor dh);
-void column_sum(at::Tensor x, at::Tensor out);
+void column_sum(at::Tensor x, at::Tensor out, double beta);
 void embedding_forward(at::Tensor ids, at::Tensor table, c10::optional<at::Tensor> pos, at::Tensor out, int64_t vocab_start);
 void embedding_backward(at::Tensor ids, at::Tensor grad, at::Tensor dtable, int64_t vocab_start);
 void sum_batch_into(at::Tensor grad, at::Tensor out, double beta);

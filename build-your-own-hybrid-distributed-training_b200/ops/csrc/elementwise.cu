@@ -51,20 +51,63 @@ __global__ void swiglu_backward_kernel(const __nv_bfloat16* __restrict__ h, cons
   }
 }
 
-// out[c] = sum_r x[r, c]  (fp32 accumulation; x bf16 or fp32).  Each CTA takes a column strip of
-// 32*8 columns and a row range; partial sums are combined with atomics into a zeroed output.
-template <typename T>
-__global__ void column_sum_kernel(const T* __restrict__ x, float* __restrict__ out, long long rows, int cols, int rows_per_block) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+// Column sums of a row block: CTA (strip of 32 * VEC columns) x (block of rows); warp w adds
+// rows w, w + 8, ... with VEC contiguous columns per lane, then the eight warps are summed in a
+// fixed order.  part[blockIdx.y, c] receives the block's sums (deterministic: no atomics).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) column_partial_kernel(const T* __restrict__ x, float* __restrict__ part, long long rows,
+                                                             int cols, int rows_per_block) {
+  __shared__ float red[8][32 * VEC];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int strip0 = blockIdx.x * 32 * VEC;
+  const int c0 = strip0 + lane * VEC;
   const long long r0 = (long long)blockIdx.y * rows_per_block;
   const long long r1 = min(rows, r0 + rows_per_block);
-  float s = 0.f;
-  for (long long r = r0; r < r1; ++r) {
-    if constexpr (std::is_same<T, float>::value) s += x[r * cols + c];
-    else s += bf2f(x[r * cols + c]);
+  float acc[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+  if (c0 < cols) {
+#pragma unroll 4
+    for (long long r = r0 + warp; r < r1; r += 8) {
+      const T* p = x + r * cols + c0;
+      if constexpr (VEC == 8 && std::is_same<T, __nv_bfloat16>::value) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(p);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          acc[2 * q] += f.x;
+          acc[2 * q + 1] += f.y;
+        }
+      } else if constexpr (VEC == 4 && std::is_same<T, float>::value) {
+        const float4 f = *reinterpret_cast<const float4*>(p);
+        acc[0] += f.x;
+        acc[1] += f.y;
+        acc[2] += f.z;
+        acc[3] += f.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          if (c0 + e < cols) {
+            if constexpr (std::is_same<T, float>::value) acc[e] += p[e];
+            else acc[e] += bf2f(p[e]);
+          }
+        }
+      }
+    }
   }
-  atomicAdd(out + c, s);
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) red[warp][lane * VEC + e] = acc[e];
+  __syncthreads();
+  for (int i = threadIdx.x; i < 32 * VEC; i += blockDim.x) {
+    const int c = strip0 + i;
+    if (c < cols) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t += red[k][i];
+      part[(long long)blockIdx.y * cols + c] = t;
+    }
+  }
 }
 
 // out[b, s, :] = (ids in shard ? table[ids - start] : 0) + pos[s]   (fp32 out)
@@ -171,25 +214,41 @@ void swiglu_backward(at::Tensor h, at::Tensor g, at::Tensor dh) {
   HT_CUDA_CHECK(cudaGetLastError());
 }
 
-void column_sum(at::Tensor x, at::Tensor out) {
+void sum_rows(at::Tensor part, at::Tensor out, double beta);
+
+// out = column sums of x + beta * out (deterministic): per-row-block partial sums, then sum_rows.
+void column_sum(at::Tensor x, at::Tensor out, double beta) {
   const c10::cuda::CUDAGuard guard(x.device());
   HT_CHECK(x.dim() == 2 && x.is_contiguous() && out.scalar_type() == at::kFloat && out.numel() == x.size(1), "column_sum shapes");
-  out.zero_();
   const long long rows = x.size(0);
   const int cols = x.size(1);
-  if (rows == 0 || cols == 0) return;
-  const int threads = 256;
-  const int col_blocks = (cols + threads - 1) / threads;
-  int row_blocks = std::max(1, std::min<int>((int)((rows + 63) / 64), (num_sms() * 4 + col_blocks - 1) / col_blocks));
+  if (cols == 0) return;
+  if (rows == 0) {
+    if (beta == 0.0) out.zero_();
+    else out.mul_(beta);
+    return;
+  }
+  const bool bf16 = x.scalar_type() == at::kBFloat16;
+  HT_CHECK(bf16 || x.scalar_type() == at::kFloat, "column_sum takes bf16 or fp32");
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 && cols % (bf16 ? 8 : 4) == 0;
+  const int vec = vec_ok ? (bf16 ? 8 : 4) : 1;
+  const int strips = (cols + 32 * vec - 1) / (32 * vec);
+  int row_blocks = (int)std::max<long long>(1, std::min<long long>((rows + 63) / 64, (2LL * num_sms() + strips - 1) / strips));
   const int rpb = (int)((rows + row_blocks - 1) / row_blocks);
   row_blocks = (int)((rows + rpb - 1) / rpb);
-  dim3 grid(col_blocks, row_blocks);
-  if (x.scalar_type() == at::kBFloat16)
-    ew::column_sum_kernel<__nv_bfloat16><<<grid, threads, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-                                                                         out.data_ptr<float>(), rows, cols, rpb);
-  else
-    ew::column_sum_kernel<float><<<grid, threads, 0, stream()>>>(x.data_ptr<float>(), out.data_ptr<float>(), rows, cols, rpb);
+  at::Tensor part = at::empty({row_blocks, cols}, out.options());
+  const dim3 grid(strips, row_blocks);
+  cudaStream_t s = stream();
+  if (bf16) {
+    const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+    if (vec == 8) ew::column_partial_kernel<__nv_bfloat16, 8><<<grid, 256, 0, s>>>(xp, part.data_ptr<float>(), rows, cols, rpb);
+    else ew::column_partial_kernel<__nv_bfloat16, 1><<<grid, 256, 0, s>>>(xp, part.data_ptr<float>(), rows, cols, rpb);
+  } else {
+    if (vec == 4) ew::column_partial_kernel<float, 4><<<grid, 256, 0, s>>>(x.data_ptr<float>(), part.data_ptr<float>(), rows, cols, rpb);
+    else ew::column_partial_kernel<float, 1><<<grid, 256, 0, s>>>(x.data_ptr<float>(), part.data_ptr<float>(), rows, cols, rpb);
+  }
   HT_CUDA_CHECK(cudaGetLastError());
+  sum_rows(part, out, beta);
 }
 
 void embedding_forward(at::Tensor ids, at::Tensor table, c10::optional<at::Tensor> pos, at::Tensor out, int64_t vocab_start) {

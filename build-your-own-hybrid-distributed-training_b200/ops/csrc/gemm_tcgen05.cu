@@ -57,7 +57,16 @@ struct EpiParams {
   int tma_d;       // write D through the output tensor map
   int tma_aux;     // write the GELU pre-activation through the aux tensor map
   int reduce_add;  // D (fp32) += result through TMA reduce-add (beta == 1)
+  int splits;      // split-K factor: work unit u covers tile u / splits, K-range u % splits
+  int split_rows;  // rows per split slice of the fp32 workspace (split-K only)
 };
+
+// K-blocks [kb0, kb1) of work unit `split` when the K loop is split `splits` ways.
+__device__ __forceinline__ void split_range(int kblocks, int splits, int split, int& kb0, int& kb1) {
+  const int per = (kblocks + splits - 1) / splits;
+  kb0 = split * per;
+  kb1 = min(kblocks, kb0 + per);
+}
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -246,9 +255,11 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
   constexpr int PIECES = BN / CW;
   int acc = 0;
   uint32_t acc_phase = 0;
-  for (int tile_id = blockIdx.x; tile_id < num_tiles; tile_id += gridDim.x) {
+  const int num_units = num_tiles * ep.splits;
+  for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
     int mb, nb;
-    tile_coords(tile_id, num_m, num_n, mb, nb);
+    tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
+    const int out_row0 = (unit % ep.splits) * ep.split_rows + mb * BM + quarter * 32;
     if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 4)) break;
     tc_fence_after();
     const int row = mb * BM + row_in_tile;
@@ -261,7 +272,7 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
 #pragma unroll
       for (int s = 0; s < CW / 32; ++s) tmem_ld_32x32b_x32(taddr + 32 * s, v + 32 * s);
       if (ep.tma_d) {
-        epilogue_piece_tma<CW>(ep, map_d, map_aux, tile, lane, row, M, col0, N, mb * BM + quarter * 32, alpha, v);
+        epilogue_piece_tma<CW>(ep, map_d, map_aux, tile, lane, row, M, col0, N, out_row0, alpha, v);
       } else if (row < M) {
 #pragma unroll
         for (int s = 0; s < CW / 32; ++s)
@@ -303,6 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int num_m = (M + BM - 1) / BM;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
+  const int num_units = num_tiles * ep.splits;
   const int kblocks = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -331,11 +343,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+    for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+      int mb, nb, kb0, kb1;
+      tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
+      split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
       const int m0 = mb * BM, n0 = nb * BN;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, 1)) {
           ok = false;
           break;
@@ -373,11 +386,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+      int kb0, kb1;
+      split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
       if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, err, 2)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full_bar[stage], phase, err, 3)) {
           ok = false;
           break;
@@ -392,7 +407,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                         : umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, BK * 128, 1024)
                                         : umma_desc_sw128(b_addr + k * 32, 16, 1024);
-            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           tc_commit(&empty_bar[stage]);
         }
@@ -422,6 +437,58 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// D = beta * D + sum over s of W[s] (fixed order), W: fp32 [splits, split_rows, ldw].
+template <typename DT>
+__global__ void split_reduce_kernel(const float* __restrict__ w, DT* __restrict__ d, int M, int N, long long ldd, int ldw,
+                                    int splits, long long split_stride, float beta) {
+  const long long n4 = (N + 3) / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)M * n4; i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / n4);
+    const int c = (int)(i - (long long)m * n4) * 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sidx = 0; sidx < splits; ++sidx) {
+      const float4 v = *reinterpret_cast<const float4*>(w + sidx * split_stride + (long long)m * ldw + c);
+      acc[0] += v.x;
+      acc[1] += v.y;
+      acc[2] += v.z;
+      acc[3] += v.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (c + e < N) {
+        DT* p = d + (long long)m * ldd + c + e;
+        float o = acc[e];
+        if constexpr (std::is_same<DT, float>::value) {
+          if (beta != 0.f) o += beta * *p;
+          *p = o;
+        } else {
+          if (beta != 0.f) o += beta * bf2f(*p);
+          *p = f2bf(o);
+        }
+      }
+    }
+  }
+}
+
+// Split factor for a GEMM with `tiles` output tiles: the factor (<= 16, >= 4 K-blocks each) that
+// fills the most SMs in its last wave; 1 when the tiles already fill the GPU.
+static int choose_splits(int tiles, int kblocks, int sms) {
+  if (tiles * 2 > sms || kblocks < 8) return 1;
+  int best = 1;
+  double best_eff = (double)tiles / (double)(((tiles + sms - 1) / sms) * sms);
+  for (int sp = 2; sp <= 16; ++sp) {
+    const int per = (kblocks + sp - 1) / sp;
+    if (per < 4 || (sp - 1) * per >= kblocks) break;
+    const int units = tiles * sp;
+    const double eff = (double)units / (double)(((units + sms - 1) / sms) * sms);
+    if (eff > best_eff + 0.02) {
+      best = sp;
+      best_eff = eff;
+    }
+  }
+  return best;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -498,8 +565,8 @@ static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
     HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     configured = true;
   }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = std::min(tiles, num_sms());
+  const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * ep.splits;
+  const int grid = std::min(units, num_sms());
   kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, md, maux, M, N, K, ep, err);
   HT_CUDA_CHECK(cudaGetLastError());
 }
@@ -555,10 +622,26 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   const CUtensorMap mb = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64)
                                     : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
   // TMA output path: aligned rows, and a store or an fp32 accumulate (beta = 1); the GELU
-  // pre-activation is written through its own map when D is bf16.
+  // pre-activation is written through its own map when D is bf16.  GEMMs with too few output
+  // tiles to fill the GPU (weight gradients: small M x N, long K) split K over several CTAs
+  // that store fp32 partial tiles into a workspace, summed in a fixed order afterwards.
   CUtensorMap md{}, maux{};
-  const bool tma_out = ep.vec_ok && (beta == 0.0 || (beta == 1.0 && d32)) && !(epilogue == kGelu && d32);
-  if (tma_out) {
+  ep.splits = 1;
+  const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
+  const int kblocks = (int)((K + BK - 1) / BK);
+  const int splits = (epilogue == kPlain && ep.bias_f32 == nullptr && ep.bias_bf16 == nullptr) ? choose_splits(tiles, kblocks, num_sms()) : 1;
+  at::Tensor workspace;
+  const int64_t split_rows = (M + BM - 1) / BM * BM, ldw = (N + 3) / 4 * 4;
+  if (splits > 1) {
+    workspace = at::empty({splits * split_rows, ldw}, a.options().dtype(at::kFloat));
+    md = make_out_map(workspace.data_ptr(), splits * split_rows, N, ldw, true);
+    ep.splits = splits;
+    ep.split_rows = (int)split_rows;
+    ep.tma_d = 1;
+    ep.reduce_add = 0;
+    ep.d_fp32 = 1;
+    ep.beta = 0.f;
+  } else if (ep.vec_ok && (beta == 0.0 || (beta == 1.0 && d32)) && !(epilogue == kGelu && d32)) {
     md = make_out_map(d.data_ptr(), M, N, d.stride(0), d32);
     if (epilogue == kGelu) maux = make_out_map(aux->data_ptr(), M, N, aux->stride(0), false);
     ep.tma_d = 1;
@@ -571,6 +654,18 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, md, maux, M, N, K, ep, err, s);
   else if (a_mn_major && b_mn_major) launch<true, true>(ma, mb, md, maux, M, N, K, ep, err, s);
   else launch<true, false>(ma, mb, md, maux, M, N, K, ep, err, s);
+  if (splits > 1) {
+    const long long work = M * ((N + 3) / 4);
+    const int blocks = (int)std::min<long long>((work + 255) / 256, 8LL * num_sms());
+    if (d32)
+      split_reduce_kernel<float><<<blocks, 256, 0, s>>>(workspace.data_ptr<float>(), d.data_ptr<float>(), (int)M, (int)N, d.stride(0),
+                                                        (int)ldw, splits, split_rows * ldw, (float)beta);
+    else
+      split_reduce_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(workspace.data_ptr<float>(),
+                                                                reinterpret_cast<__nv_bfloat16*>(d.data_ptr()), (int)M, (int)N,
+                                                                d.stride(0), (int)ldw, splits, split_rows * ldw, (float)beta);
+    HT_CUDA_CHECK(cudaGetLastError());
+  }
 }
 
 at::Tensor gemm_error_word(at::Tensor like) { return at::from_blob(tcg::error_word(like.device()), {4}, like.options().dtype(at::kInt)); }

@@ -6,6 +6,11 @@
 //   y = r * rstd * w                     (RMSNorm)
 // Backward (a grid of CTAs strides over rows; each keeps its columns' dw/db partial sums in
 // registers and writes one partial row per CTA, reduced by sum_rows):
+//
+// Two implementations: for the common case (hidden size a multiple of 4 and at most 1024, fp32
+// weight, bf16 branch tensors) one warp owns a row, loads and stores 16-byte (fp32) or 8-byte
+// (bf16) vectors and reduces with shuffles only; every other case uses a CTA per row with eight
+// scalar elements per thread.
 //   xhat = (r - mean) * rstd, g = dy * w
 //   dr_total = rstd * (g - mean(g) - xhat * mean(g * xhat)) + dr_in      (LayerNorm)
 //   dr_total = rstd * (g - xhat * mean(g * xhat)) + dr_in                 (RMSNorm)
@@ -13,6 +18,9 @@
 #include "common.cuh"
 
 namespace ht {
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 namespace norm {
 
 constexpr int VPT = 8;  // elements per thread
@@ -134,13 +142,210 @@ __global__ void norm_backward_kernel(const DyT* __restrict__ dy, const float* __
   }
 }
 
-// out[c] = sum_b part[b, c] + beta * out[c]
-__global__ void sum_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows, int d, float beta) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= d) return;
+// ---------------------------------------------------------------------------------------------
+// Warp-per-row kernels (hidden size d % 4 == 0, d <= 32 * 4 * NV).
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void ld4(const float* p, float* v) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+__device__ __forceinline__ void ld4(const __nv_bfloat16* p, float* v) {
+  const uint2 a = *reinterpret_cast<const uint2*>(p);
+  const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.x));
+  const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.y));
+  v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+}
+__device__ __forceinline__ void st4(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void st4(__nv_bfloat16* p, const float* v) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 a;
+  a.x = *reinterpret_cast<uint32_t*>(&lo);
+  a.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p) = a;
+}
+
+constexpr int WARP_ROWS_THREADS = 256;
+
+// Lane `l` owns the 4-element vectors l, l + 32, ..., l + 32 * (NV - 1) of every row it visits.
+template <bool RMS, bool HAS_DELTA, int NV>
+__global__ void __launch_bounds__(WARP_ROWS_THREADS)
+    norm_forward_warp_kernel(const float* __restrict__ res, const __nv_bfloat16* __restrict__ delta, const float* __restrict__ w,
+                             const float* __restrict__ b, float* __restrict__ r_out, __nv_bfloat16* __restrict__ y,
+                             float* __restrict__ mean_out, float* __restrict__ rstd_out, int rows, int d, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = d >> 2;
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  float wv[NV][4], bv[NV][4];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = lane + 32 * j;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) wv[j][e] = bv[j][e] = 0.f;
+    if (v < nvec) {
+      ld4(w + 4 * v, wv[j]);
+      if (!RMS && b != nullptr) ld4(b + 4 * v, bv[j]);
+    }
+  }
+  for (int row = warp_global; row < rows; row += warps) {
+    const long long base = (long long)row * d;
+    float x[NV][4];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = lane + 32 * j;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[j][e] = 0.f;
+      if (v < nvec) {
+        ld4(res + base + 4 * v, x[j]);
+        if (HAS_DELTA) {
+          float t[4];
+          ld4(delta + base + 4 * v, t);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[j][e] += t[e];
+        }
+        st4(r_out + base + 4 * v, x[j]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s += x[j][e];
+      }
+    }
+    const float mean = RMS ? 0.f : warp_sum(s) / d;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      if (lane + 32 * j < nvec) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float t = x[j][e] - mean;
+          q += t * t;
+        }
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(q) / d + eps);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = lane + 32 * j;
+      if (v < nvec) {
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = (x[j][e] - mean) * rstd * wv[j][e] + bv[j][e];
+        st4(y + base + 4 * v, o);
+      }
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+// Every CTA writes one full partial row of dw (and db): zeros for columns it never touched.
+template <bool RMS, bool HAS_DY, bool HAS_DR, int NV>
+__global__ void __launch_bounds__(WARP_ROWS_THREADS, 1)
+    norm_backward_warp_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ dr_in, const float* __restrict__ r,
+                              const float* __restrict__ w, const float* __restrict__ mean, const float* __restrict__ rstd,
+                              float* __restrict__ dres, __nv_bfloat16* __restrict__ ddelta, float* __restrict__ part_w,
+                              float* __restrict__ part_b, int rows, int d) {
+  extern __shared__ float red[];  // [WARP_ROWS_THREADS / 32][d]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = d >> 2;
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  float wv[NV][4], aw[NV][4], ab[NV][4];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) wv[j][e] = aw[j][e] = ab[j][e] = 0.f;
+    if (lane + 32 * j < nvec) ld4(w + 4 * (lane + 32 * j), wv[j]);
+  }
+  for (int row = warp_global; row < rows; row += warps) {
+    const long long base = (long long)row * d;
+    const float mu = RMS ? 0.f : mean[row], rs = rstd[row];
+    float xh[NV][4], g[NV][4];
+    float sg = 0.f, sgx = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = lane + 32 * j;
+      float rv[4] = {0.f, 0.f, 0.f, 0.f}, gy[4] = {0.f, 0.f, 0.f, 0.f};
+      if (v < nvec) {
+        ld4(r + base + 4 * v, rv);
+        if (HAS_DY) ld4(dy + base + 4 * v, gy);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float xhat = v < nvec ? (rv[e] - mu) * rs : 0.f;
+        xh[j][e] = xhat;
+        g[j][e] = gy[e] * wv[j][e];
+        aw[j][e] += gy[e] * xhat;
+        ab[j][e] += gy[e];
+        sg += g[j][e];
+        sgx += g[j][e] * xhat;
+      }
+    }
+    const float mg = RMS ? 0.f : warp_sum(sg) / d;
+    const float mgx = warp_sum(sgx) / d;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = lane + 32 * j;
+      if (v < nvec) {
+        float o[4], din[4] = {0.f, 0.f, 0.f, 0.f};
+        if (HAS_DR) ld4(dr_in + base + 4 * v, din);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = rs * (g[j][e] - mg - xh[j][e] * mgx) + din[e];
+        st4(dres + base + 4 * v, o);
+        if (ddelta != nullptr) st4(ddelta + base + 4 * v, o);
+      }
+    }
+  }
+  // CTA reduction of the per-warp partial sums, in a fixed order.
+  constexpr int WARPS = WARP_ROWS_THREADS / 32;
+  for (int pass = 0; pass < (part_b != nullptr ? 2 : 1); ++pass) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = lane + 32 * j;
+      if (v < nvec) st4(red + warp * d + 4 * v, pass == 0 ? aw[j] : ab[j]);
+    }
+    __syncthreads();
+    float* dst = pass == 0 ? part_w : part_b;
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < WARPS; ++k) t += red[k * d + c];
+      dst[(long long)blockIdx.x * d + c] = t;
+    }
+    __syncthreads();
+  }
+}
+
+// out[c] = sum_b part[b, c] + beta * out[c]: 32 columns per CTA, 8 row groups summed in a fixed
+// order through shared memory.
+__global__ void __launch_bounds__(256) sum_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows, int d,
+                                                       float beta) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.f;
-  for (int r = 0; r < nrows; ++r) s += part[(long long)r * d + c];
-  out[c] = s + (beta != 0.f ? beta * out[c] : 0.f);
+  if (c < d) {
+#pragma unroll 4
+    for (int r = ty; r < nrows; r += 8) s += part[(long long)r * d + c];
+  }
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][tx];
+    out[c] = t + (beta != 0.f ? beta * out[c] : 0.f);
+  }
+}
+
+// Vectors of 4 per lane for the warp-per-row kernels (2, 4, 6 or 8), or 0 when d does not fit.
+inline int warp_vectors(int d) {
+  if (d % 4 != 0 || d > 32 * 4 * 8) return 0;
+  const int nv = (d / 4 + 31) / 32;
+  return nv <= 2 ? 2 : (nv + 1) / 2 * 2;
 }
 
 inline int threads_for(int d) {
@@ -175,6 +380,38 @@ void norm_forward(at::Tensor res, c10::optional<at::Tensor> delta, at::Tensor w,
   if (rows == 0) return;
   const int threads = norm::threads_for(d);
   cudaStream_t s = stream();
+  const bool delta_ok = !has_delta || (delta->scalar_type() == at::kBFloat16 && aligned16(delta->data_ptr()));
+  const int nv = norm::warp_vectors(d);
+  if (nv > 0 && delta_ok && w.scalar_type() == at::kFloat && (!has_b || b->scalar_type() == at::kFloat) &&
+      y.scalar_type() == at::kBFloat16 && y.is_contiguous() && r_out.is_contiguous() && aligned16(res.data_ptr()) &&
+      aligned16(r_out.data_ptr()) && aligned16(y.data_ptr()) && aligned16(w.data_ptr()) &&
+      (!has_b || aligned16(b->data_ptr()))) {
+    const int blocks = (int)std::min<int64_t>((rows + 7) / 8, 16LL * num_sms());
+    auto go = [&](auto rms_tag, auto delta_tag, auto nv_tag) {
+      norm::norm_forward_warp_kernel<decltype(rms_tag)::value, decltype(delta_tag)::value, decltype(nv_tag)::value>
+          <<<blocks, norm::WARP_ROWS_THREADS, 0, s>>>(
+              res.data_ptr<float>(), has_delta ? reinterpret_cast<const __nv_bfloat16*>(delta->data_ptr()) : nullptr,
+              w.data_ptr<float>(), has_b ? b->data_ptr<float>() : nullptr, r_out.data_ptr<float>(),
+              reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, d,
+              static_cast<float>(eps));
+    };
+    auto with_nv = [&](auto rms_tag, auto delta_tag) {
+      switch (nv) {
+        case 2: go(rms_tag, delta_tag, std::integral_constant<int, 2>{}); break;
+        case 4: go(rms_tag, delta_tag, std::integral_constant<int, 4>{}); break;
+        case 6: go(rms_tag, delta_tag, std::integral_constant<int, 6>{}); break;
+        default: go(rms_tag, delta_tag, std::integral_constant<int, 8>{}); break;
+      }
+    };
+    auto with_delta = [&](auto rms_tag) {
+      if (has_delta) with_nv(rms_tag, std::true_type{});
+      else with_nv(rms_tag, std::false_type{});
+    };
+    if (rms) with_delta(std::true_type{});
+    else with_delta(std::false_type{});
+    HT_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   auto launch = [&](auto rms_tag, auto* delta_ptr, auto* w_ptr, auto* y_ptr) {
     using DeltaT = std::remove_const_t<std::remove_pointer_t<decltype(delta_ptr)>>;
     using WT = std::remove_const_t<std::remove_pointer_t<decltype(w_ptr)>>;
@@ -216,6 +453,41 @@ void norm_backward(c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dr, a
   const float* drp = (dr.has_value() && dr->defined()) ? dr->data_ptr<float>() : nullptr;
   float* pbp = (part_b.has_value() && part_b->defined()) ? part_b->data_ptr<float>() : nullptr;
   const bool has_dd = ddelta.has_value() && ddelta->defined();
+  const int nv = norm::warp_vectors(d);
+  if (nv > 0 && (!has_dy || (dy->scalar_type() == at::kBFloat16 && aligned16(dy->data_ptr()))) &&
+      (!has_dd || (ddelta->scalar_type() == at::kBFloat16 && aligned16(ddelta->data_ptr()))) &&
+      (drp == nullptr || aligned16(drp)) && w.scalar_type() == at::kFloat && aligned16(w.data_ptr()) &&
+      aligned16(r.data_ptr()) && aligned16(dres.data_ptr())) {
+    const size_t smem = (size_t)(norm::WARP_ROWS_THREADS / 32) * d * sizeof(float);
+    auto go = [&](auto rms_tag, auto dy_tag, auto dr_tag, auto nv_tag) {
+      auto kernel = norm::norm_backward_warp_kernel<decltype(rms_tag)::value, decltype(dy_tag)::value,
+                                                    decltype(dr_tag)::value, decltype(nv_tag)::value>;
+      kernel<<<blocks, norm::WARP_ROWS_THREADS, smem, s>>>(
+          has_dy ? reinterpret_cast<const __nv_bfloat16*>(dy->data_ptr()) : nullptr, drp, r.data_ptr<float>(),
+          w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), dres.data_ptr<float>(),
+          has_dd ? reinterpret_cast<__nv_bfloat16*>(ddelta->data_ptr()) : nullptr, part_w.data_ptr<float>(), pbp, rows, d);
+    };
+    auto with_nv = [&](auto rms_tag, auto dy_tag, auto dr_tag) {
+      switch (nv) {
+        case 2: go(rms_tag, dy_tag, dr_tag, std::integral_constant<int, 2>{}); break;
+        case 4: go(rms_tag, dy_tag, dr_tag, std::integral_constant<int, 4>{}); break;
+        case 6: go(rms_tag, dy_tag, dr_tag, std::integral_constant<int, 6>{}); break;
+        default: go(rms_tag, dy_tag, dr_tag, std::integral_constant<int, 8>{}); break;
+      }
+    };
+    auto with_dr = [&](auto rms_tag, auto dy_tag) {
+      if (drp != nullptr) with_nv(rms_tag, dy_tag, std::true_type{});
+      else with_nv(rms_tag, dy_tag, std::false_type{});
+    };
+    auto with_dy = [&](auto rms_tag) {
+      if (has_dy) with_dr(rms_tag, std::true_type{});
+      else with_dr(rms_tag, std::false_type{});
+    };
+    if (rms) with_dy(std::true_type{});
+    else with_dy(std::false_type{});
+    HT_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   auto launch = [&](auto rms_tag, auto* dy_ptr, auto* w_ptr, auto* dd_ptr) {
     using DyT = std::remove_const_t<std::remove_pointer_t<decltype(dy_ptr)>>;
     using WT = std::remove_const_t<std::remove_pointer_t<decltype(w_ptr)>>;
@@ -249,7 +521,8 @@ void sum_rows(at::Tensor part, at::Tensor out, double beta) {
   HT_CHECK(part.scalar_type() == at::kFloat && out.scalar_type() == at::kFloat && out.is_contiguous(), "sum_rows takes fp32");
   const int nrows = part.size(0), d = part.size(1);
   HT_CHECK(out.numel() == d, "sum_rows output size mismatch");
-  norm::sum_rows_kernel<<<(d + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), out.data_ptr<float>(), nrows, d,
+  HT_CHECK(part.is_contiguous() && part.dim() == 2, "sum_rows takes a contiguous [rows, d] tensor");
+  norm::sum_rows_kernel<<<(d + 31) / 32, 256, 0, stream()>>>(part.data_ptr<float>(), out.data_ptr<float>(), nrows, d,
                                                                static_cast<float>(beta));
   HT_CUDA_CHECK(cudaGetLastError());
 }

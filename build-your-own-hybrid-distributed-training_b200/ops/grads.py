@@ -29,11 +29,15 @@ def main_grad_beta(param: torch.Tensor) -> float:
 
 
 def deliver_grad(param: torch.Tensor, compute: Callable[[torch.Tensor, float], None] | None = None,
-                 value: torch.Tensor | None = None) -> torch.Tensor | None:
+                 value: torch.Tensor | None = None, *, native: bool = True) -> torch.Tensor | None:
     """Write a weight gradient into ``param.main_grad`` (or return ``value`` for autograd).
 
     ``compute(out, beta)`` must write ``out = grad + beta * out``; when it is
-    not given, ``value`` is copied or added.
+    not given, ``value`` is copied or added.  A parameter used by several native
+    ops in one backward (a tied embedding/head weight) declares the count in
+    ``param.native_grad_uses``; ``grad_ready_hook`` then runs after the last of
+    those deliveries.  Deliveries of autograd-accumulated gradients
+    (``native=False``) already hold every contribution.
     """
     main = getattr(param, "main_grad", None)
     if main is None:
@@ -48,6 +52,13 @@ def deliver_grad(param: torch.Tensor, compute: Callable[[torch.Tensor, float], N
     else:
         main.add_(value.reshape(main.shape))
     param.main_grad_fresh = False
+    uses = getattr(param, "native_grad_uses", 1) if native else 1
+    if uses > 1:
+        seen = getattr(param, "_native_deliveries", 0) + 1
+        if seen < uses:
+            param._native_deliveries = seen
+            return None
+        param._native_deliveries = 0
     hook = getattr(param, "grad_ready_hook", None)
     if hook is not None:
         hook(param)
@@ -59,3 +70,5 @@ def reset_main_grad_state(params: list[torch.Tensor]) -> None:
     for p in params:
         if getattr(p, "main_grad", None) is not None:
             p.main_grad_fresh = True
+        if getattr(p, "_native_deliveries", 0):
+            p._native_deliveries = 0

@@ -129,12 +129,17 @@ def compute_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return weight.detach().to(dtype)
 
 
-def _column_sum(x: torch.Tensor) -> torch.Tensor:
-    """fp32 sum over rows (the bias gradient)."""
+def _column_sum(x: torch.Tensor, out: torch.Tensor | None = None, beta: float = 0.0) -> torch.Tensor:
+    """fp32 sum over rows (the bias gradient), written as ``out = sum + beta * out``."""
     if not x.is_cuda:
-        return x.float().sum(0)
-    out = torch.empty(x.shape[1], dtype=torch.float32, device=x.device)
-    extension().column_sum(x, out)
+        s = x.float().sum(0)
+        if out is None:
+            return s
+        out.mul_(beta).add_(s) if beta else out.copy_(s)
+        return out
+    if out is None:
+        out = torch.empty(x.shape[1], dtype=torch.float32, device=x.device)
+    extension().column_sum(x, out, float(beta))
     return out
 
 
@@ -176,7 +181,8 @@ class _LinearFunction(torch.autograd.Function):
                               value=None if getattr(weight, "main_grad", None) is not None else
                               gemm(g, x2, out_dtype=weight.dtype, a_mn_major=True, b_mn_major=True))
         if bias is not None and ctx.needs_input_grad[2]:
-            db = deliver_grad(bias, value=_column_sum(g).to(bias.dtype))
+            db = deliver_grad(bias, compute=lambda out, beta: _column_sum(g, out, beta),
+                              value=None if getattr(bias, "main_grad", None) is not None else _column_sum(g).to(bias.dtype))
         return dx, dw, db, None
 
 

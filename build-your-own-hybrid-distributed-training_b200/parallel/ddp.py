@@ -249,7 +249,7 @@ class DistributedDataParallel(nn.Module):
 
         grad = param.grad
         param.grad = None
-        deliver_grad(param, value=grad.detach().to(param.main_grad.dtype))
+        deliver_grad(param, value=grad.detach().to(param.main_grad.dtype), native=False)
 
     def _on_grad_ready(self, param: torch.Tensor) -> None:
         if not self._require_backward_grad_sync:

@@ -97,6 +97,13 @@ def build_model(config: ExperimentConfig, context: DistributedContext, *, device
     sequence = context.group("sequence_effective")
     sp = config.topology.sequence_parallel_enabled
     if config.model.kind == "transformer":
+        if device.type == "cuda" and config.mixed_precision.compute_dtype != torch.bfloat16:
+            raise ConfigurationError(format_error(
+                "hybrid.build_model", "the transformer's CUDA kernels (tcgen05 GEMMs, attention, fused norms) compute in "
+                "bf16 with fp32 master weights", rank=context.rank, world_size=context.world_size,
+                expected="mixed_precision.enabled=True with param_dtype='bfloat16' on CUDA",
+                observed=str(config.mixed_precision.compute_dtype),
+                resolution="enable bf16 mixed precision (fp32 compute is available on the CPU path)"))
         plan = ParallelPlan(tensor_group=tensor, sequence_group=sequence, sequence_parallel=sp, vocab_parallel=tensor.size > 1)
         return TinyTransformer(config.model, plan, seed=config.training.seed, device=device,
                                compute_dtype=config.mixed_precision.compute_dtype)

@@ -201,3 +201,65 @@ def engine_worker(rank: int, world: int, overrides: dict[str, Any], steps: int, 
         return out
     finally:
         ctx.shutdown()
+
+
+def _cuda_experiment(world: int, *, fused: bool = True, steps: int = 3) -> dict[str, Any]:
+    return {"name": "multigpu-test", "backend": "nccl", "device": "cuda", "timeout_seconds": 120.0,
+            "topology": {"data_parallel_size": world},
+            "model": {"kind": "transformer", "hidden_size": 128, "num_layers": 2, "num_heads": 2, "vocab_size": 512,
+                      "max_sequence_length": 64},
+            "data": {"micro_batch_size": 4, "sequence_length": 64, "num_train_samples": 4096, "num_eval_samples": 0,
+                     "shuffle": False},
+            "optimizer": {"learning_rate": 1e-3},
+            "mixed_precision": {"enabled": True, "param_dtype": "bfloat16"},
+            "ddp": {"bucket_cap_mb": 0.05, "fused_allreduce": fused},
+            "training": {"max_steps": steps, "log_every_steps": 0}}
+
+
+def bucket_allreduce_worker(rank: int, world: int) -> dict[str, Any]:
+    """In-kernel bucket all-reduce over NVLink peer memory against NCCL's all-reduce (average)."""
+    import torch.distributed as dist
+
+    from hybrid_training.ops.comm import bucket_all_reduce
+
+    cfg = ExperimentConfig.from_dict(_cuda_experiment(world))
+    ctx = init_distributed(cfg)
+    try:
+        ws = ctx.symmetric_workspace("data_parallel")
+        assert ws is not None, "symmetric memory is unavailable"
+        numel = 3_000_011
+        flat = ws.allocate(numel + 5, torch.float32)
+        gen = torch.Generator(device="cuda").manual_seed(100 + rank)
+        errors = []
+        for start, n in ((0, numel), (4, 1001), (1024, 17), (8, 2_000_000)):
+            flat.normal_(generator=gen)
+            expect = flat[start:start + n].clone()
+            dist.all_reduce(expect, op=dist.ReduceOp.SUM, group=ctx.group("data_parallel").process_group)
+            expect /= world
+            outside = torch.cat([flat[:start], flat[start + n:]]).clone()
+            bucket_all_reduce(ws, flat, start, n, 1.0 / world)
+            torch.cuda.synchronize()
+            ws.check_status()
+            errors.append(float((flat[start:start + n] - expect).abs().max()))
+            assert torch.equal(torch.cat([flat[:start], flat[start + n:]]), outside), "wrote outside the bucket"
+        return {"errors": errors}
+    finally:
+        ctx.shutdown()
+
+
+def ddp_cuda_worker(rank: int, world: int, fused: bool, steps: int) -> dict[str, Any]:
+    """A few DDP steps on CUDA; returns the losses and the final parameters."""
+    cfg = ExperimentConfig.from_dict(_cuda_experiment(world, fused=fused, steps=steps))
+    ctx = init_distributed(cfg)
+    try:
+        engine = TrainingEngine(cfg, ctx)
+        ddp = getattr(engine.model, "_ddp", None)
+        used_fused = ddp is not None and getattr(ddp, "_workspace", None) is not None
+        engine.train(max_steps=steps)
+        full = engine.model.full_state_dict()
+        out = {"losses": [m.loss for m in engine.history], "fused": used_fused,
+               "full": {k: v.detach().float().cpu().clone() for k, v in full.items()}}
+        engine.close()
+        return out
+    finally:
+        ctx.shutdown()

@@ -66,6 +66,41 @@ def test_gemm_epilogues() -> None:
     assert _rel(out, ref_acc) < 1e-5
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_gemm_split_k_weight_gradient_shapes(out_dtype: torch.dtype) -> None:
+    """Few output tiles and a long K: the K loop is split and the partials are summed in order."""
+    ops = _ops()
+    dev = torch.device("cuda")
+    k, m, n = 4096, 296, 200
+    g = torch.randn(k, m, device=dev).bfloat16()
+    x = torch.randn(k, n, device=dev).bfloat16()
+    alpha = torch.tensor([0.25], device=dev)
+    c = torch.randn(m, n, device=dev).to(out_dtype)
+    out = c.clone()
+    ops.gemm(g, x, out=out, a_mn_major=True, b_mn_major=True, beta=1.0 if out_dtype == torch.float32 else 0.0, alpha=alpha)
+    ref, _ = ops.reference_gemm(g, x, a_mn_major=True, b_mn_major=True, c=c if out_dtype == torch.float32 else None,
+                                beta=1.0 if out_dtype == torch.float32 else 0.0, alpha=alpha)
+    assert _rel(out, ref) < (1e-5 if out_dtype == torch.float32 else 1e-2), _rel(out, ref)
+    again = c.clone()
+    ops.gemm(g, x, out=again, a_mn_major=True, b_mn_major=True, beta=1.0 if out_dtype == torch.float32 else 0.0, alpha=alpha)
+    assert torch.equal(again, out), "split-K result must be deterministic"
+
+
+def test_column_sum_and_sum_rows() -> None:
+    ops = _ops()
+    ext = ops.extension()
+    dev = torch.device("cuda")
+    for rows, cols, dt in ((8192, 768, torch.bfloat16), (1000, 3000, torch.bfloat16), (777, 130, torch.float32), (5, 7, torch.bfloat16)):
+        x = torch.randn(rows, cols, device=dev).to(dt)
+        out = torch.randn(cols, device=dev)
+        base = out.clone()
+        ext.column_sum(x, out, 1.0)
+        ref = x.float().sum(0) + base
+        assert _rel(out, ref) < 1e-5, (rows, cols, _rel(out, ref))
+        ext.column_sum(x, out, 0.0)
+        assert _rel(out, x.float().sum(0)) < 1e-5
+
+
 def test_gemm_padded_output_rows() -> None:
     ops = _ops()
     dev = torch.device("cuda")

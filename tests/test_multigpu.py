@@ -1,0 +1,35 @@
+"""Multi-GPU paths on real devices: the in-kernel NVLink bucket all-reduce and DDP training over NCCL.
+
+Each test spawns one process per GPU (two ranks) with the NCCL backend.  No rank is made to fail:
+fault handling is covered by the CPU (Gloo) tests.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from hybrid_training.distributed import launch_workers
+
+from . import dist_workers as W
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def test_in_kernel_bucket_all_reduce_matches_nccl() -> None:
+    results = launch_workers(W.bucket_allreduce_worker, 2, timeout_seconds=300,
+                             extra_env={"NCCL_NVLS_ENABLE": "0"})
+    for r in results:
+        for err in r.value["errors"]:
+            assert err < 1e-5, r.value["errors"]
+
+
+def test_ddp_fused_and_nccl_reductions_train_alike() -> None:
+    fused = launch_workers(W.ddp_cuda_worker, 2, args=(True, 3), timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    nccl = launch_workers(W.ddp_cuda_worker, 2, args=(False, 3), timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    assert fused[0].value["fused"] and not nccl[0].value["fused"]
+    # DDP keeps every replica identical.
+    for name, t in fused[0].value["full"].items():
+        assert torch.equal(t, fused[1].value["full"][name]), name
+    for a, b in zip(fused[0].value["losses"], nccl[0].value["losses"]):
+        assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (fused[0].value["losses"], nccl[0].value["losses"])
