@@ -15,6 +15,8 @@
 
 #include "common.cuh"
 
+#include <cstdlib>
+
 namespace ht {
 namespace attn {
 
@@ -502,11 +504,17 @@ static void attn_check(const at::Tensor& qkv, int64_t H, int64_t HKV, int64_t D)
   HT_CHECK(qkv.size(2) == (H + 2 * HKV) * D, "packed width mismatch");
 }
 
+bool attention_forward_tcgen05(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal,
+                               double scale);
+
 void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale) {
   attn_check(qkv, H, HKV, D);
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int B = qkv.size(0), S = qkv.size(1);
   if (B == 0 || S == 0) return;
+  // The tcgen05 kernel (attention_tcgen05.cu) covers contiguous, 16-byte aligned tensors; the
+  // mma.sync kernel below remains for any other layout.
+  if (std::getenv("HT_ATTN_MMA_SYNC") == nullptr && attention_forward_tcgen05(qkv, out, lse, H, HKV, D, causal, scale)) return;
   dim3 grid((S + attn::BQ - 1) / attn::BQ, H, B);
   const float sl2 = (float)scale * attn::LOG2E;
   const auto* q = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());

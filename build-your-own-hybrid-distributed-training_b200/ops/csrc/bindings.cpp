@@ -5,6 +5,7 @@ namespace ht {
 void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
           c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta);
 at::Tensor gemm_error_word(at::Tensor like);
+at::Tensor attention_error_word_tensor(at::Tensor like);
 void norm_forward(at::Tensor res, c10::optional<at::Tensor> delta, at::Tensor w, c10::optional<at::Tensor> b, at::Tensor r_out,
                   at::Tensor y, at::Tensor mean, at::Tensor rstd, double eps, bool rms);
 void norm_backward(c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dr, at::Tensor r, at::Tensor w, at::Tensor mean,
@@ -39,6 +40,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hybrid_training native kernels (sm_100a)";
   m.def("gemm", &ht::gemm, "tcgen05 GEMM with fused epilogue");
   m.def("gemm_error_word", &ht::gemm_error_word, "device error word written by timed-out GEMM waits");
+  m.def("attention_error_word", &ht::attention_error_word_tensor, "device error word written by timed-out attention waits");
   m.def("norm_forward", &ht::norm_forward);
   m.def("norm_backward", &ht::norm_backward);
   m.def("norm_backward_blocks", &ht::norm_backward_blocks);

@@ -140,20 +140,41 @@ def test_add_norm_forward_backward(rms: bool, d: int) -> None:
         assert _rel(b.grad, b_c.grad) < 1e-2
 
 
-@pytest.mark.parametrize("d,h,hkv,s", [(64, 4, 4, 128), (64, 4, 2, 100), (128, 4, 1, 192), (128, 2, 2, 64)])
-def test_attention_forward_backward(d: int, h: int, hkv: int, s: int) -> None:
+@pytest.mark.parametrize("d,h,hkv,s,causal", [(64, 4, 4, 128, True), (64, 4, 2, 100, True), (128, 4, 1, 192, True),
+                                               (128, 2, 2, 64, True), (64, 2, 1, 700, True), (64, 2, 2, 300, False),
+                                               (128, 2, 1, 260, False)])
+def test_attention_forward_backward(d: int, h: int, hkv: int, s: int, causal: bool) -> None:
     ops = _ops()
     dev = torch.device("cuda")
     bsz = 2
     qkv = (torch.randn(bsz, s, (h + 2 * hkv) * d, device=dev) * 0.5).bfloat16().requires_grad_(True)
-    out = ops.attention(qkv, h, hkv, d)
+    out = ops.attention(qkv, h, hkv, d, causal=causal)
     ref_in = qkv.detach().float().cpu().requires_grad_(True)
-    ref = ops.reference_attention(ref_in, h, hkv, d)
+    ref = ops.reference_attention(ref_in, h, hkv, d, causal=causal)
     assert _rel(out, ref) < 2e-2, _rel(out, ref)
     g = torch.randn_like(ref)
     out.backward(g.to(dev).bfloat16())
     ref.backward(g.bfloat16().float())
     assert _rel(qkv.grad, ref_in.grad) < 3e-2, _rel(qkv.grad, ref_in.grad)
+
+
+def test_attention_lse_and_error_word() -> None:
+    """The forward's log-sum-exp (used by the backward) and the kernel's timeout word."""
+    ops = _ops()
+    ext = ops.extension()
+    dev = torch.device("cuda")
+    b, s, h, hkv, d = 2, 384, 4, 2, 64
+    qkv = (torch.randn(b, s, (h + 2 * hkv) * d, device=dev) * 0.5).bfloat16()
+    out = torch.empty(b, s, h * d, device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(b, h, s, device=dev)
+    ext.attention_forward(qkv, out, lse, h, hkv, d, True, 1.0 / math.sqrt(d))
+    q = qkv[..., : h * d].float().view(b, s, h, d).transpose(1, 2)
+    k = qkv[..., h * d:(h + hkv) * d].float().view(b, s, hkv, d).transpose(1, 2).repeat_interleave(h // hkv, dim=1)
+    scores = (q @ k.transpose(-1, -2)) / math.sqrt(d)
+    scores = scores.masked_fill(torch.triu(torch.ones(s, s, dtype=torch.bool, device=dev), 1), float("-inf"))
+    ref = torch.logsumexp(scores, dim=-1)
+    assert float((lse - ref).abs().max()) < 1e-2
+    assert int(ext.attention_error_word(qkv).abs().sum()) == 0
 
 
 def test_head_cross_entropy_matches_torch() -> None:
