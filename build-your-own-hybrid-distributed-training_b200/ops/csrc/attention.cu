@@ -533,6 +533,9 @@ void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H
   HT_CUDA_CHECK(cudaGetLastError());
 }
 
+bool attention_backward_tcgen05(at::Tensor qkv, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv, int64_t H,
+                                int64_t HKV, int64_t D, bool causal, double scale);
+
 void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv,
                         int64_t H, int64_t HKV, int64_t D, bool causal, double scale) {
   attn_check(qkv, H, HKV, D);
@@ -550,8 +553,15 @@ void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Ten
   const int dgrid = (int)((rows * 32 + dthreads - 1) / dthreads);
   const float sl2 = (float)scale * attn::LOG2E;
   dim3 gq((S + attn::BQ - 1) / attn::BQ, H, B), gk((S + attn::BKV - 1) / attn::BKV, HKV, B);
+  if (D == 64) attn::delta_kernel<64><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
+  else attn::delta_kernel<128><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
+  // The tcgen05 kernels (attention_bwd_tcgen05.cu) cover contiguous, 16-byte aligned tensors.
+  if (std::getenv("HT_ATTN_MMA_SYNC") == nullptr &&
+      attention_backward_tcgen05(qkv, dout, lse, delta, dqkv, H, HKV, D, causal, scale)) {
+    HT_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   if (D == 64) {
-    attn::delta_kernel<64><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
     constexpr int smem_q = 6 * attn::BQ * 64 * 2;
     constexpr int smem_k = 6 * attn::BQ * 64 * 2 + 4 * attn::BQ * 4;
     static bool once = (attn::set_smem(attn::dq_kernel<64>, smem_q), attn::set_smem(attn::dkdv_kernel<64>, smem_k), true);
@@ -561,7 +571,6 @@ void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Ten
     attn::dkdv_kernel<64><<<gk, attn::THREADS, smem_k, s>>>(q, d, lse.data_ptr<float>(), delta.data_ptr<float>(), dq, S, H, HKV,
                                                             causal, (float)scale, sl2);
   } else {
-    attn::delta_kernel<128><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
     constexpr int smem_q = 6 * attn::BQ * 128 * 2;
     constexpr int smem_k = 6 * attn::BQ * 128 * 2 + 4 * attn::BQ * 4;
     static bool once = (attn::set_smem(attn::dq_kernel<128>, smem_q), attn::set_smem(attn::dkdv_kernel<128>, smem_k), true);
