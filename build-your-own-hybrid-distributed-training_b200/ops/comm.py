@@ -25,9 +25,10 @@ import torch
 
 from ._ext import extension
 
-__all__ = ["HAS_FUSED_TENSOR_PARALLEL", "all_gather_linear", "bucket_all_reduce", "linear_reduce_scatter"]
+__all__ = ["HAS_FUSED_TENSOR_PARALLEL", "all_gather_linear", "bucket_all_reduce", "can_fuse_sequence_parallel",
+           "linear_reduce_scatter"]
 
-HAS_FUSED_TENSOR_PARALLEL = False
+HAS_FUSED_TENSOR_PARALLEL = True
 _TIMEOUT_S = float(os.environ.get("HT_COLLECTIVE_TIMEOUT_S", "30"))
 
 
@@ -49,10 +50,209 @@ def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int
     return workspace.status
 
 
+class _TensorParallelSites:
+    """Per-group state of the fused tensor-parallel collectives.
+
+    * one peer-mapped int32 flag array ``[site][8]``: peer ``p`` writes the epoch it published
+      for a call site into word ``[site][p]`` of every other rank;
+    * one local int32 counter pair per site (epoch, completed CTAs), advanced on the device so
+      that replaying a captured CUDA graph advances it too;
+    * peer-mapped shard / receive buffers per call site, allocated on first use (every rank
+      reaches the same call sites in the same order, which keeps the collective allocation
+      and the site numbering aligned across ranks).
+    """
+
+    MAX_SITES = 512
+
+    def __init__(self, workspace: Any) -> None:
+        self.workspace = workspace
+        self.flags = workspace.allocate(self.MAX_SITES * 8, torch.int32)
+        self.flag_ptrs = [int(p) for p in workspace.handle_of(self.flags).buffer_ptrs]
+        self.counters = torch.zeros(self.MAX_SITES * 2, dtype=torch.int32, device=self.flags.device)
+        self.sites: dict[tuple[Any, str], int] = {}
+        self.buffers: dict[tuple[Any, str], tuple[torch.Tensor, list[int]]] = {}
+        self.rank = int(workspace.group.local_rank)
+        self.world = int(workspace.group.size)
+
+    def site(self, owner: Any, kind: str) -> int:
+        key = (owner, kind)
+        if key not in self.sites:
+            if len(self.sites) >= self.MAX_SITES:
+                raise RuntimeError("too many fused tensor-parallel call sites")
+            self.sites[key] = len(self.sites)
+        return self.sites[key]
+
+    def buffer(self, owner: Any, kind: str, shape: tuple[int, ...]) -> tuple[torch.Tensor, list[int]]:
+        key = (owner, kind)
+        numel = 1
+        for d in shape:
+            numel *= d
+        hit = self.buffers.get(key)
+        if hit is None or hit[0].numel() != numel:
+            t = self.workspace.allocate(numel, torch.bfloat16)
+            hit = (t, [int(p) for p in self.workspace.handle_of(t).buffer_ptrs])
+            self.buffers[key] = hit
+        return hit[0].view(shape), hit[1]
+
+
+_SITES: dict[int, _TensorParallelSites] = {}
+
+
+def _sites(workspace: Any) -> _TensorParallelSites:
+    st = _SITES.get(id(workspace))
+    if st is None:
+        st = _SITES[id(workspace)] = _TensorParallelSites(workspace)
+    return st
+
+
+def can_fuse_sequence_parallel(x: torch.Tensor, group: Any, *, sharded_rows: int, features: tuple[int, ...]) -> bool:
+    """Whether the fused kernels cover this call: bf16 on CUDA, 2..8 ranks, 128-row shards, 16-byte rows."""
+    return (x.is_cuda and x.dtype == torch.bfloat16 and 2 <= group.size <= 8 and sharded_rows % 128 == 0
+            and all(f % 8 == 0 for f in features))
+
+
+class _AllGatherLinear(torch.autograd.Function):
+    """``Y = AllGather_seq(X) W^T (+ b, GELU)`` with the gather inside the GEMM's operand loads."""
+
+    @staticmethod
+    def forward(ctx: Any, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, workspace: Any, owner: Any,
+                activation: str | None) -> torch.Tensor:
+        from .linear import EPI_GELU, EPI_PLAIN, compute_weight
+
+        st = _sites(workspace)
+        ext = extension()
+        b, r, k = x.shape
+        w = compute_weight(weight, x.dtype)
+        n = w.shape[0]
+        slot, ptrs = st.buffer(owner, "ag.x", (b, r, k))
+        slot.copy_(x)
+        site = st.site(owner, "ag")
+        y = torch.empty(b * r * st.world, n, dtype=x.dtype, device=x.device)
+        pre = torch.empty_like(y) if activation == "gelu" else None
+        ext.gemm_collective(slot, w, y, bias, pre, False, False, EPI_GELU if pre is not None else EPI_PLAIN, 0.0,
+                            1, ptrs, 0, [], 0, [], st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
+        ctx.save_for_backward(w, pre)
+        ctx.st, ctx.owner, ctx.site, ctx.shape = st, owner, site, (b, r, k)
+        ctx.weight, ctx.bias = weight, bias
+        return y.view(b, r * st.world, n)
+
+    @staticmethod
+    def backward(ctx: Any, dy: torch.Tensor) -> tuple[Any, ...]:
+        from .grads import deliver_grad
+        from .linear import EPI_PLAIN, _column_sum, gelu_backward
+
+        w, pre = ctx.saved_tensors
+        st, owner = ctx.st, ctx.owner
+        ext = extension()
+        b, r, k = ctx.shape
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        g = gelu_backward(dy2, pre) if pre is not None else dy2
+        dx = None
+        if ctx.needs_input_grad[0]:
+            recv, rptrs = st.buffer(owner, "ag.dx_recv", (st.world, b, r, k))
+            site = st.site(owner, "ag.rs")
+            ext.gemm_collective(g, w, recv, None, None, False, True, EPI_PLAIN, 0.0, 0, [], 0, [], 1, rptrs,
+                                st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
+            dx = torch.empty(b, r, k, dtype=dy.dtype, device=dy.device)
+            ext.reduce_scatter_sum(recv, dx, st.flags, st.counters, site, st.rank, _TIMEOUT_S)
+        slot, ptrs = st.buffer(owner, "ag.x", (b, r, k))
+        weight, bias = ctx.weight, ctx.bias
+
+        def wgrad(out: torch.Tensor, beta: float) -> None:
+            ext.gemm_collective(g, slot, out, None, None, True, True, EPI_PLAIN, float(beta), 0, [], 2, ptrs, 0, [],
+                                st.flags, st.flag_ptrs, st.counters, ctx.site, 0, st.rank, _TIMEOUT_S)
+
+        dw = None
+        if ctx.needs_input_grad[1]:
+            value = None
+            if getattr(weight, "main_grad", None) is None:
+                value = torch.empty(weight.shape, dtype=torch.float32, device=dy.device)
+                wgrad(value, 0.0)
+                value = value.to(weight.dtype)
+            dw = deliver_grad(weight, compute=wgrad if value is None else None, value=value)
+        db = None
+        if bias is not None and ctx.needs_input_grad[2]:
+            db = deliver_grad(bias, compute=lambda out, beta: _column_sum(g, out, beta),
+                              value=None if getattr(bias, "main_grad", None) is not None else _column_sum(g).to(bias.dtype))
+        return dx, dw, db, None, None, None
+
+
+class _LinearReduceScatter(torch.autograd.Function):
+    """``out = ReduceScatter_seq(X W^T)`` with the scatter inside the GEMM epilogue."""
+
+    @staticmethod
+    def forward(ctx: Any, x: torch.Tensor, weight: torch.Tensor, workspace: Any, owner: Any) -> torch.Tensor:
+        from .linear import EPI_PLAIN, compute_weight
+
+        st = _sites(workspace)
+        ext = extension()
+        b, s, kr = x.shape
+        r = s // st.world
+        w = compute_weight(weight, x.dtype)
+        n = w.shape[0]
+        x2 = x.reshape(b * s, kr).contiguous()
+        recv, rptrs = st.buffer(owner, "rs.recv", (st.world, b, r, n))
+        site = st.site(owner, "rs")
+        ext.gemm_collective(x2, w, recv, None, None, False, False, EPI_PLAIN, 0.0, 0, [], 0, [], 1, rptrs,
+                            st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
+        out = torch.empty(b, r, n, dtype=x.dtype, device=x.device)
+        ext.reduce_scatter_sum(recv, out, st.flags, st.counters, site, st.rank, _TIMEOUT_S)
+        ctx.save_for_backward(x2, w)
+        ctx.st, ctx.owner, ctx.dims, ctx.weight = st, owner, (b, s, kr, n), weight
+        return out
+
+    @staticmethod
+    def backward(ctx: Any, dout: torch.Tensor) -> tuple[Any, ...]:
+        from .grads import deliver_grad
+        from .linear import EPI_PLAIN
+
+        x2, w = ctx.saved_tensors
+        st, owner = ctx.st, ctx.owner
+        ext = extension()
+        b, s, kr, n = ctx.dims
+        r = s // st.world
+        slot, ptrs = st.buffer(owner, "rs.dout", (b, r, n))
+        slot.copy_(dout.reshape(b, r, n))
+        site = st.site(owner, "rs.ag")
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(b * s, kr, dtype=dout.dtype, device=dout.device)
+            ext.gemm_collective(slot, w, dx, None, None, False, True, EPI_PLAIN, 0.0, 1, ptrs, 0, [], 0, [],
+                                st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
+            advance = 0
+        else:
+            advance = 1
+        weight = ctx.weight
+
+        def wgrad(out: torch.Tensor, beta: float, adv: int = advance) -> None:
+            ext.gemm_collective(slot, x2, out, None, None, True, True, EPI_PLAIN, float(beta), 2, ptrs, 0, [], 0, [],
+                                st.flags, st.flag_ptrs, st.counters, site, adv, st.rank, _TIMEOUT_S)
+
+        dw = None
+        if ctx.needs_input_grad[1]:
+            value = None
+            if getattr(weight, "main_grad", None) is None:
+                value = torch.empty(weight.shape, dtype=torch.float32, device=dout.device)
+                wgrad(value, 0.0)
+                value = value.to(weight.dtype)
+            dw = deliver_grad(weight, compute=wgrad if value is None else None, value=value)
+        return (None if dx is None else dx.view(b, s, kr)), dw, None, None
+
+
 def all_gather_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, workspace: Any, group: Any, *,
-                      activation: str | None = None) -> torch.Tensor:
-    raise NotImplementedError("fused all-gather GEMM is not available in this build")
+                      activation: str | None = None, owner: Any = None) -> torch.Tensor | None:
+    """Column-parallel linear on a sequence-sharded ``x`` [B, S/T, K]; ``None`` when the fused kernel does not apply."""
+    if activation not in (None, "gelu") or x.dim() != 3:
+        return None
+    if not can_fuse_sequence_parallel(x, group, sharded_rows=x.shape[1], features=(x.shape[2], weight.shape[0])):
+        return None
+    return _AllGatherLinear.apply(x.contiguous(), weight, bias, workspace, owner if owner is not None else id(weight), activation)
 
 
-def linear_reduce_scatter(x: torch.Tensor, weight: torch.Tensor, workspace: Any, group: Any) -> torch.Tensor:
-    raise NotImplementedError("fused GEMM reduce-scatter is not available in this build")
+def linear_reduce_scatter(x: torch.Tensor, weight: torch.Tensor, workspace: Any, group: Any, *, owner: Any = None) -> torch.Tensor | None:
+    """Row-parallel linear whose output is reduce-scattered along the sequence; ``None`` when not applicable."""
+    if x.dim() != 3 or x.shape[1] % group.size:
+        return None
+    if not can_fuse_sequence_parallel(x, group, sharded_rows=x.shape[1] // group.size, features=(x.shape[2], weight.shape[0])):
+        return None
+    return _LinearReduceScatter.apply(x.contiguous(), weight, workspace, owner if owner is not None else id(weight))

@@ -5,6 +5,13 @@ namespace ht {
 void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
           c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta);
 at::Tensor gemm_error_word(at::Tensor like);
+void gemm_collective(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
+                     bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta, int64_t a_mode, std::vector<int64_t> a_ptrs,
+                     int64_t b_mode, std::vector<int64_t> b_ptrs, int64_t rs, std::vector<int64_t> out_ptrs, at::Tensor flags_local,
+                     std::vector<int64_t> flag_ptrs, at::Tensor counters, int64_t site, int64_t advance, int64_t rank,
+                     double timeout_s);
+void reduce_scatter_sum(at::Tensor recv, at::Tensor out, at::Tensor flags_local, at::Tensor counters, int64_t site, int64_t rank,
+                        double timeout_s);
 at::Tensor attention_error_word_tensor(at::Tensor like);
 void norm_forward(at::Tensor res, c10::optional<at::Tensor> delta, at::Tensor w, c10::optional<at::Tensor> b, at::Tensor r_out,
                   at::Tensor y, at::Tensor mean, at::Tensor rstd, double eps, bool rms);
@@ -40,6 +47,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hybrid_training native kernels (sm_100a)";
   m.def("gemm", &ht::gemm, "tcgen05 GEMM with fused epilogue");
   m.def("gemm_error_word", &ht::gemm_error_word, "device error word written by timed-out GEMM waits");
+  m.def("gemm_collective", &ht::gemm_collective, "GEMM with peer-sharded operands or a reduce-scatter epilogue");
+  m.def("reduce_scatter_sum", &ht::reduce_scatter_sum, "sum of the reduce-scatter receive slots");
   m.def("attention_error_word", &ht::attention_error_word_tensor, "device error word written by timed-out attention waits");
   m.def("norm_forward", &ht::norm_forward);
   m.def("norm_backward", &ht::norm_backward);

@@ -23,6 +23,8 @@
 
 #include "common.cuh"
 
+#include <cstring>
+
 namespace ht {
 namespace tcg {
 
@@ -60,6 +62,78 @@ struct EpiParams {
   int splits;      // split-K factor: work unit u covers tile u / splits, K-range u % splits
   int split_rows;  // rows per split slice of the fp32 workspace (split-K only)
 };
+
+// ------------------------------------------------------------------------------------------------
+// Collective mode (tensor / sequence parallelism over NVLink peer memory).
+//
+// Operand rows that are sequence positions may live on another GPU: every rank holds a shard of
+// `rows_per_rank` positions of each of the `batch` sequences in a peer-mapped buffer, and the
+// logical operand is the concatenation of the shards.  The producer warp then loads each tile
+// straight from the owner's shard with a (non-multicast) TMA load through that peer's tensor
+// map, after the owner has published the shard (a device-side epoch written into this rank's
+// flag word).  In reduce-scatter mode the epilogue stores every output tile into the receive
+// slot of the rank that owns its rows; the last CTA to finish publishes the epoch to all peers.
+// Epochs live in device memory, so the same launch can be replayed from a CUDA graph.
+// ------------------------------------------------------------------------------------------------
+constexpr int MAX_PEERS = 8;
+
+struct CollParams {
+  CUtensorMap a[MAX_PEERS];    // per-owner A shard maps (a_mode != 0)
+  CUtensorMap b[MAX_PEERS];    // per-owner B shard maps (b_mode != 0)
+  CUtensorMap out[MAX_PEERS];  // per-owner receive maps [world * batch][rows_per_rank][N] (rs)
+  uint32_t* flags_local;       // this rank's flag words [site][MAX_PEERS], written by the peers
+  uint32_t* flags_peer[MAX_PEERS];
+  uint32_t* epoch;             // this call site's epoch counter (local memory)
+  int* done;                   // this call site's completion counter (local memory)
+  int site;
+  int advance;                 // 1: a new collective call (epoch + 1, publish); 0: reuse the epoch
+  int a_mode;                  // 0 local; 1 owner by M block (K-major A); 2 owner by K block (MN-major A)
+  int b_mode;                  // 0 local; 2 owner by K block (MN-major B)
+  int rs;                      // epilogue writes rows into their owner's receive slot
+  int rank, world, batch, seq, rows_per_rank;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Owner rank, local row and sequence index of logical sequence row `g`.
+__device__ __forceinline__ void seq_owner(const CollParams& c, int g, int& owner, int& local_row, int& bidx) {
+  bidx = g / c.seq;
+  const int s = g - bidx * c.seq;
+  owner = s / c.rows_per_rank;
+  local_row = s - owner * c.rows_per_rank;
+}
+
+// Bounded wait until `owner` has published epoch `epoch` for this call site.
+__device__ __forceinline__ bool wait_published(const CollParams& c, int owner, uint32_t epoch, int* err) {
+  const uint32_t* f = c.flags_local + c.site * MAX_PEERS + owner;
+  const unsigned long long deadline = globaltimer_ns() + c.timeout_ns;
+  while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+    if (globaltimer_ns() > deadline || *((volatile int*)err) != 0) {
+      atomicCAS(err, 0, 40);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void publish_epoch(const CollParams& c, uint32_t epoch) {
+  __threadfence_system();
+  for (int q = 0; q < c.world; ++q)
+    if (q != c.rank) st_release_sys(c.flags_peer[q] + c.site * MAX_PEERS + c.rank, epoch);
+}
 
 // K-blocks [kb0, kb1) of work unit `split` when the K loop is split `splits` ways.
 __device__ __forceinline__ void split_range(int kblocks, int splits, int split, int& kb0, int& kb1) {
@@ -165,6 +239,11 @@ __device__ __forceinline__ void stage_row(uint8_t* tile, int r, const uint4* uni
   for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = units[j];
 }
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 __device__ __forceinline__ void pack_bf16x64(const float* v, uint4* units) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -180,7 +259,7 @@ __device__ __forceinline__ void pack_bf16x64(const float* v, uint4* units) {
 template <int CW>
 __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
                                                    uint8_t* tile, int lane, int row, int M, int col0, int N, int tile_row0,
-                                                   float alpha, float* v) {
+                                                   float alpha, float* v, int z = -1) {
   const bool full = col0 + CW <= N;
 #pragma unroll
   for (int i = 0; i < CW; ++i) {
@@ -237,7 +316,8 @@ __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CU
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    if (ep.reduce_add) tma_reduce_add_2d(map_d, tile, col0, tile_row0);
+    if (z >= 0) tma_store_3d(map_d, tile, col0, tile_row0, z);
+    else if (ep.reduce_add) tma_reduce_add_2d(map_d, tile, col0, tile_row0);
     else tma_store_2d(map_d, tile, col0, tile_row0);
     bulk_commit();
   }
@@ -247,7 +327,8 @@ __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CU
 template <int CW>
 __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
                                               uint8_t* tile, uint32_t tmem_base, uint64_t* tfull_bar, uint64_t* tempty_bar,
-                                              int M, int N, int num_m, int num_n, int num_tiles, int warp, int lane, int* err) {
+                                              int M, int N, int num_m, int num_n, int num_tiles, int warp, int lane, int* err,
+                                              const CollParams* coll = nullptr) {
   const int quarter = warp & 3;
   const int half = (warp - 2) >> 2;
   const int row_in_tile = quarter * 32 + lane;
@@ -259,7 +340,16 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
   for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
     int mb, nb;
     tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
-    const int out_row0 = (unit % ep.splits) * ep.split_rows + mb * BM + quarter * 32;
+    int out_row0 = (unit % ep.splits) * ep.split_rows + mb * BM + quarter * 32;
+    const CUtensorMap* dmap = map_d;
+    int z = -1;
+    if (coll != nullptr && coll->rs) {  // rows go to their owner's receive slot for this rank
+      int owner, lrow, bidx;
+      seq_owner(*coll, mb * BM, owner, lrow, bidx);
+      dmap = &coll->out[owner];
+      out_row0 = lrow + quarter * 32;
+      z = coll->rank * coll->batch + bidx;
+    }
     if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 4)) break;
     tc_fence_after();
     const int row = mb * BM + row_in_tile;
@@ -272,7 +362,7 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
 #pragma unroll
       for (int s = 0; s < CW / 32; ++s) tmem_ld_32x32b_x32(taddr + 32 * s, v + 32 * s);
       if (ep.tma_d) {
-        epilogue_piece_tma<CW>(ep, map_d, map_aux, tile, lane, row, M, col0, N, out_row0, alpha, v);
+        epilogue_piece_tma<CW>(ep, dmap, map_aux, tile, lane, row, M, col0, N, out_row0, alpha, v, z);
       } else if (row < M) {
 #pragma unroll
         for (int s = 0; s < CW / 32; ++s)
@@ -287,15 +377,22 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
       acc_phase ^= 1u;
     }
   }
-  if (lane == 0) bulk_wait_all();
+  if (lane == 0) {
+    bulk_wait_all();
+    if (coll != nullptr && coll->rs) {
+      // The stores went to peers' memory: order them before this CTA's completion signal at
+      // system scope (the publishing thread is another warp).
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __threadfence_system();
+    }
+  }
   __syncwarp();
 }
 
-template <bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
-                EpiParams ep, int* err) {
+template <bool A_MN, bool B_MN, bool COLL>
+__device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtensorMap& tma_b, const CUtensorMap& tma_d,
+                                          const CUtensorMap& tma_aux, int M, int N, int K, const EpiParams& ep, int* err,
+                                          const CollParams* coll) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -332,6 +429,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (ep.tma_d) prefetch_tensormap(&tma_d);
     if (ep.tma_aux) prefetch_tensormap(&tma_aux);
   }
+  uint32_t epoch = 0;
+  if constexpr (COLL) {
+    epoch = *((volatile uint32_t*)coll->epoch) + (uint32_t)coll->advance;
+    // Gather-side publication: this rank's shard (written by earlier work on this stream) is
+    // ready for the peers' loads.
+    if (blockIdx.x == 0 && threadIdx.x == 0 && coll->advance && !coll->rs && (coll->a_mode || coll->b_mode))
+      publish_epoch(*coll, epoch);
+  }
   if (warp == 1) tmem_alloc(&tmem_base_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -343,6 +448,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
+    uint32_t ready_mask = 0;
+    (void)ready_mask;
     for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
       int mb, nb, kb0, kb1;
       tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
@@ -353,7 +460,45 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        if (lane == 0) {
+        if (COLL && lane == 0) {
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          int a_owner = coll->rank, a_row = 0, a_b = 0, b_owner = coll->rank, b_row = 0, b_b = 0;
+          if (coll->a_mode == 1) seq_owner(*coll, m0, a_owner, a_row, a_b);
+          if (coll->a_mode == 2) seq_owner(*coll, k0, a_owner, a_row, a_b);
+          if (coll->b_mode == 2) seq_owner(*coll, k0, b_owner, b_row, b_b);
+          if (a_owner != coll->rank && !(ready_mask >> a_owner & 1u)) {
+            ok = wait_published(*coll, a_owner, epoch, err);
+            ready_mask |= 1u << a_owner;
+          }
+          if (ok && b_owner != coll->rank && !(ready_mask >> b_owner & 1u)) {
+            ok = wait_published(*coll, b_owner, epoch, err);
+            ready_mask |= 1u << b_owner;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
+          if (coll->a_mode == 1) {
+            tma_load_3d(a_dst, &coll->a[a_owner], &full_bar[stage], k0, a_row, a_b);
+          } else if (coll->a_mode == 2) {
+            tma_load_3d(a_dst, &coll->a[a_owner], &full_bar[stage], m0, a_row, a_b);
+            tma_load_3d(a_dst + BK * 128, &coll->a[a_owner], &full_bar[stage], m0 + 64, a_row, a_b);
+          } else if (A_MN) {
+            tma_load_2d(a_dst, &tma_a, &full_bar[stage], m0, k0);
+            tma_load_2d(a_dst + BK * 128, &tma_a, &full_bar[stage], m0 + 64, k0);
+          } else {
+            tma_load_2d(a_dst, &tma_a, &full_bar[stage], k0, m0);
+          }
+          if (coll->b_mode == 2) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(b_dst + j * BK * 128, &coll->b[b_owner], &full_bar[stage], n0 + 64 * j, b_row, b_b);
+          } else if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], n0 + 64 * j, k0);
+          } else {
+            tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, n0);
+          }
+        } else if (lane == 0) {
           uint8_t* a_dst = sA + stage * A_BYTES;
           uint8_t* b_dst = sB + stage * B_BYTES;
           const int k0 = kb * BK;
@@ -371,6 +516,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, n0);
           }
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
         __syncwarp();
         if (++stage == STAGES) {
           stage = 0;
@@ -429,14 +576,93 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- epilogue ----------------
     uint8_t* tile = sEpi + (warp - 2) * EPI_STAGE_BYTES;
     if (ep.d_fp32)
-      epilogue_loop<32>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err);
+      epilogue_loop<32>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err,
+                        COLL ? coll : nullptr);
     else
-      epilogue_loop<64>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err);
+      epilogue_loop<64>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err,
+                        COLL ? coll : nullptr);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  if constexpr (COLL) {
+    // Completion: the last CTA advances the call site's epoch and, in reduce-scatter mode,
+    // tells every peer that this rank's slots in their receive buffers are written.
+    if (threadIdx.x == 0 && coll->advance) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __threadfence_system();
+      if (atomicAdd(coll->done, 1) == (int)gridDim.x - 1) {
+        __threadfence_system();
+        if (coll->rs) publish_epoch(*coll, epoch);
+        *((volatile uint32_t*)coll->epoch) = epoch;
+        *((volatile int*)coll->done) = 0;
+        __threadfence();
+      }
+    }
+  }
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
+                EpiParams ep, int* err) {
+  gemm_body<A_MN, B_MN, false>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, nullptr);
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_coll_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
+                     EpiParams ep, int* err, const __grid_constant__ CollParams coll) {
+  gemm_body<A_MN, B_MN, true>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, &coll);
+}
+
+// out[b, r, n] = sum over ranks p (in order) of recv[p][b, r, n], after every peer has published
+// its slots for this call site's current epoch.  bf16 in/out, fp32 accumulation.
+__global__ void __launch_bounds__(256) rs_sum_kernel(const __nv_bfloat16* __restrict__ recv, __nv_bfloat16* __restrict__ out,
+                                                     long long slot_elems, int world, int rank, const uint32_t* flags_row,
+                                                     const uint32_t* epoch_ptr, unsigned long long timeout_ns, int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const uint32_t epoch = *((volatile const uint32_t*)epoch_ptr);
+    const unsigned long long deadline = globaltimer_ns() + timeout_ns;
+    int good = 1;
+    for (int p = 0; p < world && good; ++p) {
+      if (p == rank) continue;
+      while ((int)(ld_acquire_sys(flags_row + p) - epoch) < 0) {
+        if (globaltimer_ns() > deadline || *((volatile int*)err) != 0) {
+          atomicCAS(err, 0, 41);
+          good = 0;
+          break;
+        }
+      }
+    }
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const long long vecs = slot_elems / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < vecs; i += (long long)gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int p = 0; p < world; ++p) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(recv + p * slot_elems + i * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + i * 8) = o;
+  }
 }
 
 // D = beta * D + sum over s of W[s] (fixed order), W: fp32 [splits, split_rows, ldw].
@@ -666,6 +892,188 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
                                                                 d.stride(0), (int)ldw, splits, split_rows * ldw, (float)beta);
     HT_CUDA_CHECK(cudaGetLastError());
   }
+}
+
+namespace tcg {
+
+// bf16 [d2][d1][d0] map (d0 innermost, contiguous) with box {box0, box1, 1} and the 128-byte swizzle.
+static CUtensorMap make_map3(int64_t base, int64_t d0, int64_t d1, int64_t d2, int box0, int box1) {
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)(d0 * 2), (cuuint64_t)(d0 * d1 * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  HT_CHECK(base % 16 == 0 && (d0 * 2) % 16 == 0, "peer shard must be 16-byte aligned with 16-byte rows");
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, reinterpret_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  HT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (peer shard) failed with code ", (int)r);
+  return map;
+}
+
+template <bool A_MN, bool B_MN>
+static void launch_coll(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
+                        int N, int K, const EpiParams& ep, int* err, const CollParams& coll, cudaStream_t s) {
+  auto kernel = gemm_coll_kernel<A_MN, B_MN>;
+  static bool configured = false;
+  if (!configured) {
+    HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    configured = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms());
+  kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, md, maux, M, N, K, ep, err, coll);
+  HT_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace tcg
+
+// GEMM with operands gathered from, or results scattered to, the peers of a tensor-parallel group
+// (see CollParams).  a_mode 1: `a` is this rank's [B, R, K] shard of A (K-major, rows = sequence);
+// a_mode 2: `a` is the [B, R, M] shard of an MN-major A whose K dimension is the sequence;
+// b_mode 2: `b` is the [B, R, N] shard of an MN-major B whose K dimension is the sequence;
+// rs: `d` is this rank's receive buffer [world, B, R, N] and every output row goes to the slot
+// `rank` of its owner's buffer; otherwise `d` is a local [M, N] output as in `gemm`.
+void gemm_collective(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
+                     bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta, int64_t a_mode, std::vector<int64_t> a_ptrs,
+                     int64_t b_mode, std::vector<int64_t> b_ptrs, int64_t rs, std::vector<int64_t> out_ptrs, at::Tensor flags_local,
+                     std::vector<int64_t> flag_ptrs, at::Tensor counters, int64_t site, int64_t advance, int64_t rank,
+                     double timeout_s) {
+  using namespace tcg;
+  const c10::cuda::CUDAGuard guard(a.device());
+  bind_context(a.device().index());
+  const int world = (int)flag_ptrs.size();
+  HT_CHECK(world >= 2 && world <= MAX_PEERS, "gemm_collective supports 2..8 ranks");
+  HT_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_collective takes bf16 operands");
+  HT_CHECK(a_mode == 0 || a_mode == 1 || a_mode == 2, "bad a_mode");
+  HT_CHECK(b_mode == 0 || b_mode == 2, "bad b_mode");
+  HT_CHECK((a_mode == 2) == (a_mode == 2 && a_mn_major) && (a_mode != 1 || !a_mn_major), "a_mode and A majorness disagree");
+  HT_CHECK(b_mode != 2 || b_mn_major, "b_mode 2 needs an MN-major B");
+  int64_t batch = 0, rows = 0, M = 0, N = 0, K = 0;
+  const at::Tensor& sharded = a_mode ? a : (b_mode ? b : d);
+  if (a_mode || b_mode) {
+    HT_CHECK(sharded.dim() == 3 && sharded.is_contiguous(), "a peer-sharded operand must be a contiguous [B, R, C] shard");
+    batch = sharded.size(0);
+    rows = sharded.size(1);
+  } else {
+    HT_CHECK(rs && d.dim() == 4, "a local-only collective GEMM must reduce-scatter");
+    batch = d.size(1);
+    rows = d.size(2);
+  }
+  const int64_t total = batch * rows * world;
+  if (a_mode == 1) { M = total; K = a.size(2); }
+  else if (a_mode == 2) { K = total; M = a.size(2); }
+  else {
+    check_operand(a, "A");
+    M = a_mn_major ? a.size(1) : a.size(0);
+    K = a_mn_major ? a.size(0) : a.size(1);
+  }
+  if (b_mode == 2) {
+    N = b.size(2);
+    HT_CHECK(K == total, "peer-sharded B must share the sequence K dimension");
+  } else {
+    check_operand(b, "B");
+    N = b_mn_major ? b.size(1) : b.size(0);
+    HT_CHECK((b_mn_major ? b.size(0) : b.size(1)) == K, "GEMM reduction sizes differ");
+  }
+  if (a_mode == 1 || rs) HT_CHECK(rows % BM == 0, "sequence rows per rank must be a multiple of 128 for this mode");
+  if (a_mode == 2 || b_mode == 2) HT_CHECK(rows % BK == 0, "sequence rows per rank must be a multiple of 64");
+  HT_CHECK((int)a_ptrs.size() == (a_mode ? world : 0) && (int)b_ptrs.size() == (b_mode ? world : 0) &&
+               (int)out_ptrs.size() == (rs ? world : 0), "one peer pointer per rank expected");
+
+  CollParams coll;
+  std::memset(&coll, 0, sizeof(coll));
+  for (int p = 0; p < world; ++p) {
+    if (a_mode == 1) coll.a[p] = make_map3(a_ptrs[p], K, rows, batch, 64, BM);
+    if (a_mode == 2) coll.a[p] = make_map3(a_ptrs[p], M, rows, batch, 64, BK);
+    if (b_mode == 2) coll.b[p] = make_map3(b_ptrs[p], N, rows, batch, 64, BK);
+    if (rs) coll.out[p] = make_map3(out_ptrs[p], N, rows, (int64_t)world * batch, 64, 32);
+    coll.flags_peer[p] = reinterpret_cast<uint32_t*>(flag_ptrs[p]);
+  }
+  HT_CHECK(flags_local.scalar_type() == at::kInt && counters.scalar_type() == at::kInt && counters.is_cuda(), "int32 flags expected");
+  HT_CHECK(site >= 0 && (site + 1) * MAX_PEERS <= flags_local.numel() && (site + 1) * 2 <= counters.numel(), "call site out of range");
+  coll.flags_local = reinterpret_cast<uint32_t*>(flags_local.data_ptr<int>());
+  coll.epoch = reinterpret_cast<uint32_t*>(counters.data_ptr<int>() + 2 * site);
+  coll.done = counters.data_ptr<int>() + 2 * site + 1;
+  coll.site = (int)site;
+  coll.advance = advance ? 1 : 0;
+  coll.a_mode = (int)a_mode;
+  coll.b_mode = (int)b_mode;
+  coll.rs = rs ? 1 : 0;
+  coll.rank = (int)rank;
+  coll.world = world;
+  coll.batch = (int)batch;
+  coll.rows_per_rank = (int)rows;
+  coll.seq = (int)(rows * world);
+  coll.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+
+  EpiParams ep{};
+  ep.splits = 1;
+  CUtensorMap ma{}, mb{}, md{}, maux{};
+  if (a_mode == 0) ma = a_mn_major ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64) : make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
+  if (b_mode == 0) mb = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
+  if (rs) {
+    HT_CHECK(d.scalar_type() == at::kBFloat16 && d.is_contiguous() && d.size(0) == world && d.size(3) == N,
+             "receive buffer must be a contiguous bf16 [world, B, R, N]");
+    HT_CHECK(epilogue == kPlain && !(bias.has_value() && bias->defined()), "reduce-scatter GEMMs take a plain epilogue");
+    ep.d = d.data_ptr();
+    ep.ldd = N;
+    ep.tma_d = 1;
+    ep.vec_ok = 1;
+  } else {
+    HT_CHECK(d.dim() == 2 && d.size(0) == M && d.size(1) == N && d.stride(1) == 1, "D must be [M, N] with unit inner stride");
+    const bool d32 = d.scalar_type() == at::kFloat;
+    ep.d = d.data_ptr();
+    ep.ldd = d.stride(0);
+    ep.d_fp32 = d32 ? 1 : 0;
+    ep.beta = (float)beta;
+    ep.epi = (int)epilogue;
+    ep.vec_ok = ((d.stride(0) * d.element_size()) % 16 == 0 && reinterpret_cast<uintptr_t>(d.data_ptr()) % 16 == 0) ? 1 : 0;
+    if (bias.has_value() && bias->defined()) {
+      HT_CHECK(bias->is_contiguous() && bias->numel() == N, "bias must be a contiguous [N] tensor");
+      if (bias->scalar_type() == at::kFloat) ep.bias_f32 = bias->data_ptr<float>();
+      else ep.bias_bf16 = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+    }
+    if (epilogue != kPlain) {
+      HT_CHECK(aux.has_value() && aux->defined() && aux->scalar_type() == at::kBFloat16 && aux->size(0) == M && aux->size(1) == N,
+               "GELU epilogues need a bf16 [M, N] aux tensor");
+      ep.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+      ep.ldaux = aux->stride(0);
+      if ((aux->stride(0) * 2) % 16 != 0 || reinterpret_cast<uintptr_t>(aux->data_ptr()) % 16 != 0) ep.vec_ok = 0;
+    }
+    HT_CHECK(ep.vec_ok && (beta == 0.0 || (beta == 1.0 && d32)) && !(epilogue == kGelu && d32),
+             "collective GEMM outputs need 16-byte aligned rows and beta 0 (or 1 into fp32)");
+    md = make_out_map(d.data_ptr(), M, N, d.stride(0), d32);
+    if (epilogue == kGelu) maux = make_out_map(aux->data_ptr(), M, N, aux->stride(0), false);
+    ep.tma_d = 1;
+    ep.tma_aux = epilogue == kGelu ? 1 : 0;
+    ep.reduce_add = beta == 1.0 ? 1 : 0;
+  }
+  int* err = error_word(a.device());
+  cudaStream_t s = stream();
+  const bool amn = a_mode == 2 || (a_mode == 0 && a_mn_major);
+  if (!amn && !b_mn_major) launch_coll<false, false>(ma, mb, md, maux, (int)M, (int)N, (int)K, ep, err, coll, s);
+  else if (!amn && b_mn_major) launch_coll<false, true>(ma, mb, md, maux, (int)M, (int)N, (int)K, ep, err, coll, s);
+  else if (amn && b_mn_major) launch_coll<true, true>(ma, mb, md, maux, (int)M, (int)N, (int)K, ep, err, coll, s);
+  else launch_coll<true, false>(ma, mb, md, maux, (int)M, (int)N, (int)K, ep, err, coll, s);
+}
+
+// out = sum over ranks of this rank's receive slots, once every peer has published them.
+void reduce_scatter_sum(at::Tensor recv, at::Tensor out, at::Tensor flags_local, at::Tensor counters, int64_t site, int64_t rank,
+                        double timeout_s) {
+  const c10::cuda::CUDAGuard guard(recv.device());
+  HT_CHECK(recv.dim() == 4 && recv.is_contiguous() && recv.scalar_type() == at::kBFloat16, "receive buffer must be bf16 [world, B, R, N]");
+  const int world = (int)recv.size(0);
+  const long long slot = recv.numel() / world;
+  HT_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == slot, "output must be a contiguous bf16 slot");
+  HT_CHECK(slot % 8 == 0, "slot size must be a multiple of 8 elements");
+  const int blocks = (int)std::min<long long>((slot / 8 + 255) / 256, 4LL * num_sms());
+  tcg::rs_sum_kernel<<<std::max(blocks, 1), 256, 0, stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(recv.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), slot, world,
+      (int)rank, reinterpret_cast<const uint32_t*>(flags_local.data_ptr<int>()) + site * tcg::MAX_PEERS,
+      reinterpret_cast<const uint32_t*>(counters.data_ptr<int>() + 2 * site), (unsigned long long)(timeout_s * 1e9),
+      tcg::error_word(recv.device()));
+  HT_CUDA_CHECK(cudaGetLastError());
 }
 
 at::Tensor gemm_error_word(at::Tensor like) { return at::from_blob(tcg::error_word(like.device()), {4}, like.options().dtype(at::kInt)); }

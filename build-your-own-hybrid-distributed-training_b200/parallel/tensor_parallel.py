@@ -171,8 +171,9 @@ class ColumnParallelLinear(nn.Module):
             if workspace is not None:
                 from ..ops.comm import all_gather_linear
 
-                out = all_gather_linear(x, self.weight, self.bias, workspace, self.group, activation=self.activation)
-                return out
+                out = all_gather_linear(x, self.weight, self.bias, workspace, self.group, activation=self.activation, owner=id(self))
+                if out is not None:
+                    return out
             x = gather_from_sequence_parallel_region(x, self.group, dim=SEQUENCE_DIM)
         else:
             x = copy_to_group(x, self.group)
@@ -247,8 +248,9 @@ class RowParallelLinear(nn.Module):
             if workspace is not None:
                 from ..ops.comm import linear_reduce_scatter
 
-                out = linear_reduce_scatter(x, self.weight, workspace, self.group)
-                return out if self.bias is None else out + self.bias.to(out.dtype)
+                out = linear_reduce_scatter(x, self.weight, workspace, self.group, owner=id(self))
+                if out is not None:
+                    return out if self.bias is None else out + self.bias.to(out.dtype)
         partial = ops.linear(x, self.weight, fused_bias)
         if self.group.is_trivial:
             return partial

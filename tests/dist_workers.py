@@ -263,3 +263,48 @@ def ddp_cuda_worker(rank: int, world: int, fused: bool, steps: int) -> dict[str,
         return out
     finally:
         ctx.shutdown()
+
+
+def tp_fused_collectives_worker(rank: int, world: int) -> dict[str, Any]:
+    """Column- and row-parallel SP linears with the fused collective kernels against the NCCL path."""
+    from hybrid_training.parallel.tensor_parallel import ColumnParallelLinear, RowParallelLinear
+
+    cfg = ExperimentConfig.from_dict({
+        "name": "tp-fused", "backend": "nccl", "device": "cuda", "timeout_seconds": 120.0,
+        "topology": {"tensor_parallel_size": world, "sequence_parallel_mode": "tensor_group"},
+        "tensor_parallel": {"sequence_parallel": True, "fused_collectives": True},
+        "mixed_precision": {"enabled": True, "param_dtype": "bfloat16"},
+        "model": {"kind": "transformer", "hidden_size": 256, "num_layers": 1, "num_heads": 4, "vocab_size": 512,
+                  "max_sequence_length": 128 * world}})
+    ctx = init_distributed(cfg)
+    try:
+        group = ctx.group("tensor")
+        dev = ctx.device
+        b, r, k, n = 2, 128, 256, 512
+        col = ColumnParallelLinear(k, n, group, bias=True, sequence_parallel=True, activation="gelu", init_seed=3, device=dev)
+        row = RowParallelLinear(n, k, group, bias=True, sequence_parallel=True, init_seed=4, device=dev)
+        gen = torch.Generator(device="cpu").manual_seed(7)
+        x_full = torch.randn(b, r * world, k, generator=gen)
+        g_full = torch.randn(b, r * world, k, generator=gen)
+        x_shard = x_full[:, rank * r:(rank + 1) * r].to(dev).bfloat16()
+        g_shard = g_full[:, rank * r:(rank + 1) * r].to(dev).bfloat16()
+        results = {}
+        for fused in (True, False):
+            ctx.fused_tensor_collectives = fused
+            for prm in list(col.parameters()) + list(row.parameters()):
+                prm.grad = None
+            x = x_shard.clone().requires_grad_(True)
+            h = col(x)
+            y = row(h)
+            y.backward(g_shard)
+            torch.cuda.synchronize()
+            results[fused] = {"y": y.detach().float().cpu(), "h": h.detach().float().cpu(), "dx": x.grad.float().cpu(),
+                              "dw_col": col.weight.grad.float().cpu(), "db_col": col.bias.grad.float().cpu(),
+                              "dw_row": row.weight.grad.float().cpu()}
+        from hybrid_training.ops import extension
+
+        errs = {key: float((results[True][key] - results[False][key]).norm() / (results[False][key].norm() + 1e-12))
+                for key in results[True]}
+        return {"errors": errs, "error_word": int(extension().gemm_error_word(x_shard).abs().sum())}
+    finally:
+        ctx.shutdown()

@@ -33,3 +33,12 @@ def test_ddp_fused_and_nccl_reductions_train_alike() -> None:
         assert torch.equal(t, fused[1].value["full"][name]), name
     for a, b in zip(fused[0].value["losses"], nccl[0].value["losses"]):
         assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (fused[0].value["losses"], nccl[0].value["losses"])
+
+
+def test_fused_tensor_parallel_collectives_match_nccl_path() -> None:
+    """All-gather fused into the column GEMM's loads, reduce-scatter fused into the row GEMM's epilogue."""
+    results = launch_workers(W.tp_fused_collectives_worker, 2, timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    for r in results:
+        assert r.value["error_word"] == 0
+        for key, err in r.value["errors"].items():
+            assert err < 2e-2, (key, r.value["errors"])
