@@ -51,8 +51,12 @@ class SymmetricWorkspace:
     def allocate(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
         """A zero-initialised tensor in peer-mapped memory (collective: every member must call it)."""
         t = self._symm.empty(numel, dtype=dtype, device=self.device)
-        handle = self._symm.rendezvous(t, self.group.process_group)
+        # Zero before the handle exchange and wait for it: once any rank returns from the
+        # rendezvous (a collective), every rank's zeroing is complete, so a peer's first write
+        # into this buffer can never be overwritten by the owner's initialisation.
         t.zero_()
+        torch.cuda.synchronize(self.device)
+        handle = self._symm.rendezvous(t, self.group.process_group)
         self._allocations.append((t, handle))
         return t
 

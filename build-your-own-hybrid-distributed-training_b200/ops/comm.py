@@ -71,6 +71,7 @@ class _TensorParallelSites:
         self.counters = torch.zeros(self.MAX_SITES * 2, dtype=torch.int32, device=self.flags.device)
         self.sites: dict[tuple[Any, str], int] = {}
         self.buffers: dict[tuple[Any, str], tuple[torch.Tensor, list[int]]] = {}
+        self.local: dict[tuple[Any, str], torch.Tensor] = {}
         self.rank = int(workspace.group.local_rank)
         self.world = int(workspace.group.size)
 
@@ -95,6 +96,19 @@ class _TensorParallelSites:
         return hit[0].view(shape), hit[1]
 
 
+    def local_buffer(self, owner: Any, kind: str, shape: tuple[int, ...], dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        """A persistent buffer of this rank only (gathered copies, block flags); flags start at zero."""
+        key = (owner, kind)
+        t = self.local.get(key)
+        numel = 1
+        for d in shape:
+            numel *= d
+        if t is None or t.numel() != numel or t.dtype != dtype:
+            t = torch.zeros(numel, dtype=dtype, device=self.flags.device)
+            self.local[key] = t
+        return t.view(shape)
+
+
 _SITES: dict[int, _TensorParallelSites] = {}
 
 
@@ -108,7 +122,7 @@ def _sites(workspace: Any) -> _TensorParallelSites:
 def can_fuse_sequence_parallel(x: torch.Tensor, group: Any, *, sharded_rows: int, features: tuple[int, ...]) -> bool:
     """Whether the fused kernels cover this call: bf16 on CUDA, 2..8 ranks, 128-row shards, 16-byte rows."""
     return (x.is_cuda and x.dtype == torch.bfloat16 and 2 <= group.size <= 8 and sharded_rows % 128 == 0
-            and all(f % 8 == 0 for f in features))
+            and all(f % 64 == 0 for f in features))
 
 
 class _AllGatherLinear(torch.autograd.Function):
@@ -129,8 +143,11 @@ class _AllGatherLinear(torch.autograd.Function):
         site = st.site(owner, "ag")
         y = torch.empty(b * r * st.world, n, dtype=x.dtype, device=x.device)
         pre = torch.empty_like(y) if activation == "gelu" else None
+        gathered = st.local_buffer(owner, "ag.gathered", (b, r * st.world, k))
+        flags = st.local_buffer(owner, "ag.blocks", (b * r * st.world // 128 * (k // 64),), torch.int32)
         ext.gemm_collective(slot, w, y, bias, pre, False, False, EPI_GELU if pre is not None else EPI_PLAIN, 0.0,
-                            1, ptrs, 0, [], 0, [], st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
+                            1, ptrs, 0, [], 0, [], st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S,
+                            gathered, flags)
         ctx.save_for_backward(w, pre)
         ctx.st, ctx.owner, ctx.site, ctx.shape = st, owner, site, (b, r, k)
         ctx.weight, ctx.bias = weight, bias
@@ -139,7 +156,7 @@ class _AllGatherLinear(torch.autograd.Function):
     @staticmethod
     def backward(ctx: Any, dy: torch.Tensor) -> tuple[Any, ...]:
         from .grads import deliver_grad
-        from .linear import EPI_PLAIN, _column_sum, gelu_backward
+        from .linear import EPI_PLAIN, _column_sum, gelu_backward, gemm
 
         w, pre = ctx.saved_tensors
         st, owner = ctx.st, ctx.owner
@@ -152,15 +169,14 @@ class _AllGatherLinear(torch.autograd.Function):
             recv, rptrs = st.buffer(owner, "ag.dx_recv", (st.world, b, r, k))
             site = st.site(owner, "ag.rs")
             ext.gemm_collective(g, w, recv, None, None, False, True, EPI_PLAIN, 0.0, 0, [], 0, [], 1, rptrs,
-                                st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
+                                st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S, None, None)
             dx = torch.empty(b, r, k, dtype=dy.dtype, device=dy.device)
             ext.reduce_scatter_sum(recv, dx, st.flags, st.counters, site, st.rank, _TIMEOUT_S)
-        slot, ptrs = st.buffer(owner, "ag.x", (b, r, k))
+        gathered = st.local_buffer(owner, "ag.gathered", (b, r * st.world, k)).view(-1, k)
         weight, bias = ctx.weight, ctx.bias
 
         def wgrad(out: torch.Tensor, beta: float) -> None:
-            ext.gemm_collective(g, slot, out, None, None, True, True, EPI_PLAIN, float(beta), 0, [], 2, ptrs, 0, [],
-                                st.flags, st.flag_ptrs, st.counters, ctx.site, 0, st.rank, _TIMEOUT_S)
+            gemm(g, gathered, out=out, a_mn_major=True, b_mn_major=True, beta=beta)
 
         dw = None
         if ctx.needs_input_grad[1]:
@@ -194,7 +210,7 @@ class _LinearReduceScatter(torch.autograd.Function):
         recv, rptrs = st.buffer(owner, "rs.recv", (st.world, b, r, n))
         site = st.site(owner, "rs")
         ext.gemm_collective(x2, w, recv, None, None, False, False, EPI_PLAIN, 0.0, 0, [], 0, [], 1, rptrs,
-                            st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
+                            st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S, None, None)
         out = torch.empty(b, r, n, dtype=x.dtype, device=x.device)
         ext.reduce_scatter_sum(recv, out, st.flags, st.counters, site, st.rank, _TIMEOUT_S)
         ctx.save_for_backward(x2, w)
@@ -204,7 +220,7 @@ class _LinearReduceScatter(torch.autograd.Function):
     @staticmethod
     def backward(ctx: Any, dout: torch.Tensor) -> tuple[Any, ...]:
         from .grads import deliver_grad
-        from .linear import EPI_PLAIN
+        from .linear import EPI_PLAIN, gemm
 
         x2, w = ctx.saved_tensors
         st, owner = ctx.st, ctx.owner
@@ -214,19 +230,18 @@ class _LinearReduceScatter(torch.autograd.Function):
         slot, ptrs = st.buffer(owner, "rs.dout", (b, r, n))
         slot.copy_(dout.reshape(b, r, n))
         site = st.site(owner, "rs.ag")
-        dx = None
-        if ctx.needs_input_grad[0]:
-            dx = torch.empty(b * s, kr, dtype=dout.dtype, device=dout.device)
-            ext.gemm_collective(slot, w, dx, None, None, False, True, EPI_PLAIN, 0.0, 1, ptrs, 0, [], 0, [],
-                                st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S)
-            advance = 0
-        else:
-            advance = 1
+        gathered = st.local_buffer(owner, "rs.gathered", (b, s, n))
+        flags = st.local_buffer(owner, "rs.blocks", (b * s // 128 * (n // 64),), torch.int32)
+        # dX = AllGather(dout) W: the gather happens inside this GEMM and leaves the gathered copy
+        # that the weight gradient reads.
+        dx = torch.empty(b * s, kr, dtype=dout.dtype, device=dout.device)
+        ext.gemm_collective(slot, w, dx, None, None, False, True, EPI_PLAIN, 0.0, 1, ptrs, 0, [], 0, [],
+                            st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S, gathered, flags)
         weight = ctx.weight
+        g2 = gathered.view(b * s, n)
 
-        def wgrad(out: torch.Tensor, beta: float, adv: int = advance) -> None:
-            ext.gemm_collective(slot, x2, out, None, None, True, True, EPI_PLAIN, float(beta), 2, ptrs, 0, [], 0, [],
-                                st.flags, st.flag_ptrs, st.counters, site, adv, st.rank, _TIMEOUT_S)
+        def wgrad(out: torch.Tensor, beta: float) -> None:
+            gemm(g2, x2, out=out, a_mn_major=True, b_mn_major=True, beta=beta)
 
         dw = None
         if ctx.needs_input_grad[1]:
@@ -236,7 +251,7 @@ class _LinearReduceScatter(torch.autograd.Function):
                 wgrad(value, 0.0)
                 value = value.to(weight.dtype)
             dw = deliver_grad(weight, compute=wgrad if value is None else None, value=value)
-        return (None if dx is None else dx.view(b, s, kr)), dw, None, None
+        return dx.view(b, s, kr), dw, None, None
 
 
 def all_gather_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, workspace: Any, group: Any, *,

@@ -9,7 +9,7 @@ void gemm_collective(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at:
                      bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta, int64_t a_mode, std::vector<int64_t> a_ptrs,
                      int64_t b_mode, std::vector<int64_t> b_ptrs, int64_t rs, std::vector<int64_t> out_ptrs, at::Tensor flags_local,
                      std::vector<int64_t> flag_ptrs, at::Tensor counters, int64_t site, int64_t advance, int64_t rank,
-                     double timeout_s);
+                     double timeout_s, c10::optional<at::Tensor> gathered, c10::optional<at::Tensor> block_flags);
 void reduce_scatter_sum(at::Tensor recv, at::Tensor out, at::Tensor flags_local, at::Tensor counters, int64_t site, int64_t rank,
                         double timeout_s);
 at::Tensor attention_error_word_tensor(at::Tensor like);

@@ -92,7 +92,32 @@ struct CollParams {
   int rs;                      // epilogue writes rows into their owner's receive slot
   int rank, world, batch, seq, rows_per_rank;
   unsigned long long timeout_ns;
+  // a_mode 1 (all-gather of a K-major A): every remote 128-row block crosses NVLink once.  The
+  // copy warp of each CTA pulls blocks from the owners' shards (a_src) into the local gathered
+  // buffer and flags them (block_flags, indexed by physical M block); tiles of remote blocks are
+  // then loaded from the gathered buffer through `gathered_map`.  The gathered buffer also
+  // serves the backward pass.
+  CUtensorMap gathered_map;
+  const __nv_bfloat16* a_src[MAX_PEERS];
+  __nv_bfloat16* gathered;
+  uint32_t* block_flags;
+  int k_dim;
 };
+
+constexpr int COLL_THREADS = THREADS + 32;  // + one copy warp
+
+// a_mode 1 schedules M blocks by owner, starting with this rank's own shard: logical block L
+// -> physical block.  Both the producer and the epilogue use it.
+__device__ __forceinline__ int coll_phys_mblock(const CollParams& c, int L) {
+  const int per_batch = c.rows_per_rank / BM;
+  const int per_owner = c.batch * per_batch;
+  const int q = L / per_owner;
+  const int rem = L - q * per_owner;
+  const int bidx = rem / per_batch;
+  const int j = rem - bidx * per_batch;
+  const int owner = (c.rank + q) % c.world;
+  return (bidx * c.seq + owner * c.rows_per_rank) / BM + j;
+}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -340,6 +365,7 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
   for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
     int mb, nb;
     tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
+    if (coll != nullptr && coll->a_mode == 1) mb = coll_phys_mblock(*coll, mb);
     int out_row0 = (unit % ep.splits) * ep.split_rows + mb * BM + quarter * 32;
     const CUtensorMap* dmap = map_d;
     int z = -1;
@@ -387,6 +413,66 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
     }
   }
   __syncwarp();
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Copies A slices of 128 rows x 64 columns (16 KB) from the owners' shards into the gathered
+// buffer: remote owners rank+1, rank+2, ... first in the order the GEMM consumes them, this
+// rank's own shard last (it is only needed by the backward pass).  The slices are spread over
+// the copy warps of every CTA so that enough bytes are in flight to fill NVLink; each slice is
+// flagged (per 128-row block and 64-column block) once its bytes are visible to TMA loads.
+__device__ __noinline__ void coll_copy_warp(const CollParams& c, uint32_t epoch, int lane, int* err) {
+  const int per_batch = c.rows_per_rank / BM;
+  const int per_owner = c.batch * per_batch;
+  const int kbs = c.k_dim / BK;
+  const int total = c.world * per_owner * kbs;
+  uint32_t ready = 0;
+  for (int ci = blockIdx.x; ci < total; ci += gridDim.x) {
+    const int blk = ci / kbs;
+    const int kb = ci - blk * kbs;
+    const int q = (blk / per_owner + 1) % c.world;  // remote owners first, own shard last
+    const int rem = blk % per_owner;
+    const int bidx = rem / per_batch;
+    const int j = rem - bidx * per_batch;
+    const int owner = (c.rank + q) % c.world;
+    if (owner != c.rank && !(ready >> owner & 1u)) {
+      bool ok = true;
+      if (lane == 0) ok = wait_published(c, owner, epoch, err);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return;
+      ready |= 1u << owner;
+    }
+    const __nv_bfloat16* src = c.a_src[owner] + ((long long)bidx * c.rows_per_rank + j * BM) * c.k_dim + kb * BK;
+    const int row0 = bidx * c.seq + owner * c.rows_per_rank + j * BM;
+    __nv_bfloat16* dst = c.gathered + (long long)row0 * c.k_dim + kb * BK;
+    // 128 rows x 8 vectors of 16 bytes: 32 per lane, in two waves of 16 loads in flight.
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint4 buf[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int v = (half * 16 + u) * 32 + lane;
+        buf[u] = *reinterpret_cast<const uint4*>(src + (long long)(v >> 3) * c.k_dim + (v & 7) * 8);
+      }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int v = (half * 16 + u) * 32 + lane;
+        *reinterpret_cast<uint4*>(dst + (long long)(v >> 3) * c.k_dim + (v & 7) * 8) = buf[u];
+      }
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence();
+    __syncwarp();
+    if (lane == 0 && owner != c.rank) {
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(c.block_flags + (row0 / BM) * kbs + kb), "r"(epoch)
+                   : "memory");
+    }
+  }
 }
 
 template <bool A_MN, bool B_MN, bool COLL>
@@ -450,11 +536,45 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
     bool ok = true;
     uint32_t ready_mask = 0;
     (void)ready_mask;
+    // Collective-mode constants, read from the parameter block once.
+    const int c_rank = COLL ? coll->rank : 0;
+    const int c_amode = COLL ? coll->a_mode : 0;
+    const int c_bmode = COLL ? coll->b_mode : 0;
+    const CUtensorMap* own_map = COLL ? &coll->a[c_rank] : nullptr;
+    const CUtensorMap* gathered_map = COLL ? &coll->gathered_map : nullptr;
     for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
       int mb, nb, kb0, kb1;
       tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
+      if (COLL && coll->a_mode == 1) mb = coll_phys_mblock(*coll, mb);
       split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
       const int m0 = mb * BM, n0 = nb * BN;
+      int tile_src = 0, tile_lrow = 0, tile_b = 0;  // A source of this tile: 0 local map, 1 own shard, 2 gathered copy
+      if (COLL && c_amode == 1) {
+        // A tile of a remote block: the whole warp polls the block's slice flags in parallel
+        // until every slice is in the gathered copy (one round trip per tile, not per slice).
+        int owner;
+        seq_owner(*coll, m0, owner, tile_lrow, tile_b);
+        tile_src = owner == c_rank ? 1 : 2;
+        if (owner != c_rank) {
+          const int kbs = coll->k_dim / BK;
+          const uint32_t* f = coll->block_flags + mb * kbs;
+          const unsigned long long deadline = globaltimer_ns() + coll->timeout_ns;
+          while (true) {
+            bool mine = true;
+            for (int i = lane; i < kbs; i += 32) mine = mine && (int)(ld_acquire_gpu(f + i) - epoch) >= 0;
+            if (__all_sync(0xffffffffu, mine)) break;
+            if (globaltimer_ns() > deadline || *((volatile int*)err) != 0) {
+              if (lane == 0) atomicCAS(err, 0, 42);
+              ok = false;
+              break;
+            }
+          }
+          __syncwarp();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, 1)) {
           ok = false;
@@ -464,31 +584,32 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
           uint8_t* a_dst = sA + stage * A_BYTES;
           uint8_t* b_dst = sB + stage * B_BYTES;
           const int k0 = kb * BK;
-          int a_owner = coll->rank, a_row = 0, a_b = 0, b_owner = coll->rank, b_row = 0, b_b = 0;
-          if (coll->a_mode == 1) seq_owner(*coll, m0, a_owner, a_row, a_b);
-          if (coll->a_mode == 2) seq_owner(*coll, k0, a_owner, a_row, a_b);
-          if (coll->b_mode == 2) seq_owner(*coll, k0, b_owner, b_row, b_b);
-          if (a_owner != coll->rank && !(ready_mask >> a_owner & 1u)) {
-            ok = wait_published(*coll, a_owner, epoch, err);
-            ready_mask |= 1u << a_owner;
+          int b_owner = c_rank, b_row = 0, b_b = 0, a_owner2 = c_rank, a_row2 = 0, a_b2 = 0;
+          if (c_amode == 2) seq_owner(*coll, k0, a_owner2, a_row2, a_b2);
+          if (c_bmode == 2) seq_owner(*coll, k0, b_owner, b_row, b_b);
+          if (c_amode == 2 && a_owner2 != c_rank && !(ready_mask >> a_owner2 & 1u)) {
+            ok = wait_published(*coll, a_owner2, epoch, err);
+            ready_mask |= 1u << a_owner2;
           }
-          if (ok && b_owner != coll->rank && !(ready_mask >> b_owner & 1u)) {
+          if (ok && c_bmode == 2 && b_owner != c_rank && !(ready_mask >> b_owner & 1u)) {
             ok = wait_published(*coll, b_owner, epoch, err);
             ready_mask |= 1u << b_owner;
           }
           mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
-          if (coll->a_mode == 1) {
-            tma_load_3d(a_dst, &coll->a[a_owner], &full_bar[stage], k0, a_row, a_b);
-          } else if (coll->a_mode == 2) {
-            tma_load_3d(a_dst, &coll->a[a_owner], &full_bar[stage], m0, a_row, a_b);
-            tma_load_3d(a_dst + BK * 128, &coll->a[a_owner], &full_bar[stage], m0 + 64, a_row, a_b);
+          if (tile_src == 1) {
+            tma_load_3d(a_dst, own_map, &full_bar[stage], k0, tile_lrow, tile_b);
+          } else if (tile_src == 2) {
+            tma_load_2d(a_dst, gathered_map, &full_bar[stage], k0, m0);
+          } else if (c_amode == 2) {
+            tma_load_3d(a_dst, &coll->a[a_owner2], &full_bar[stage], m0, a_row2, a_b2);
+            tma_load_3d(a_dst + BK * 128, &coll->a[a_owner2], &full_bar[stage], m0 + 64, a_row2, a_b2);
           } else if (A_MN) {
             tma_load_2d(a_dst, &tma_a, &full_bar[stage], m0, k0);
             tma_load_2d(a_dst + BK * 128, &tma_a, &full_bar[stage], m0 + 64, k0);
           } else {
             tma_load_2d(a_dst, &tma_a, &full_bar[stage], k0, m0);
           }
-          if (coll->b_mode == 2) {
+          if (c_bmode == 2) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
               tma_load_3d(b_dst + j * BK * 128, &coll->b[b_owner], &full_bar[stage], n0 + 64 * j, b_row, b_b);
@@ -572,6 +693,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
         acc_phase ^= 1u;
       }
     }
+  } else if (COLL && warp == 2 + EPI_WARPS) {
+    // ---------------- copy warp (a_mode 1) ----------------
+    if (coll->a_mode == 1) coll_copy_warp(*coll, epoch, lane, err);
   } else {
     // ---------------- epilogue ----------------
     uint8_t* tile = sEpi + (warp - 2) * EPI_STAGE_BYTES;
@@ -612,7 +736,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(COLL_THREADS, 1)
     gemm_coll_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
                      EpiParams ep, int* err, const __grid_constant__ CollParams coll) {
@@ -922,8 +1046,16 @@ static void launch_coll(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, num_sms());
-  kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, md, maux, M, N, K, ep, err, coll);
-  HT_CUDA_CHECK(cudaGetLastError());
+  // CTAs wait for blocks that other CTAs' copy warps bring in: a cooperative launch guarantees
+  // that every CTA of the grid is resident.
+  int m = M, n = N, k = K;
+  const EpiParams e = ep;
+  int* w = err;
+  const CollParams c = coll;
+  void* args[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb), const_cast<CUtensorMap*>(&md),
+                  const_cast<CUtensorMap*>(&maux), &m, &n, &k, const_cast<EpiParams*>(&e), &w, const_cast<CollParams*>(&c)};
+  HT_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(grid), dim3(COLL_THREADS), args,
+                                            (size_t)SMEM_BYTES, s));
 }
 
 }  // namespace tcg
@@ -938,7 +1070,7 @@ void gemm_collective(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at:
                      bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta, int64_t a_mode, std::vector<int64_t> a_ptrs,
                      int64_t b_mode, std::vector<int64_t> b_ptrs, int64_t rs, std::vector<int64_t> out_ptrs, at::Tensor flags_local,
                      std::vector<int64_t> flag_ptrs, at::Tensor counters, int64_t site, int64_t advance, int64_t rank,
-                     double timeout_s) {
+                     double timeout_s, c10::optional<at::Tensor> gathered, c10::optional<at::Tensor> block_flags) {
   using namespace tcg;
   const c10::cuda::CUDAGuard guard(a.device());
   bind_context(a.device().index());
@@ -1006,6 +1138,21 @@ void gemm_collective(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at:
   coll.rows_per_rank = (int)rows;
   coll.seq = (int)(rows * world);
   coll.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  if (a_mode == 1) {
+    HT_CHECK(gathered.has_value() && gathered->defined() && block_flags.has_value() && block_flags->defined(),
+             "the all-gather mode needs a gathered buffer and block flags");
+    HT_CHECK(gathered->scalar_type() == at::kBFloat16 && gathered->is_contiguous() && gathered->numel() == M * K,
+             "gathered buffer must be a contiguous bf16 [B, S, K]");
+    HT_CHECK(K % BK == 0, "K must be a multiple of 64 for the all-gather mode");
+    HT_CHECK(block_flags->scalar_type() == at::kInt && block_flags->numel() >= (M / BM) * (K / BK),
+             "one int32 flag per 128-row x 64-column slice");
+    coll.gathered_map = make_map(gathered->data_ptr(), M, K, K, 64, BM);
+    coll.gathered = reinterpret_cast<__nv_bfloat16*>(gathered->data_ptr());
+    coll.block_flags = reinterpret_cast<uint32_t*>(block_flags->data_ptr<int>());
+    coll.k_dim = (int)K;
+    HT_CHECK(K % 8 == 0, "K must be a multiple of 8");
+    for (int p = 0; p < world; ++p) coll.a_src[p] = reinterpret_cast<const __nv_bfloat16*>(a_ptrs[p]);
+  }
 
   EpiParams ep{};
   ep.splits = 1;
