@@ -308,3 +308,35 @@ def tp_fused_collectives_worker(rank: int, world: int) -> dict[str, Any]:
         return {"errors": errs, "error_word": int(extension().gemm_error_word(x_shard).abs().sum())}
     finally:
         ctx.shutdown()
+
+
+def _llama_experiment(world: int, topology: dict[str, Any], *, fused_tp: bool = True, steps: int = 3) -> dict[str, Any]:
+    return {"name": "multigpu-llama", "backend": "nccl", "device": "cuda", "timeout_seconds": 120.0,
+            "topology": topology,
+            "tensor_parallel": {"sequence_parallel": topology.get("sequence_parallel_mode") == "tensor_group",
+                                "fused_collectives": fused_tp},
+            "model": {"kind": "transformer", "hidden_size": 256, "num_layers": 2, "num_heads": 4, "num_kv_heads": 2,
+                      "ffn_hidden_size": 512, "vocab_size": 1024, "max_sequence_length": 256, "norm": "rmsnorm",
+                      "position_embedding": "rope", "activation": "swiglu", "bias": False},
+            "data": {"micro_batch_size": 2, "sequence_length": 256, "num_train_samples": 4096, "num_eval_samples": 0,
+                     "shuffle": False},
+            "optimizer": {"learning_rate": 1e-3},
+            "mixed_precision": {"enabled": True, "param_dtype": "bfloat16"},
+            "fsdp": {"auto_wrap_min_num_params": 10000},
+            "training": {"max_steps": steps, "log_every_steps": 0}}
+
+
+def llama_cuda_worker(rank: int, world: int, topology: dict[str, Any], fused_tp: bool, steps: int) -> dict[str, Any]:
+    """A few engine steps of a Llama-style decoder on CUDA under the given topology."""
+    cfg = ExperimentConfig.from_dict(_llama_experiment(world, topology, fused_tp=fused_tp, steps=steps))
+    ctx = init_distributed(cfg)
+    try:
+        engine = TrainingEngine(cfg, ctx)
+        engine.train(max_steps=steps)
+        full = engine.model.full_state_dict()
+        out = {"losses": [m.loss for m in engine.history],
+               "full": {k: v.detach().float().cpu().clone() for k, v in full.items()}}
+        engine.close()
+        return out
+    finally:
+        ctx.shutdown()

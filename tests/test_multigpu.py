@@ -42,3 +42,19 @@ def test_fused_tensor_parallel_collectives_match_nccl_path() -> None:
         assert r.value["error_word"] == 0
         for key, err in r.value["errors"].items():
             assert err < 2e-2, (key, r.value["errors"])
+
+
+def test_fsdp_llama_trains_on_two_gpus() -> None:
+    results = launch_workers(W.llama_cuda_worker, 2, args=({"shard_parallel_size": 2}, True, 3), timeout_seconds=300,
+                             extra_env={"NCCL_NVLS_ENABLE": "0"})
+    losses = results[0].value["losses"]
+    assert len(losses) == 3 and all(l == l and 0 < l < 20 for l in losses), losses
+    assert losses == results[1].value["losses"]
+
+
+def test_tensor_sequence_parallel_llama_fused_matches_nccl_path() -> None:
+    topo = {"tensor_parallel_size": 2, "sequence_parallel_mode": "tensor_group"}
+    fused = launch_workers(W.llama_cuda_worker, 2, args=(topo, True, 3), timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    nccl = launch_workers(W.llama_cuda_worker, 2, args=(topo, False, 3), timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    for a, b in zip(fused[0].value["losses"], nccl[0].value["losses"]):
+        assert abs(a - b) < 2e-2 * max(1.0, abs(b)), (fused[0].value["losses"], nccl[0].value["losses"])
