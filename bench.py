@@ -42,6 +42,12 @@ METRIC = "tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; exposed com
 MODEL_NAME = "GPT-2-124M-shape (12L, d768, 12h, V50257, tied), DDP"
 SEQ = 1024
 MICRO_BATCH = 8
+CONFIGS = {  # name -> (model, micro-batch per replica, sequence, gradient accumulation)
+    "gpt2_ddp": (MODEL_NAME, MICRO_BATCH, SEQ, 1),
+    "llama_fsdp": ("Llama-style 1.3B (24L, d2048, 16h, SwiGLU 5504, V32000), FSDP full shard", 4, 2048, 1),
+    "llama_tp_sp": ("Llama-3-8B shape (32L, d4096, 32q/8kv, ffn 14336, V128256), TP+SP", 1, 4096, 1),
+    "llama_hybrid": ("Llama-3-8B shape, DP2 x TP(N/2) + SP", 2, 4096, 4),
+}
 
 
 def _args() -> argparse.Namespace:
@@ -51,6 +57,10 @@ def _args() -> argparse.Namespace:
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["native", "reference"], default="native")
     p.add_argument("--no-graph", action="store_true", help="native arm: run eagerly instead of replaying a CUDA graph")
+    p.add_argument("--config", choices=list(CONFIGS), default="gpt2_ddp",
+                   help="gpt2_ddp (the headline, default); llama_fsdp (1.3B full shard, S2048, 4/GPU); llama_tp_sp "
+                        "(Llama-3-8B, TP=N with SP, S4096, micro-batch 1); llama_hybrid (Llama-3-8B, DP2 x TP N/2 with SP, "
+                        "S4096, global batch 16 by accumulation)")
     return p.parse_args()
 
 
@@ -118,6 +128,17 @@ def _visible_gpu_indices(n: int) -> list[int]:
     return list(range(n))
 
 
+def _parallelism(config: str, n: int) -> str:
+    if config == "gpt2_ddp":
+        return f"dp{n}"
+    if config == "llama_fsdp":
+        return f"fsdp{n}"
+    if config == "llama_tp_sp":
+        return f"tp{n}+sp"
+    tp = max(1, n // 2)
+    return f"dp{n // tp}xtp{tp}+sp"
+
+
 def _emit(result: dict) -> None:
     print(json.dumps(result), flush=True)
 
@@ -129,6 +150,10 @@ def _baseline_value() -> float | None:
 
 def main() -> None:
     args = _args()
+    if args.impl == "reference" and args.config != "gpt2_ddp":
+        _emit({"impl": "reference", "unavailable": f"the reference has no Llama-style model (RMSNorm/RoPE/SwiGLU/GQA) for "
+                                                   f"--config {args.config}"})
+        return
     if args.impl == "reference":
         sys.path[:] = [p for p in sys.path if os.path.abspath(p or ".") != ROOT]
         sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
@@ -151,12 +176,15 @@ def main() -> None:
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
     sampler = ClockSampler(_visible_gpu_indices(args.gpus)) if rank == 0 else None
-    result = runner(steps=args.steps, warmup=args.warmup, micro_batch=MICRO_BATCH, seq=SEQ,
+    model_name, micro_batch, seq, accum = CONFIGS[args.config]
+    extra = {} if args.impl == "reference" else {"config": args.config, "grad_accum": accum}
+    result = runner(steps=args.steps, warmup=args.warmup, micro_batch=micro_batch, seq=seq,
                     use_graph=not args.no_graph, clock_start=(sampler.start if sampler else None),
-                    clock_stop=(sampler.stop if sampler else None))
+                    clock_stop=(sampler.stop if sampler else None), **extra)
     if rank == 0:
         n = args.gpus
-        tokens = n * MICRO_BATCH * SEQ * args.steps
+        tokens_per_step = result.get("tokens_per_step") or n * micro_batch * seq
+        tokens = tokens_per_step * args.steps
         value = tokens / (result["device_ms"] / 1000.0)
         e2e = tokens / (result["e2e_ms"] / 1000.0)
         out = {
@@ -172,8 +200,9 @@ def main() -> None:
             "vs_baseline": None if _baseline_value() is None else value / _baseline_value(),
             "dtype": "bf16",
             "data": "synthetic: uniform random token ids, random-init weights",
-            "config": {"model": MODEL_NAME, "global_batch": n * MICRO_BATCH, "seq_len": SEQ, "parallelism": f"dp{n}",
-                       "micro_batch_per_gpu": MICRO_BATCH, "bucket_cap_mb": 25, "optimizer": "AdamW fp32 master",
+            "config": {"model": model_name, "global_batch": tokens_per_step // seq, "seq_len": seq,
+                       "parallelism": _parallelism(args.config, n), "micro_batch_per_replica": micro_batch,
+                       "grad_accum": accum, "bucket_cap_mb": 25, "optimizer": "AdamW fp32 master",
                        "l2": "no flush: per-step working set of several GB exceeds the 126 MB L2",
                        "cuda_graph": (not args.no_graph) if args.impl == "native" else False},
             "clocks": result.get("clocks", {}),

@@ -20,10 +20,12 @@ import torch.distributed as dist
 from .config import (
     DataConfig,
     DDPConfig,
+    FSDPConfig,
     ExperimentConfig,
     MixedPrecisionConfig,
     ModelConfig,
     OptimizerConfig,
+    TensorParallelConfig,
     TopologyConfig,
     TrainingConfig,
 )
@@ -65,46 +67,76 @@ def _timed(fn: Callable[[], None]) -> float:
     return _max_over_ranks(start.elapsed_time(stop))
 
 
-def experiment(world: int, *, micro_batch: int, seq: int, samples: int, use_graph: bool) -> ExperimentConfig:
-    return ExperimentConfig(
-        name="bench-gpt2-124m-ddp",
-        backend="nccl",
-        device="cuda",
-        timeout_seconds=600.0,
-        topology=TopologyConfig(data_parallel_size=world),
-        model=ModelConfig.gpt2_124m(),
-        data=DataConfig(micro_batch_size=micro_batch, sequence_length=seq, num_train_samples=samples, num_eval_samples=0,
-                        token_distribution="uniform", shuffle=False),
-        optimizer=OptimizerConfig(learning_rate=6e-4, weight_decay=0.1, betas=(0.9, 0.95)),
-        training=TrainingConfig(max_steps=1_000_000, log_every_steps=0, deterministic=False, cuda_graph=use_graph),
-        ddp=DDPConfig(bucket_cap_mb=25.0),
-        mixed_precision=MixedPrecisionConfig(enabled=True, param_dtype="bfloat16"),
-    )
+# Benchmark configurations: name -> (description, parallelism, builder).
+CONFIGS = ("gpt2_ddp", "llama_fsdp", "llama_tp_sp", "llama_hybrid")
+
+
+def experiment(world: int, *, micro_batch: int, seq: int, samples: int, use_graph: bool, config: str = "gpt2_ddp",
+               grad_accum: int = 1) -> ExperimentConfig:
+    """The ExperimentConfig of one benchmark configuration on ``world`` GPUs."""
+    common = dict(backend="nccl", device="cuda", timeout_seconds=600.0,
+                  data=DataConfig(micro_batch_size=micro_batch, sequence_length=seq, num_train_samples=samples,
+                                  num_eval_samples=0, token_distribution="uniform", shuffle=False),
+                  mixed_precision=MixedPrecisionConfig(enabled=True, param_dtype="bfloat16"))
+    # CUDA-graph replay is used for the data-parallel step; the sharded / tensor-parallel
+    # configurations run eagerly.
+    training = TrainingConfig(max_steps=1_000_000, log_every_steps=0, deterministic=False,
+                              cuda_graph=use_graph and config == "gpt2_ddp", gradient_accumulation_steps=grad_accum)
+    if config == "gpt2_ddp":
+        return ExperimentConfig(name="bench-gpt2-124m-ddp", topology=TopologyConfig(data_parallel_size=world),
+                                model=ModelConfig.gpt2_124m(),
+                                optimizer=OptimizerConfig(learning_rate=6e-4, weight_decay=0.1, betas=(0.9, 0.95)),
+                                training=training, ddp=DDPConfig(bucket_cap_mb=25.0), **common)
+    if config == "llama_fsdp":  # full shard, one flat parameter per decoder block
+        return ExperimentConfig(name="bench-llama-1b3-fsdp", topology=TopologyConfig(shard_parallel_size=world),
+                                model=ModelConfig.llama_1b3(), optimizer=OptimizerConfig(learning_rate=3e-4, weight_decay=0.1),
+                                training=training, fsdp=FSDPConfig(auto_wrap_min_num_params=10_000_000), **common)
+    if config == "llama_tp_sp":  # tensor + sequence parallel over every GPU
+        return ExperimentConfig(name="bench-llama3-8b-tp-sp",
+                                topology=TopologyConfig(tensor_parallel_size=world,
+                                                        sequence_parallel_mode="tensor_group" if world > 1 else "disabled"),
+                                tensor_parallel=TensorParallelConfig(sequence_parallel=world > 1),
+                                model=ModelConfig.llama3_8b(), optimizer=OptimizerConfig(learning_rate=3e-4, weight_decay=0.1),
+                                training=training, **common)
+    if config == "llama_hybrid":  # DP2 x TP(world/2) with SP
+        tp = max(1, world // 2)
+        return ExperimentConfig(name="bench-llama3-8b-hybrid",
+                                topology=TopologyConfig(data_parallel_size=world // tp, tensor_parallel_size=tp,
+                                                        sequence_parallel_mode="tensor_group" if tp > 1 else "disabled"),
+                                tensor_parallel=TensorParallelConfig(sequence_parallel=tp > 1),
+                                model=ModelConfig.llama3_8b(), optimizer=OptimizerConfig(learning_rate=3e-4, weight_decay=0.1),
+                                training=training, ddp=DDPConfig(bucket_cap_mb=25.0), **common)
+    raise ValueError(f"unknown benchmark config {config!r}; expected one of {CONFIGS}")
 
 
 def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool = True,
-        clock_start: Callable[[], None] | None = None, clock_stop: Callable[[], dict] | None = None) -> dict:
+        clock_start: Callable[[], None] | None = None, clock_stop: Callable[[], dict] | None = None,
+        config: str = "gpt2_ddp", grad_accum: int = 1) -> dict:
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    cfg = experiment(world, micro_batch=micro_batch, seq=seq, samples=micro_batch * world * (2 * steps + warmup + 8),
-                     use_graph=use_graph)
+    cfg = experiment(world, micro_batch=micro_batch, seq=seq,
+                     samples=micro_batch * world * grad_accum * (2 * steps + warmup + 8), use_graph=use_graph,
+                     config=config, grad_accum=grad_accum)
     ctx = init_distributed(cfg)
     engine = TrainingEngine(cfg, ctx)
     stream = engine.batch_stream(host=True)
     dev = ctx.device
 
-    def step(batch: Batch, read: bool) -> Any:
-        return engine.train_step(iter([batch]), read_metrics=read)
+    def step(batch: list[Batch], read: bool) -> Any:
+        return engine.train_step(iter(batch), read_metrics=read)
 
     launches_per_step = 0
+    def take() -> list[Batch]:
+        return [next(stream) for _ in range(grad_accum)]
+
     for i in range(warmup):
-        b = next(stream)
+        b = take()
         if i == 0 and ctx.rank == 0 and os.environ.get("HT_COUNT_LAUNCHES", "1") != "0":
             launches_per_step = count_native_launches(lambda: step(b, True))
         else:
             step(b, True)
     # device-resident batches for the device-timed loop
-    dev_batches = [next(stream).to(dev) for _ in range(steps)]
-    host_batches = [next(stream) for _ in range(steps)]
+    dev_batches = [[mb.to(dev) for mb in take()] for _ in range(steps)]
+    host_batches = [take() for _ in range(steps)]
     torch.cuda.synchronize()
 
     def device_loop() -> None:
@@ -122,10 +154,12 @@ def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool 
             losses.append(step(b, True).loss)
 
     e2e_ms = _timed(e2e_loop)
-    h2d = host_batches[0].inputs.numel() * host_batches[0].inputs.element_size() + \
-        host_batches[0].targets.numel() * host_batches[0].targets.element_size()
+    h2d = sum(mb.inputs.numel() * mb.inputs.element_size() + mb.targets.numel() * mb.targets.element_size()
+              for mb in host_batches[0])
+    replicas = cfg.topology.data_parallel_size * cfg.topology.shard_parallel_size
     engine.close()
     ctx.shutdown()
     return {"device_ms": device_ms, "e2e_ms": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
             "gpu_launches": launches_per_step * steps, "clocks": clocks, "loss": losses[-1] if losses else None,
-            "exposed_comm_ms_per_step": None}
+            "exposed_comm_ms_per_step": None, "tokens_per_step": micro_batch * seq * grad_accum * replicas,
+            "parallelism": cfg.topology.describe() if hasattr(cfg.topology, "describe") else None}
