@@ -10,7 +10,7 @@ from ._ext import build_extension, extension, extension_path, has_extension
 from .attention import apply_rope, attention, reference_attention, rope_tables
 from .embedding import embedding
 from .grads import deliver_grad, has_main_grad, reset_main_grad_state
-from .linear import EPI_GELU, EPI_GELU_BWD, EPI_PLAIN, compute_weight, gelu_backward, gemm, linear, reference_gemm, swiglu
+from .linear import EPI_GELU, EPI_GELU_BWD, EPI_PLAIN, compute_weight, gelu_backward, gelu_mlp, gemm, linear, reference_gemm, swiglu
 from .loss import cross_entropy, lm_head_cross_entropy, reference_vocab_parallel_cross_entropy
 from .norm import add_norm, layer_norm, rms_norm
 from .optim import HYPER_SLOTS, adamw_flat, grad_sumsq, reference_adamw
@@ -37,6 +37,7 @@ __all__ = [
     "has_extension",
     "has_main_grad",
     "layer_norm",
+    "gelu_mlp",
     "linear",
     "lm_head_cross_entropy",
     "reference_adamw",

@@ -29,7 +29,7 @@ import torch.nn.functional as F
 from ._ext import extension
 from .grads import deliver_grad
 
-__all__ = ["EPI_GELU", "EPI_GELU_BWD", "EPI_PLAIN", "compute_weight", "gelu_backward", "gemm", "linear",
+__all__ = ["EPI_GELU", "EPI_GELU_BWD", "EPI_PLAIN", "compute_weight", "gelu_backward", "gelu_mlp", "gemm", "linear",
            "reference_gemm", "swiglu"]
 
 EPI_PLAIN = 0
@@ -184,6 +184,67 @@ class _LinearFunction(torch.autograd.Function):
             db = deliver_grad(bias, compute=lambda out, beta: _column_sum(g, out, beta),
                               value=None if getattr(bias, "main_grad", None) is not None else _column_sum(g).to(bias.dtype))
         return dx, dw, db, None
+
+
+class _GeluMLPFunction(torch.autograd.Function):
+    """``fc2(gelu(fc1(x)))`` with the GELU derivative applied inside fc2's data-gradient GEMM.
+
+    Forward: the fc1 GEMM epilogue adds the bias, stores the pre-activation and applies the GELU;
+    backward: the fc2 data-gradient GEMM multiplies by gelu'(pre) in its epilogue, so the
+    gradient at fc1's output is produced directly (no separate element-wise pass over the
+    hidden activations).
+    """
+
+    @staticmethod
+    def forward(ctx: Any, x: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor | None, w2: torch.Tensor,
+                b2: torch.Tensor | None) -> torch.Tensor:
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        w1c, w2c = compute_weight(w1, x.dtype), compute_weight(w2, x.dtype)
+        h = torch.empty(x2.shape[0], w1c.shape[0], dtype=x.dtype, device=x.device)
+        pre = torch.empty_like(h)
+        gemm(x2, w1c, out=h, bias=b1, aux=pre, epilogue=EPI_GELU)
+        y = gemm(h, w2c, bias=b2)
+        ctx.save_for_backward(x2, w1c, w2c, h, pre)
+        ctx.params = (w1, b1, w2, b2)
+        return y.view(*lead, w2c.shape[0])
+
+    @staticmethod
+    def backward(ctx: Any, dy: torch.Tensor) -> tuple[Any, ...]:
+        x2, w1c, w2c, h, pre = ctx.saved_tensors
+        w1, b1, w2, b2 = ctx.params
+        dy2 = dy.reshape(-1, dy.shape[-1])
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        g = gemm(dy2, w2c, b_mn_major=True, aux=pre, epilogue=EPI_GELU_BWD)
+
+        def weight_grad(param: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor | None:
+            return deliver_grad(param, compute=lambda out, beta: gemm(a, b, out=out, a_mn_major=True, b_mn_major=True, beta=beta),
+                                value=None if getattr(param, "main_grad", None) is not None else
+                                gemm(a, b, out_dtype=param.dtype, a_mn_major=True, b_mn_major=True))
+
+        def bias_grad(param: torch.Tensor | None, a: torch.Tensor) -> torch.Tensor | None:
+            if param is None:
+                return None
+            return deliver_grad(param, compute=lambda out, beta: _column_sum(a, out, beta),
+                                value=None if getattr(param, "main_grad", None) is not None else _column_sum(a).to(param.dtype))
+
+        dw2 = weight_grad(w2, dy2, h) if ctx.needs_input_grad[3] else None
+        db2 = bias_grad(b2, dy2) if ctx.needs_input_grad[4] else None
+        dx = gemm(g, w1c, b_mn_major=True).view(*dy.shape[:-1], w1c.shape[1]) if ctx.needs_input_grad[0] else None
+        dw1 = weight_grad(w1, g, x2) if ctx.needs_input_grad[1] else None
+        db1 = bias_grad(b1, g) if ctx.needs_input_grad[2] else None
+        return dx, dw1, db1, dw2, db2
+
+
+def gelu_mlp(x: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor | None, w2: torch.Tensor, b2: torch.Tensor | None) -> torch.Tensor:
+    """``gelu(x w1^T + b1) w2^T + b2`` (tanh GELU) with both GELU passes fused into GEMM epilogues on CUDA."""
+    if not x.is_cuda:
+        h = _gelu_tanh(F.linear(x, w1.to(x.dtype), None if b1 is None else b1.to(x.dtype)))
+        return F.linear(h, w2.to(x.dtype), None if b2 is None else b2.to(x.dtype))
+    return _GeluMLPFunction.apply(x, w1, b1, w2, b2)
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, activation: str | None = None) -> torch.Tensor:

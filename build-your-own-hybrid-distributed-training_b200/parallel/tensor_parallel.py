@@ -402,6 +402,9 @@ class TensorParallelFeedForward(nn.Module):
         self._activation = None if activation in ("gelu", "swiglu") else _activation_fn(activation)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.activation_name == "gelu" and self.fc1.group.is_trivial and x.is_cuda:
+            # Width-1 group: both linears and the GELU as one fused op (GELU' in fc2's dgrad epilogue).
+            return ops.gelu_mlp(x, self.fc1.weight, self.fc1.bias, self.fc2.weight, self.fc2.bias)
         h = self.fc1(x)
         if self.activation_name == "swiglu":
             h = ops.swiglu(h)

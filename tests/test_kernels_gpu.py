@@ -86,6 +86,27 @@ def test_gemm_split_k_weight_gradient_shapes(out_dtype: torch.dtype) -> None:
     assert torch.equal(again, out), "split-K result must be deterministic"
 
 
+def test_gelu_mlp_matches_fp32() -> None:
+    ops = _ops()
+    dev = torch.device("cuda")
+    x = torch.randn(3, 100, 256, device=dev).bfloat16().requires_grad_(True)
+    w1 = (torch.randn(512, 256, device=dev) * 0.05).requires_grad_(True)
+    b1 = (torch.randn(512, device=dev) * 0.1).requires_grad_(True)
+    w2 = (torch.randn(256, 512, device=dev) * 0.05).requires_grad_(True)
+    b2 = (torch.randn(256, device=dev) * 0.1).requires_grad_(True)
+    y = ops.gelu_mlp(x, w1, b1, w2, b2)
+    ref_in = [t.detach().float().cpu().requires_grad_(True) for t in (x, w1, b1, w2, b2)]
+    xr, w1r, b1r, w2r, b2r = ref_in
+    h = F.gelu(xr @ w1r.bfloat16().float().t() + b1r, approximate="tanh")
+    ref = h @ w2r.bfloat16().float().t() + b2r
+    assert _rel(y, ref) < 2e-2, _rel(y, ref)
+    g = torch.randn_like(ref)
+    y.backward(g.to(dev).bfloat16())
+    ref.backward(g.bfloat16().float())
+    for got, want in zip((x, w1, b1, w2, b2), ref_in):
+        assert _rel(got.grad, want.grad) < 3e-2, _rel(got.grad, want.grad)
+
+
 def test_column_sum_and_sum_rows() -> None:
     ops = _ops()
     ext = ops.extension()
