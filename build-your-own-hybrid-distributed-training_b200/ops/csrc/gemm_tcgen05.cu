@@ -44,6 +44,12 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA exce
 
 enum Epilogue : int { kPlain = 0, kGelu = 1, kGeluBwd = 2 };
 
+// Compile-time epilogue kind of a kernel instance.  Each instance carries only its own epilogue
+// code, which keeps the kernel small enough that the epilogue warps do not evict the MMA
+// issue loop from the instruction cache.  kKindGeneric decides everything at run time (the
+// fallback for unaligned outputs and the collective kernels).
+enum EpiKind : int { kKindGeneric = 0, kKindBf16 = 1, kKindF32 = 2, kKindGelu = 3, kKindGeluBwd = 4 };
+
 struct EpiParams {
   void* d;
   long long ldd;
@@ -281,21 +287,37 @@ __device__ __forceinline__ void pack_bf16x64(const float* v, uint4* units) {
 
 // Epilogue of one 128-byte column piece (CW = 64 bf16 or 32 fp32 output columns) of one row,
 // through the staging tile and a TMA store.  `v` holds the raw accumulator values.
-template <int CW>
+template <int CW, int KIND>
 __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
                                                    uint8_t* tile, int lane, int row, int M, int col0, int N, int tile_row0,
                                                    float alpha, float* v, int z = -1) {
   const bool full = col0 + CW <= N;
 #pragma unroll
-  for (int i = 0; i < CW; ++i) {
-    float x = v[i] * alpha;
-    const int c = col0 + i;
-    if (ep.bias_f32 != nullptr) x += (full || c < N) ? __ldg(ep.bias_f32 + c) : 0.f;
-    if (ep.bias_bf16 != nullptr) x += (full || c < N) ? bf2f(ep.bias_bf16[c]) : 0.f;
-    v[i] = x;
+  for (int i = 0; i < CW; ++i) v[i] *= alpha;
+  if (ep.bias_f32 != nullptr) {
+    const float* bp = ep.bias_f32 + col0;
+    if (full && (reinterpret_cast<uintptr_t>(bp) & 15) == 0) {  // the same 16-byte vectors for every lane
+#pragma unroll
+      for (int q = 0; q < CW / 4; ++q) {
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(bp) + q);
+        v[4 * q] += b4.x;
+        v[4 * q + 1] += b4.y;
+        v[4 * q + 2] += b4.z;
+        v[4 * q + 3] += b4.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < CW; ++i)
+        if (col0 + i < N) v[i] += __ldg(bp + i);
+    }
+  } else if (ep.bias_bf16 != nullptr) {
+#pragma unroll
+    for (int i = 0; i < CW; ++i)
+      if (col0 + i < N) v[i] += bf2f(ep.bias_bf16[col0 + i]);
   }
   uint4 units[8];
-  if (ep.epi == kGeluBwd) {
+  constexpr bool GENERIC = KIND == kKindGeneric;
+  if (KIND == kKindGeluBwd || (GENERIC && ep.epi == kGeluBwd)) {
     const __nv_bfloat16* aux = ep.aux + (long long)row * ep.ldaux + col0;
     if (row < M && full) {
 #pragma unroll
@@ -310,7 +332,7 @@ __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CU
       for (int i = 0; i < CW; ++i) v[i] *= (col0 + i < N) ? gelu_tanh_grad(bf2f(aux[i])) : 0.f;
     }
   }
-  if (ep.tma_aux) {  // GELU forward: store the pre-activation first (bf16 only, CW == 64)
+  if (KIND == kKindGelu || (GENERIC && ep.tma_aux)) {  // GELU forward: store the pre-activation first (bf16, CW == 64)
     if (CW == 64) {
       pack_bf16x64(v, units);
       if (lane == 0) bulk_wait_read_all();
@@ -324,7 +346,7 @@ __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CU
       }
     }
   }
-  if (ep.epi == kGelu) {
+  if (KIND == kKindGelu || (GENERIC && ep.epi == kGelu)) {
 #pragma unroll
     for (int i = 0; i < CW; ++i) v[i] = gelu_tanh(v[i]);
   }
@@ -341,15 +363,15 @@ __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CU
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    if (z >= 0) tma_store_3d(map_d, tile, col0, tile_row0, z);
-    else if (ep.reduce_add) tma_reduce_add_2d(map_d, tile, col0, tile_row0);
+    if (GENERIC && z >= 0) tma_store_3d(map_d, tile, col0, tile_row0, z);
+    else if ((KIND == kKindF32 || GENERIC) && ep.reduce_add) tma_reduce_add_2d(map_d, tile, col0, tile_row0);
     else tma_store_2d(map_d, tile, col0, tile_row0);
     bulk_commit();
   }
 }
 
 // All output tiles of one epilogue warp.  CW = output columns per 128-byte piece.
-template <int CW>
+template <int CW, int KIND>
 __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
                                               uint8_t* tile, uint32_t tmem_base, uint64_t* tfull_bar, uint64_t* tempty_bar,
                                               int M, int N, int num_m, int num_n, int num_tiles, int warp, int lane, int* err,
@@ -387,8 +409,8 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * CW;
 #pragma unroll
       for (int s = 0; s < CW / 32; ++s) tmem_ld_32x32b_x32(taddr + 32 * s, v + 32 * s);
-      if (ep.tma_d) {
-        epilogue_piece_tma<CW>(ep, dmap, map_aux, tile, lane, row, M, col0, N, out_row0, alpha, v, z);
+      if (KIND != kKindGeneric || ep.tma_d) {
+        epilogue_piece_tma<CW, KIND>(ep, dmap, map_aux, tile, lane, row, M, col0, N, out_row0, alpha, v, z);
       } else if (row < M) {
 #pragma unroll
         for (int s = 0; s < CW / 32; ++s)
@@ -475,7 +497,7 @@ __device__ __noinline__ void coll_copy_warp(const CollParams& c, uint32_t epoch,
   }
 }
 
-template <bool A_MN, bool B_MN, bool COLL>
+template <bool A_MN, bool B_MN, bool COLL, int KIND>
 __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtensorMap& tma_b, const CUtensorMap& tma_d,
                                           const CUtensorMap& tma_aux, int M, int N, int K, const EpiParams& ep, int* err,
                                           const CollParams* coll) {
@@ -699,12 +721,17 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
   } else {
     // ---------------- epilogue ----------------
     uint8_t* tile = sEpi + (warp - 2) * EPI_STAGE_BYTES;
-    if (ep.d_fp32)
-      epilogue_loop<32>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err,
-                        COLL ? coll : nullptr);
-    else
-      epilogue_loop<64>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp, lane, err,
-                        COLL ? coll : nullptr);
+    if constexpr (KIND == kKindGeneric) {
+      if (ep.d_fp32)
+        epilogue_loop<32, KIND>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp,
+                                lane, err, COLL ? coll : nullptr);
+      else
+        epilogue_loop<64, KIND>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp,
+                                lane, err, COLL ? coll : nullptr);
+    } else {
+      epilogue_loop<KIND == kKindF32 ? 32 : 64, KIND>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m,
+                                                      num_n, num_tiles, warp, lane, err, nullptr);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -727,12 +754,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
   }
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int KIND>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
                 EpiParams ep, int* err) {
-  gemm_body<A_MN, B_MN, false>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, nullptr);
+  gemm_body<A_MN, B_MN, false, KIND>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, nullptr);
 }
 
 template <bool A_MN, bool B_MN>
@@ -740,7 +767,7 @@ __global__ void __launch_bounds__(COLL_THREADS, 1)
     gemm_coll_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
                      EpiParams ep, int* err, const __grid_constant__ CollParams coll) {
-  gemm_body<A_MN, B_MN, true>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, &coll);
+  gemm_body<A_MN, B_MN, true, kKindGeneric>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, &coll);
 }
 
 // out[b, r, n] = sum over ranks p (in order) of recv[p][b, r, n], after every peer has published
@@ -906,10 +933,10 @@ static void check_operand(const at::Tensor& t, const char* name) {
   HT_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
 }
 
-template <bool A_MN, bool B_MN>
-static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
-                   int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
-  auto kernel = gemm_kernel<A_MN, B_MN>;
+template <bool A_MN, bool B_MN, int KIND>
+static void launch_kind(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
+                        int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
+  auto kernel = gemm_kernel<A_MN, B_MN, KIND>;
   static bool configured = false;
   if (!configured) {
     HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
@@ -919,6 +946,28 @@ static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   const int grid = std::min(units, num_sms());
   kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, md, maux, M, N, K, ep, err);
   HT_CUDA_CHECK(cudaGetLastError());
+}
+
+// The epilogue kind that covers `ep` with the least code.
+static int epilogue_kind(const EpiParams& ep) {
+  if (!ep.tma_d || ep.tma_aux != (ep.epi == kGelu)) return kKindGeneric;
+  if (ep.d_fp32) return ep.epi == kPlain ? kKindF32 : kKindGeneric;
+  if (ep.reduce_add) return kKindGeneric;
+  if (ep.epi == kGelu) return kKindGelu;
+  if (ep.epi == kGeluBwd) return kKindGeluBwd;
+  return kKindBf16;
+}
+
+template <bool A_MN, bool B_MN>
+static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
+                   int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
+  switch (epilogue_kind(ep)) {
+    case kKindBf16: launch_kind<A_MN, B_MN, kKindBf16>(ma, mb, md, maux, M, N, K, ep, err, s); break;
+    case kKindF32: launch_kind<A_MN, B_MN, kKindF32>(ma, mb, md, maux, M, N, K, ep, err, s); break;
+    case kKindGelu: launch_kind<A_MN, B_MN, kKindGelu>(ma, mb, md, maux, M, N, K, ep, err, s); break;
+    case kKindGeluBwd: launch_kind<A_MN, B_MN, kKindGeluBwd>(ma, mb, md, maux, M, N, K, ep, err, s); break;
+    default: launch_kind<A_MN, B_MN, kKindGeneric>(ma, mb, md, maux, M, N, K, ep, err, s); break;
+  }
 }
 
 }  // namespace tcg

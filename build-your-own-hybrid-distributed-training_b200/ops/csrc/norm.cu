@@ -242,8 +242,11 @@ __global__ void __launch_bounds__(WARP_ROWS_THREADS)
 }
 
 // Every CTA writes one full partial row of dw (and db): zeros for columns it never touched.
+// The second pass re-reads the row's r and dy (cache hits: the same warp read them moments
+// before) instead of keeping xhat and dy*w in registers, which keeps the kernel at two CTAs per
+// SM; with only eight resident warps it was latency-bound.
 template <bool RMS, bool HAS_DY, bool HAS_DR, int NV>
-__global__ void __launch_bounds__(WARP_ROWS_THREADS, 1)
+__global__ void __launch_bounds__(WARP_ROWS_THREADS, 2)
     norm_backward_warp_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ dr_in, const float* __restrict__ r,
                               const float* __restrict__ w, const float* __restrict__ mean, const float* __restrict__ rstd,
                               float* __restrict__ dres, __nv_bfloat16* __restrict__ ddelta, float* __restrict__ part_w,
@@ -253,35 +256,33 @@ __global__ void __launch_bounds__(WARP_ROWS_THREADS, 1)
   const int nvec = d >> 2;
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int warps = (gridDim.x * blockDim.x) >> 5;
-  float wv[NV][4], aw[NV][4], ab[NV][4];
+  float aw[NV][4], ab[NV][4];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) wv[j][e] = aw[j][e] = ab[j][e] = 0.f;
-    if (lane + 32 * j < nvec) ld4(w + 4 * (lane + 32 * j), wv[j]);
+    for (int e = 0; e < 4; ++e) aw[j][e] = ab[j][e] = 0.f;
   }
   for (int row = warp_global; row < rows; row += warps) {
     const long long base = (long long)row * d;
     const float mu = RMS ? 0.f : mean[row], rs = rstd[row];
-    float xh[NV][4], g[NV][4];
     float sg = 0.f, sgx = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int v = lane + 32 * j;
-      float rv[4] = {0.f, 0.f, 0.f, 0.f}, gy[4] = {0.f, 0.f, 0.f, 0.f};
       if (v < nvec) {
+        float rv[4], gy[4] = {0.f, 0.f, 0.f, 0.f}, wv[4];
         ld4(r + base + 4 * v, rv);
         if (HAS_DY) ld4(dy + base + 4 * v, gy);
-      }
+        ld4(w + 4 * v, wv);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float xhat = v < nvec ? (rv[e] - mu) * rs : 0.f;
-        xh[j][e] = xhat;
-        g[j][e] = gy[e] * wv[j][e];
-        aw[j][e] += gy[e] * xhat;
-        ab[j][e] += gy[e];
-        sg += g[j][e];
-        sgx += g[j][e] * xhat;
+        for (int e = 0; e < 4; ++e) {
+          const float xhat = (rv[e] - mu) * rs;
+          const float g = gy[e] * wv[e];
+          aw[j][e] += gy[e] * xhat;
+          ab[j][e] += gy[e];
+          sg += g;
+          sgx += g * xhat;
+        }
       }
     }
     const float mg = RMS ? 0.f : warp_sum(sg) / d;
@@ -290,10 +291,16 @@ __global__ void __launch_bounds__(WARP_ROWS_THREADS, 1)
     for (int j = 0; j < NV; ++j) {
       const int v = lane + 32 * j;
       if (v < nvec) {
-        float o[4], din[4] = {0.f, 0.f, 0.f, 0.f};
+        float rv[4], gy[4] = {0.f, 0.f, 0.f, 0.f}, wv[4], o[4], din[4] = {0.f, 0.f, 0.f, 0.f};
+        ld4(r + base + 4 * v, rv);
+        if (HAS_DY) ld4(dy + base + 4 * v, gy);
+        ld4(w + 4 * v, wv);
         if (HAS_DR) ld4(dr_in + base + 4 * v, din);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] = rs * (g[j][e] - mg - xh[j][e] * mgx) + din[e];
+        for (int e = 0; e < 4; ++e) {
+          const float xhat = (rv[e] - mu) * rs;
+          o[e] = rs * (gy[e] * wv[e] - mg - xhat * mgx) + din[e];
+        }
         st4(dres + base + 4 * v, o);
         if (ddelta != nullptr) st4(ddelta + base + 4 * v, o);
       }
