@@ -46,7 +46,7 @@ def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int
     base, max_blocks = _slots(handle, world)
     mc = int(handle.multicast_ptr) if os.environ.get("HT_NVLS", "0") == "1" else 0
     extension().bucket_all_reduce(flat, list(handle.buffer_ptrs), list(handle.signal_pad_ptrs), mc, int(start), int(numel),
-                                  float(scale), int(handle.rank), base, min(max_blocks, 64), workspace.status, _TIMEOUT_S)
+                                  float(scale), int(handle.rank), base, min(max_blocks, 128), workspace.status, _TIMEOUT_S)
     return workspace.status
 
 

@@ -112,29 +112,51 @@ __global__ void __launch_bounds__(THREADS) bucket_allreduce_kernel(Peers pp, flo
     block_barrier(pp, rank, world, slot_base, status, 2, timeout_ns);
     return;
   }
-  // two-shot: reduce-scatter my chunk
-  for (long long i = lo + threadIdx.x * 4; i < hi; i += THREADS * 4) {
-    if (i + 3 < hi) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  // two-shot: reduce-scatter my chunk.  Each thread keeps UNROLL independent 16-byte vectors
+  // (UNROLL x world peer loads) in flight: the loop is bound by NVLink latency otherwise.
+  constexpr int UNROLL = 4;
+  constexpr long long STEP = (long long)THREADS * 4 * UNROLL;
+  for (long long i0 = lo + threadIdx.x * 4; i0 < hi; i0 += STEP) {
+    float4 acc[UNROLL];
+    bool vec[UNROLL];
 #pragma unroll
-      for (int p = 0; p < MAX_RANKS; ++p) {
-        if (p >= world) break;
-        const float4 v = *reinterpret_cast<const float4*>(pp.buf[p] + start + i);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+    for (int u = 0; u < UNROLL; ++u) {
+      const long long i = i0 + (long long)u * THREADS * 4;
+      vec[u] = i + 3 < hi;
+      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int p = 0; p < MAX_RANKS; ++p) {
+      if (p >= world) break;
+      float4 v[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+        if (vec[u]) v[u] = *reinterpret_cast<const float4*>(pp.buf[p] + start + i0 + (long long)u * THREADS * 4);
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        if (vec[u]) {
+          acc[u].x += v[u].x;
+          acc[u].y += v[u].y;
+          acc[u].z += v[u].z;
+          acc[u].w += v[u].w;
+        }
       }
-      acc.x *= scale;
-      acc.y *= scale;
-      acc.z *= scale;
-      acc.w *= scale;
-      *reinterpret_cast<float4*>(pp.buf[rank] + start + i) = acc;
-    } else {
-      for (long long j = i; j < hi; ++j) {
-        float s = 0.f;
-        for (int p = 0; p < world; ++p) s += pp.buf[p][start + j];
-        pp.buf[rank][start + j] = s * scale;
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const long long i = i0 + (long long)u * THREADS * 4;
+      if (vec[u]) {
+        acc[u].x *= scale;
+        acc[u].y *= scale;
+        acc[u].z *= scale;
+        acc[u].w *= scale;
+        *reinterpret_cast<float4*>(pp.buf[rank] + start + i) = acc[u];
+      } else {
+        for (long long j = i; j < hi; ++j) {  // ragged tail of the range
+          float sum = 0.f;
+          for (int p = 0; p < world; ++p) sum += pp.buf[p][start + j];
+          pp.buf[rank][start + j] = sum * scale;
+        }
       }
     }
   }
@@ -143,11 +165,19 @@ __global__ void __launch_bounds__(THREADS) bucket_allreduce_kernel(Peers pp, flo
   for (int q = 1; q < world; ++q) {
     const int p = (rank + q) % world;
     range(p, lo, hi);
-    for (long long i = lo + threadIdx.x * 4; i < hi; i += THREADS * 4) {
-      if (i + 3 < hi) {
-        *reinterpret_cast<float4*>(pp.buf[rank] + start + i) = *reinterpret_cast<const float4*>(pp.buf[p] + start + i);
-      } else {
-        for (long long j = i; j < hi; ++j) pp.buf[rank][start + j] = pp.buf[p][start + j];
+    for (long long i0 = lo + threadIdx.x * 4; i0 < hi; i0 += STEP) {
+      float4 v[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const long long i = i0 + (long long)u * THREADS * 4;
+        if (i + 3 < hi) v[u] = *reinterpret_cast<const float4*>(pp.buf[p] + start + i);
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const long long i = i0 + (long long)u * THREADS * 4;
+        if (i + 3 < hi) *reinterpret_cast<float4*>(pp.buf[rank] + start + i) = v[u];
+        else
+          for (long long j = i; j < hi; ++j) pp.buf[rank][start + j] = pp.buf[p][start + j];
       }
     }
   }
