@@ -1,0 +1,47 @@
+"""Static checks over the native sources: forbidden instruction forms and calls never appear.
+
+* no TMA / bulk load with cluster multicast anywhere (peer memory may be read by our kernels);
+* no batched asynchronous memcpy entry points;
+* every in-tree CUDA source is compiled for sm_100a only.
+"""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+PKG = ROOT / "build-your-own-hybrid-distributed-training_b200"
+SOURCES = sorted([*PKG.rglob("*.cu"), *PKG.rglob("*.cuh"), *PKG.rglob("*.cpp"), *PKG.rglob("*.py"), ROOT / "bench.py",
+                  ROOT / "__graft_entry__.py"])
+
+
+def _text(p: Path) -> str:
+    return p.read_text(encoding="utf-8", errors="replace")
+
+
+def test_no_cluster_multicast_loads() -> None:
+    pattern = re.compile(r"multicast::cluster")
+    offenders = [str(p.relative_to(ROOT)) for p in SOURCES if pattern.search(_text(p))]
+    assert not offenders, offenders
+
+
+def test_no_batched_memcpy_calls() -> None:
+    names = ["cuda" + "MemcpyBatchAsync", "cuda" + "Memcpy3DBatchAsync", "cu" + "MemcpyBatchAsync", "cu" + "Memcpy3DBatchAsync"]
+    offenders = [str(p.relative_to(ROOT)) for p in SOURCES for n in names if n in _text(p)]
+    assert not offenders, offenders
+
+
+def test_extension_targets_sm100a_only() -> None:
+    ext = _text(PKG / "ops" / "_ext.py")
+    assert "arch=compute_100a,code=sm_100a" in ext
+    assert "sm_90" not in ext and "compute_90" not in ext
+
+
+def test_device_waits_are_bounded() -> None:
+    """Spin loops on mbarriers or flags go through the bounded helpers (iteration or time limits)."""
+    csrc = PKG / "ops" / "csrc"
+    for p in csrc.glob("*.cu"):
+        text = _text(p)
+        for m in re.finditer(r"while \(\s*!\s*mbar_try_wait", text):
+            raise AssertionError(f"unbounded mbarrier wait in {p.name} at offset {m.start()}")
