@@ -109,6 +109,37 @@ def experiment(world: int, *, micro_batch: int, seq: int, samples: int, use_grap
     raise ValueError(f"unknown benchmark config {config!r}; expected one of {CONFIGS}")
 
 
+def _exposed_communication_ms(engine: TrainingEngine, stream: Any, take: Callable[[], list[Batch]], steps: int,
+                               grad_accum: int, cfg: ExperimentConfig) -> float | None:
+    """Per-step time that gradient communication adds to the data-parallel step.
+
+    Both loops run eagerly: the same steps with and without the gradient reduction
+    (``no_sync``); the difference is the communication the backward pass did not hide.
+    Only defined for data-parallel (DDP) configurations.
+    """
+    if cfg.topology.data_parallel_size <= 1 or cfg.topology.shard_parallel_size > 1 or cfg.topology.tensor_parallel_size > 1:
+        return None
+    dev = engine.context.device
+    engine.graph_enabled = False
+    batches = [[mb.to(dev) for mb in take()] for _ in range(2 * steps + 2)]
+    for b in batches[:2]:
+        engine.train_step(iter(b), read_metrics=False)
+
+    def synced() -> None:
+        for b in batches[2:2 + steps]:
+            engine.train_step(iter(b), read_metrics=False)
+
+    def local() -> None:
+        with engine.model.no_sync():
+            for b in batches[2 + steps:]:
+                engine.train_step(iter(b), read_metrics=False)
+
+    full = _timed(synced)
+    compute = _timed(local)
+    engine.graph_enabled = True
+    return max(0.0, (full - compute) / steps)
+
+
 def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool = True,
         clock_start: Callable[[], None] | None = None, clock_stop: Callable[[], dict] | None = None,
         config: str = "gpt2_ddp", grad_accum: int = 1) -> dict:
@@ -154,6 +185,7 @@ def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool 
             losses.append(step(b, True).loss)
 
     e2e_ms = _timed(e2e_loop)
+    exposed = _exposed_communication_ms(engine, stream, take, steps, grad_accum, cfg) if world > 1 else 0.0
     h2d = sum(mb.inputs.numel() * mb.inputs.element_size() + mb.targets.numel() * mb.targets.element_size()
               for mb in host_batches[0])
     replicas = cfg.topology.data_parallel_size * cfg.topology.shard_parallel_size
@@ -161,5 +193,5 @@ def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool 
     ctx.shutdown()
     return {"device_ms": device_ms, "e2e_ms": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
             "gpu_launches": launches_per_step * steps, "clocks": clocks, "loss": losses[-1] if losses else None,
-            "exposed_comm_ms_per_step": None, "tokens_per_step": micro_batch * seq * grad_accum * replicas,
+            "exposed_comm_ms_per_step": exposed, "tokens_per_step": micro_batch * seq * grad_accum * replicas,
             "parallelism": cfg.topology.describe() if hasattr(cfg.topology, "describe") else None}

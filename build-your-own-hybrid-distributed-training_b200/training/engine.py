@@ -117,6 +117,7 @@ class TrainingEngine:
         self._criterion: Callable[[torch.Tensor, torch.Tensor], torch.Tensor] = cross_entropy_loss if self._transformer else mse_loss
         self._build_data()
         self._graph: torch.cuda.CUDAGraph | None = None
+        self.graph_enabled = True  # replay the captured step when TrainingConfig.cuda_graph is set
         self._graph_io: dict[str, Any] = {}
         self._eager_steps = 0
         self._graph_done: torch.cuda.Event | None = None
@@ -177,7 +178,7 @@ class TrainingEngine:
         return self.state
 
     def _use_graph(self) -> bool:
-        return bool(self.config.training.cuda_graph and self.context.device.type == "cuda")
+        return bool(self.config.training.cuda_graph and self.graph_enabled and self.context.device.type == "cuda")
 
     def _loss(self, inputs: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         if self._fused_loss:
