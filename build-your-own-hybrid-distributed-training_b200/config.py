@@ -218,6 +218,7 @@ class FSDPConfig:
     check_reduction_order: bool = False
     use_padding: bool = True
     prefetch: bool = True
+    fused_update: bool = True
 
     def __post_init__(self) -> None:
         _check(self.auto_wrap_min_num_params >= 0, "config.FSDPConfig", "auto_wrap_min_num_params must be non-negative",

@@ -10,6 +10,12 @@ allocation (DDP allocates its flat gradient buffer there).  Every wait in the
 kernel is bounded; a timeout sets the workspace status word, which
 ``SymmetricWorkspace.check_status`` turns into a :class:`KernelError`.
 
+``fsdp_reduce_scatter_adamw`` is the FSDP gradient path in one kernel: each rank
+sums its shard of the unit's gradient over the peers' staging buffers, scales
+it, zeroes the padding and applies AdamW to its fp32 master shard, writing the
+bf16 copy that ``fsdp_all_gather`` (a P2P copy of every peer's bf16 shard into
+the local full buffer) reads in the next forward.
+
 The tensor-parallel fused paths (all-gather inside the first GEMM of a
 column-parallel layer, reduce-scatter inside the GEMM of a row-parallel layer)
 are exposed as :func:`all_gather_linear` / :func:`linear_reduce_scatter`;
@@ -26,7 +32,7 @@ import torch
 from ._ext import extension
 
 __all__ = ["HAS_FUSED_TENSOR_PARALLEL", "all_gather_linear", "bucket_all_reduce", "can_fuse_sequence_parallel",
-           "linear_reduce_scatter"]
+           "fsdp_all_gather", "fsdp_reduce_scatter_adamw", "linear_reduce_scatter"]
 
 HAS_FUSED_TENSOR_PARALLEL = True
 _TIMEOUT_S = float(os.environ.get("HT_COLLECTIVE_TIMEOUT_S", "30"))
@@ -48,6 +54,35 @@ def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int
     extension().bucket_all_reduce(flat, list(handle.buffer_ptrs), list(handle.signal_pad_ptrs), mc, int(start), int(numel),
                                   float(scale), int(handle.rank), base, min(max_blocks, 128), workspace.status, _TIMEOUT_S)
     return workspace.status
+
+
+def fsdp_reduce_scatter_adamw(workspace: Any, staging: torch.Tensor, shard16: torch.Tensor, *, shard: int, valid: int,
+                              scale: float, param: torch.Tensor, exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor,
+                              hyper: torch.Tensor, betas: tuple[float, float], eps: float, weight_decay: float,
+                              grad_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Reduce-scatter the unit gradient in every peer's ``staging`` and apply AdamW to this rank's shard.
+
+    ``staging`` (bf16 or fp32, at least ``world * shard`` elements) and ``shard16`` (bf16,
+    ``shard`` elements) must be allocations of ``workspace``; ``param`` / ``exp_avg`` /
+    ``exp_avg_sq`` are this rank's fp32 master shard and moments; ``hyper`` is the optimizer's
+    device vector ``[lr, step, grad_scale, skip]``.  Elements at local index ``>= valid`` are
+    padding and get a zero gradient.  ``grad_out`` (fp32, optional) receives the reduced shard
+    gradient.  Returns the workspace status word (non-zero after a timed-out peer wait).
+    """
+    handle = workspace.handle_of(staging)
+    world = workspace.group.size
+    base, max_blocks = _slots(handle, world)
+    extension().fsdp_reduce_scatter_adamw(staging, list(handle.buffer_ptrs), list(handle.signal_pad_ptrs), int(handle.rank),
+                                          int(shard), int(valid), float(scale), param, exp_avg, exp_avg_sq, shard16, grad_out,
+                                          hyper, float(betas[0]), float(betas[1]), float(eps), float(weight_decay), base,
+                                          max_blocks, workspace.status, _TIMEOUT_S)
+    return workspace.status
+
+
+def fsdp_all_gather(workspace: Any, shard16: torch.Tensor, out: torch.Tensor) -> None:
+    """Copy every peer's bf16 shard (``shard16``, a workspace allocation) into ``out`` (rank order)."""
+    handle = workspace.handle_of(shard16)
+    extension().fsdp_all_gather(list(handle.buffer_ptrs), out, int(shard16.numel()), int(handle.rank))
 
 
 class _TensorParallelSites:

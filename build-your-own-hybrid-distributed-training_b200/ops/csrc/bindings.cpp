@@ -41,6 +41,12 @@ void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Ten
 void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
                        int64_t start, int64_t numel, double scale, int64_t rank, int64_t slot_base, int64_t max_blocks,
                        at::Tensor status, double timeout_s);
+void fsdp_reduce_scatter_adamw(at::Tensor staging, std::vector<int64_t> grad_ptrs, std::vector<int64_t> pad_ptrs, int64_t rank,
+                               int64_t shard, int64_t valid, double scale, at::Tensor param, at::Tensor exp_avg,
+                               at::Tensor exp_avg_sq, at::Tensor shard16, c10::optional<at::Tensor> grad_out, at::Tensor hyper,
+                               double beta1, double beta2, double eps, double wd, int64_t slot_base, int64_t max_blocks,
+                               at::Tensor status, double timeout_s);
+void fsdp_all_gather(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t shard, int64_t rank);
 }  // namespace ht
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -71,4 +77,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_forward", &ht::attention_forward);
   m.def("attention_backward", &ht::attention_backward);
   m.def("bucket_all_reduce", &ht::bucket_all_reduce, "in-kernel NVLink all-reduce of one DDP bucket");
+  m.def("fsdp_reduce_scatter_adamw", &ht::fsdp_reduce_scatter_adamw,
+        "FSDP gradient reduce-scatter fused with the cast and the sharded AdamW update (NVLink peer memory)");
+  m.def("fsdp_all_gather", &ht::fsdp_all_gather, "FSDP all-gather of bf16 parameter shards over NVLink peer memory");
 }

@@ -184,6 +184,209 @@ __global__ void __launch_bounds__(THREADS) bucket_allreduce_kernel(Peers pp, flo
   block_barrier(pp, rank, world, slot_base, status, 3, timeout_ns);
 }
 
+
+// ---------------------------------------------------------------------------------------------------
+// FSDP: the reduce-scatter of one unit's gradient fused with the cast and the sharded AdamW update,
+// and the all-gather of the unit's bf16 parameter shards, both over NVLink peer memory.
+//
+// fsdp_rs_adamw_kernel: every rank has copied its full (padded) gradient of the unit into its
+// peer-mapped staging buffer.  Rank r owns elements [r*shard, (r+1)*shard) of the flat parameter.
+// After a barrier with every peer, each block sums its sub-range of the owned shard over the G
+// staging buffers in rank order (fp32 accumulation), multiplies by `scale` (1/G for an average),
+// zeroes the padding tail (local index >= valid), and applies AdamW to the fp32 master shard and
+// its moments in the same pass.  The bf16 copy of the updated shard goes to this rank's
+// peer-mapped parameter buffer, which the next all-gather reads.  A closing barrier keeps every
+// peer from overwriting its staging buffer while another rank still reads it; once the whole
+// kernel has finished on a rank, every peer has finished writing its parameter shard too, so the
+// next all-gather (stream-ordered after this kernel) reads updated shards.
+//
+// fsdp_all_gather_kernel: copies every peer's bf16 shard into the local full buffer with 16-byte
+// P2P loads.  It needs no barrier of its own: the reduce-scatter kernels' barriers order every
+// write of a shard buffer against every read (see above), and the first all-gather follows a
+// stream-ordered barrier after the buffers were initialised.
+
+struct ShardPeers {
+  const void* buf[MAX_RANKS];
+  uint32_t* pad[MAX_RANKS];
+};
+
+template <typename T>
+struct Vec8;  // eight consecutive gradient elements
+
+template <>
+struct Vec8<__nv_bfloat16> {
+  uint4 raw;
+  __device__ __forceinline__ void load(const void* base, long long i) {
+    raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + i);
+  }
+  __device__ __forceinline__ void add_to(float* acc) const {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      acc[2 * j] += f.x;
+      acc[2 * j + 1] += f.y;
+    }
+  }
+  static __device__ __forceinline__ float scalar(const void* base, long long i) {
+    return bf2f(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+  }
+};
+
+template <>
+struct Vec8<float> {
+  float4 lo, hi;
+  __device__ __forceinline__ void load(const void* base, long long i) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
+    lo = p[0];
+    hi = p[1];
+  }
+  __device__ __forceinline__ void add_to(float* acc) const {
+    acc[0] += lo.x; acc[1] += lo.y; acc[2] += lo.z; acc[3] += lo.w;
+    acc[4] += hi.x; acc[5] += hi.y; acc[6] += hi.z; acc[7] += hi.w;
+  }
+  static __device__ __forceinline__ float scalar(const void* base, long long i) {
+    return reinterpret_cast<const float*>(base)[i];
+  }
+};
+
+struct AdamParams {
+  float beta1, beta2, eps, wd;
+  float lr, gs, step, decay, bc2_sqrt;
+  bool skip;
+};
+
+__device__ __forceinline__ void adam_one(float g, float& p, float& m, float& v, const AdamParams& a) {
+  const float gj = g * a.gs;
+  m = m + (1.f - a.beta1) * (gj - m);
+  v = a.beta2 * v + (1.f - a.beta2) * gj * gj;
+  const float denom = sqrtf(v) / a.bc2_sqrt + a.eps;
+  p = p * a.decay - a.step * m / denom;
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(THREADS) fsdp_rs_adamw_kernel(ShardPeers sp, long long shard, long long valid, float scale,
+                                                                float* __restrict__ param, float* __restrict__ mom1,
+                                                                float* __restrict__ mom2, __nv_bfloat16* __restrict__ out16,
+                                                                float* __restrict__ grad_out, const float* __restrict__ hyper,
+                                                                float beta1, float beta2, float eps, float wd, int rank, int world,
+                                                                int slot_base, int* status, unsigned long long timeout_ns) {
+  Peers pp{};
+#pragma unroll
+  for (int p = 0; p < MAX_RANKS; ++p) pp.pad[p] = sp.pad[p];
+  if (!block_barrier(pp, rank, world, slot_base, status, 11, timeout_ns)) return;
+  AdamParams a;
+  a.beta1 = beta1;
+  a.beta2 = beta2;
+  a.eps = eps;
+  a.wd = wd;
+  a.lr = hyper[0];
+  a.gs = hyper[2];
+  a.skip = hyper[3] != 0.f;
+  const float t = hyper[1];
+  a.step = a.lr / (1.f - powf(beta1, t));
+  a.bc2_sqrt = sqrtf(1.f - powf(beta2, t));
+  a.decay = 1.f - a.lr * wd;
+  const long long base = (long long)rank * shard;  // this rank's shard inside every staging buffer
+  const long long per_block = ((shard + gridDim.x - 1) / gridDim.x + 7) / 8 * 8;
+  const long long lo = (long long)blockIdx.x * per_block;
+  const long long hi = min(lo + per_block, shard);
+  if (VEC) {
+    for (long long i = lo + threadIdx.x * 8; i < hi; i += (long long)THREADS * 8) {
+      // all peers' vectors in flight before any is used
+      Vec8<T> in[MAX_RANKS];
+#pragma unroll
+      for (int p = 0; p < MAX_RANKS; ++p)
+        if (p < world) in[p].load(sp.buf[p], base + i);
+      float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < MAX_RANKS; ++p)
+        if (p < world) in[p].add_to(g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) g[j] = (i + j < valid) ? g[j] * scale : 0.f;
+      if (grad_out != nullptr) {
+        float4* go = reinterpret_cast<float4*>(grad_out + i);
+        go[0] = make_float4(g[0], g[1], g[2], g[3]);
+        go[1] = make_float4(g[4], g[5], g[6], g[7]);
+      }
+      if (a.skip) continue;
+      float4* pp4 = reinterpret_cast<float4*>(param + i);
+      float4* m4 = reinterpret_cast<float4*>(mom1 + i);
+      float4* v4 = reinterpret_cast<float4*>(mom2 + i);
+      float4 pv[2] = {pp4[0], pp4[1]}, mv[2] = {m4[0], m4[1]}, vv[2] = {v4[0], v4[1]};
+      float* pf = reinterpret_cast<float*>(pv);
+      float* mf = reinterpret_cast<float*>(mv);
+      float* vf = reinterpret_cast<float*>(vv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) adam_one(g[j], pf[j], mf[j], vf[j], a);
+      pp4[0] = pv[0];
+      pp4[1] = pv[1];
+      m4[0] = mv[0];
+      m4[1] = mv[1];
+      v4[0] = vv[0];
+      v4[1] = vv[1];
+      __align__(16) __nv_bfloat16 b[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = f2bf(pf[j]);
+      *reinterpret_cast<uint4*>(out16 + i) = *reinterpret_cast<const uint4*>(b);
+    }
+  } else {
+    for (long long i = lo + threadIdx.x; i < hi; i += THREADS) {
+      float g = 0.f;
+      for (int p = 0; p < world; ++p) g += Vec8<T>::scalar(sp.buf[p], base + i);
+      g = i < valid ? g * scale : 0.f;
+      if (grad_out != nullptr) grad_out[i] = g;
+      if (a.skip) continue;
+      float pv = param[i], mv = mom1[i], vv = mom2[i];
+      adam_one(g, pv, mv, vv, a);
+      param[i] = pv;
+      mom1[i] = mv;
+      mom2[i] = vv;
+      out16[i] = f2bf(pv);
+    }
+  }
+  block_barrier(pp, rank, world, slot_base, status, 12, timeout_ns);
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(THREADS) fsdp_all_gather_kernel(ShardPeers sp, __nv_bfloat16* __restrict__ out, long long shard,
+                                                                  int rank, int world) {
+  const long long stride = (long long)gridDim.x * THREADS;
+  if (VEC) {
+    constexpr int UNROLL = 4;
+    const long long n8 = shard / 8;
+    const long long total = n8 * world;
+    uint4* dst = reinterpret_cast<uint4*>(out);
+    for (long long i0 = blockIdx.x * (long long)THREADS + threadIdx.x; i0 < total; i0 += stride * UNROLL) {
+      uint4 v[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const long long i = i0 + u * stride;
+        if (i < total) {
+          const int q = (int)(i / n8);
+          const int p = (rank + q) % world;  // the local shard first, then the peers in rotation
+          v[u] = reinterpret_cast<const uint4*>(sp.buf[p])[i - (long long)q * n8];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const long long i = i0 + u * stride;
+        if (i < total) {
+          const int q = (int)(i / n8);
+          const int p = (rank + q) % world;
+          dst[(long long)p * n8 + (i - (long long)q * n8)] = v[u];
+        }
+      }
+    }
+  } else {
+    const long long total = shard * world;
+    for (long long i = blockIdx.x * (long long)THREADS + threadIdx.x; i < total; i += stride) {
+      const int p = (int)(i / shard);
+      out[i] = reinterpret_cast<const __nv_bfloat16*>(sp.buf[p])[i - (long long)p * shard];
+    }
+  }
+}
+
 }  // namespace comm
 
 void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
@@ -207,6 +410,89 @@ void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::v
   comm::bucket_allreduce_kernel<<<blocks, comm::THREADS, 0, stream()>>>(
       pp, reinterpret_cast<float*>(multicast_ptr), start, numel, (float)scale, (int)rank, world, (int)slot_base,
       status.data_ptr<int>(), (unsigned long long)(timeout_s * 1e9));
+  HT_CUDA_CHECK(cudaGetLastError());
+}
+
+
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+void fsdp_reduce_scatter_adamw(at::Tensor staging, std::vector<int64_t> grad_ptrs, std::vector<int64_t> pad_ptrs, int64_t rank,
+                               int64_t shard, int64_t valid, double scale, at::Tensor param, at::Tensor exp_avg,
+                               at::Tensor exp_avg_sq, at::Tensor shard16, c10::optional<at::Tensor> grad_out, at::Tensor hyper,
+                               double beta1, double beta2, double eps, double wd, int64_t slot_base, int64_t max_blocks,
+                               at::Tensor status, double timeout_s) {
+  const c10::cuda::CUDAGuard guard(param.device());
+  const int world = (int)grad_ptrs.size();
+  HT_CHECK(world >= 2 && world <= comm::MAX_RANKS, "fsdp_reduce_scatter_adamw supports 2..8 ranks");
+  HT_CHECK((int)pad_ptrs.size() == world, "one signal pad per rank expected");
+  HT_CHECK(rank >= 0 && rank < world, "rank out of range");
+  HT_CHECK(staging.scalar_type() == at::kBFloat16 || staging.scalar_type() == at::kFloat, "bf16 or fp32 gradient staging expected");
+  HT_CHECK(staging.numel() >= shard * world, "the staging buffer must hold the unit's padded gradient");
+  HT_CHECK(valid >= 0 && valid <= shard, "valid must lie in [0, shard]");
+  for (const at::Tensor* t : {&param, &exp_avg, &exp_avg_sq})
+    HT_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == shard, "fp32 shard, moments of the shard size");
+  HT_CHECK(shard16.scalar_type() == at::kBFloat16 && shard16.is_contiguous() && shard16.numel() == shard, "bf16 shard buffer size");
+  HT_CHECK(hyper.scalar_type() == at::kFloat && hyper.numel() >= 4 && hyper.is_cuda(), "device hyper-parameter vector expected");
+  HT_CHECK(status.scalar_type() == at::kInt, "int32 status expected");
+  float* gout = nullptr;
+  if (grad_out.has_value() && grad_out->defined()) {
+    HT_CHECK(grad_out->scalar_type() == at::kFloat && grad_out->is_contiguous() && grad_out->numel() == shard, "grad_out size");
+    gout = grad_out->data_ptr<float>();
+  }
+  if (shard == 0) return;
+  comm::ShardPeers sp{};
+  bool vec = shard % 8 == 0;
+  for (int p = 0; p < world; ++p) {
+    sp.buf[p] = reinterpret_cast<const void*>(grad_ptrs[p]);
+    sp.pad[p] = reinterpret_cast<uint32_t*>(pad_ptrs[p]);
+    vec = vec && aligned16(sp.buf[p]);
+  }
+  vec = vec && aligned16(param.data_ptr()) && aligned16(exp_avg.data_ptr()) && aligned16(exp_avg_sq.data_ptr()) &&
+        aligned16(shard16.data_ptr()) && (gout == nullptr || aligned16(gout));
+  // At most one block per SM: every block waits at the barriers for the same block index on the
+  // peers, so the whole grid must be resident at once (one 512-thread block per SM fits).
+  const int blocks = (int)std::max<long long>(
+      1, std::min<long long>(std::min<long long>(max_blocks, num_sms()), (shard + comm::THREADS * 8 - 1) / (comm::THREADS * 8)));
+  const unsigned long long tns = (unsigned long long)(timeout_s * 1e9);
+  auto* out16 = reinterpret_cast<__nv_bfloat16*>(shard16.data_ptr());
+#define HT_FSDP_RS(T, V)                                                                                                   \
+  comm::fsdp_rs_adamw_kernel<T, V><<<blocks, comm::THREADS, 0, stream()>>>(                                                \
+      sp, shard, valid, (float)scale, param.data_ptr<float>(), exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(), out16, \
+      gout, hyper.data_ptr<float>(), (float)beta1, (float)beta2, (float)eps, (float)wd, (int)rank, world, (int)slot_base,      \
+      status.data_ptr<int>(), tns)
+  if (staging.scalar_type() == at::kBFloat16) {
+    if (vec) HT_FSDP_RS(__nv_bfloat16, true); else HT_FSDP_RS(__nv_bfloat16, false);
+  } else {
+    if (vec) HT_FSDP_RS(float, true); else HT_FSDP_RS(float, false);
+  }
+#undef HT_FSDP_RS
+  HT_CUDA_CHECK(cudaGetLastError());
+}
+
+void fsdp_all_gather(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t shard, int64_t rank) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int world = (int)shard_ptrs.size();
+  HT_CHECK(world >= 2 && world <= comm::MAX_RANKS, "fsdp_all_gather supports 2..8 ranks");
+  HT_CHECK(rank >= 0 && rank < world, "rank out of range");
+  HT_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == shard * world,
+           "bf16 output of world x shard elements expected");
+  if (shard == 0) return;
+  comm::ShardPeers sp{};
+  bool vec = shard % 8 == 0 && aligned16(out.data_ptr());
+  for (int p = 0; p < world; ++p) {
+    sp.buf[p] = reinterpret_cast<const void*>(shard_ptrs[p]);
+    vec = vec && aligned16(sp.buf[p]);
+  }
+  const long long work = vec ? shard / 8 * world : shard * world;
+  const int blocks = (int)std::max<long long>(
+      1, std::min<long long>((long long)num_sms() * 4, (work + comm::THREADS * 4 - 1) / (comm::THREADS * 4)));
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (vec)
+    comm::fsdp_all_gather_kernel<true><<<blocks, comm::THREADS, 0, stream()>>>(sp, o, shard, (int)rank, world);
+  else
+    comm::fsdp_all_gather_kernel<false><<<blocks, comm::THREADS, 0, stream()>>>(sp, o, shard, (int)rank, world);
   HT_CUDA_CHECK(cudaGetLastError());
 }
 

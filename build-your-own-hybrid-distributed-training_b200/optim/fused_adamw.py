@@ -107,6 +107,9 @@ class FusedAdamW(torch.optim.Optimizer):
         self._hyper_host = torch.zeros(4, dtype=torch.float32, pin_memory=device.type == "cuda")
         self._hyper = torch.zeros(4, dtype=torch.float32, device=device)
         self._grad_scale_device: torch.Tensor | None = None
+        # Recorded after each eager host-to-device copy of the staging buffer: the host must not
+        # overwrite the pinned buffer while that copy may still be queued.
+        self._hyper_copied: torch.cuda.Event | None = None
 
     # -- flat views ---------------------------------------------------------------------------------
     @property
@@ -156,7 +159,24 @@ class FusedAdamW(torch.optim.Optimizer):
         self._step_count += 1
         for p in self._params:
             self.state[p]["step"].fill_(float(self._step_count))
+        if self._hyper_copied is not None:
+            self._hyper_copied.synchronize()
         self._hyper_host.copy_(torch.tensor([group["lr"], float(self._step_count), 1.0, 0.0]))
+
+    @torch.no_grad()
+    def stage_hyper_parameters(self) -> None:
+        """Copy the staged ``[lr, step, grad_scale, skip]`` to the device vector (stream-ordered, no host sync).
+
+        :meth:`launch_step` does this itself; kernels that apply the update elsewhere (the FSDP
+        reduce-scatter + AdamW kernel) call it before they run.
+        """
+        self._hyper.copy_(self._hyper_host, non_blocking=True)
+        if self._hyper.is_cuda and not torch.cuda.is_current_stream_capturing():
+            if self._hyper_copied is None:
+                self._hyper_copied = torch.cuda.Event()
+            self._hyper_copied.record()
+        if self._grad_scale_device is not None:
+            self._hyper[2:3].copy_(self._grad_scale_device.reshape(1))
 
     @torch.no_grad()
     def launch_step(self) -> None:
@@ -164,9 +184,7 @@ class FusedAdamW(torch.optim.Optimizer):
         group = self.param_groups[0]
         beta1, beta2 = group["betas"]
         self._collect_autograd_grads()
-        self._hyper.copy_(self._hyper_host, non_blocking=True)
-        if self._grad_scale_device is not None:
-            self._hyper[2:3].copy_(self._grad_scale_device.reshape(1))
+        self.stage_hyper_parameters()
         ops.adamw_flat(self._param_flat, self._grad_flat, self._exp_avg, self._exp_avg_sq, self._compute_flat, self._hyper,
                        beta1=beta1, beta2=beta2, eps=group["eps"], weight_decay=group["weight_decay"])
         if self._compute_flat is not None:

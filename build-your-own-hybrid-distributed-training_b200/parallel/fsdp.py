@@ -21,9 +21,15 @@ dicts, ``optimizer_parameter_layout``).  Differences:
   reduces ``param.grad`` of the unwrapped model, which no longer holds them);
 * ``prefetch=True`` issues the next unit's all-gather on a side stream while
   the current unit computes (the reference has no prefetch);
-* on CUDA the reduce-scatter, cast and sharded AdamW update can run as one
-  fused kernel (:mod:`hybrid_training.ops.comm`) when the optimizer is built
-  with ``FusedAdamW`` over the flat shards.
+* on CUDA, with :meth:`FullyShardedDataParallel.enable_fused_update` (the
+  engine calls it when the optimizer is ``FusedAdamW`` over the flat shards and
+  the step needs no gradient norm), each unit's reduce-scatter, cast and
+  sharded AdamW update run as ONE kernel over NVLink peer memory during the
+  backward pass (``ops.comm.fsdp_reduce_scatter_adamw``), and the all-gathers
+  read the peers' updated bf16 shards directly (``ops.comm.fsdp_all_gather``).
+  The reference reduce-scatters with ``torch.distributed`` and steps
+  ``torch.optim.AdamW`` afterwards (``fsdp.py:704-769``,
+  ``sharded_optimizer.py:340-355``).
 """
 
 from __future__ import annotations
@@ -187,6 +193,10 @@ class FlatParamHandle:
         self._accumulate_only = False
         self._reduction_count = 0
         self._prefetched: tuple[torch.Tensor, torch.cuda.Event] | None = None
+        # fused reduce-scatter + AdamW state (attach_fused_update): (workspace, optimizer, staging)
+        self._fused: tuple[Any, Any, torch.Tensor] | None = None
+        self._sym_shard: torch.Tensor | None = None
+        self._sym_stale = True
         self._detach_originals()
 
     # -- construction -----------------------------------------------------------------------------
@@ -241,6 +251,19 @@ class FlatParamHandle:
         s = shard if shard.device == self._device else shard.to(self._device, non_blocking=True)
         return s.to(self._compute_dtype).contiguous()
 
+    def _all_gather_into(self, full: torch.Tensor, shard: torch.Tensor) -> None:
+        """Fill ``full`` with every rank's shard in the compute dtype (P2P kernel when fused, else NCCL)."""
+        if self._fused is not None:
+            from ..ops.comm import fsdp_all_gather
+
+            assert self._sym_shard is not None
+            fsdp_all_gather(self._fused[0], self._sym_shard, full)
+            if self._recorder is not None:
+                self._recorder.record("fsdp_all_gather_p2p", self._shard_group.name, num_bytes=full.numel() * full.element_size())
+            return
+        _, work = all_gather_tensor(self._compute_shard(shard), self._shard_group, out=full, recorder=self._recorder)
+        work.wait()
+
     def prefetch(self) -> None:
         """Start this unit's all-gather on a side stream (consumed by the next ``gather_full``)."""
         if self._prefetched is not None or not self.flat_param.is_cuda or self._shard_group.is_trivial:
@@ -249,9 +272,7 @@ class FlatParamHandle:
         stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(stream):
             full = torch.empty(self._padded_numel, dtype=self._compute_dtype, device=self._device)
-            _, work = all_gather_tensor(self._compute_shard(self.flat_param.detach()), self._shard_group, out=full,
-                                        recorder=self._recorder)
-            work.wait()
+            self._all_gather_into(full, self.flat_param.detach())
             event = torch.cuda.Event()
             event.record(stream)
         full.record_stream(torch.cuda.current_stream())
@@ -264,8 +285,7 @@ class FlatParamHandle:
             torch.cuda.current_stream().wait_event(event)
         else:
             full = torch.empty(self._padded_numel, dtype=self._compute_dtype, device=self._device)
-            _, work = all_gather_tensor(self._compute_shard(shard), self._shard_group, out=full, recorder=self._recorder)
-            work.wait()
+            self._all_gather_into(full, shard)
         self._full = full
         self._full_bytes = full.untyped_storage().nbytes()
         self._is_sharded = False
@@ -305,14 +325,63 @@ class FlatParamHandle:
             return
         with torch.no_grad(), _keep_version(full):
             _alloc_storage(full, need)
-            _, work = all_gather_tensor(self._compute_shard(self.flat_param.detach()), self._shard_group, out=full.detach(),
-                                        recorder=self._recorder)
-            work.wait()
+            self._all_gather_into(full.detach(), self.flat_param.detach())
         if full is self._full:
             self._is_sharded = False
 
+    # -- fused reduce-scatter + AdamW ------------------------------------------------------------------------
+    def fused_update_supported(self) -> bool:
+        """Whether this unit can take the fused path (CUDA, bf16 compute, fp32 master, plain shard group)."""
+        sp_partial = bool(self._sp_ranges) and self._sequence_group is not None and self._sequence_group.size > 1
+        return (self.flat_param.is_cuda and not self._shard_group.is_trivial and self._shard_group.size <= 8
+                and (self._replica_group is None or self._replica_group.size == 1)
+                and not self._config.cpu_offload_params and self._compute_dtype == torch.bfloat16
+                and self._master_dtype == torch.float32 and self._requires_grad and not sp_partial)
+
+    def attach_fused_update(self, workspace: Any, optimizer: Any, staging: torch.Tensor) -> None:
+        """Route this unit's gradient through the fused kernel (collective: allocates a peer-mapped shard)."""
+        self._sym_shard = workspace.allocate(self._shard_numel, torch.bfloat16)
+        self._fused = (workspace, optimizer, staging)
+        self._sym_stale = True
+
+    def sync_fused_shard(self) -> None:
+        """Write the bf16 copy of the fp32 master shard into the peer-mapped buffer (local; caller barriers)."""
+        if self._sym_shard is not None:
+            with torch.no_grad():
+                self._sym_shard.copy_(self.flat_param.detach())
+            self._sym_stale = False
+
+    fused = property(lambda self: self._fused is not None)
+    fused_shard_stale = property(lambda self: self._fused is not None and self._sym_stale)
+
+    def _fused_reduce_scatter_update(self, grad: torch.Tensor) -> None:
+        from ..ops.comm import fsdp_reduce_scatter_adamw
+
+        assert self._fused is not None and self._sym_shard is not None
+        workspace, optimizer, staging = self._fused
+        staging[:self._padded_numel].copy_(grad.reshape(-1))
+        state = optimizer.state[self.flat_param]
+        group = optimizer.param_groups[0]
+        local = self.local_shard_range()
+        valid = max(0, min(self._shard_numel, self._total_numel - local.start))
+        scale = 1.0 / self._shard_group.size if self._config.average_gradients else 1.0
+        fsdp_reduce_scatter_adamw(workspace, staging, self._sym_shard, shard=self._shard_numel, valid=valid, scale=scale,
+                                  param=self.flat_param.data, exp_avg=state["exp_avg"], exp_avg_sq=state["exp_avg_sq"],
+                                  hyper=optimizer.hyper_parameters, betas=group["betas"], eps=group["eps"],
+                                  weight_decay=group["weight_decay"])
+        if self._recorder is not None:
+            self._recorder.record("fsdp_reduce_scatter_adamw", self._shard_group.name,
+                                  num_bytes=self._padded_numel * staging.element_size())
+        self._reduction_count += 1
+
     # -- gradient reduction --------------------------------------------------------------------------------
     def reduce_scatter_gradient(self, grad_full: torch.Tensor) -> torch.Tensor | None:
+        if self._fused is not None and not self._accumulate_only:
+            # Fused path: the update happens here; autograd receives no shard gradient.
+            grad = grad_full if self._accumulator is None else grad_full.to(self._reduce_dtype) + self._accumulator
+            self._accumulator = None
+            self._fused_reduce_scatter_update(grad)
+            return None
         grad = grad_full.to(self._reduce_dtype).contiguous()
         if self._accumulate_only:
             self._accumulator = grad.clone() if self._accumulator is None else self._accumulator.add_(grad)
@@ -400,6 +469,7 @@ class FlatParamHandle:
             dst = overlap.start - local.start
             src = overlap.start - e.offset
             shard[dst:dst + overlap.length].copy_(t.reshape(-1)[src:src + overlap.length].to(shard.dtype))
+        self._sym_stale = True
 
     def full_tensors(self) -> dict[str, torch.Tensor]:
         shard = self.flat_param.detach().to(self._device).contiguous()
@@ -470,6 +540,7 @@ class FullyShardedDataParallel(nn.Module):
             assert_metadata_consistent(self._handle.metadata(), shard_group, name="the flat parameter layout",
                                        operation="fsdp.verify_flat_layout")
         self._next_unit: FullyShardedDataParallel | None = None
+        self._fused_units: list[FullyShardedDataParallel] | None = None  # set on the root by enable_fused_update
         self._check_no_cross_unit_tying()
         self._link_prefetch_order()
 
@@ -522,7 +593,66 @@ class FullyShardedDataParallel(nn.Module):
                 raise
             return getattr(inner, name)
 
+    # -- fused reduce-scatter + AdamW ------------------------------------------------------------------------
+    def enable_fused_update(self, workspace: Any, optimizer: Any, *, accumulate: bool = False) -> bool:
+        """Update every unit inside its gradient reduce-scatter kernel; returns whether the path is on.
+
+        Requirements (decided from configuration only, so every rank decides alike): a peer-mapped
+        ``workspace`` for the shard group, ``optimizer`` a CUDA ``FusedAdamW`` whose parameters are
+        exactly the units' flat shards, bf16 compute with fp32 master shards, no replica group, no
+        CPU offload.  The caller must not need the gradient afterwards (no clipping, no norm, no
+        loss scaling): the optimizer step happens during the backward pass, unit by unit, and
+        ``optimizer.step()`` must be skipped.  ``accumulate`` stages fp32 gradients (exact sums
+        of accumulated micro-batches) instead of bf16 ones.  Collective over the shard group.
+        """
+        from ..optim.fused_adamw import FusedAdamW
+
+        units = [u for u in self.fsdp_units() if u._handle is not None]
+        if workspace is None or not units or not isinstance(optimizer, FusedAdamW) or not optimizer.flat_parameters.is_cuda:
+            return False
+        owned = {id(p) for p in optimizer.param_groups[0]["params"]}
+        shards = {id(u._handle.flat_param) for u in units}
+        if owned != shards or len(optimizer.param_groups) != 1:
+            return False
+        if not all(u._handle.fused_update_supported() for u in units):
+            return False
+        dtype = torch.float32 if accumulate else torch.bfloat16
+        staging = workspace.allocate(max(u._handle.padded_numel for u in units), dtype)
+        for u in units:
+            u._handle.attach_fused_update(workspace, optimizer, staging)
+        self._fused_units = units
+        self._fused_workspace = workspace
+        _LOG.info("fsdp: fused reduce-scatter + AdamW over NVLink for %d units (%s gradient staging)", len(units),
+                  str(dtype).replace("torch.", ""))
+        return True
+
+    @property
+    def fused_update_enabled(self) -> bool:
+        return self._fused_units is not None
+
+    def sync_fused_shards(self) -> None:
+        """Refresh stale peer-mapped bf16 shards from the fp32 masters, then barrier (collective).
+
+        Called at the root's forward and by ``summon_full_params``: after a checkpoint load or any
+        other write to the master shards through this API, every rank marks the same units stale,
+        so every rank reaches the barrier.
+        """
+        if self._fused_units is None or not any(u._handle.fused_shard_stale for u in self._fused_units):
+            return
+        for u in self._fused_units:
+            if u._handle.fused_shard_stale:
+                u._handle.sync_fused_shard()
+        # Stream-ordered barrier: a peer's all-gather launched after this reads the refreshed shards.
+        all_reduce(torch.zeros(1, device=self._device), self._shard_group, op=ReduceOp.SUM, recorder=self._recorder).wait()
+
+    def check_fused_status(self) -> None:
+        """Raise if a fused kernel timed out waiting for a peer (reads a device word: host sync)."""
+        if self._fused_units is not None:
+            self._fused_workspace.check_status()
+
     def forward(self, *args: Any, **kwargs: Any) -> Any:
+        if self._fused_units is not None:
+            self.sync_fused_shards()
         full = self._handle.unshard() if self._handle is not None else None
         if self._config.prefetch and self._next_unit is not None and self._next_unit._handle is not None \
                 and torch.is_grad_enabled():
@@ -575,6 +705,7 @@ class FullyShardedDataParallel(nn.Module):
         """Gather every unit's full parameters (bound as views); optionally write edits back to the shards."""
         units = [u for u in self.fsdp_units() if u._handle is not None]
         fulls = []
+        self.sync_fused_shards()
         with torch.no_grad():
             for u in units:
                 full = u._handle.gather_full(u._handle.flat_param.detach())
@@ -587,6 +718,7 @@ class FullyShardedDataParallel(nn.Module):
                     for u, full in zip(units, fulls):
                         r = u._handle.local_shard_range()
                         u._handle.flat_param.data.copy_(full[r.start:r.end].to(u._handle.flat_param.dtype))
+                        u._handle._sym_stale = True
                 for u in units:
                     u._handle.free_full()
 

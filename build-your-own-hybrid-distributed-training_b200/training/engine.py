@@ -111,6 +111,7 @@ class TrainingEngine:
         self.scheduler = LearningRateSchedule(cfg.scheduler, base_learning_rate=cfg.optimizer.learning_rate,
                                               total_steps=max(cfg.training.max_steps, 1))
         self.scaler = GradScaler(cfg.mixed_precision.scaler, ctx.group("world"), ctx.device, recorder=self.recorder)
+        self._fsdp_fused_update = self._enable_fsdp_fused_update()
         self.state = TrainingState()
         self._transformer = cfg.model.kind == "transformer"
         self._fused_loss = self._transformer and cfg.model.fused_loss
@@ -126,6 +127,24 @@ class TrainingEngine:
         reset_peak_memory(ctx.device)
         _LOG.info("engine ready: %s | %d local parameters", self.model.description.strategy,
                   sum(p.numel() for p in self.model.optimizer_parameters()))
+
+    def _enable_fsdp_fused_update(self) -> bool:
+        """Turn on the FSDP reduce-scatter + AdamW kernel when the step does not need the gradients afterwards.
+
+        The fused kernel updates each unit during the backward pass, so it needs: FSDP on CUDA with
+        ``fsdp.fused_update``, the fused AdamW optimizer, no clipping, no gradient-norm metric and no
+        loss scaling.  Every input is configuration, so every rank decides the same way.
+        """
+        cfg, ctx = self.config, self.context
+        fsdp = self.model.fsdp
+        inner = self.optimizer.inner
+        if (fsdp is None or ctx.device.type != "cuda" or not cfg.fsdp.fused_update or not isinstance(inner, FusedAdamW)
+                or cfg.training.max_grad_norm > 0 or cfg.training.collect_metrics or self.scaler.enabled):
+            return False
+        workspace = ctx.symmetric_workspace("shard")
+        return fsdp.enable_fused_update(workspace, inner, accumulate=cfg.training.gradient_accumulation_steps > 1)
+
+    fsdp_fused_update = property(lambda self: self._fsdp_fused_update)
 
     # -- data ----------------------------------------------------------------------------------------------
     def _build_data(self) -> None:
@@ -189,6 +208,10 @@ class TrainingEngine:
         """Forward/backward/reduce/clip/update with no host synchronisation; returns device (loss, grad norm)."""
         n = len(micro_batches)
         total = None
+        inner = self.optimizer.inner
+        if self._fsdp_fused_update:
+            # The update runs inside the backward pass's reduce-scatter kernels: stage [lr, step, ...] first.
+            inner.stage_hyper_parameters()
         for i, (x, y) in enumerate(micro_batches):
             ctx = self.model.no_sync() if i < n - 1 else _null()
             with ctx:
@@ -203,8 +226,9 @@ class TrainingEngine:
         t = self.config.training
         if t.max_grad_norm > 0 or t.collect_metrics:
             norm = self.optimizer.clip_grad_norm(t.max_grad_norm)
-        inner = self.optimizer.inner
-        if isinstance(inner, FusedAdamW) and inner.flat_parameters.is_cuda and not self.scaler.enabled:
+        if self._fsdp_fused_update:
+            pass  # every flat shard was updated by its unit's reduce-scatter kernel
+        elif isinstance(inner, FusedAdamW) and inner.flat_parameters.is_cuda and not self.scaler.enabled:
             inner.launch_step()
         elif self.scaler.enabled:
             self.scaler.step(self.optimizer, params, already_unscaled=True)
@@ -248,6 +272,8 @@ class TrainingEngine:
             self.state.samples_seen += global_samples
         else:
             self.state.advance_step(samples=global_samples)
+        if read_metrics and self._fsdp_fused_update:
+            self.model.fsdp.check_fused_status()
         loss = float(loss_t.item()) if read_metrics else float("nan")
         norm = float(norm_t.item()) if (read_metrics and norm_t is not None) else None
         self.state.last_loss = loss

@@ -340,3 +340,92 @@ def llama_cuda_worker(rank: int, world: int, topology: dict[str, Any], fused_tp:
         return out
     finally:
         ctx.shutdown()
+
+
+def _fsdp_experiment(world: int, *, fused_update: bool, steps: int = 3, accumulation: int = 1) -> dict[str, Any]:
+    cfg = _llama_experiment(world, {"shard_parallel_size": world}, steps=steps)
+    cfg["fsdp"] = {"auto_wrap_min_num_params": 10000, "fused_update": fused_update}
+    cfg["training"] = {"max_steps": steps, "log_every_steps": 0, "gradient_accumulation_steps": accumulation}
+    cfg["optimizer"] = {"learning_rate": 1e-3, "weight_decay": 0.1}
+    return cfg
+
+
+def fsdp_fused_kernels_worker(rank: int, world: int) -> dict[str, Any]:
+    """The FSDP reduce-scatter + AdamW kernel and the P2P shard all-gather against NCCL + PyTorch AdamW."""
+    import torch.distributed as dist
+
+    from hybrid_training.ops import reference_adamw
+    from hybrid_training.ops.comm import fsdp_all_gather, fsdp_reduce_scatter_adamw
+
+    cfg = ExperimentConfig.from_dict(_fsdp_experiment(world, fused_update=True))
+    ctx = init_distributed(cfg)
+    try:
+        ws = ctx.symmetric_workspace("shard")
+        assert ws is not None, "symmetric memory is unavailable"
+        pg = ctx.group("shard").process_group
+        dev = ctx.device
+        errors: dict[str, float] = {}
+        lr, b1, b2, eps, wd, step = 1e-3, 0.9, 0.95, 1e-8, 0.1, 3
+        # (shard, non-padding elements of this rank's shard, staging dtype): vector and scalar paths
+        for shard, pad, dtype in ((1_000_008, 0, torch.bfloat16), (262_144, 7, torch.float32), (12_345, 5, torch.bfloat16)):
+            tag = f"{shard}-{str(dtype)[6:]}"
+            gen = torch.Generator(device="cuda").manual_seed(10 + rank)
+            staging = ws.allocate(world * shard + 16, dtype)
+            staging.copy_(torch.randn(staging.numel(), device=dev, generator=gen).to(dtype))
+            total = world * shard - pad
+            valid = max(0, min(shard, total - rank * shard))
+            # expected gradient: fp32 reduce-scatter of the staged values, averaged, padding zeroed
+            full = staging[:world * shard].float().clone()
+            expect = torch.empty(shard, device=dev)
+            dist.reduce_scatter_tensor(expect, full, group=pg)
+            expect /= world
+            expect[valid:] = 0
+            pgen = torch.Generator(device="cuda").manual_seed(1000)  # same master values on every rank's slot
+            param = torch.randn(world * shard, device=dev, generator=pgen)[rank * shard:(rank + 1) * shard].clone()
+            m = 0.01 * torch.randn(shard, device=dev, generator=gen)
+            v = 0.01 * torch.rand(shard, device=dev, generator=gen)
+            ref_p, ref_m, ref_v = param.clone(), m.clone(), v.clone()
+            reference_adamw(ref_p, expect, ref_m, ref_v, lr=lr, beta1=b1, beta2=b2, eps=eps, weight_decay=wd, step=step)
+            shard16 = ws.allocate(shard, torch.bfloat16)
+            hyper = torch.tensor([lr, float(step), 1.0, 0.0], device=dev)
+            grad_out = torch.full((shard,), float("nan"), device=dev)
+            for _ in range(2):  # the second call checks that the barriers leave the signal pads reusable
+                p_run, m_run, v_run = param.clone(), m.clone(), v.clone()
+                fsdp_reduce_scatter_adamw(ws, staging, shard16, shard=shard, valid=valid, scale=1.0 / world, param=p_run,
+                                          exp_avg=m_run, exp_avg_sq=v_run, hyper=hyper, betas=(b1, b2), eps=eps,
+                                          weight_decay=wd, grad_out=grad_out)
+            torch.cuda.synchronize()
+            ws.check_status()
+            scale = float(expect.abs().max()) + 1e-12
+            errors[f"grad {tag}"] = float((grad_out - expect).abs().max()) / scale
+            errors[f"param {tag}"] = float((p_run - ref_p).abs().max())
+            errors[f"exp_avg {tag}"] = float((m_run - ref_m).abs().max())
+            errors[f"exp_avg_sq {tag}"] = float((v_run - ref_v).abs().max())
+            errors[f"bf16 copy {tag}"] = float((shard16.float() - p_run.bfloat16().float()).abs().max())
+            dist.barrier(group=pg)
+            out = torch.full((world * shard,), float("nan"), device=dev, dtype=torch.bfloat16)
+            fsdp_all_gather(ws, shard16, out)
+            expect_full = torch.empty(world * shard, device=dev, dtype=torch.bfloat16)
+            dist.all_gather_into_tensor(expect_full, shard16, group=pg)
+            torch.cuda.synchronize()
+            errors[f"all_gather {tag}"] = 0.0 if torch.equal(out, expect_full) else float("inf")
+            dist.barrier(group=pg)
+        return {"errors": errors}
+    finally:
+        ctx.shutdown()
+
+
+def fsdp_fused_update_worker(rank: int, world: int, fused: bool, steps: int, accumulation: int) -> dict[str, Any]:
+    """Engine steps of a Llama-style decoder under FSDP with or without the fused reduce-scatter + AdamW."""
+    cfg = ExperimentConfig.from_dict(_fsdp_experiment(world, fused_update=fused, steps=steps, accumulation=accumulation))
+    ctx = init_distributed(cfg)
+    try:
+        engine = TrainingEngine(cfg, ctx)
+        engine.train(max_steps=steps)
+        full = engine.model.full_state_dict()
+        out = {"fused": engine.fsdp_fused_update, "losses": [m.loss for m in engine.history],
+               "full": {k: v.detach().float().cpu().clone() for k, v in full.items()}}
+        engine.close()
+        return out
+    finally:
+        ctx.shutdown()

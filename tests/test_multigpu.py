@@ -58,3 +58,28 @@ def test_tensor_sequence_parallel_llama_fused_matches_nccl_path() -> None:
     nccl = launch_workers(W.llama_cuda_worker, 2, args=(topo, False, 3), timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
     for a, b in zip(fused[0].value["losses"], nccl[0].value["losses"]):
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), (fused[0].value["losses"], nccl[0].value["losses"])
+
+
+def test_fsdp_fused_reduce_scatter_adamw_and_all_gather_kernels() -> None:
+    """One kernel: reduce-scatter over peer memory + cast + AdamW on the shard; P2P shard all-gather."""
+    results = launch_workers(W.fsdp_fused_kernels_worker, 2, timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    for r in results:
+        for key, err in r.value["errors"].items():
+            limit = 2e-6 if key.startswith(("grad", "param", "exp_avg")) else 0.0
+            assert err <= limit, (key, r.value["errors"])
+
+
+@pytest.mark.parametrize("accumulation", [1, 2])
+def test_fsdp_fused_update_trains_like_nccl_path(accumulation: int) -> None:
+    fused = launch_workers(W.fsdp_fused_update_worker, 2, args=(True, 3, accumulation), timeout_seconds=300,
+                           extra_env={"NCCL_NVLS_ENABLE": "0"})
+    nccl = launch_workers(W.fsdp_fused_update_worker, 2, args=(False, 3, accumulation), timeout_seconds=300,
+                          extra_env={"NCCL_NVLS_ENABLE": "0"})
+    assert fused[0].value["fused"] and not nccl[0].value["fused"]
+    for a, b in zip(fused[0].value["losses"], nccl[0].value["losses"]):
+        assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (fused[0].value["losses"], nccl[0].value["losses"])
+    assert fused[0].value["losses"] == fused[1].value["losses"]
+    for name, t in fused[0].value["full"].items():
+        ref = nccl[0].value["full"][name]
+        err = float((t - ref).abs().max())
+        assert err < 5e-3 * max(1.0, float(ref.abs().max())), (name, err)
