@@ -21,7 +21,8 @@ def _text(p: Path) -> str:
 
 
 def test_no_cluster_multicast_loads() -> None:
-    pattern = re.compile(r"multicast::cluster")
+    # the forbidden qualifier, assembled so that this file does not spell it out
+    pattern = re.compile(re.escape("::".join(["multicast", "cluster"])))
     offenders = [str(p.relative_to(ROOT)) for p in SOURCES if pattern.search(_text(p))]
     assert not offenders, offenders
 
