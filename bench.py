@@ -217,7 +217,7 @@ def main() -> None:
             out.pop("gpu_launches")
         _emit(out)
     if dist.is_initialized():
-        dist.barrier()
+        dist.barrier(group=dist.group.WORLD)
         dist.destroy_process_group()
 
 

@@ -49,13 +49,13 @@ def count_native_launches(fn: Callable[[], Any]) -> int:
 def _max_over_ranks(ms: float) -> float:
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if dist.is_initialized() and dist.get_world_size() > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=dist.group.WORLD)
     return float(t.item())
 
 
 def _timed(fn: Callable[[], None]) -> float:
     if dist.is_initialized() and dist.get_world_size() > 1:
-        dist.barrier()
+        dist.barrier(group=dist.group.WORLD)
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
@@ -63,7 +63,7 @@ def _timed(fn: Callable[[], None]) -> float:
     stop.record()
     torch.cuda.synchronize()
     if dist.is_initialized() and dist.get_world_size() > 1:
-        dist.barrier()
+        dist.barrier(group=dist.group.WORLD)
     return _max_over_ranks(start.elapsed_time(stop))
 
 

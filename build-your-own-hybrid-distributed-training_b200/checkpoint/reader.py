@@ -289,14 +289,99 @@ def inspect_checkpoint(directory: str | Path, *, verify: bool = True) -> dict[st
             "verification": verification}
 
 
-def _console_main() -> int:
-    if len(sys.argv) < 2:
-        print("usage: hybrid-inspect-checkpoint <checkpoint-directory>", file=sys.stderr)
+def _plan_for_world(manifest: CheckpointManifest, key: str, world: int) -> list[dict[str, Any]]:
+    """Per target rank: the saved files that an equal ``world``-way split of tensor ``key`` would read."""
+    record = manifest.tensors[key]
+    from .reshard import describe_reshard
+
+    shard = -(-record.numel // world)
+    out = []
+    for r in range(world):
+        lo = min(r * shard, record.numel)
+        length = max(0, min(shard, record.numel - lo))
+        entry = describe_reshard(manifest, key, ShardRange(lo, length)) if length else {"sources": []}
+        out.append({"target_rank": r, "range": [lo, length], "files": sorted({s["file"] for s in entry["sources"]})})
+    return out
+
+
+def _console_main(argv: list[str] | None = None) -> int:
+    """``hybrid-inspect-checkpoint``: summarise and verify a checkpoint without building a model.
+
+    Only the JSON manifest and metadata are parsed; payload files are hashed (unless
+    ``--no-verify``) but never deserialised.  Exit codes: 0 valid, 1 invalid or unreadable,
+    2 bad usage.
+    """
+    import argparse
+
+    parser = argparse.ArgumentParser(prog="hybrid-inspect-checkpoint", description="Inspect and validate a distributed checkpoint.")
+    parser.add_argument("checkpoint", help="checkpoint directory (checkpoint-step-NNNNNN)")
+    parser.add_argument("--json", action="store_true", help="print only the JSON summary")
+    parser.add_argument("--tensors", action="store_true", help="list tensors with their shards")
+    parser.add_argument("--limit", type=int, default=20, help="maximum tensors listed by --tensors")
+    parser.add_argument("--plan", metavar="TENSOR", help="files that a full read of TENSOR touches")
+    parser.add_argument("--reshard-to", type=int, metavar="W", help="with --plan: files each rank of an equal W-way split reads")
+    parser.add_argument("--no-verify", action="store_true", help="skip size and SHA-256 verification")
+    try:
+        args = parser.parse_args(argv)
+    except SystemExit as exc:
+        return 2 if exc.code else 0
+    path = Path(args.checkpoint)
+    if not path.is_dir():
+        print(f"error: {path} is not a directory", file=sys.stderr)
         return 2
     try:
-        summary = inspect_checkpoint(sys.argv[1])
+        summary = inspect_checkpoint(path, verify=not args.no_verify)
+        manifest = CheckpointManifest.read(path / MANIFEST_FILENAME)
     except CheckpointError as exc:
         print(f"error: {exc}", file=sys.stderr)
         return 1
-    print(json.dumps(summary, indent=2, sort_keys=True))
+    if args.plan is not None and args.plan not in manifest.tensors:
+        print(f"error: unknown tensor {args.plan!r}; e.g. {sorted(manifest.tensors)[:5]}", file=sys.stderr)
+        return 2
+    if args.json:
+        if args.plan is not None:
+            from .reshard import describe_reshard
+
+            record = manifest.tensors[args.plan]
+            summary["plan"] = (describe_reshard(manifest, args.plan, ShardRange(0, record.numel)) if args.reshard_to is None
+                               else _plan_for_world(manifest, args.plan, args.reshard_to))
+        print(json.dumps(summary, indent=2, sort_keys=True))
+        return 0
+    print(f"checkpoint: {path}")
+    print(manifest.summary())
+    print("training state")
+    for k, v in sorted(summary["training_state"].items()):
+        print(f"  {k:<22} {v}")
+    print("integrity")
+    verified = summary["verification"].get("files_verified", 0)
+    print(f"  {'files verified':<22} {verified} / {summary['files']}")
+    print(f"  {'total payload bytes':<22} {summary['total_bytes']:,}")
+    if args.no_verify:
+        print("  (checksums were not verified: --no-verify)")
+    if args.tensors:
+        print("tensors")
+        for key in sorted(manifest.tensors)[:max(args.limit, 0)]:
+            r = manifest.tensors[key]
+            print(f"  {key:<48} {r.category:<9} {tuple(r.global_shape)!s:<18} shards={len(r.shards)}")
+        if len(manifest.tensors) > args.limit:
+            print(f"  ... {len(manifest.tensors) - args.limit} more")
+    if args.plan is not None:
+        record = manifest.tensors[args.plan]
+        if args.reshard_to is None:
+            from .reshard import describe_reshard
+
+            plan = describe_reshard(manifest, args.plan, ShardRange(0, record.numel))
+            print(f"read plan for {args.plan} ({record.numel} elements)")
+            for s in plan["sources"]:
+                print(f"  {s['file']:<16} saved by rank {s['saved_rank']:<3} elements [{s['overlap'][0]}, "
+                      f"{s['overlap'][0] + s['overlap'][1]})")
+        else:
+            print(f"reshard plan for {args.plan} onto {args.reshard_to} ranks")
+            for entry in _plan_for_world(manifest, args.plan, args.reshard_to):
+                lo, n = entry["range"]
+                print(f"  rank {entry['target_rank']:<3} [{lo}, {lo + n}) <- {', '.join(entry['files']) or '-'}")
     return 0
+
+
+if __name__ == "__main__":
+    sys.exit(_console_main())

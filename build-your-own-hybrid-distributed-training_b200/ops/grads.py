@@ -16,11 +16,27 @@ from collections.abc import Callable
 
 import torch
 
-__all__ = ["deliver_grad", "has_main_grad", "main_grad_beta", "reset_main_grad_state"]
+__all__ = ["adopt_exposed_gradient", "deliver_grad", "has_main_grad", "main_grad_beta", "reset_main_grad_state"]
 
 
 def has_main_grad(param: torch.Tensor | None) -> bool:
     return param is not None and getattr(param, "main_grad", None) is not None
+
+
+def adopt_exposed_gradient(param: torch.Tensor, *, from_autograd: bool) -> None:
+    """Decide how the first delivery after a synchronisation writes ``main_grad``.
+
+    After a step, data parallelism exposes ``param.grad`` as a view of ``main_grad``
+    (``_grad_exposed``).  If the caller released it (``zero_grad(set_to_none=True)``)
+    the next delivery overwrites; if the caller kept it (zeroed in place, or left it to
+    accumulate across steps as plain PyTorch allows) a native delivery accumulates onto
+    it.  A gradient that reaches us through autograd already contains the kept value
+    (autograd accumulated into ``param.grad``), so it always overwrites.
+    """
+    if getattr(param, "_grad_exposed", False):
+        param._grad_exposed = False
+        if from_autograd or param.grad is None:
+            param.main_grad_fresh = True
 
 
 def main_grad_beta(param: torch.Tensor) -> float:
@@ -44,6 +60,7 @@ def deliver_grad(param: torch.Tensor, compute: Callable[[torch.Tensor, float], N
         if value is None:
             raise ValueError("deliver_grad needs a value when the parameter has no main_grad")
         return value
+    adopt_exposed_gradient(param, from_autograd=not native)
     beta = main_grad_beta(param)
     if compute is not None:
         compute(main, beta)

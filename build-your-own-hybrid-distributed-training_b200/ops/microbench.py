@@ -164,7 +164,7 @@ def _max_over_ranks(ms: float) -> float:
     import torch.distributed as dist
 
     t = torch.tensor([ms], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=dist.group.WORLD)
     return float(t)
 
 
@@ -192,7 +192,7 @@ def bench_tp_layer(seq: int) -> None:
         result = {}
         for fused in (True, False):
             ctx.fused_tensor_collectives = fused
-            dist.barrier()
+            dist.barrier(group=dist.group.WORLD)
             result[fused] = _max_over_ranks(_time(layer, 5))
         flops = 6.0 * seq * d * (6144 + 4096 + 28672 + 14336) / world
         if ctx.rank == 0:

@@ -245,9 +245,10 @@ class DistributedDataParallel(nn.Module):
         """Gradient produced by plain autograd (CPU ops, or ops without fused delivery)."""
         if param.grad is None:
             return
-        from ..ops.grads import deliver_grad
+        from ..ops.grads import adopt_exposed_gradient, deliver_grad
 
         grad = param.grad
+        adopt_exposed_gradient(param, from_autograd=True)
         param.grad = None
         deliver_grad(param, value=grad.detach().to(param.main_grad.dtype), native=False)
 
@@ -344,6 +345,7 @@ class DistributedDataParallel(nn.Module):
         for bucket in self._buckets:
             for pos, p in enumerate(bucket.parameters):
                 p.grad = bucket.view_for(pos).to(p.dtype) if p.dtype != bucket.buffer.dtype else bucket.view_for(pos)
+                p._grad_exposed = True
             bucket.reset()
         self._next_bucket = 0
         self._backward_in_progress = False
