@@ -79,10 +79,15 @@ def fsdp_reduce_scatter_adamw(workspace: Any, staging: torch.Tensor, shard16: to
     return workspace.status
 
 
-def fsdp_all_gather(workspace: Any, shard16: torch.Tensor, out: torch.Tensor) -> None:
-    """Copy every peer's bf16 shard (``shard16``, a workspace allocation) into ``out`` (rank order)."""
+def fsdp_all_gather(workspace: Any, shard16: torch.Tensor, out: torch.Tensor, *, copy_engine: bool = False) -> None:
+    """Copy every peer's bf16 shard (``shard16``, a workspace allocation) into ``out`` (rank order).
+
+    ``copy_engine=False`` runs the P2P load kernel; ``True`` issues one peer ``cudaMemcpyAsync``
+    per rank, which occupies no SMs and so overlaps a concurrently running compute kernel.
+    """
     handle = workspace.handle_of(shard16)
-    extension().fsdp_all_gather(list(handle.buffer_ptrs), out, int(shard16.numel()), int(handle.rank))
+    fn = extension().fsdp_all_gather_copy_engine if copy_engine else extension().fsdp_all_gather
+    fn(list(handle.buffer_ptrs), out, int(shard16.numel()), int(handle.rank))
 
 
 class _TensorParallelSites:

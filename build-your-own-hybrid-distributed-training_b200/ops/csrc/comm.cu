@@ -496,4 +496,23 @@ void fsdp_all_gather(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t sh
   HT_CUDA_CHECK(cudaGetLastError());
 }
 
+
+// All-gather of bf16 shards by the copy engines: one cudaMemcpyAsync per peer (the local shard first,
+// then the peers in rotation).  Uses no SMs, so it overlaps a compute kernel that occupies all of them.
+void fsdp_all_gather_copy_engine(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t shard, int64_t rank) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int world = (int)shard_ptrs.size();
+  HT_CHECK(world >= 1 && world <= comm::MAX_RANKS, "fsdp_all_gather_copy_engine supports 1..8 ranks");
+  HT_CHECK(rank >= 0 && rank < world, "rank out of range");
+  HT_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == shard * world,
+           "bf16 output of world x shard elements expected");
+  const size_t bytes = (size_t)shard * sizeof(__nv_bfloat16);
+  char* dst = reinterpret_cast<char*>(out.data_ptr());
+  for (int q = 0; q < world; ++q) {
+    const int p = (int)((rank + q) % world);
+    HT_CUDA_CHECK(cudaMemcpyAsync(dst + (size_t)p * bytes, reinterpret_cast<const void*>(shard_ptrs[p]), bytes,
+                                  cudaMemcpyDeviceToDevice, stream()));
+  }
+}
+
 }  // namespace ht

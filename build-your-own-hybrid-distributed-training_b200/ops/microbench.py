@@ -10,6 +10,7 @@ Several GPUs (one process per GPU, e.g. ``torchrun --nproc-per-node 2 --master-a
 
     python -m hybrid_training.ops.microbench tp-layer [--seq 4096]
     python -m hybrid_training.ops.microbench allreduce [--mb 154]
+    python -m hybrid_training.ops.microbench fsdp [--numel 50597888]
 
 ``--once`` launches each kernel a fixed small number of times without timing, which is the
 form to run under a profiler.  Each timed line reports the median of the timed iterations and
@@ -226,6 +227,68 @@ def bench_allreduce(mb: float) -> None:
         ctx.shutdown()
 
 
+def bench_fsdp(numel: int) -> None:
+    """FSDP unit of ``numel`` parameters: fused reduce-scatter + AdamW and P2P all-gather against NCCL.
+
+    Baseline gradient path: bf16 gradient cast to fp32, NCCL reduce-scatter (average), fused AdamW
+    kernel on the fp32 shard.  Fused path: bf16 gradient copied into the peer-mapped staging buffer,
+    then one kernel.  All-gather: NCCL ``all_gather_into_tensor`` of the bf16 shard, the P2P kernel,
+    and one copy-engine ``cudaMemcpyAsync`` per peer from the peer-mapped shard.
+    """
+    import torch.distributed as dist
+
+    from .comm import fsdp_all_gather, fsdp_reduce_scatter_adamw
+    from .optim import adamw_flat
+
+    ctx, world = _init_group("dp", 256, 256)
+    try:
+        ws = ctx.symmetric_workspace("data_parallel")
+        pg = ctx.group("data_parallel").process_group
+        shard = -(-numel // world // 8) * 8
+        padded = shard * world
+        dev = ctx.device
+        grad = torch.randn(padded, device=dev).bfloat16()
+        staging = ws.allocate(padded, torch.bfloat16)
+        shard16 = ws.allocate(shard, torch.bfloat16)
+        param, m, v = torch.randn(shard, device=dev), torch.zeros(shard, device=dev), torch.zeros(shard, device=dev)
+        hyper = torch.tensor([1e-4, 1.0, 1.0, 0.0], device=dev)
+        g32 = torch.empty(shard, device=dev)
+        copy16 = torch.empty(shard, device=dev, dtype=torch.bfloat16)
+
+        def fused() -> None:
+            staging.copy_(grad)
+            fsdp_reduce_scatter_adamw(ws, staging, shard16, shard=shard, valid=shard, scale=1.0 / world, param=param,
+                                      exp_avg=m, exp_avg_sq=v, hyper=hyper, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+
+        def baseline() -> None:
+            full = grad.float()
+            full.div_(world)
+            dist.reduce_scatter_tensor(g32, full, group=pg)
+            adamw_flat(param, g32, m, v, copy16, hyper, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1)
+
+        out = torch.empty(padded, device=dev, dtype=torch.bfloat16)
+
+        def copy_engine() -> None:
+            fsdp_all_gather(ws, shard16, out, copy_engine=True)
+
+        dist.barrier(group=dist.group.WORLD)
+        t_fused = _max_over_ranks(_time(fused, 10))
+        t_base = _max_over_ranks(_time(baseline, 10))
+        t_ag_p2p = _max_over_ranks(_time(lambda: fsdp_all_gather(ws, shard16, out), 10))
+        t_ag_ce = _max_over_ranks(_time(copy_engine, 10))
+        t_ag_nccl = _max_over_ranks(_time(lambda: dist.all_gather_into_tensor(out, shard16, group=pg), 10))
+        ws.check_status()
+        remote = (world - 1) / world * padded * 2  # bf16 bytes each rank reads over NVLink
+        if ctx.rank == 0:
+            print(f"fsdp unit {numel / 1e6:.1f}M params, {world} ranks: reduce-scatter + AdamW fused {t_fused * 1e3:.1f} us "
+                  f"(NVLink {remote / t_fused / 1e6:.0f} GB/s per rank), NCCL + AdamW kernel {t_base * 1e3:.1f} us", flush=True)
+            print(f"fsdp unit all-gather bf16: P2P kernel {t_ag_p2p * 1e3:.1f} us ({remote / t_ag_p2p / 1e6:.0f} GB/s), "
+                  f"copy engine {t_ag_ce * 1e3:.1f} us ({remote / t_ag_ce / 1e6:.0f} GB/s), NCCL {t_ag_nccl * 1e3:.1f} us "
+                  f"({remote / t_ag_nccl / 1e6:.0f} GB/s)", flush=True)
+    finally:
+        ctx.shutdown()
+
+
 def main(argv: list[str] | None = None) -> None:
     p = argparse.ArgumentParser(description="Native kernel micro-benchmarks")
     sub = p.add_subparsers(dest="what", required=True)
@@ -241,6 +304,8 @@ def main(argv: list[str] | None = None) -> None:
     t.add_argument("--seq", type=int, default=4096)
     r = sub.add_parser("allreduce")
     r.add_argument("--mb", type=float, default=154.0)
+    f = sub.add_parser("fsdp")
+    f.add_argument("--numel", type=int, default=50_597_888)
     args = p.parse_args(argv)
     if args.what == "gemm":
         bench_gemm(args.only, args.iters)
@@ -250,6 +315,8 @@ def main(argv: list[str] | None = None) -> None:
         bench_norm(args.once)
     elif args.what == "tp-layer":
         bench_tp_layer(args.seq)
+    elif args.what == "fsdp":
+        bench_fsdp(args.numel)
     else:
         bench_allreduce(args.mb)
 

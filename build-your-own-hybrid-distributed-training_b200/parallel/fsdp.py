@@ -251,13 +251,17 @@ class FlatParamHandle:
         s = shard if shard.device == self._device else shard.to(self._device, non_blocking=True)
         return s.to(self._compute_dtype).contiguous()
 
-    def _all_gather_into(self, full: torch.Tensor, shard: torch.Tensor) -> None:
-        """Fill ``full`` with every rank's shard in the compute dtype (P2P kernel when fused, else NCCL)."""
+    def _all_gather_into(self, full: torch.Tensor, shard: torch.Tensor, *, background: bool = False) -> None:
+        """Fill ``full`` with every rank's shard in the compute dtype (peer memory when fused, else NCCL).
+
+        On the fused path a ``background`` gather (the prefetch, which overlaps the current unit's
+        kernels) uses the copy engines; an on-demand gather uses the P2P load kernel.
+        """
         if self._fused is not None:
             from ..ops.comm import fsdp_all_gather
 
             assert self._sym_shard is not None
-            fsdp_all_gather(self._fused[0], self._sym_shard, full)
+            fsdp_all_gather(self._fused[0], self._sym_shard, full, copy_engine=background)
             if self._recorder is not None:
                 self._recorder.record("fsdp_all_gather_p2p", self._shard_group.name, num_bytes=full.numel() * full.element_size())
             return
@@ -272,7 +276,7 @@ class FlatParamHandle:
         stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(stream):
             full = torch.empty(self._padded_numel, dtype=self._compute_dtype, device=self._device)
-            self._all_gather_into(full, self.flat_param.detach())
+            self._all_gather_into(full, self.flat_param.detach(), background=True)
             event = torch.cuda.Event()
             event.record(stream)
         full.record_stream(torch.cuda.current_stream())
