@@ -301,7 +301,11 @@ def all_gather_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor 
         return None
     if not can_fuse_sequence_parallel(x, group, sharded_rows=x.shape[1], features=(x.shape[2], weight.shape[0])):
         return None
-    return _AllGatherLinear.apply(x.contiguous(), weight, bias, workspace, owner if owner is not None else id(weight), activation)
+    from ..utils.tracing import trace_range
+
+    with trace_range("tp/all-gather GEMM"):
+        return _AllGatherLinear.apply(x.contiguous(), weight, bias, workspace, owner if owner is not None else id(weight),
+                                      activation)
 
 
 def linear_reduce_scatter(x: torch.Tensor, weight: torch.Tensor, workspace: Any, group: Any, *, owner: Any = None) -> torch.Tensor | None:
@@ -310,4 +314,7 @@ def linear_reduce_scatter(x: torch.Tensor, weight: torch.Tensor, workspace: Any,
         return None
     if not can_fuse_sequence_parallel(x, group, sharded_rows=x.shape[1] // group.size, features=(x.shape[2], weight.shape[0])):
         return None
-    return _LinearReduceScatter.apply(x.contiguous(), weight, workspace, owner if owner is not None else id(weight))
+    from ..utils.tracing import trace_range
+
+    with trace_range("tp/GEMM reduce-scatter"):
+        return _LinearReduceScatter.apply(x.contiguous(), weight, workspace, owner if owner is not None else id(weight))

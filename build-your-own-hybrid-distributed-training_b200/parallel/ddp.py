@@ -56,6 +56,7 @@ from ..distributed.collectives import (
 from ..distributed.groups import GroupHandle
 from ..errors import ShardingError, format_error
 from ..logging import get_logger
+from ..utils.tracing import trace_range
 
 __all__ = ["BucketLayout", "DDPStatistics", "DistributedDataParallel", "GradientBucket"]
 
@@ -280,6 +281,10 @@ class DistributedDataParallel(nn.Module):
             self._next_bucket += 1
 
     def _launch(self, bucket: GradientBucket) -> None:
+        with trace_range(f"ddp/bucket {bucket.layout.index} all-reduce"):
+            self._launch_bucket(bucket)
+
+    def _launch_bucket(self, bucket: GradientBucket) -> None:
         average = self._config.average_gradients
         if self._workspace is not None and bucket.buffer.is_cuda:
             from ..ops.comm import bucket_all_reduce

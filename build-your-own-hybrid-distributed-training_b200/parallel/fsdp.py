@@ -58,6 +58,7 @@ from ..distributed.groups import GroupHandle
 from ..errors import ParameterConsistencyError, ShardingError, UnsupportedFeatureError, format_error
 from ..logging import get_logger
 from ..utils.tensors import FlatEntry, ShardRange, build_flat_layout, intersect_ranges
+from ..utils.tracing import trace_range
 
 __all__ = ["FlatParamHandle", "FullyShardedDataParallel", "PieceLayout", "ShardedTensorPiece", "reshard_state_dict_pieces"]
 
@@ -252,6 +253,10 @@ class FlatParamHandle:
         return s.to(self._compute_dtype).contiguous()
 
     def _all_gather_into(self, full: torch.Tensor, shard: torch.Tensor, *, background: bool = False) -> None:
+        with trace_range(f"fsdp/all-gather {self._names[0]}"):
+            self._all_gather_into_impl(full, shard, background=background)
+
+    def _all_gather_into_impl(self, full: torch.Tensor, shard: torch.Tensor, *, background: bool) -> None:
         """Fill ``full`` with every rank's shard in the compute dtype (peer memory when fused, else NCCL).
 
         On the fused path a ``background`` gather (the prefetch, which overlaps the current unit's
@@ -380,6 +385,10 @@ class FlatParamHandle:
 
     # -- gradient reduction --------------------------------------------------------------------------------
     def reduce_scatter_gradient(self, grad_full: torch.Tensor) -> torch.Tensor | None:
+        with trace_range(f"fsdp/reduce-scatter {self._names[0]}"):
+            return self._reduce_scatter_gradient(grad_full)
+
+    def _reduce_scatter_gradient(self, grad_full: torch.Tensor) -> torch.Tensor | None:
         if self._fused is not None and not self._accumulate_only:
             # Fused path: the update happens here; autograd receives no shard gradient.
             grad = grad_full if self._accumulator is None else grad_full.to(self._reduce_dtype) + self._accumulator

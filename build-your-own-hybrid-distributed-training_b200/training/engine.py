@@ -44,6 +44,7 @@ from ..optim.sharded_optimizer import ShardedOptimizer
 from ..parallel.hybrid import HybridModel, build_parallel_model
 from ..utils.memory import MemorySnapshot, capture_memory, reset_peak_memory
 from ..utils.reproducibility import seed_everything
+from ..utils.tracing import trace_range
 from .data import Batch, DistributedBatchSampler, SyntheticDataLoader, build_dataset
 from .state import LearningRateSchedule, TrainingState
 
@@ -215,10 +216,13 @@ class TrainingEngine:
         for i, (x, y) in enumerate(micro_batches):
             ctx = self.model.no_sync() if i < n - 1 else _null()
             with ctx:
-                loss = self._loss(x, y) / n
-                self.scaler.scale(loss).backward()
+                with trace_range(f"step/forward {i}"):
+                    loss = self._loss(x, y) / n
+                with trace_range(f"step/backward {i}"):
+                    self.scaler.scale(loss).backward()
             total = loss.detach() if total is None else total + loss.detach()
-        self.model.finish_backward()
+        with trace_range("step/finish_backward"):
+            self.model.finish_backward()
         params = self.model.optimizer_parameters()
         if self.scaler.enabled:
             self.scaler.unscale_(params)
@@ -229,7 +233,8 @@ class TrainingEngine:
         if self._fsdp_fused_update:
             pass  # every flat shard was updated by its unit's reduce-scatter kernel
         elif isinstance(inner, FusedAdamW) and inner.flat_parameters.is_cuda and not self.scaler.enabled:
-            inner.launch_step()
+            with trace_range("step/adamw"):
+                inner.launch_step()
         elif self.scaler.enabled:
             self.scaler.step(self.optimizer, params, already_unscaled=True)
         else:

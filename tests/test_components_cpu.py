@@ -100,3 +100,17 @@ def test_causal_attention_ignores_future_tokens() -> None:
     q, k, v = qkv.view(b, s, 3, h, d).unbind(2)
     expect = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
     assert torch.allclose(out.view(b, s, h, d), expect.transpose(1, 2), atol=1e-5)
+
+
+def test_trace_ranges_are_inert_without_a_gpu_and_toggle() -> None:
+    from hybrid_training.utils.tracing import set_tracing, trace_range, tracing_enabled
+
+    set_tracing(True)
+    try:
+        with trace_range("test/range"):
+            x = torch.ones(2) + 1
+        assert torch.equal(x, torch.full((2,), 2.0))
+        assert tracing_enabled() == torch.cuda.is_available()
+    finally:
+        set_tracing(False)
+    assert not tracing_enabled()
