@@ -78,6 +78,33 @@ def read_metadata(directory: str | Path) -> dict[str, Any]:
     return data
 
 
+def _load_verdict(failure: Exception | None, context: DistributedContext) -> None:
+    """Collective verdict after the rank-local load: if any rank failed, every rank raises.
+
+    Ranks read different files (a reshard reads only the overlapping shards), so a corrupt file
+    may be seen by one rank only.  Without a verdict that rank would raise while its peers
+    continued into the next collective and waited there until the process-group timeout.
+    """
+    from .. import errors as error_types
+    from ..distributed.collectives import all_gather_object_in_group
+
+    mine = None if failure is None else (type(failure).__name__, str(failure))
+    verdicts = all_gather_object_in_group(mine, context.group("world"))
+    failed = [(r, v) for r, v in enumerate(verdicts) if v is not None]
+    if not failed:
+        return
+    if failure is not None:
+        raise failure
+    origin, (kind, message) = failed[0]
+    cls = getattr(error_types, kind, None)
+    if not (isinstance(cls, type) and issubclass(cls, CheckpointError)):
+        cls = CheckpointError
+    raise cls(format_error("checkpoint.load_checkpoint", f"rank {origin} failed while loading its part of the checkpoint",
+                           rank=context.rank, world_size=context.world_size, expected="every rank to load its shards",
+                           observed=message.splitlines()[0][:300] if message else kind,
+                           resolution="see that rank's error; every rank stops so none waits in a collective"))
+
+
 def _validate_topology_transition(manifest: CheckpointManifest, context: DistributedContext) -> None:
     sizes = dict(manifest.topology.get("sizes", {}))
     saved_t, now_t = int(sizes.get("tensor", 1)), context.topology.size("tensor")
@@ -123,13 +150,18 @@ def load_checkpoint(directory: str | Path, *, model: HybridModel, context: Distr
     if config is not None:
         _warn_on_config_drift(metadata.get("config"), config)
     cache = ShardFileCache(path, manifest, verify_checksums=verify_checksums)
-    info_of = model.parameter_parallel_info()
-    loaded = _load_model_tensors(model, manifest, cache, info_of, context, strict)
-    if load_optimizer and optimizer is not None:
-        _load_optimizer_state(model, optimizer, manifest, cache, info_of, metadata, context, strict)
-    rng = False
-    if load_rng and metadata.get("rng", {}).get("saved"):
-        rng = _restore_rng(path, manifest, metadata, cache, context)
+    failure: Exception | None = None
+    loaded, rng = [], False
+    try:  # rank-local: reads only the files this rank needs, issues no collective
+        info_of = model.parameter_parallel_info()
+        loaded = _load_model_tensors(model, manifest, cache, info_of, context, strict)
+        if load_optimizer and optimizer is not None:
+            _load_optimizer_state(model, optimizer, manifest, cache, info_of, metadata, context, strict)
+        if load_rng and metadata.get("rng", {}).get("saved"):
+            rng = _restore_rng(path, manifest, metadata, cache, context)
+    except Exception as exc:  # noqa: BLE001 - re-raised below, on every rank
+        failure = exc
+    _load_verdict(failure, context)
     state = TrainingState.from_dict(metadata.get("training_state", {}))
     result = LoadedCheckpoint(path, manifest, metadata, state, dict(metadata.get("scheduler", {})), dict(metadata.get("scaler", {})),
                               time.perf_counter() - start, loaded, cache.loaded_files, rng)

@@ -157,3 +157,75 @@ def test_prune_and_find_latest(tmp_path: Path) -> None:
     assert find_latest_checkpoint(tmp_path).name == checkpoint_directory_name(5)
     removed = prune_checkpoints(tmp_path, keep_last=2)
     assert sorted(p.name for p in removed) == [checkpoint_directory_name(1), checkpoint_directory_name(3)]
+
+
+@pytest.fixture(scope="module")
+def fsdp_checkpoint(tmp_path_factory: pytest.TempPathFactory) -> Path:
+    root = tmp_path_factory.mktemp("integrity")
+    saved = launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 1, str(root), None), timeout_seconds=600)
+    return Path(saved[0].value["path"])
+
+
+def _copy(src: Path, tmp_path: Path, name: str) -> Path:
+    dst = tmp_path / name / src.name
+    shutil.copytree(src, dst)
+    return dst
+
+
+def test_publish_protocol_leaves_manifest_last_and_no_staging(fsdp_checkpoint: Path) -> None:
+    manifest_time = (fsdp_checkpoint / "manifest.json").stat().st_mtime_ns
+    for f in fsdp_checkpoint.iterdir():
+        assert f.stat().st_mtime_ns <= manifest_time, f"{f.name} written after the manifest"
+    assert not [p for p in fsdp_checkpoint.parent.iterdir() if p.name.startswith(".staging-")]
+    summary = inspect_checkpoint(fsdp_checkpoint)
+    assert summary["complete"] and summary["verification"]["files_verified"] == 2
+
+
+def test_version_mismatch_is_rejected(fsdp_checkpoint: Path, tmp_path: Path) -> None:
+    from hybrid_training.errors import CheckpointVersionError
+
+    bad = _copy(fsdp_checkpoint, tmp_path, "version")
+    m = json.loads((bad / "manifest.json").read_text())
+    m["format_version"] = "9.0"
+    (bad / "manifest.json").write_text(json.dumps(m))
+    with pytest.raises(CheckpointVersionError):
+        inspect_checkpoint(bad)
+
+
+def test_dropped_shard_record_breaks_coverage(fsdp_checkpoint: Path, tmp_path: Path) -> None:
+    bad = _copy(fsdp_checkpoint, tmp_path, "dropped")
+    m = json.loads((bad / "manifest.json").read_text())
+    key = next(k for k, r in m["tensors"].items() if len(r["shards"]) == 2)
+    m["tensors"][key]["shards"].pop()
+    (bad / "manifest.json").write_text(json.dumps(m))
+    with pytest.raises(CheckpointError):
+        inspect_checkpoint(bad)
+
+
+def test_hostile_file_name_in_manifest_is_rejected(fsdp_checkpoint: Path, tmp_path: Path) -> None:
+    bad = _copy(fsdp_checkpoint, tmp_path, "hostile")
+    m = json.loads((bad / "manifest.json").read_text())
+    key = next(iter(m["tensors"]))
+    m["tensors"][key]["shards"][0]["file"] = "../../outside.pt"
+    (bad / "manifest.json").write_text(json.dumps(m))
+    with pytest.raises(CheckpointError):
+        inspect_checkpoint(bad)
+
+
+def test_corruption_is_caught_by_a_real_load(fsdp_checkpoint: Path, tmp_path: Path) -> None:
+    bad = _copy(fsdp_checkpoint, tmp_path, "load")
+    blob = bytearray((bad / "rank-00000.pt").read_bytes())
+    blob[len(blob) // 2] ^= 0x5A
+    (bad / "rank-00000.pt").write_bytes(bytes(blob))
+    results = launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 0, None, str(bad)), timeout_seconds=600,
+                             raise_on_failure=False)
+    assert all("CheckpointCorruptionError" in (r.traceback_text or "") for r in results)
+
+
+def test_verify_files_returns_the_recorded_digests(fsdp_checkpoint: Path) -> None:
+    from hybrid_training.checkpoint.reshard import verify_files
+
+    manifest = CheckpointManifest.read(fsdp_checkpoint / "manifest.json")
+    digests = verify_files(fsdp_checkpoint, manifest)
+    assert set(digests) == {"rank-00000.pt", "rank-00001.pt"}
+    assert all(digests[name] == record.sha256 for name, record in manifest.files.items())
