@@ -63,9 +63,11 @@ bench-scaling:
 	done
 
 examples-cpu:
-	for ex in train_ddp train_fsdp train_tensor_parallel train_sequence_parallel; do \
+	for pair in train_ddp:ddp_2gpu train_fsdp:fsdp_2gpu train_tensor_parallel:tensor_parallel_2gpu \
+	            train_sequence_parallel:sequence_parallel_2gpu; do \
+	  ex=$${pair%%:*}; cfg=$${pair##*:}; \
 	  $(PYTHON) -m torch.distributed.run --nnodes=1 --nproc-per-node 2 --master-addr 127.0.0.1 --master-port $(PORT) \
-	    examples/$$ex.py --backend gloo --device cpu --steps 2 || exit 1; \
+	    examples/$$ex.py --config configs/$$cfg.yaml --backend gloo --device cpu --steps 2 || exit 1; \
 	done
 
 example-hybrid:
