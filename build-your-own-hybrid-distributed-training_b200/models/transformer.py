@@ -32,7 +32,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops
-from ..autograd.collectives import copy_to_group, gather_from_sequence_parallel_region
+from ..autograd.collectives import copy_to_group, gather_from_sequence_parallel_region, reduce_from_group
 from ..config import ModelConfig
 from ..distributed.groups import GroupHandle
 from ..errors import ConfigurationError, UnsupportedFeatureError, format_error
@@ -77,6 +77,15 @@ class ParallelPlan:
     sequence_group: GroupHandle
     sequence_parallel: bool = False
     vocab_parallel: bool = True
+
+    @property
+    def context_parallel(self) -> bool:
+        """Sequence parallelism over its own group (``independent`` mode): attention needs every chunk.
+
+        Position-wise layers then run on the local chunk with full weights, and attention
+        gathers the keys and values of the whole sequence (see ``TensorParallelAttention``).
+        """
+        return self.sequence_parallel and self.sequence_group.ranks != self.tensor_group.ranks
 
     @classmethod
     def single_process(cls) -> ParallelPlan:
@@ -139,6 +148,8 @@ class TensorParallelAttention(nn.Module):
     def forward(self, x: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
         qkv = self.qkv(x)
         h, hkv, d = self.heads_per_partition, self.kv_heads_per_partition, self.head_dim
+        if self.plan.context_parallel:
+            return self.output(self._context_parallel(qkv, attention_mask))
         if self.rope_theta is not None:
             cos, sin = self._rope(qkv.shape[1], qkv.device)
             qkv = ops.apply_rope(qkv, cos, sin, h, hkv, d)
@@ -147,6 +158,47 @@ class TensorParallelAttention(nn.Module):
         else:
             context = ops.attention(qkv, h, hkv, d, causal=self.causal)
         return self.output(context)
+
+
+    def _context_parallel(self, qkv: torch.Tensor, attention_mask: torch.Tensor | None) -> torch.Tensor:
+        """Attention of this rank's query chunk against the keys/values of the whole sequence.
+
+        The sequence group's ranks hold consecutive chunks of ``S / C`` positions.  Rotary
+        positions are offset by the chunk start; keys and values are all-gathered along the
+        sequence (the gather's adjoint reduce-scatters their gradients, so each rank's
+        contribution to every key reaches its owner); causal masking compares global
+        positions.  Scores are materialised per chunk (``S / C x S``): this is the all-gather
+        form of context parallelism, which the reference describes but does not implement
+        (``docs/06_sequence_parallelism.md:234-256``; its ``independent`` mode gives
+        attention only the local chunk).  A ring with online softmax is the form that also
+        bounds memory; it is not built.
+        """
+        if attention_mask is not None:
+            raise UnsupportedFeatureError(format_error(
+                "models.attention", "explicit attention masks are not supported with context parallelism",
+                expected="attention_mask=None", observed="a mask", resolution="rely on causal masking"))
+        cp = self.plan.sequence_group
+        h, hkv, d = self.heads_per_partition, self.kv_heads_per_partition, self.head_dim
+        local = qkv.shape[1]
+        offset = cp.local_rank * local
+        if self.rope_theta is not None:
+            cos, sin = self._rope(local * cp.size, qkv.device)
+            qkv = ops.apply_rope(qkv, cos[offset:offset + local].contiguous(), sin[offset:offset + local].contiguous(), h, hkv, d)
+        q = qkv[..., : h * d]
+        kv = gather_from_sequence_parallel_region(qkv[..., h * d:].contiguous(), cp, dim=SEQUENCE_DIM)
+        b, total = q.shape[0], kv.shape[1]
+        qf = q.reshape(b, local, h, d).transpose(1, 2).float()
+        kf = kv[..., : hkv * d].reshape(b, total, hkv, d).transpose(1, 2).float().repeat_interleave(h // hkv, 1)
+        vf = kv[..., hkv * d:].reshape(b, total, hkv, d).transpose(1, 2).float().repeat_interleave(h // hkv, 1)
+        scores = qf @ kf.transpose(-1, -2) / d**0.5
+        if self.causal:
+            q_pos = torch.arange(offset, offset + local, device=qkv.device)[:, None]
+            k_pos = torch.arange(total, device=qkv.device)[None, :]
+            scores = scores.masked_fill(k_pos > q_pos, float("-inf"))
+        w = torch.softmax(scores, dim=-1)
+        if self.dropout > 0.0 and self.training:
+            w = F.dropout(w, p=self.dropout)
+        return (w @ vf).transpose(1, 2).reshape(b, local, h * d).to(qkv.dtype)
 
 
 def _explicit_attention(qkv: torch.Tensor, h: int, hkv: int, d: int, causal: bool, mask: torch.Tensor | None,
@@ -250,6 +302,11 @@ class TinyTransformer(nn.Module):
         self.output_projection = VocabParallelHead(config.hidden_size, config.vocab_size, tp, bias=False, gather_output=True,
                                                    sequence_parallel=False, init_seed=derive_seed(seed, "output-projection"),
                                                    device=device, dtype=dtype)
+        if self.plan.context_parallel:
+            # Every rank runs every layer on its own chunk of positions with full weights, so every
+            # gradient is a partial sum over the sequence group (reduced like the SP norm weights).
+            for p in self.parameters():
+                p.sequence_parallel_partial_grad = True
         if config.tie_word_embeddings:
             self.output_projection.weight = self.token_embedding.weight
             # The native backward of the head and of the embedding each write into the shared
@@ -298,6 +355,8 @@ class TinyTransformer(nn.Module):
         else:
             _, h = self.final_norm(residual, delta, out_dtype=self.compute_dtype)
         head = self.output_projection
+        if self.plan.context_parallel:
+            return self._context_parallel_head(h, targets, info)
         vocab_split = targets is not None and head.group.size > 1
         if self.plan.sequence_parallel:
             # With a vocab-split loss every rank's head produces a partial gradient for the whole
@@ -308,6 +367,23 @@ class TinyTransformer(nn.Module):
         elif vocab_split:
             h = copy_to_group(h, head.group)
         return head(h) if targets is None else head(h, targets=targets)
+
+    def _context_parallel_head(self, h: torch.Tensor, targets: torch.Tensor | None, info: SequenceShardInfo | None) -> torch.Tensor:
+        """Head and loss on the local chunk; the mean loss is summed over the sequence group."""
+        cp = self.plan.sequence_group
+        if targets is None:
+            logits = gather_sequence(self.output_projection(h), cp, dim=SEQUENCE_DIM)
+            return logits if info is None else unpad_sequence_dimension(logits, info, dim=SEQUENCE_DIM)
+        if info is not None and info.requires_padding:
+            raise UnsupportedFeatureError(format_error(
+                "models.TinyTransformer.forward", "the loss under context parallelism needs a sequence length divisible by "
+                "the sequence-parallel size", expected=f"length % {cp.size} == 0", observed=targets.shape[1],
+                resolution="pad the batch to a multiple of the sequence-parallel size"))
+        lo, hi = local_sequence_slice(targets.shape[1], cp)
+        local_mean = self.output_projection(h, targets=targets[:, lo:hi].contiguous())
+        # Chunks have equal token counts: the global mean is the average of the chunk means.  The
+        # reduction's adjoint passes the gradient through, so each rank backpropagates its chunk.
+        return reduce_from_group(local_mean / cp.size, cp)
 
     def local_positions(self, sequence_length: int) -> tuple[int, int]:
         if not self.plan.sequence_parallel:

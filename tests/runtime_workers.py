@@ -278,3 +278,30 @@ def comm_volume_worker(rank: int, world: int, strategy: str, reshard: bool) -> d
 
 def env_probe_worker(rank: int, world: int) -> dict[str, str]:
     return {k: os.environ.get(k, "") for k in ("RANK", "WORLD_SIZE", "MASTER_ADDR", "LOCAL_RANK")}
+
+
+def independent_sp_worker(rank: int, world: int, kind: str) -> dict[str, Any]:
+    """Sequence parallelism over its own grid dimension (``independent`` mode, tensor width 1)."""
+    import dataclasses as dc
+
+    from hybrid_training.config import ExperimentConfig
+    from hybrid_training.parallel import all_reduce_sequence_parallel_gradients, build_model
+
+    from .dist_workers import _tiny_transformer
+
+    topo = TopologyConfig(sequence_parallel_size=world, sequence_parallel_mode="independent")
+    cfg = ExperimentConfig(backend="gloo", device="cpu", topology=topo, model=_tiny_transformer(kind),
+                           tensor_parallel=dc.replace(ExperimentConfig().tensor_parallel, sequence_parallel=True))
+    ctx = init_distributed(cfg)
+    try:
+        model = build_model(cfg, ctx)
+        tokens = torch.randint(0, 64, (2, 17), generator=torch.Generator().manual_seed(7))
+        logits = model(tokens[:, :-1])
+        loss = model(tokens[:, :-1], targets=tokens[:, 1:])
+        loss.backward()
+        all_reduce_sequence_parallel_gradients(model, ctx.group("sequence_effective"))
+        grads = {n: p.grad.clone() for n, p in model.named_parameters()
+                 if p.grad is not None and ("input_norm.weight" in n or "qkv.weight" in n)}
+        return {"loss": float(loss.detach()), "logits": logits.detach().clone(), "grads": grads}
+    finally:
+        ctx.shutdown()

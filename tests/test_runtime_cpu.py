@@ -170,3 +170,43 @@ def test_launcher_exports_the_rendezvous_environment() -> None:
     results = launch_workers(R.env_probe_worker, 2, timeout_seconds=120)
     assert [r.value["RANK"] for r in results] == ["0", "1"]
     assert all(r.value["WORLD_SIZE"] == "2" and r.value["MASTER_ADDR"] == "127.0.0.1" for r in results)
+
+
+@pytest.mark.parametrize("kind", ["gpt2", "llama"])
+def test_independent_sequence_parallel_matches_single_process(kind: str) -> None:
+    """``independent`` mode is context parallelism: every chunk attends to the whole prefix."""
+    ref = launch_workers(W.transformer_forward_worker, 1, args=(1, False, kind), timeout_seconds=300)[0].value
+    for r in launch_workers(R.independent_sp_worker, 2, args=(kind,), timeout_seconds=300):
+        assert abs(r.value["loss"] - ref["loss"]) < 1e-5
+        assert torch.allclose(r.value["logits"], ref["logits"], atol=1e-5)
+        assert set(r.value["grads"]) == set(ref["grads"])
+        for name, g in ref["grads"].items():
+            assert torch.allclose(r.value["grads"][name], g, atol=1e-5), name
+
+
+def test_engine_with_context_parallel_trains_like_data_parallel_alone(tmp_path) -> None:
+    """dp2 x seq2 (independent) sees the same global batch as dp2; their losses and weights agree."""
+    base = {"backend": "gloo", "device": "cpu",
+            "model": {"kind": "transformer", "hidden_size": 32, "num_layers": 2, "num_heads": 4, "vocab_size": 64,
+                      "max_sequence_length": 16},
+            "data": {"micro_batch_size": 2, "sequence_length": 16, "num_train_samples": 64, "num_eval_samples": 0,
+                     "shuffle": False},
+            "optimizer": {"learning_rate": 0.003}, "training": {"max_steps": 3, "log_every_steps": 0}}
+    dp = dict(base, topology={"data_parallel_size": 2})
+    cp = dict(base, topology={"data_parallel_size": 2, "sequence_parallel_size": 2, "sequence_parallel_mode": "independent"},
+              tensor_parallel={"sequence_parallel": True})
+    ref = launch_workers(W.engine_worker, 2, args=(dp, 3, None, None), timeout_seconds=300)[0].value
+    got = launch_workers(W.engine_worker, 4, args=(cp, 3, None, None), timeout_seconds=300)
+    for r in got:
+        for a, b in zip(r.value["losses"], ref["losses"]):
+            assert abs(a - b) < 1e-5, (r.value["losses"], ref["losses"])
+        diffs = {}
+        for name, t in ref["full"].items():
+            mine = r.value["full"][name]
+            if name.endswith("qkv.bias"):
+                # The key bias shifts every score of a query row equally, so softmax makes its gradient
+                # exactly zero; the computed values are rounding noise that AdamW normalises to steps of
+                # the learning rate's size in either direction.  Compare the query and value biases.
+                mine, t = torch.cat([mine[:32], mine[64:]]), torch.cat([t[:32], t[64:]])
+            diffs[name] = float((mine - t).abs().max())
+        assert max(diffs.values()) < 1e-5, sorted(diffs.items(), key=lambda kv: -kv[1])[:4]
