@@ -47,6 +47,7 @@ void fsdp_reduce_scatter_adamw(at::Tensor staging, std::vector<int64_t> grad_ptr
                                double beta1, double beta2, double eps, double wd, int64_t slot_base, int64_t max_blocks,
                                at::Tensor status, double timeout_s);
 void fsdp_all_gather(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t shard, int64_t rank);
+void barrier_probe(at::Tensor pads, at::Tensor status, double timeout_s);
 void fsdp_all_gather_copy_engine(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t shard, int64_t rank);
 }  // namespace ht
 
@@ -80,6 +81,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bucket_all_reduce", &ht::bucket_all_reduce, "in-kernel NVLink all-reduce of one DDP bucket");
   m.def("fsdp_reduce_scatter_adamw", &ht::fsdp_reduce_scatter_adamw,
         "FSDP gradient reduce-scatter fused with the cast and the sharded AdamW update (NVLink peer memory)");
+  m.def("barrier_probe", &ht::barrier_probe, "one block running the bounded peer barrier against local pads (tests)");
   m.def("fsdp_all_gather", &ht::fsdp_all_gather, "FSDP all-gather of bf16 parameter shards over NVLink peer memory");
   m.def("fsdp_all_gather_copy_engine", &ht::fsdp_all_gather_copy_engine, "FSDP all-gather by one peer cudaMemcpyAsync per rank");
 }

@@ -387,6 +387,19 @@ __global__ void __launch_bounds__(THREADS) fsdp_all_gather_kernel(ShardPeers sp,
   }
 }
 
+
+// One block running the peer barrier of rank 0 in a group of two, with both "signal pads" in local
+// memory.  Used by the tests to exercise the bounded wait: with nothing setting this rank's slot
+// the wait runs out and the status word records the stage; with the slot pre-set (a peer that
+// already arrived) the barrier completes at once.
+__global__ void __launch_bounds__(THREADS) barrier_probe_kernel(uint32_t* pad0, uint32_t* pad1, int* status,
+                                                                 unsigned long long timeout_ns) {
+  Peers pp{};
+  pp.pad[0] = pad0;
+  pp.pad[1] = pad1;
+  block_barrier(pp, 0, 2, 0, status, 99, timeout_ns);
+}
+
 }  // namespace comm
 
 void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
@@ -513,6 +526,19 @@ void fsdp_all_gather_copy_engine(std::vector<int64_t> shard_ptrs, at::Tensor out
     HT_CUDA_CHECK(cudaMemcpyAsync(dst + (size_t)p * bytes, reinterpret_cast<const void*>(shard_ptrs[p]), bytes,
                                   cudaMemcpyDeviceToDevice, stream()));
   }
+}
+
+
+void barrier_probe(at::Tensor pads, at::Tensor status, double timeout_s) {
+  const c10::cuda::CUDAGuard guard(pads.device());
+  HT_CHECK(pads.is_cuda() && pads.scalar_type() == at::kInt && pads.dim() == 2 && pads.size(0) == 2 && pads.size(1) >= 2 &&
+               pads.is_contiguous(), "pads: int32 [2, >=2] on the device");
+  HT_CHECK(status.is_cuda() && status.scalar_type() == at::kInt && status.numel() >= 2, "status: int32 [>=2] on the device");
+  HT_CHECK(timeout_s > 0 && timeout_s <= 10, "the probe's timeout must lie in (0, 10] seconds");
+  auto* base = reinterpret_cast<uint32_t*>(pads.data_ptr());
+  comm::barrier_probe_kernel<<<1, comm::THREADS, 0, stream()>>>(base, base + pads.size(1), status.data_ptr<int>(),
+                                                                  (unsigned long long)(timeout_s * 1e9));
+  HT_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace ht
