@@ -239,10 +239,15 @@ class TensorParallelConfig:
     async_input_gradient_allreduce: bool = True
     init_method_std: float = 0.02
     fused_collectives: bool = True
+    context_parallel_algorithm: str = "all_gather"
 
     def __post_init__(self) -> None:
         _check(self.init_method_std > 0, "config.TensorParallelConfig", "init_method_std must be positive", "> 0",
                self.init_method_std, "use a small positive value such as 0.02")
+        _check(self.context_parallel_algorithm in ("all_gather", "ring"), "config.TensorParallelConfig",
+               "unknown context_parallel_algorithm (attention under sequence_parallel_mode='independent')",
+               ["all_gather", "ring"], self.context_parallel_algorithm,
+               "use 'all_gather' (fewer transfers) or 'ring' (memory per rank independent of the sequence length)")
 
 
 @dataclass(frozen=True)

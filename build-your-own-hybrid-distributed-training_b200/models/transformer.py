@@ -77,6 +77,7 @@ class ParallelPlan:
     sequence_group: GroupHandle
     sequence_parallel: bool = False
     vocab_parallel: bool = True
+    ring_attention: bool = False  # context parallelism: pass keys/values around the ring instead of all-gathering
 
     @property
     def context_parallel(self) -> bool:
@@ -185,6 +186,20 @@ class TensorParallelAttention(nn.Module):
             cos, sin = self._rope(local * cp.size, qkv.device)
             qkv = ops.apply_rope(qkv, cos[offset:offset + local].contiguous(), sin[offset:offset + local].contiguous(), h, hkv, d)
         q = qkv[..., : h * d]
+        if self.plan.ring_attention:
+            from ..parallel.context_parallel import ring_attention
+
+            if self.dropout > 0.0 and self.training:
+                raise UnsupportedFeatureError(format_error(
+                    "models.attention", "attention dropout is not implemented by ring attention", expected="dropout=0",
+                    observed=self.dropout, resolution="disable attention dropout or use context_parallel_algorithm='all_gather'"))
+
+            b = q.shape[0]
+            qh = q.reshape(b, local, h, d).transpose(1, 2)
+            kh = qkv[..., h * d:(h + hkv) * d].reshape(b, local, hkv, d).transpose(1, 2).repeat_interleave(h // hkv, 1)
+            vh = qkv[..., (h + hkv) * d:].reshape(b, local, hkv, d).transpose(1, 2).repeat_interleave(h // hkv, 1)
+            out = ring_attention(qh, kh, vh, cp, causal=self.causal)
+            return out.transpose(1, 2).reshape(b, local, h * d).to(qkv.dtype)
         kv = gather_from_sequence_parallel_region(qkv[..., h * d:].contiguous(), cp, dim=SEQUENCE_DIM)
         b, total = q.shape[0], kv.shape[1]
         qf = q.reshape(b, local, h, d).transpose(1, 2).float()

@@ -1,0 +1,128 @@
+"""Ring attention: context parallelism whose memory per rank does not grow with the sequence.
+
+The ranks of a sequence group hold consecutive chunks of the sequence.  Each rank keeps its
+query chunk and passes key/value chunks around the ring (send to ``r + 1``, receive from
+``r - 1``), merging each chunk's contribution into running softmax statistics (maximum,
+normaliser, weighted sum), so no rank ever holds more than two key/value chunks or a score
+block larger than ``S/C x S/C``.  Under causal masking a chunk from a later position block
+contributes nothing and its computation is skipped (it is still passed on).
+
+The backward pass recomputes the probabilities from the saved log-sum-exp; the key/value
+chunks travel the ring again together with their gradient accumulators, which return to
+their owners after a full turn.
+
+The reference describes ring attention (``docs/06_sequence_parallelism.md:239-245``) and
+provides its primitives (``topology.py:377``, ``collectives.py:669-750``) but does not
+implement it.  This implementation is plain PyTorch math over the collective wrappers' point-
+to-point transfers (Gloo or NCCL); it is the memory-bounded alternative to the all-gather form
+in :class:`hybrid_training.models.transformer.TensorParallelAttention`.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import torch
+
+from ..distributed.collectives import recv_tensor, send_tensor
+from ..distributed.groups import GroupHandle
+
+__all__ = ["ring_attention"]
+
+
+def _ring_pass(tensors: list[torch.Tensor], group: GroupHandle) -> list[torch.Tensor]:
+    """Send every tensor to the next rank of the ring and return the ones from the previous rank.
+
+    Even ranks send first and odd ranks receive first, so blocking transfers cannot deadlock
+    (with an odd group size the last rank is odd-indexed or the first is even; either way one
+    side of every pair is receiving).
+    """
+    me, n = group.local_rank, group.size
+    nxt, prv = (me + 1) % n, (me - 1) % n
+    out = [torch.empty_like(t) for t in tensors]
+    if me % 2 == 0:
+        for t in tensors:
+            send_tensor(t.contiguous(), group, destination_local_rank=nxt)
+        for o in out:
+            recv_tensor(o, group, source_local_rank=prv)
+    else:
+        for o in out:
+            recv_tensor(o, group, source_local_rank=prv)
+        for t in tensors:
+            send_tensor(t.contiguous(), group, destination_local_rank=nxt)
+    return out
+
+
+def _scores(q: torch.Tensor, k: torch.Tensor, scale: float, diagonal: bool) -> torch.Tensor:
+    s = (q @ k.transpose(-1, -2)) * scale
+    if diagonal:
+        n = s.shape[-1]
+        s = s.masked_fill(torch.ones(n, n, dtype=torch.bool, device=s.device).triu(1), float("-inf"))
+    return s
+
+
+class _RingAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx: Any, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group: GroupHandle, causal: bool) -> torch.Tensor:
+        # q: [B, H, L, D]; k, v: [B, H, L, D] (key/value heads already expanded to H), fp32
+        me, n = group.local_rank, group.size
+        scale = 1.0 / math.sqrt(q.shape[-1])
+        m = torch.full(q.shape[:-1], float("-inf"), dtype=q.dtype, device=q.device)
+        l = torch.zeros_like(m)
+        acc = torch.zeros_like(q)
+        kv = [k, v]
+        for step in range(n):
+            src = (me - step) % n  # owner of the chunk held at this step
+            if not (causal and src > me):
+                s = _scores(q, kv[0], scale, causal and src == me)
+                m_new = torch.maximum(m, s.amax(-1))
+                alpha = torch.exp(m - m_new)
+                p = torch.exp(s - m_new[..., None])
+                l = l * alpha + p.sum(-1)
+                acc = acc * alpha[..., None] + p @ kv[1]
+                m = m_new
+            if step < n - 1:
+                kv = _ring_pass(kv, group)
+        out = acc / l[..., None]
+        lse = m + torch.log(l)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.group, ctx.causal = group, causal
+        return out
+
+    @staticmethod
+    def backward(ctx: Any, dout: torch.Tensor) -> tuple[Any, ...]:
+        q, k, v, out, lse = ctx.saved_tensors
+        group, causal = ctx.group, ctx.causal
+        me, n = group.local_rank, group.size
+        scale = 1.0 / math.sqrt(q.shape[-1])
+        dout = dout.contiguous()
+        delta = (dout * out).sum(-1)
+        dq = torch.zeros_like(q)
+        travel = [k, v, torch.zeros_like(k), torch.zeros_like(v)]  # chunk and its gradient accumulators
+        for step in range(n):
+            src = (me - step) % n
+            kc, vc, dk, dv = travel
+            if not (causal and src > me):
+                p = torch.exp(_scores(q, kc, scale, causal and src == me) - lse[..., None])
+                dv = dv + p.transpose(-1, -2) @ dout
+                ds = p * (dout @ vc.transpose(-1, -2) - delta[..., None])
+                dq = dq + (ds @ kc) * scale
+                dk = dk + (ds.transpose(-1, -2) @ q) * scale
+            # a full turn brings every chunk (and its accumulated gradient) back to its owner
+            travel = _ring_pass([kc, vc, dk, dv], group)
+        return dq, travel[2], travel[3], None, None
+
+
+def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group: GroupHandle, *, causal: bool = True) -> torch.Tensor:
+    """Attention of this rank's query chunk over the whole sequence, keys/values passed around the ring.
+
+    ``q``, ``k``, ``v``: ``[B, H, L, D]`` with ``L`` the local chunk length (equal on every rank)
+    and key/value heads already repeated to ``H``.  Returns ``[B, H, L, D]`` in ``q``'s dtype;
+    the arithmetic runs in fp32.
+    """
+    dtype = q.dtype
+    if group.size == 1:
+        s = _scores(q.float(), k.float(), 1.0 / math.sqrt(q.shape[-1]), causal)
+        return (torch.softmax(s, -1) @ v.float()).to(dtype)
+    return _RingAttention.apply(q.float().contiguous(), k.float().contiguous(), v.float().contiguous(), group, causal).to(dtype)

@@ -360,6 +360,10 @@ class FlatParamHandle:
                 self._sym_shard.copy_(self.flat_param.detach())
             self._sym_stale = False
 
+    def mark_fused_shard_stale(self) -> None:
+        """The fp32 master shard changed outside the fused kernel; refresh the bf16 copy before the next gather."""
+        self._sym_stale = True
+
     fused = property(lambda self: self._fused is not None)
     fused_shard_stale = property(lambda self: self._fused is not None and self._sym_stale)
 
@@ -482,7 +486,7 @@ class FlatParamHandle:
             dst = overlap.start - local.start
             src = overlap.start - e.offset
             shard[dst:dst + overlap.length].copy_(t.reshape(-1)[src:src + overlap.length].to(shard.dtype))
-        self._sym_stale = True
+        self.mark_fused_shard_stale()
 
     def full_tensors(self) -> dict[str, torch.Tensor]:
         shard = self.flat_param.detach().to(self._device).contiguous()
@@ -731,7 +735,7 @@ class FullyShardedDataParallel(nn.Module):
                     for u, full in zip(units, fulls):
                         r = u._handle.local_shard_range()
                         u._handle.flat_param.data.copy_(full[r.start:r.end].to(u._handle.flat_param.dtype))
-                        u._handle._sym_stale = True
+                        u._handle.mark_fused_shard_stale()
                 for u in units:
                     u._handle.free_full()
 

@@ -104,7 +104,8 @@ def build_model(config: ExperimentConfig, context: DistributedContext, *, device
                 expected="mixed_precision.enabled=True with param_dtype='bfloat16' on CUDA",
                 observed=str(config.mixed_precision.compute_dtype),
                 resolution="enable bf16 mixed precision (fp32 compute is available on the CPU path)"))
-        plan = ParallelPlan(tensor_group=tensor, sequence_group=sequence, sequence_parallel=sp, vocab_parallel=tensor.size > 1)
+        plan = ParallelPlan(tensor_group=tensor, sequence_group=sequence, sequence_parallel=sp, vocab_parallel=tensor.size > 1,
+                            ring_attention=config.tensor_parallel.context_parallel_algorithm == "ring")
         return TinyTransformer(config.model, plan, seed=config.training.seed, device=device,
                                compute_dtype=config.mixed_precision.compute_dtype)
     if sp:

@@ -280,7 +280,7 @@ def env_probe_worker(rank: int, world: int) -> dict[str, str]:
     return {k: os.environ.get(k, "") for k in ("RANK", "WORLD_SIZE", "MASTER_ADDR", "LOCAL_RANK")}
 
 
-def independent_sp_worker(rank: int, world: int, kind: str) -> dict[str, Any]:
+def independent_sp_worker(rank: int, world: int, kind: str, algorithm: str = "all_gather") -> dict[str, Any]:
     """Sequence parallelism over its own grid dimension (``independent`` mode, tensor width 1)."""
     import dataclasses as dc
 
@@ -291,7 +291,8 @@ def independent_sp_worker(rank: int, world: int, kind: str) -> dict[str, Any]:
 
     topo = TopologyConfig(sequence_parallel_size=world, sequence_parallel_mode="independent")
     cfg = ExperimentConfig(backend="gloo", device="cpu", topology=topo, model=_tiny_transformer(kind),
-                           tensor_parallel=dc.replace(ExperimentConfig().tensor_parallel, sequence_parallel=True))
+                           tensor_parallel=dc.replace(ExperimentConfig().tensor_parallel, sequence_parallel=True,
+                                                      context_parallel_algorithm=algorithm))
     ctx = init_distributed(cfg)
     try:
         model = build_model(cfg, ctx)

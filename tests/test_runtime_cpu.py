@@ -172,11 +172,12 @@ def test_launcher_exports_the_rendezvous_environment() -> None:
     assert all(r.value["WORLD_SIZE"] == "2" and r.value["MASTER_ADDR"] == "127.0.0.1" for r in results)
 
 
-@pytest.mark.parametrize("kind", ["gpt2", "llama"])
-def test_independent_sequence_parallel_matches_single_process(kind: str) -> None:
-    """``independent`` mode is context parallelism: every chunk attends to the whole prefix."""
+@pytest.mark.parametrize("kind,algorithm,world", [("gpt2", "all_gather", 2), ("llama", "all_gather", 2), ("gpt2", "ring", 2),
+                                                  ("llama", "ring", 4)])
+def test_independent_sequence_parallel_matches_single_process(kind: str, algorithm: str, world: int) -> None:
+    """``independent`` mode is context parallelism: every chunk attends to the whole prefix (all-gather or ring)."""
     ref = launch_workers(W.transformer_forward_worker, 1, args=(1, False, kind), timeout_seconds=300)[0].value
-    for r in launch_workers(R.independent_sp_worker, 2, args=(kind,), timeout_seconds=300):
+    for r in launch_workers(R.independent_sp_worker, world, args=(kind, algorithm), timeout_seconds=300):
         assert abs(r.value["loss"] - ref["loss"]) < 1e-5
         assert torch.allclose(r.value["logits"], ref["logits"], atol=1e-5)
         assert set(r.value["grads"]) == set(ref["grads"])
