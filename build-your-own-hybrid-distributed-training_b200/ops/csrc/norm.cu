@@ -328,22 +328,35 @@ __global__ void __launch_bounds__(WARP_ROWS_THREADS, 2)
 
 // out[c] = sum_b part[b, c] + beta * out[c]: 32 columns per CTA, 8 row groups summed in a fixed
 // order through shared memory.
-__global__ void __launch_bounds__(256) sum_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows, int d,
-                                                       float beta) {
-  __shared__ float red[8][33];
+// out[c] = sum_r part[r, c] (+ beta * out[c]).  A block owns 32 columns (128-byte row segments);
+// its 32 warps take interleaved rows, four independent loads in flight per thread, and the 32
+// per-warp sums are added in a fixed order, so the result is deterministic.  The partial-row
+// counts here are small (a few hundred rows), so the kernel is bound by load latency: more warps
+// per column strip shorten each thread's dependent chain.
+constexpr int SR_WARPS = 32;
+
+__global__ void __launch_bounds__(SR_WARPS * 32) sum_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows,
+                                                                  int d, float beta) {
+  __shared__ float red[SR_WARPS][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
-  float s = 0.f;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
   if (c < d) {
-#pragma unroll 4
-    for (int r = ty; r < nrows; r += 8) s += part[(long long)r * d + c];
+    int r = ty;
+    for (; r + 3 * SR_WARPS < nrows; r += 4 * SR_WARPS) {
+      s0 += part[(long long)r * d + c];
+      s1 += part[(long long)(r + SR_WARPS) * d + c];
+      s2 += part[(long long)(r + 2 * SR_WARPS) * d + c];
+      s3 += part[(long long)(r + 3 * SR_WARPS) * d + c];
+    }
+    for (; r < nrows; r += SR_WARPS) s0 += part[(long long)r * d + c];
   }
-  red[ty][tx] = s;
+  red[ty][tx] = (s0 + s1) + (s2 + s3);
   __syncthreads();
   if (ty == 0 && c < d) {
     float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += red[k][tx];
+    for (int k = 0; k < SR_WARPS; ++k) t += red[k][tx];
     out[c] = t + (beta != 0.f ? beta * out[c] : 0.f);
   }
 }
@@ -529,8 +542,8 @@ void sum_rows(at::Tensor part, at::Tensor out, double beta) {
   const int nrows = part.size(0), d = part.size(1);
   HT_CHECK(out.numel() == d, "sum_rows output size mismatch");
   HT_CHECK(part.is_contiguous() && part.dim() == 2, "sum_rows takes a contiguous [rows, d] tensor");
-  norm::sum_rows_kernel<<<(d + 31) / 32, 256, 0, stream()>>>(part.data_ptr<float>(), out.data_ptr<float>(), nrows, d,
-                                                               static_cast<float>(beta));
+  norm::sum_rows_kernel<<<(d + 31) / 32, norm::SR_WARPS * 32, 0, stream()>>>(part.data_ptr<float>(), out.data_ptr<float>(), nrows,
+                                                                              d, static_cast<float>(beta));
   HT_CUDA_CHECK(cudaGetLastError());
 }
 
