@@ -242,25 +242,35 @@ __global__ void __launch_bounds__(WARP_ROWS_THREADS)
 }
 
 // Every CTA writes one full partial row of dw (and db): zeros for columns it never touched.
-// The second pass re-reads the row's r and dy (cache hits: the same warp read them moments
-// before) instead of keeping xhat and dy*w in registers, which keeps the kernel at two CTAs per
-// SM; with only eight resident warps it was latency-bound.
+// Each warp accumulates its rows' dw/db contributions in its own slice of shared memory rather
+// than in registers, which keeps the kernel at 64 registers and four CTAs (32 warps) per SM:
+// profiled at two CTAs per SM it was latency bound (long-scoreboard stalls, 22 % warps active,
+// 24 % of DRAM peak).  The second pass re-reads the row's r and dy (cache hits: the same warp
+// read them moments before).  Per-warp sums and the final fixed-order CTA reduction keep the
+// result deterministic.
 template <bool RMS, bool HAS_DY, bool HAS_DR, int NV>
-__global__ void __launch_bounds__(WARP_ROWS_THREADS, 2)
+__global__ void __launch_bounds__(WARP_ROWS_THREADS, 4)
     norm_backward_warp_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ dr_in, const float* __restrict__ r,
                               const float* __restrict__ w, const float* __restrict__ mean, const float* __restrict__ rstd,
                               float* __restrict__ dres, __nv_bfloat16* __restrict__ ddelta, float* __restrict__ part_w,
                               float* __restrict__ part_b, int rows, int d) {
-  extern __shared__ float red[];  // [WARP_ROWS_THREADS / 32][d]
+  constexpr int WARPS = WARP_ROWS_THREADS / 32;
+  extern __shared__ float red[];  // dw accumulators [WARPS][d], then db accumulators [WARPS][d] when part_b is given
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = d >> 2;
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int warps = (gridDim.x * blockDim.x) >> 5;
-  float aw[NV][4], ab[NV][4];
+  const bool with_b = part_b != nullptr;
+  float* acc_w = red + warp * d;
+  float* acc_b = red + (WARPS + warp) * d;
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) aw[j][e] = ab[j][e] = 0.f;
+    const int v = lane + 32 * j;
+    if (v < nvec) {
+      st4(acc_w + 4 * v, zero);
+      if (with_b) st4(acc_b + 4 * v, zero);
+    }
   }
   for (int row = warp_global; row < rows; row += warps) {
     const long long base = (long long)row * d;
@@ -270,19 +280,23 @@ __global__ void __launch_bounds__(WARP_ROWS_THREADS, 2)
     for (int j = 0; j < NV; ++j) {
       const int v = lane + 32 * j;
       if (v < nvec) {
-        float rv[4], gy[4] = {0.f, 0.f, 0.f, 0.f}, wv[4];
+        float rv[4], gy[4] = {0.f, 0.f, 0.f, 0.f}, wv[4], aw[4], ab[4];
         ld4(r + base + 4 * v, rv);
         if (HAS_DY) ld4(dy + base + 4 * v, gy);
         ld4(w + 4 * v, wv);
+        ld4(acc_w + 4 * v, aw);
+        if (with_b) ld4(acc_b + 4 * v, ab);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float xhat = (rv[e] - mu) * rs;
           const float g = gy[e] * wv[e];
-          aw[j][e] += gy[e] * xhat;
-          ab[j][e] += gy[e];
+          aw[e] += gy[e] * xhat;
+          ab[e] += gy[e];
           sg += g;
           sgx += g * xhat;
         }
+        st4(acc_w + 4 * v, aw);
+        if (with_b) st4(acc_b + 4 * v, ab);
       }
     }
     const float mg = RMS ? 0.f : warp_sum(sg) / d;
@@ -307,27 +321,21 @@ __global__ void __launch_bounds__(WARP_ROWS_THREADS, 2)
     }
   }
   // CTA reduction of the per-warp partial sums, in a fixed order.
-  constexpr int WARPS = WARP_ROWS_THREADS / 32;
-  for (int pass = 0; pass < (part_b != nullptr ? 2 : 1); ++pass) {
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float t = 0.f;
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int v = lane + 32 * j;
-      if (v < nvec) st4(red + warp * d + 4 * v, pass == 0 ? aw[j] : ab[j]);
-    }
-    __syncthreads();
-    float* dst = pass == 0 ? part_w : part_b;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-      float t = 0.f;
+    for (int k = 0; k < WARPS; ++k) t += red[k * d + c];
+    part_w[(long long)blockIdx.x * d + c] = t;
+    if (with_b) {
+      float tb = 0.f;
 #pragma unroll
-      for (int k = 0; k < WARPS; ++k) t += red[k * d + c];
-      dst[(long long)blockIdx.x * d + c] = t;
+      for (int k = 0; k < WARPS; ++k) tb += red[(WARPS + k) * d + c];
+      part_b[(long long)blockIdx.x * d + c] = tb;
     }
-    __syncthreads();
   }
 }
 
-// out[c] = sum_b part[b, c] + beta * out[c]: 32 columns per CTA, 8 row groups summed in a fixed
-// order through shared memory.
 // out[c] = sum_r part[r, c] (+ beta * out[c]).  A block owns 32 columns (128-byte row segments);
 // its 32 warps take interleaved rows, four independent loads in flight per thread, and the 32
 // per-warp sums are added in a fixed order, so the result is deterministic.  The partial-row
@@ -375,7 +383,7 @@ inline int threads_for(int d) {
 
 }  // namespace norm
 
-int64_t norm_backward_blocks(int64_t rows) { return std::max<int64_t>(1, std::min<int64_t>(rows, 2 * num_sms())); }
+int64_t norm_backward_blocks(int64_t rows) { return std::max<int64_t>(1, std::min<int64_t>(rows, 4 * num_sms())); }
 
 #define HT_DISPATCH_W(WT_TENSOR, ...)                                                   \
   if ((WT_TENSOR).scalar_type() == at::kFloat) {                                        \
@@ -478,10 +486,11 @@ void norm_backward(c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dr, a
       (!has_dd || (ddelta->scalar_type() == at::kBFloat16 && aligned16(ddelta->data_ptr()))) &&
       (drp == nullptr || aligned16(drp)) && w.scalar_type() == at::kFloat && aligned16(w.data_ptr()) &&
       aligned16(r.data_ptr()) && aligned16(dres.data_ptr())) {
-    const size_t smem = (size_t)(norm::WARP_ROWS_THREADS / 32) * d * sizeof(float);
+    const size_t smem = (size_t)(pbp != nullptr ? 2 : 1) * (norm::WARP_ROWS_THREADS / 32) * d * sizeof(float);
     auto go = [&](auto rms_tag, auto dy_tag, auto dr_tag, auto nv_tag) {
       auto kernel = norm::norm_backward_warp_kernel<decltype(rms_tag)::value, decltype(dy_tag)::value,
                                                     decltype(dr_tag)::value, decltype(nv_tag)::value>;
+      if (smem > 48 * 1024) HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       kernel<<<blocks, norm::WARP_ROWS_THREADS, smem, s>>>(
           has_dy ? reinterpret_cast<const __nv_bfloat16*>(dy->data_ptr()) : nullptr, drp, r.data_ptr<float>(),
           w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), dres.data_ptr<float>(),
