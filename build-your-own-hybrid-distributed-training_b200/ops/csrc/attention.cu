@@ -244,6 +244,38 @@ __global__ void delta_kernel(const __nv_bfloat16* __restrict__ out, const __nv_b
   }
 }
 
+// delta with 16-byte loads: D / 8 lanes per (token, head) row, 8 products per lane, the row's lanes
+// reduced with shuffles inside their aligned group (both tensors contiguous and 16-byte aligned).
+template <int D>
+__global__ void __launch_bounds__(256) delta_vec_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ dout,
+                                                        float* __restrict__ delta, int S, int H, long long rows) {
+  constexpr int LPR = D / 8;
+  static_assert(32 % LPR == 0, "a row's lanes must be an aligned group inside one warp");
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long row = t / LPR;
+  const int sub = (int)(t % LPR);
+  float acc = 0.f;
+  if (row < rows) {
+    const long long off = row * D + sub * 8;  // [B*S, H, D] contiguous: row = (b*S + s)*H + h
+    const uint4 a = *reinterpret_cast<const uint4*>(out + off);
+    const uint4 g = *reinterpret_cast<const uint4*>(dout + off);
+    const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&g);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 x = __bfloat1622float2(ah[q]), y = __bfloat1622float2(gh[q]);
+      acc += x.x * y.x + x.y * y.y;
+    }
+  }
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (row < rows && sub == 0) {
+    const long long bs = row / H, h = row % H;
+    const long long b = bs / S, s = bs % S;
+    delta[(b * H + h) * S + s] = acc;
+  }
+}
+
 // dQ for one query tile of one head.
 template <int D>
 __global__ void __launch_bounds__(THREADS) dq_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ dout,
@@ -553,8 +585,17 @@ void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Ten
   const int dgrid = (int)((rows * 32 + dthreads - 1) / dthreads);
   const float sl2 = (float)scale * attn::LOG2E;
   dim3 gq((S + attn::BQ - 1) / attn::BQ, H, B), gk((S + attn::BKV - 1) / attn::BKV, HKV, B);
-  if (D == 64) attn::delta_kernel<64><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
-  else attn::delta_kernel<128><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
+  const bool vec = out.is_contiguous() && (reinterpret_cast<uintptr_t>(o) & 15) == 0 && (reinterpret_cast<uintptr_t>(d) & 15) == 0;
+  if (vec) {
+    const long long threads_total = rows * (D / 8);
+    const int vgrid = (int)((threads_total + dthreads - 1) / dthreads);
+    if (D == 64) attn::delta_vec_kernel<64><<<vgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
+    else attn::delta_vec_kernel<128><<<vgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
+  } else if (D == 64) {
+    attn::delta_kernel<64><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
+  } else {
+    attn::delta_kernel<128><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
+  }
   // The tcgen05 kernels (attention_bwd_tcgen05.cu) cover contiguous, 16-byte aligned tensors.
   if (std::getenv("HT_ATTN_MMA_SYNC") == nullptr &&
       attention_backward_tcgen05(qkv, dout, lse, delta, dqkv, H, HKV, D, causal, scale)) {

@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(256) column_partial_kernel(const T* __restrict
 #pragma unroll
   for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
   if (c0 < cols) {
-#pragma unroll 4
+#pragma unroll 8
     for (long long r = r0 + warp; r < r1; r += 8) {
       const T* p = x + r * cols + c0;
       if constexpr (VEC == 8 && std::is_same<T, __nv_bfloat16>::value) {
@@ -233,7 +233,7 @@ void column_sum(at::Tensor x, at::Tensor out, double beta) {
   const bool vec_ok = (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 && cols % (bf16 ? 8 : 4) == 0;
   const int vec = vec_ok ? (bf16 ? 8 : 4) : 1;
   const int strips = (cols + 32 * vec - 1) / (32 * vec);
-  int row_blocks = (int)std::max<long long>(1, std::min<long long>((rows + 63) / 64, (2LL * num_sms() + strips - 1) / strips));
+  int row_blocks = (int)std::max<long long>(1, std::min<long long>((rows + 63) / 64, (4LL * num_sms() + strips - 1) / strips));
   const int rpb = (int)((rows + row_blocks - 1) / row_blocks);
   row_blocks = (int)((rows + rpb - 1) / rpb);
   at::Tensor part = at::empty({row_blocks, cols}, out.options());
