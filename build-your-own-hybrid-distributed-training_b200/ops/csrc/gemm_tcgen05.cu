@@ -850,17 +850,24 @@ __global__ void split_reduce_kernel(const float* __restrict__ w, DT* __restrict_
 }
 
 // Split factor for a GEMM with `tiles` output tiles: the factor (<= 16, >= 4 K-blocks each) that
-// fills the most SMs in its last wave; 1 when the tiles already fill the GPU.
+// fills the most SMs in its last wave; 1 when the tiles already fill the GPU.  GEMMs with enough
+// tiles but a long K (>= 128 K-blocks, e.g. the LM head's input gradient: 192 tiles, K = 50257)
+// are split too when their last wave is mostly idle: there the fp32 partial tiles (one extra
+// write and read of the output per split) cost far less than an idle half wave.
 static int choose_splits(int tiles, int kblocks, int sms) {
-  if (tiles * 2 > sms || kblocks < 8) return 1;
+  if (kblocks < 8) return 1;
+  const bool long_k = kblocks >= 128;
+  if (tiles * 2 > sms && !long_k) return 1;
   int best = 1;
   double best_eff = (double)tiles / (double)(((tiles + sms - 1) / sms) * sms);
-  for (int sp = 2; sp <= 16; ++sp) {
+  const int max_split = tiles * 2 > sms ? 4 : 16;
+  const double margin = tiles * 2 > sms ? 0.10 : 0.02;
+  for (int sp = 2; sp <= max_split; ++sp) {
     const int per = (kblocks + sp - 1) / sp;
     if (per < 4 || (sp - 1) * per >= kblocks) break;
     const int units = tiles * sp;
     const double eff = (double)units / (double)(((units + sms - 1) / sms) * sms);
-    if (eff > best_eff + 0.02) {
+    if (eff > best_eff + margin) {
       best = sp;
       best_eff = eff;
     }

@@ -122,6 +122,21 @@ def test_column_sum_and_sum_rows() -> None:
         assert _rel(out, x.float().sum(0)) < 1e-5
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_gemm_split_k_long_reduction_with_many_tiles(out_dtype: torch.dtype) -> None:
+    """80 output tiles (more than half the SMs) and K = 8192: split three ways so the last wave fills."""
+    ops = _ops()
+    dev = torch.device("cuda")
+    m, n, k = 1280, 2048, 8192
+    a = torch.randn(m, k, device=dev).bfloat16()
+    b = torch.randn(n, k, device=dev).bfloat16()
+    out = torch.empty(m, n, device=dev, dtype=out_dtype)
+    ops.gemm(a, b, out=out)
+    ref = a.float() @ b.float().t()
+    err = float((out.float() - ref).abs().max()) / float(ref.abs().max())
+    assert err < (1e-5 if out_dtype == torch.float32 else 1e-2), err
+
+
 def test_gemm_padded_output_rows() -> None:
     ops = _ops()
     dev = torch.device("cuda")
