@@ -290,7 +290,9 @@ class DistributedDataParallel(nn.Module):
             from ..ops.comm import bucket_all_reduce
 
             if self._comm_stream is None:
-                self._comm_stream = torch.cuda.Stream(device=bucket.buffer.device)
+                # High priority: when compute kernels free SMs, the reduction's CTAs are scheduled
+                # first, so the all-reduce keeps pace with the backward pass instead of trailing it.
+                self._comm_stream = torch.cuda.Stream(device=bucket.buffer.device, priority=-1)
             self._comm_stream.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(self._comm_stream):
                 status = bucket_all_reduce(self._workspace, self._flat_grad, bucket.start, bucket.layout.total_numel,
