@@ -816,33 +816,71 @@ __global__ void __launch_bounds__(256) rs_sum_kernel(const __nv_bfloat16* __rest
   }
 }
 
-// D = beta * D + sum over s of W[s] (fixed order), W: fp32 [splits, split_rows, ldw].
+// D = beta * D + sum over s of W[s] (fixed order), W: fp32 [splits, split_rows, ldw].  Four
+// independent partial loads are in flight per thread; when D's rows allow it (`vec_d`: 16-byte
+// aligned fp32 or 8-byte aligned bf16 rows) a full group of four outputs is read and written as
+// one vector.
 template <typename DT>
 __global__ void split_reduce_kernel(const float* __restrict__ w, DT* __restrict__ d, int M, int N, long long ldd, int ldw,
-                                    int splits, long long split_stride, float beta) {
+                                    int splits, long long split_stride, float beta, int vec_d) {
   const long long n4 = (N + 3) / 4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)M * n4; i += (long long)gridDim.x * blockDim.x) {
     const int m = (int)(i / n4);
     const int c = (int)(i - (long long)m * n4) * 4;
+    const float* src = w + (long long)m * ldw + c;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int sidx = 0; sidx < splits; ++sidx) {
-      const float4 v = *reinterpret_cast<const float4*>(w + sidx * split_stride + (long long)m * ldw + c);
+    int sidx = 0;
+    for (; sidx + 3 < splits; sidx += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(src + (sidx + u) * split_stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // still added in split order
+        acc[0] += v[u].x;
+        acc[1] += v[u].y;
+        acc[2] += v[u].z;
+        acc[3] += v[u].w;
+      }
+    }
+    for (; sidx < splits; ++sidx) {
+      const float4 v = *reinterpret_cast<const float4*>(src + sidx * split_stride);
       acc[0] += v.x;
       acc[1] += v.y;
       acc[2] += v.z;
       acc[3] += v.w;
     }
+    DT* p = d + (long long)m * ldd + c;
+    if (vec_d && c + 3 < N) {
+      if constexpr (std::is_same<DT, float>::value) {
+        float4 o = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (beta != 0.f) {
+          const float4 old = *reinterpret_cast<const float4*>(p);
+          o.x += beta * old.x;
+          o.y += beta * old.y;
+          o.z += beta * old.z;
+          o.w += beta * old.w;
+        }
+        *reinterpret_cast<float4*>(p) = o;
+      } else {
+        __align__(8) __nv_bfloat16 o[4];
+        __align__(8) __nv_bfloat16 old[4];
+        if (beta != 0.f) *reinterpret_cast<uint2*>(old) = *reinterpret_cast<const uint2*>(p);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = f2bf(acc[e] + (beta != 0.f ? beta * bf2f(old[e]) : 0.f));
+        *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(o);
+      }
+      continue;
+    }
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       if (c + e < N) {
-        DT* p = d + (long long)m * ldd + c + e;
         float o = acc[e];
         if constexpr (std::is_same<DT, float>::value) {
-          if (beta != 0.f) o += beta * *p;
-          *p = o;
+          if (beta != 0.f) o += beta * p[e];
+          p[e] = o;
         } else {
-          if (beta != 0.f) o += beta * bf2f(*p);
-          *p = f2bf(o);
+          if (beta != 0.f) o += beta * bf2f(p[e]);
+          p[e] = f2bf(o);
         }
       }
     }
@@ -1063,13 +1101,15 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   if (splits > 1) {
     const long long work = M * ((N + 3) / 4);
     const int blocks = (int)std::min<long long>((work + 255) / 256, 8LL * num_sms());
+    const uintptr_t dp = reinterpret_cast<uintptr_t>(d.data_ptr());
+    const int vec_d = d32 ? (dp % 16 == 0 && d.stride(0) % 4 == 0) : (dp % 8 == 0 && d.stride(0) % 4 == 0);
     if (d32)
       split_reduce_kernel<float><<<blocks, 256, 0, s>>>(workspace.data_ptr<float>(), d.data_ptr<float>(), (int)M, (int)N, d.stride(0),
-                                                        (int)ldw, splits, split_rows * ldw, (float)beta);
+                                                        (int)ldw, splits, split_rows * ldw, (float)beta, vec_d);
     else
       split_reduce_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(workspace.data_ptr<float>(),
                                                                 reinterpret_cast<__nv_bfloat16*>(d.data_ptr()), (int)M, (int)N,
-                                                                d.stride(0), (int)ldw, splits, split_rows * ldw, (float)beta);
+                                                                d.stride(0), (int)ldw, splits, split_rows * ldw, (float)beta, vec_d);
     HT_CUDA_CHECK(cudaGetLastError());
   }
 }
