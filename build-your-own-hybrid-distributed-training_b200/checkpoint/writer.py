@@ -1,28 +1,35 @@
-"""Collective checkpoint writing: staged, checksummed, manifest-last, atomically renamed.
+"""Collective checkpoint writer.
 
-The protocol (``src/hybrid_training/checkpoint/writer.py:147-695``) makes every
-rank raise together or none at all:
+The on-disk result is the reference's format (``src/hybrid_training/checkpoint/writer.py:147-695``
+writes the same directory): ``checkpoint-step-NNNNNN/`` with one ``rank-NNNNN.pt`` payload per
+rank, ``metadata.json`` and ``manifest.json``, built in a ``.staging-<final>-<token>`` directory
+that is renamed into place only after the manifest, written last, has validated.  The code here is
+organised differently:
 
-1. rank 0 decides (new directory? staging token) and all ranks adopt its
-   verdict; an existing destination is an error everywhere;
-2. rank 0 creates ``.staging-<name>-<token>``; the outcome is shared; barrier;
-3. each rank writes ``rank-NNNNN.pt`` holding its pieces, keyed
-   ``"<category>::<key>@<offset>"`` (model / buffer / optimizer), plus its RNG
-   state under ``"rng::<name>"``; model and optimizer pieces come only from
-   ranks with ``data_parallel == 0`` and ``sequence == 0`` (their replicas hold
-   identical data); per-file SHA-256 and size are exchanged;
-4. rank 0 builds and validates the manifest, writes ``metadata.json`` then
-   ``manifest.json`` (last), and renames the staging directory into place;
-   the outcome is shared; barrier; optional pruning; barrier.
+* A save is a :class:`_SaveTransaction` that every rank runs in lock-step through four phases
+  (reserve, write, commit, retire).  Each phase ends in a *vote*: every rank contributes
+  ``(ok, reason)`` in one object all-gather and every rank evaluates the same list, so a failure on
+  any rank -- not only on the coordinator -- makes all ranks raise the same error before the next
+  phase starts.  The coordinator (global rank 0) is the only rank that touches shared directory
+  state (create the staging directory, write the manifest, rename, prune).
+* Payload bytes are hashed while they stream to disk (:class:`_DigestingFile`), then the file is
+  fsync'ed; nothing re-reads a payload to checksum it.
+* :class:`_PayloadBuilder` turns the model's global-coordinate pieces, its buffers, the optimizer
+  state (one flat interval per parameter piece, keyed ``"<storage key>::<state>"``) and this rank's
+  RNG streams into the payload dictionary plus one manifest record per piece.  Replicated tensors
+  are written by the ranks at ``data_parallel == 0`` and ``sequence == 0`` only; RNG state by every
+  rank.
 """
 
 from __future__ import annotations
 
+import hashlib
 import json
+import os
 import shutil
 import time
 import uuid
-from dataclasses import asdict
+from dataclasses import asdict, dataclass, field
 from pathlib import Path
 from typing import Any
 
@@ -44,7 +51,6 @@ from .format import (
     MANIFEST_FILENAME,
     METADATA_FILENAME,
     checkpoint_directory_name,
-    file_digest,
     shard_filename,
     staging_directory_name,
     step_from_directory_name,
@@ -54,26 +60,264 @@ from .manifest import CheckpointManifest, FileRecord, ShardRecord, TensorRecord
 __all__ = ["CheckpointWriteResult", "find_latest_checkpoint", "prune_checkpoints", "save_checkpoint"]
 
 _LOG = get_logger(__name__)
-_RNG = "rng::"
+_RNG_PREFIX = "rng::"
+_COORDINATOR = 0
 
 
+@dataclass(frozen=True)
 class CheckpointWriteResult:
-    def __init__(self, path: Path, step: int, seconds: float, bytes_written: int, num_tensors: int) -> None:
-        self.path, self.step, self.seconds, self.bytes_written, self.num_tensors = path, step, seconds, bytes_written, num_tensors
+    """What one rank's part of a save produced."""
+
+    path: Path
+    step: int
+    seconds: float
+    bytes_written: int
+    num_tensors: int
+    sha256: str = ""
 
     def __repr__(self) -> str:
-        return (f"CheckpointWriteResult(path={self.path.name!r}, step={self.step}, {self.seconds:.3f}s, {self.bytes_written} bytes, "
-                f"{self.num_tensors} tensors)")
+        return (f"CheckpointWriteResult({self.path.name}, step {self.step}: {self.num_tensors} pieces, "
+                f"{self.bytes_written} bytes in {self.seconds:.3f}s)")
 
 
-def _writes_replicated_tensors(context: DistributedContext) -> bool:
-    c = context.topology.coordinates_of(context.rank)
-    return c.data_parallel == 0 and c.sequence == 0
+class _DigestingFile:
+    """Binary file that feeds every written byte to SHA-256 and counts it."""
+
+    def __init__(self, path: Path) -> None:
+        self._file = path.open("wb")
+        self._hash = hashlib.sha256()
+        self.size = 0
+
+    def write(self, data: Any) -> int:
+        view = memoryview(data)
+        self._hash.update(view)
+        self.size += view.nbytes
+        return self._file.write(view)
+
+    def flush(self) -> None:
+        self._file.flush()
+
+    def finish(self) -> str:
+        """Flush to stable storage, close, and return the hex digest."""
+        self._file.flush()
+        os.fsync(self._file.fileno())
+        self._file.close()
+        return self._hash.hexdigest()
+
+    def abandon(self) -> None:
+        if not self._file.closed:
+            self._file.close()
 
 
-def _agree(value: Any, context: DistributedContext) -> Any:
-    """Everyone adopts rank 0's value."""
-    return all_gather_object_in_group(value, context.group("world"))[0]
+@dataclass
+class _PayloadBuilder:
+    """Collects this rank's tensors (payload) and the manifest records that describe them."""
+
+    rank: int
+    file_name: str
+    parallel_info: dict[str, Any]
+    tensors: dict[str, torch.Tensor] = field(default_factory=dict)
+    records: list[dict[str, Any]] = field(default_factory=list)
+    scalars: dict[str, Any] = field(default_factory=dict)
+
+    def piece(self, *, category: str, key: str, name: str, global_shape: tuple[int, ...], offset: int, values: torch.Tensor,
+              state_name: str = "") -> None:
+        storage_key = f"{category}::{key}@{offset}"
+        flat = values.detach().reshape(-1).to("cpu", copy=True)
+        self.tensors[storage_key] = flat
+        info = self.parallel_info.get(name)
+        self.records.append({
+            "key": key, "name": name, "global_shape": [int(s) for s in global_shape], "dtype": str(flat.dtype),
+            "category": category, "state_name": state_name,
+            "partition_dim": info.partition_dim if info is not None else None,
+            "tensor_parallel_size": info.tensor_parallel_size if info is not None else 1,
+            "tensor_parallel_rank": info.tensor_parallel_rank if info is not None else 0,
+            "rank": self.rank, "file": self.file_name, "offset": int(offset), "length": int(flat.numel()),
+            "storage_key": storage_key})
+
+    def storage_key_of(self, name: str) -> str:
+        info = self.parallel_info.get(name)
+        return info.storage_key if info is not None else name
+
+    def add_model(self, model: HybridModel) -> None:
+        for name, piece in model.sharded_state_dict().items():
+            self.piece(category="model", key=self.storage_key_of(name), name=name, global_shape=piece.global_shape,
+                       offset=piece.offset, values=piece.data)
+        for name, buf in model.buffers_state_dict().items():
+            self.piece(category="buffer", key=name, name=name, global_shape=tuple(buf.shape), offset=0, values=buf)
+
+    def add_optimizer(self, model: HybridModel, optimizer: ShardedOptimizer) -> None:
+        layouts = model.optimizer_parameter_layout()
+        for index, param in enumerate(optimizer.parameters):
+            for state_name, value in (optimizer.inner.state.get(param) or {}).items():
+                if torch.is_tensor(value) and value.numel() == param.numel():
+                    flat = value.detach().reshape(-1)
+                    for item in layouts[index]:
+                        self.piece(category="optimizer", key=f"{self.storage_key_of(item.name)}::{state_name}", name=item.name,
+                                   global_shape=item.global_shape, offset=item.parameter_offset,
+                                   values=flat[item.local_offset:item.local_offset + item.length], state_name=state_name)
+                else:
+                    self._scalar(state_name, value)
+
+    def _scalar(self, state_name: str, value: Any) -> None:
+        if torch.is_tensor(value):
+            value = value.item() if value.numel() == 1 else [float(v) for v in value.reshape(-1).tolist()]
+        previous = self.scalars.setdefault(state_name, value)
+        if previous != value:
+            raise CheckpointError(format_error(
+                "checkpoint.save", f"the per-parameter optimizer scalar {state_name!r} is not the same for every parameter, but "
+                "the checkpoint keeps a single value per scalar name", rank=self.rank, expected=previous, observed=value,
+                resolution="save only after optimizer steps that updated every parameter (e.g. not mid-way through a "
+                           "partial step)"))
+
+    def add_rng(self) -> None:
+        for name, t in rng_state_to_serialisable(capture_rng_state())["tensors"].items():
+            self.tensors[_RNG_PREFIX + name] = t
+
+
+class _SaveTransaction:
+    """One save, driven through reserve -> write -> commit -> retire on every rank."""
+
+    def __init__(self, root: Path, context: DistributedContext, step: int) -> None:
+        self.root = root
+        self.context = context
+        self.step = step
+        self.final = root / checkpoint_directory_name(step)
+        self.staging: Path | None = None
+        self.started = time.perf_counter()
+
+    # -- voting --------------------------------------------------------------------------------------------------
+    def _vote(self, phase: str, problem: str | None, payload: Any = None) -> list[dict[str, Any]]:
+        """Every rank shares ``problem`` (None = fine); all raise together when any rank reported one."""
+        ballots = all_gather_object_in_group({"rank": self.context.rank, "problem": problem, "payload": payload},
+                                             self.context.group("world"))
+        failed = [b for b in ballots if b["problem"]]
+        if failed:
+            first = failed[0]
+            raise CheckpointError(format_error(
+                f"checkpoint.save[{phase}]", f"{len(failed)} rank(s) could not complete the {phase} phase; the checkpoint "
+                "was not published", rank=self.context.rank, world_size=self.context.world_size,
+                expected=f"every rank to finish {phase}", observed=f"rank {first['rank']}: {first['problem']}",
+                resolution=_PHASE_HINTS[phase]))
+        return ballots
+
+    # -- phases ----------------------------------------------------------------------------------------------------
+    def reserve(self) -> None:
+        problem, token = None, None
+        if self.context.rank == _COORDINATOR:
+            token = uuid.uuid4().hex[:12]
+            if self.final.exists():
+                problem = f"{self.final} is already present"
+            else:
+                try:
+                    (self.root / staging_directory_name(self.final.name, token)).mkdir(parents=True)
+                except OSError as exc:
+                    problem = f"creating the staging directory failed ({exc})"
+        ballots = self._vote("reserve", problem, token)
+        self.staging = self.root / staging_directory_name(self.final.name, ballots[_COORDINATOR]["payload"])
+
+    def write(self, builder: _PayloadBuilder) -> tuple[dict[str, Any], list[dict[str, Any]]]:
+        assert self.staging is not None
+        problem, mine = None, None
+        target = self.staging / builder.file_name
+        sink = None
+        try:
+            sink = _DigestingFile(target)
+            torch.save(builder.tensors, sink)
+            digest = sink.finish()
+            mine = {"file": {"name": builder.file_name, "sha256": digest, "bytes": sink.size}, "records": builder.records,
+                    "optimizer_scalars": builder.scalars}
+        except Exception as exc:  # reported through the vote so that every rank raises
+            if sink is not None:
+                sink.abandon()
+            problem = f"writing {target.name} failed ({type(exc).__name__}: {exc})"
+        ballots = self._vote("write", problem, mine)
+        return mine, [b["payload"] for b in ballots]
+
+    def commit(self, metadata: dict[str, Any], contributions: list[dict[str, Any]]) -> None:
+        problem = None
+        if self.context.rank == _COORDINATOR:
+            try:
+                _publish(self.staging, self.final, self.context, self.step, metadata, contributions)
+            except Exception as exc:
+                problem = f"{type(exc).__name__}: {exc} (staging directory {self.staging.name} left for inspection)"
+        self._vote("commit", problem)
+
+    def retire(self, keep_last: int) -> None:
+        problem = None
+        if self.context.rank == _COORDINATOR and keep_last > 0:
+            try:
+                prune_checkpoints(self.root, keep_last=keep_last)
+            except OSError as exc:
+                problem = f"pruning failed ({exc})"
+        self._vote("retire", problem)
+
+
+_PHASE_HINTS = {
+    "reserve": "pick another step or delete the old directory, and make sure the checkpoint root is writable",
+    "write": "look at the failing rank's filesystem: free space, quota and permissions of the checkpoint root",
+    "commit": "the coordinator's manifest or rename failed; its message names the cause",
+    "retire": "the new checkpoint is published; remove old checkpoint directories by hand",
+}
+
+
+def _publish(staging: Path, final: Path, context: DistributedContext, step: int, metadata: dict[str, Any],
+             contributions: list[dict[str, Any]]) -> None:
+    """Coordinator only: manifest from every rank's records, metadata, manifest last, then rename."""
+    manifest = CheckpointManifest(CURRENT_FORMAT_VERSION, context.world_size, context.topology.summary(), step,
+                                  created_by=f"hybrid_training {__version__}")
+    for part in contributions:
+        record = FileRecord.from_dict(part["file"])
+        on_disk = staging / record.name
+        if not on_disk.is_file() or on_disk.stat().st_size != record.bytes:
+            raise CheckpointError(format_error("checkpoint.save[commit]", "a payload file is missing or has a different size "
+                                               "than its writer reported", rank=context.rank, expected=f"{record.name}: "
+                                               f"{record.bytes} bytes", observed="missing" if not on_disk.is_file()
+                                               else f"{on_disk.stat().st_size} bytes",
+                                               resolution="the staging directory is not shared by all ranks, or a disk "
+                                                          "error occurred; use a filesystem that every rank sees"))
+        manifest.files[record.name] = record
+        for r in part["records"]:
+            tensor = TensorRecord(r["key"], r["name"], tuple(r["global_shape"]), r["dtype"], r["category"], r["partition_dim"],
+                                  r["tensor_parallel_size"], r["tensor_parallel_rank"], r["state_name"])
+            manifest.add_shard(tensor, ShardRecord(r["rank"], r["file"], r["offset"], r["length"], r["storage_key"],
+                                                   r.get("padding", 0)))
+    manifest.complete = True
+    manifest.validate()
+    (staging / METADATA_FILENAME).write_text(_to_json(metadata), encoding="utf-8")
+    manifest.write(staging / MANIFEST_FILENAME)  # written last: its presence marks a finished directory
+    os.replace(staging, final)
+    _LOG.info("published %s: %d tensors in %d payload files", final, len(manifest.tensors), len(manifest.files))
+
+
+def _metadata(*, context: DistributedContext, state: TrainingState, config: ExperimentConfig | None,
+              scheduler_state: dict[str, Any] | None, scaler_state: dict[str, Any] | None, extra: dict[str, Any] | None,
+              contributions: list[dict[str, Any]], save_rng: bool) -> dict[str, Any]:
+    scalars: dict[str, Any] = {}
+    for part in contributions:
+        scalars.update(part.get("optimizer_scalars") or {})
+    rng = {"saved": False, "ranks": [], "meta": {}}
+    if save_rng:
+        rng = {"saved": True, "ranks": list(range(context.world_size)),
+               "meta": rng_state_to_serialisable(capture_rng_state())["meta"]}
+    return {"format_version": CURRENT_FORMAT_VERSION, "created_by": f"hybrid_training {__version__}",
+            "training_state": state.as_dict(), "scheduler": dict(scheduler_state or {}), "scaler": dict(scaler_state or {}),
+            "config": config.to_dict() if config is not None else None, "topology": context.topology.summary(),
+            "world_size": context.world_size, "backend": context.backend, "rng": rng, "optimizer_scalars": scalars,
+            "extra": dict(extra or {})}
+
+
+def _to_json(obj: dict[str, Any]) -> str:
+    def encode(value: Any) -> Any:
+        if isinstance(value, (tuple, set, frozenset)):
+            return list(value)
+        if hasattr(value, "as_dict"):
+            return value.as_dict()
+        if hasattr(value, "__dataclass_fields__"):
+            return asdict(value)
+        raise TypeError(f"{type(value).__name__} cannot go into metadata.json; tensors are stored in the payload files")
+
+    return json.dumps(obj, indent=2, sort_keys=True, default=encode, allow_nan=False)
 
 
 def save_checkpoint(directory: str | Path, *, model: HybridModel, context: DistributedContext, state: TrainingState,
@@ -81,196 +325,52 @@ def save_checkpoint(directory: str | Path, *, model: HybridModel, context: Distr
                     scheduler_state: dict[str, Any] | None = None, scaler_state: dict[str, Any] | None = None,
                     extra_metadata: dict[str, Any] | None = None, save_optimizer: bool = True, save_rng: bool = True,
                     keep_last: int = 0) -> CheckpointWriteResult:
-    start = time.perf_counter()
-    root = Path(directory)
-    final_name = checkpoint_directory_name(state.step)
-    final = root / final_name
-    verdict = _agree({"token": uuid.uuid4().hex[:12], "exists": final.exists()} if context.is_primary else None, context)
-    if verdict["exists"]:
-        raise CheckpointError(format_error("checkpoint.save", "the destination checkpoint already exists", rank=context.rank,
-                                           world_size=context.world_size, expected="a fresh directory", observed=str(final),
-                                           resolution="remove the existing checkpoint or save at a different step"))
-    staging = root / staging_directory_name(final_name, verdict["token"])
-    error = ""
-    if context.is_primary:
-        try:
-            staging.mkdir(parents=True, exist_ok=True)
-        except OSError as exc:
-            error = str(exc)
-    error = _agree(error, context)
-    if error:
-        raise CheckpointError(format_error("checkpoint.save", "the staging directory could not be created", rank=context.rank,
-                                           world_size=context.world_size, expected=str(staging), observed=error,
-                                           resolution="check permissions and free space on the checkpoint filesystem"))
-    context.barrier("world", label="checkpoint-staging-created")
-    payload, records, scalars = _collect_payload(model=model, optimizer=optimizer, context=context, save_optimizer=save_optimizer,
-                                                 save_rng=save_rng)
-    name = shard_filename(context.rank)
-    path = staging / name
-    torch.save(payload, path)
-    size = path.stat().st_size
-    mine = {"file": {"name": name, "sha256": file_digest(path), "bytes": size}, "records": records, "optimizer_scalars": scalars}
-    gathered = all_gather_object_in_group(mine, context.group("world"))
-    context.barrier("world", label="checkpoint-payloads-written")
-    error = ""
-    if context.is_primary:
-        try:
-            _publish(context=context, state=state, config=config, scheduler_state=scheduler_state, scaler_state=scaler_state,
-                     extra_metadata=extra_metadata, gathered=gathered, save_rng=save_rng, staging=staging, final=final)
-        except Exception as exc:
-            error = f"{type(exc).__name__}: {exc}"
-    error = _agree(error, context)
-    if error:
-        raise CheckpointError(format_error("checkpoint.save", "the checkpoint could not be published; nothing was renamed into place",
-                                           rank=context.rank, world_size=context.world_size,
-                                           expected="a validated manifest covering every tensor exactly once", observed=error,
-                                           resolution=f"read rank 0's error; staging directory {staging.name!r} is kept for inspection"))
-    context.barrier("world", label="checkpoint-published")
-    if context.is_primary and keep_last > 0:
-        prune_checkpoints(root, keep_last=keep_last)
-    context.barrier("world", label="checkpoint-pruned")
-    return CheckpointWriteResult(final, state.step, time.perf_counter() - start, size, len(records))
+    """Write ``checkpoint-step-<step>`` under ``directory``; collective over the world group.
 
-
-def _publish(*, context: DistributedContext, state: TrainingState, config: ExperimentConfig | None,
-             scheduler_state: dict[str, Any] | None, scaler_state: dict[str, Any] | None, extra_metadata: dict[str, Any] | None,
-             gathered: list[dict[str, Any]], save_rng: bool, staging: Path, final: Path) -> None:
-    manifest = CheckpointManifest(CURRENT_FORMAT_VERSION, context.world_size, context.topology.summary(), state.step,
-                                  created_by=f"hybrid_training {__version__}")
-    for entry in gathered:
-        fr = FileRecord.from_dict(entry["file"])
-        manifest.files[fr.name] = fr
-        for item in entry["records"]:
-            manifest.add_shard(
-                TensorRecord(item["key"], item["name"], tuple(item["global_shape"]), item["dtype"], item["category"],
-                             item["partition_dim"], item["tensor_parallel_size"], item["tensor_parallel_rank"], item["state_name"]),
-                ShardRecord(item["rank"], item["file"], item["offset"], item["length"], item["storage_key"], item.get("padding", 0)))
-    manifest.complete = True
-    manifest.validate()
-    for name in manifest.referenced_files():
-        if not (staging / name).is_file():
-            raise CheckpointError(format_error("checkpoint.save", "a rank reported a file that is not in the staging directory",
-                                               rank=context.rank, world_size=context.world_size, expected=name, observed="missing",
-                                               resolution="check for a filesystem error on the reporting rank"))
-    metadata = _build_metadata(context=context, state=state, config=config, scheduler_state=scheduler_state,
-                               scaler_state=scaler_state, extra_metadata=extra_metadata, gathered=gathered, save_rng=save_rng)
-    (staging / METADATA_FILENAME).write_text(_dump_json(metadata), encoding="utf-8")
-    manifest.write(staging / MANIFEST_FILENAME)
-    staging.replace(final)
-    _LOG.info("checkpoint written: %s (%d tensors, %d files)", final, len(manifest.tensors), len(manifest.files))
-
-
-def _collect_payload(*, model: HybridModel, optimizer: ShardedOptimizer | None, context: DistributedContext, save_optimizer: bool,
-                     save_rng: bool) -> tuple[dict[str, torch.Tensor], list[dict[str, Any]], dict[str, Any]]:
-    fname = shard_filename(context.rank)
-    info_of = model.parameter_parallel_info()
-    payload: dict[str, torch.Tensor] = {}
-    records: list[dict[str, Any]] = []
-    scalars: dict[str, Any] = {}
-
-    def add(key: str, name: str, shape: tuple[int, ...], offset: int, data: torch.Tensor, category: str, state_name: str = "") -> None:
-        info = info_of.get(name)
-        storage_key = f"{category}::{key}@{offset}"
-        payload[storage_key] = data.detach().cpu().reshape(-1).clone()
-        records.append({"key": key, "name": name, "global_shape": list(shape), "dtype": str(data.dtype), "category": category,
-                        "partition_dim": None if info is None else info.partition_dim,
-                        "tensor_parallel_size": 1 if info is None else info.tensor_parallel_size,
-                        "tensor_parallel_rank": 0 if info is None else info.tensor_parallel_rank, "state_name": state_name,
-                        "rank": context.rank, "file": fname, "offset": offset, "length": int(data.numel()), "storage_key": storage_key})
-
-    if _writes_replicated_tensors(context):
-        for name, piece in model.sharded_state_dict().items():
-            info = info_of.get(name)
-            add(info.storage_key if info else name, name, piece.global_shape, piece.offset, piece.data, "model")
-        for name, buf in model.buffers_state_dict().items():
-            add(name, name, tuple(buf.shape), 0, buf.reshape(-1), "buffer")
+    Every rank returns normally or every rank raises :class:`CheckpointError`; a failed save
+    leaves no directory named like a checkpoint (a staging directory may remain for inspection).
+    """
+    tx = _SaveTransaction(Path(directory), context, state.step)
+    tx.reserve()
+    builder = _PayloadBuilder(context.rank, shard_filename(context.rank), model.parameter_parallel_info())
+    coords = context.topology.coordinates_of(context.rank)
+    if coords.data_parallel == 0 and coords.sequence == 0:  # replicas along dp / seq hold identical tensors
+        builder.add_model(model)
         if save_optimizer and optimizer is not None:
-            layouts = model.optimizer_parameter_layout()
-            inner_state = optimizer.inner.state
-            for index, param in enumerate(optimizer.parameters):
-                entry = inner_state.get(param)
-                if not entry:
-                    continue
-                for state_name, value in entry.items():
-                    if not torch.is_tensor(value) or value.numel() != param.numel():
-                        scalar = _as_scalar(value)
-                        if state_name in scalars and scalars[state_name] != scalar:
-                            raise CheckpointError(format_error(
-                                "checkpoint.save", f"optimizer state {state_name!r} differs between parameters; the format stores "
-                                "one value per state name", rank=context.rank, expected=scalars[state_name], observed=scalar,
-                                resolution="step every parameter together"))
-                        scalars[state_name] = scalar
-                        continue
-                    flat = value.detach().reshape(-1)
-                    for item in layouts[index]:
-                        info = info_of.get(item.name)
-                        base = info.storage_key if info else item.name
-                        add(f"{base}::{state_name}", item.name, item.global_shape, item.parameter_offset,
-                            flat[item.local_offset:item.local_offset + item.length], "optimizer", state_name)
+            builder.add_optimizer(model, optimizer)
     if save_rng:
-        for name, t in rng_state_to_serialisable(capture_rng_state())["tensors"].items():
-            payload[f"{_RNG}{name}"] = t
-    return payload, records, scalars
-
-
-def _as_scalar(value: Any) -> Any:
-    if torch.is_tensor(value):
-        return value.item() if value.numel() == 1 else [float(v) for v in value.reshape(-1).tolist()]
-    return value
-
-
-def _build_metadata(*, context: DistributedContext, state: TrainingState, config: ExperimentConfig | None,
-                    scheduler_state: dict[str, Any] | None, scaler_state: dict[str, Any] | None, extra_metadata: dict[str, Any] | None,
-                    gathered: list[dict[str, Any]], save_rng: bool) -> dict[str, Any]:
-    scalars: dict[str, Any] = {}
-    for entry in gathered:
-        scalars.update(entry.get("optimizer_scalars", {}))
-    return {"format_version": CURRENT_FORMAT_VERSION, "created_by": f"hybrid_training {__version__}",
-            "training_state": state.as_dict(), "scheduler": scheduler_state or {}, "scaler": scaler_state or {},
-            "config": None if config is None else config.to_dict(), "topology": context.topology.summary(),
-            "world_size": context.world_size, "backend": context.backend,
-            "rng": {"saved": save_rng, "ranks": list(range(context.world_size)) if save_rng else [],
-                    "meta": rng_state_to_serialisable(capture_rng_state())["meta"] if save_rng else {}},
-            "optimizer_scalars": scalars, "extra": extra_metadata or {}}
-
-
-def _dump_json(payload: dict[str, Any]) -> str:
-    def default(v: Any) -> Any:
-        if isinstance(v, (set, frozenset, tuple)):
-            return list(v)
-        if hasattr(v, "as_dict"):
-            return v.as_dict()
-        if hasattr(v, "__dataclass_fields__"):
-            return asdict(v)
-        raise TypeError(f"checkpoint metadata must be JSON-serialisable; {type(v).__name__} is not (tensors belong in payload files)")
-
-    return json.dumps(payload, indent=2, sort_keys=True, default=default, allow_nan=False)
+        builder.add_rng()
+    mine, contributions = tx.write(builder)
+    metadata = _metadata(context=context, state=state, config=config, scheduler_state=scheduler_state,
+                         scaler_state=scaler_state, extra=extra_metadata, contributions=contributions, save_rng=save_rng)
+    tx.commit(metadata, contributions)
+    tx.retire(keep_last)
+    return CheckpointWriteResult(tx.final, state.step, time.perf_counter() - tx.started, int(mine["file"]["bytes"]),
+                                 len(builder.records), mine["file"]["sha256"])
 
 
 def prune_checkpoints(root: str | Path, *, keep_last: int) -> list[Path]:
-    """Delete all but the newest ``keep_last`` complete-looking checkpoint directories."""
+    """Remove checkpoint directories older than the newest ``keep_last``; returns what was removed."""
     base = Path(root)
     if keep_last <= 0 or not base.is_dir():
         return []
-    found = sorted((s, c) for c in base.iterdir() if c.is_dir() and (s := step_from_directory_name(c.name)) is not None)
-    removed = []
-    for _, path in found[:max(len(found) - keep_last, 0)]:
+    by_step = {}
+    for child in base.iterdir():
+        step = step_from_directory_name(child.name) if child.is_dir() else None
+        if step is not None:
+            by_step[step] = child
+    doomed = [by_step[s] for s in sorted(by_step)[:-keep_last]] if len(by_step) > keep_last else []
+    for path in doomed:
         shutil.rmtree(path, ignore_errors=True)
-        removed.append(path)
-        _LOG.info("pruned old checkpoint %s", path.name)
-    return removed
+        _LOG.info("removed checkpoint %s (keep_last=%d)", path.name, keep_last)
+    return doomed
 
 
 def find_latest_checkpoint(root: str | Path) -> Path | None:
-    """Newest ``checkpoint-step-*`` directory that has a manifest (i.e. was published)."""
+    """The published checkpoint (one with a manifest) with the highest step under ``root``, if any."""
     base = Path(root)
     if not base.is_dir():
         return None
-    best: tuple[int, Path] | None = None
-    for child in sorted(base.iterdir()):
-        if not child.is_dir() or not CHECKPOINT_DIRECTORY_PATTERN.match(child.name) or not (child / MANIFEST_FILENAME).is_file():
-            continue
-        step = step_from_directory_name(child.name)
-        if step is not None and (best is None or step > best[0]):
-            best = (step, child)
-    return None if best is None else best[1]
+    published = [(step_from_directory_name(c.name), c) for c in base.iterdir()
+                 if c.is_dir() and CHECKPOINT_DIRECTORY_PATTERN.match(c.name) and (c / MANIFEST_FILENAME).is_file()]
+    return max(published, key=lambda sc: sc[0])[1] if published else None

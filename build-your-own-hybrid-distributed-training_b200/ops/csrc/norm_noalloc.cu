@@ -18,11 +18,14 @@
 //   * the first call on each device looks up the array's device address with
 //     cudaGetSymbolAddress (with that device current) and caches it.  Make that first call before
 //     any stream capture begins;
-//   * the entry point calls no cudaMalloc, cudaFree or allocating library routine.
+//   * the entry point calls no cudaMalloc, cudaFree or allocating library routine;
+//   * `mean` is read for LayerNorm only: RMSNorm callers may pass null or any buffer there.
 //
 // Results equal the regular path: dres = d(residual) + norm-backward(dy), ddelta = the same values
 // in the branch dtype, dw = sum over rows of dy * xhat, db = sum over rows of dy (LayerNorm only),
 // all fp32 except ddelta.
+
+#include "norm_noalloc.h"
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -33,8 +36,9 @@
 namespace {
 
 constexpr int NORM_NOALLOC_MAX_BLOCKS = 128;
-constexpr int NORM_NOALLOC_MAX_COLS = 8192;
+constexpr int NORM_NOALLOC_MAX_COLS = HT_NORM_NOALLOC_MAX_COLS;
 constexpr int VPT = 8;  // columns per thread
+constexpr int MAX_THREADS = NORM_NOALLOC_MAX_COLS / VPT;  // 1024: one block row covers the widest hidden size
 
 // Partial weight-gradient rows, then partial bias-gradient rows.
 static __device__ __align__(256) float g_norm_partials[2 * NORM_NOALLOC_MAX_BLOCKS * NORM_NOALLOC_MAX_COLS];
@@ -57,7 +61,9 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   return v;
 }
 
-__global__ void backward_kernel(const void* __restrict__ dy, int dy_bf16, const float* __restrict__ dr,
+// Bounded to 1024 threads so that the compiler keeps every thread within 64 registers: the widest
+// hidden size (8192 columns, 8 per thread) launches 1024 threads and must fit in one SM's registers.
+__global__ void __launch_bounds__(MAX_THREADS) backward_kernel(const void* __restrict__ dy, int dy_bf16, const float* __restrict__ dr,
                                 const float* __restrict__ r, const void* __restrict__ w, int w_bf16,
                                 const float* __restrict__ mean, const float* __restrict__ rstd, float* __restrict__ dres,
                                 void* __restrict__ ddelta, int ddelta_bf16, float* __restrict__ partials, int rows, int d,
@@ -72,7 +78,8 @@ __global__ void backward_kernel(const void* __restrict__ dy, int dy_bf16, const 
   }
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const long long base = (long long)row * d;
-    const float mu = mean[row], rs = rstd[row];
+    const float mu = rms ? 0.f : mean[row];  // RMSNorm normalises by the root mean square only
+    const float rs = rstd[row];
     float xh[VPT], g[VPT];
     float sg = 0.f, sgx = 0.f;
 #pragma unroll
@@ -158,22 +165,13 @@ cudaError_t partials_for_current_device(int dev, float** out) {
 extern "C" {
 
 // Fused residual-add + LayerNorm (rms = 0) or RMSNorm (rms = 1) backward without any allocation.
-//
-// dy: [rows, d] gradient of the normalised output (bf16 if dy_is_bf16, else fp32; may be null);
-// dr: [rows, d] fp32 gradient arriving on the residual stream (may be null); r: [rows, d] fp32
-// residual-stream values the forward normalised; w: [d] norm weight (bf16 or fp32); mean, rstd:
-// [rows] fp32 statistics saved by the forward (mean is read only for LayerNorm).  Outputs: dres
-// [rows, d] fp32, ddelta [rows, d] (bf16 or fp32; may be null), dw [d] fp32, db [d] fp32 (LayerNorm
-// only; ignored for RMSNorm).  Work is queued on `stream` on the current device.
-//
-// Return codes: 0 success; 1 bad sizes or a missing required pointer; 2 hidden size d above 8192;
-// 1000 + cudaError_t for a failure in the one-time set-up or in a launch.
+// The arguments, limits and return codes are documented with the declaration in norm_noalloc.h.
 __attribute__((visibility("default"))) int ht_norm_backward_noalloc(
     const void* dy, int dy_is_bf16, const float* dr, const float* r, const void* w, int w_is_bf16, const float* mean,
     const float* rstd, float* dres, void* ddelta, int ddelta_is_bf16, float* dw, float* db, int rows, int d, int rms,
     cudaStream_t stream) {
-  if (rows < 0 || d <= 0 || r == nullptr || w == nullptr || mean == nullptr || rstd == nullptr || dres == nullptr ||
-      dw == nullptr || (!rms && db == nullptr))
+  if (rows < 0 || d <= 0 || r == nullptr || w == nullptr || (!rms && mean == nullptr) || rstd == nullptr ||
+      dres == nullptr || dw == nullptr || (!rms && db == nullptr))
     return 1;
   if (d > NORM_NOALLOC_MAX_COLS) return 2;
   int dev = 0;

@@ -37,7 +37,7 @@ from .ddp import DistributedDataParallel
 from .fsdp import FullyShardedDataParallel, PieceLayout, ShardedTensorPiece
 from .tensor_parallel import all_reduce_sequence_parallel_gradients
 
-__all__ = ["HybridModel", "ParallelismDescription", "ParameterParallelInfo", "build_model", "build_parallel_model",
+__all__ = ["HybridModel", "ParallelismDescription", "PlanStep", "ParameterParallelInfo", "build_model", "build_parallel_model",
            "describe_parallel_plan"]
 
 _LOG = get_logger(__name__)
@@ -63,8 +63,25 @@ class ParameterParallelInfo:
                 "tensor_parallel_size": self.tensor_parallel_size, "tensor_parallel_rank": self.tensor_parallel_rank}
 
 
+@dataclass(frozen=True)
+class PlanStep:
+    """One collective of the training step: when it runs, what it moves, over which group, and by which code."""
+
+    phase: str           # "forward", "backward", "optimizer" or "metrics"
+    operation: str       # what is communicated
+    group: str           # process-group name of the 4-D grid
+    implementation: str  # the kernel or library call that performs it on this configuration
+
+
 @dataclass
 class ParallelismDescription:
+    """The parallel plan of one rank: placement of parameters / activations and every collective of a step.
+
+    ``steps`` lists the collectives in the order a step issues them, each with the implementation
+    this configuration selects (in-kernel NVLink collective, NCCL, or Gloo).  The list fields
+    summarise the same plan by group for programmatic checks.
+    """
+
     strategy: str
     replicated_parameters: list[str] = field(default_factory=list)
     sharded_parameters: list[str] = field(default_factory=list)
@@ -72,19 +89,22 @@ class ParallelismDescription:
     gradient_reductions: list[tuple[str, str]] = field(default_factory=list)
     metric_group: str = "dp_shard"
     notes: list[str] = field(default_factory=list)
+    steps: list[PlanStep] = field(default_factory=list)
 
     def render(self) -> str:
-        lines = [
-            f"parallel strategy: {self.strategy}",
-            f"  parameters replicated over : {self.replicated_parameters or ['-']}",
-            f"  parameters sharded over    : {self.sharded_parameters or ['-']}",
-            f"  activations sharded over   : {self.sharded_activations or ['-']}",
-            "  gradient reduction order   :",
-        ]
-        lines += [f"      {i}. {op} over {g!r}" for i, (op, g) in enumerate(self.gradient_reductions, start=1)]
-        lines.append(f"  metrics reduced over       : {self.metric_group!r}")
-        lines += [f"  note: {n}" for n in self.notes]
-        return "\n".join(lines)
+        width = max([len(s.operation) for s in self.steps] + [9])
+        out = [f"plan: {self.strategy}",
+               f"  weights   replicated over {', '.join(self.replicated_parameters) or 'nothing'}; "
+               f"split over {', '.join(self.sharded_parameters) or 'nothing'}",
+               f"  activations split over {', '.join(self.sharded_activations) or 'nothing'}",
+               f"  loss / metrics averaged over {self.metric_group}"]
+        for phase in ("forward", "backward", "optimizer", "metrics"):
+            rows = [s for s in self.steps if s.phase == phase]
+            if rows:
+                out.append(f"  {phase}:")
+                out += [f"    {s.operation:<{width}}  [{s.group}]  {s.implementation}" for s in rows]
+        out += [f"  * {n}" for n in self.notes]
+        return "\n".join(out)
 
 
 def build_model(config: ExperimentConfig, context: DistributedContext, *, device: torch.device | None = None) -> nn.Module:
@@ -117,55 +137,94 @@ def build_model(config: ExperimentConfig, context: DistributedContext, *, device
 
 
 def describe_parallel_plan(config: ExperimentConfig, context: DistributedContext) -> ParallelismDescription:
-    """Human-readable account of who holds what and which reductions run in which order."""
+    """Which rank holds what, and which collective (and which implementation of it) each step runs.
+
+    The implementations named are the ones this framework selects for ``config`` on this
+    context's device: in-kernel NVLink collectives (``ops/csrc/comm.cu``, the collective mode of
+    ``ops/csrc/gemm_tcgen05.cu``) on CUDA when their switches are on and the group has a
+    peer-mapped workspace, otherwise the process group's backend (NCCL on CUDA, Gloo on CPU).
+    """
     topo = context.topology
-    shard, replica, tensor = topo.size("shard"), topo.size("data_parallel"), topo.size("tensor")
-    labels = (["fsdp"] if shard > 1 else []) + (["ddp" if shard == 1 else "replicate"] if replica > 1 else [])
-    labels += (["tensor"] if tensor > 1 else []) + (["sequence"] if topo.sequence_parallel_enabled else [])
-    d = ParallelismDescription(strategy="+".join(labels) if labels else "single-process")
-    if tensor > 1:
-        d.sharded_parameters.append("tensor")
-        d.replicated_parameters.append("data_parallel")
+    dp, shard, tp = topo.size("data_parallel"), topo.size("shard"), topo.size("tensor")
+    sp = topo.sequence_parallel_enabled
+    independent = sp and config.topology.sequence_parallel_mode == "independent"
+    cuda = context.device.type == "cuda"
+    library = "NCCL" if cuda else "Gloo"
+    parts = [name for name, on in (("fsdp", shard > 1), ("hsdp-replicas" if shard > 1 else "ddp", dp > 1),
+                                   ("tp", tp > 1), ("context-parallel" if independent else "sp", sp)) if on]
+    plan = ParallelismDescription(strategy=" x ".join(parts) if parts else "single-process")
+    if tp > 1:
+        plan.sharded_parameters.append("tensor")
     if shard > 1:
-        d.sharded_parameters.append("shard")
-    if replica > 1 and "data_parallel" not in d.replicated_parameters:
-        d.replicated_parameters.append("data_parallel")
-    if topo.sequence_parallel_enabled:
-        d.sharded_activations.append(topo.sequence_group_name)
-    if tensor > 1:
-        d.gradient_reductions.append(("all-reduce of activation gradients (inside the layers, not of the weights)", "tensor"))
-    if shard > 1:
-        d.gradient_reductions.append(("reduce-scatter of flat gradients", "shard"))
-        if replica > 1:
-            d.gradient_reductions.append(("all-reduce of the sharded gradient", "data_parallel"))
-    elif replica > 1:
-        d.gradient_reductions.append(("bucketed all-reduce of gradients", "data_parallel"))
-    if topo.sequence_parallel_enabled and shard == 1:
-        d.gradient_reductions.append(("all-reduce of sequence-parallel partial gradients (norms, row biases)",
-                                      topo.sequence_group_name))
-    if tensor > 1:
-        d.notes.append("ranks in the same tensor group must receive identical input batches")
-    if shard > 1 and replica > 1:
-        d.notes.append("hybrid sharding: memory scales with 1/shard_size only; the replica dimension buys communication "
-                       "locality, not memory")
-    if shard > 1:
-        if config.fsdp.reshard_after_forward:
-            d.notes.append("reshard_after_forward=True: one extra all-gather per unit per step, in exchange for not holding "
-                           "the full parameters between forward and backward")
+        plan.sharded_parameters.append("shard")
+    if dp > 1:
+        plan.replicated_parameters.append("data_parallel")
+    if sp:
+        plan.sharded_activations.append(topo.sequence_group_name)
+    add = plan.steps.append
+
+    fused_tp = cuda and config.tensor_parallel.fused_collectives
+    if tp > 1:
+        add(PlanStep("forward", "vocab-parallel embedding partial rows", "tensor",
+                     f"{library} {'reduce-scatter' if sp else 'all-reduce'} after the masked gather kernel"))
+        if sp:
+            add(PlanStep("forward", "sequence all-gather into column-parallel GEMMs (fused QKV, gate/up)", "tensor",
+                         "all-gather inside the tcgen05 GEMM's operand loads" if fused_tp else f"{library} all-gather"))
+            add(PlanStep("forward", "row-parallel GEMM output to sequence shards", "tensor",
+                         "reduce-scatter in the tcgen05 GEMM epilogue" if fused_tp else f"{library} reduce-scatter"))
         else:
-            d.notes.append("reshard_after_forward=False: gathered parameters stay resident until backward, saving one "
-                           "all-gather per unit")
-        if config.fsdp.auto_wrap_min_num_params == 0:
-            d.notes.append("the whole module is one FSDP unit, so the transient all-gather buffer is the size of the entire "
-                           "model; set fsdp.auto_wrap_min_num_params to split it")
-    elif replica > 1:
-        d.notes.append(f"DDP bucket cap {config.ddp.bucket_cap_mb} MiB, async_reduction={config.ddp.async_reduction}, "
-                       f"fused_allreduce={config.ddp.fused_allreduce}")
+            add(PlanStep("forward", "row-parallel GEMM partial sums", "tensor", f"{library} all-reduce"))
+        add(PlanStep("forward", "vocab-parallel cross-entropy statistics (max, sum-exp, target logit)", "tensor",
+                     f"{library} all-reduce of 3 floats per token; no logits are gathered"))
+        add(PlanStep("backward", "column-parallel input gradients", "tensor",
+                     ("reduce-scatter in the data-gradient GEMM epilogue" if fused_tp else f"{library} reduce-scatter")
+                     if sp else f"{library} all-reduce"))
+    if independent:
+        ring = config.tensor_parallel.context_parallel_algorithm == "ring"
+        add(PlanStep("forward", "attention keys / values", topo.sequence_group_name,
+                     f"{library} send/recv ring with online-softmax merge" if ring else f"{library} all-gather"))
+    if shard > 1:
+        fused_fsdp = cuda and config.fsdp.fused_update
+        add(PlanStep("forward", "flat-parameter all-gather per unit", "shard",
+                     "peer copies of bf16 shards (copy engines, prefetching the next unit)" if fused_fsdp
+                     else f"{library} all-gather"))
+        if config.fsdp.reshard_after_forward:
+            add(PlanStep("backward", "flat-parameter re-gather per unit", "shard",
+                         "peer copies of bf16 shards" if fused_fsdp else f"{library} all-gather"))
+        add(PlanStep("backward", "flat-gradient reduce-scatter per unit", "shard",
+                     "one kernel: reduce-scatter over peer memory + 1/G + AdamW on the shard, when the step needs no "
+                     "global gradient norm or loss scaling; otherwise " + library if fused_fsdp else f"{library} reduce-scatter"))
+        if dp > 1:
+            add(PlanStep("backward", "sharded-gradient all-reduce across replicas", "data_parallel", f"{library} all-reduce"))
+    elif dp > 1:
+        add(PlanStep("backward", f"gradient buckets of {config.ddp.bucket_cap_mb:g} MiB, launched in bucket order",
+                     "data_parallel",
+                     "in-kernel NVLink all-reduce with 1/G folded in, on a high-priority stream overlapping the backward"
+                     if cuda and config.ddp.fused_allreduce else f"{library} all-reduce of pre-scaled buckets"))
+    if sp and not independent and shard == 1:
+        add(PlanStep("backward", "sequence-parallel partial gradients (norm weights, row biases)", "tensor",
+                     f"{library} all-reduce after the data-parallel buckets"))
+    if config.training.max_grad_norm > 0 or config.training.collect_metrics:
+        add(PlanStep("optimizer", "weighted squared gradient norm", "world",
+                     f"device-side sum of squares, {library} all-reduce of one scalar, no host read"))
+    add(PlanStep("metrics", "step loss", "dp_shard", f"{library} all-reduce of one scalar"))
+
+    for s in plan.steps:
+        if s.phase == "backward" and ("gradient" in s.operation) and s.group != "tensor":
+            plan.gradient_reductions.append((s.operation, s.group))
+    if tp > 1 or sp:
+        plan.notes.append("every rank of a tensor group must see the same token batch (the sampler slices by dp_shard only)")
+    if shard > 1 and dp > 1:
+        plan.notes.append(f"parameters and optimizer state are divided by shard={shard} only; the {dp} replicas each hold "
+                          "a full set of shards")
+    if shard > 1 and config.fsdp.auto_wrap_min_num_params == 0:
+        plan.notes.append("no auto-wrap threshold: the model is a single FSDP unit and its gathered copy is full size")
     if config.training.gradient_accumulation_steps > 1:
-        n = config.training.gradient_accumulation_steps
-        d.notes.append(f"{n} micro-batches per optimizer step: the first {n - 1} run inside no_sync(), so the step costs one "
-                       f"gradient reduction rather than {n}")
-    return d
+        plan.notes.append(f"{config.training.gradient_accumulation_steps} micro-batches per step: gradient collectives run "
+                          "after the last one only")
+    if config.training.cuda_graph and cuda:
+        plan.notes.append("the step (forward, backward, reductions, update) is replayed as one captured CUDA graph")
+    return plan
 
 
 def _unique_named_parameters(model: nn.Module) -> dict[str, nn.Parameter]:

@@ -114,3 +114,38 @@ def test_trace_ranges_are_inert_without_a_gpu_and_toggle() -> None:
     finally:
         set_tracing(False)
     assert not tracing_enabled()
+
+
+@pytest.mark.parametrize(("sizes", "mode", "expect_ops"), [
+    (dict(data_parallel_size=8), "disabled", {("backward", "data_parallel")}),
+    (dict(shard_parallel_size=2, data_parallel_size=2), "disabled", {("backward", "shard"), ("backward", "data_parallel")}),
+    (dict(data_parallel_size=2, tensor_parallel_size=4), "tensor_group", {("forward", "tensor"), ("backward", "tensor"),
+                                                                         ("backward", "data_parallel")}),
+])
+def test_parallel_plan_names_each_collective_and_its_implementation(sizes: dict, mode: str, expect_ops: set) -> None:
+    from types import SimpleNamespace
+
+    from hybrid_training.config import ExperimentConfig, TopologyConfig
+    from hybrid_training.distributed.topology import ParallelTopology
+    from hybrid_training.parallel import describe_parallel_plan
+
+    topo_cfg = TopologyConfig(sequence_parallel_mode=mode, **sizes)
+    cfg = ExperimentConfig(topology=topo_cfg)
+    world = 1
+    for v in sizes.values():
+        world *= v
+    for device, library in ((torch.device("cpu"), "Gloo"), (torch.device("cuda"), "NCCL")):
+        ctx = SimpleNamespace(topology=ParallelTopology(topo_cfg, world), device=device)
+        plan = describe_parallel_plan(cfg, ctx)
+        seen = {(s.phase, s.group) for s in plan.steps}
+        assert expect_ops <= seen, (expect_ops, seen)
+        text = plan.render()
+        assert plan.strategy in text and "metrics:" in text
+        for s in plan.steps:
+            assert s.implementation and s.operation in text
+        if device.type == "cpu":
+            assert all("kernel" not in s.implementation or library in s.implementation for s in plan.steps
+                       if s.group == "data_parallel"), "no in-kernel collective is claimed on CPU"
+        elif sizes.get("shard_parallel_size", 1) == 1 and "data_parallel_size" in sizes:
+            dp_step = next(s for s in plan.steps if s.group == "data_parallel")
+            assert "in-kernel NVLink" in dp_step.implementation
