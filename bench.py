@@ -144,16 +144,12 @@ def _emit(result: dict) -> None:
 
 
 def _baseline_value() -> float | None:
-    """BASELINE.md publishes no throughput for this config, so there is no ratio to report."""
+    """The reference publishes no throughput for any configuration, so there is no ratio to report."""
     return None
 
 
 def main() -> None:
     args = _args()
-    if args.impl == "reference" and args.config != "gpt2_ddp":
-        _emit({"impl": "reference", "unavailable": f"the reference has no Llama-style model (RMSNorm/RoPE/SwiGLU/GQA) for "
-                                                   f"--config {args.config}"})
-        return
     if args.impl == "reference":
         sys.path[:] = [p for p in sys.path if os.path.abspath(p or ".") != ROOT]
         sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
@@ -177,7 +173,7 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
     sampler = ClockSampler(_visible_gpu_indices(args.gpus)) if rank == 0 else None
     model_name, micro_batch, seq, accum = CONFIGS[args.config]
-    extra = {} if args.impl == "reference" else {"config": args.config, "grad_accum": accum}
+    extra = {"config": args.config, "grad_accum": accum}
     result = runner(steps=args.steps, warmup=args.warmup, micro_batch=micro_batch, seq=seq,
                     use_graph=not args.no_graph, clock_start=(sampler.start if sampler else None),
                     clock_stop=(sampler.stop if sampler else None), **extra)
@@ -211,7 +207,13 @@ def main() -> None:
             "gpu_launches": result.get("gpu_launches", 0),
             "exposed_comm_ms_per_step": result.get("exposed_comm_ms_per_step"),
             "final_loss": result.get("loss"),
+            "peak_memory_bytes": result.get("peak_memory_bytes"),
         }
+        for key in ("communication_per_step", "parameter_bytes", "master_parameter_bytes", "optimizer_state_bytes"):
+            if key in result:
+                out[key] = result[key]
+        if result.get("shape"):
+            out["config"]["reference_shape"] = result["shape"]
         if args.impl == "reference":
             out["impl"] = "reference"
             out.pop("gpu_launches")

@@ -67,7 +67,7 @@ def reduce_scatter_along_dim(tensor: torch.Tensor, group: GroupHandle, dim: int,
     dim %= tensor.dim()
     if tensor.shape[dim] % group.size:
         raise CollectiveError(format_error(
-            "autograd.reduce_scatter_along_dim", f"dimension {dim} must be divisible by the group size",
+            "autograd.reduce_scatter_along_dim", f"dimension {dim} has to split evenly over the group",
             rank=group.global_rank, expected=f"{tensor.shape[dim]} % {group.size} == 0",
             observed=tensor.shape[dim] % group.size, resolution="pad the dimension or choose a dividing parallel size"))
     moved = tensor.movedim(dim, 0).contiguous()

@@ -29,6 +29,7 @@ from .config import (
     TopologyConfig,
     TrainingConfig,
 )
+from .distributed.collectives import observe_collectives
 from .distributed.context import init_distributed
 from .training.data import Batch
 from .training.engine import TrainingEngine
@@ -145,7 +146,7 @@ def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool 
         config: str = "gpt2_ddp", grad_accum: int = 1) -> dict:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     cfg = experiment(world, micro_batch=micro_batch, seq=seq,
-                     samples=micro_batch * world * grad_accum * (2 * steps + warmup + 8), use_graph=use_graph,
+                     samples=micro_batch * world * grad_accum * (2 * steps + warmup + 9), use_graph=use_graph,
                      config=config, grad_accum=grad_accum)
     ctx = init_distributed(cfg)
     engine = TrainingEngine(cfg, ctx)
@@ -159,12 +160,21 @@ def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool 
     def take() -> list[Batch]:
         return [next(stream) for _ in range(grad_accum)]
 
+    comm: dict[str, dict[str, float]] = {}
     for i in range(warmup):
         b = take()
         if i == 0 and ctx.rank == 0 and os.environ.get("HT_COUNT_LAUNCHES", "1") != "0":
             launches_per_step = count_native_launches(lambda: step(b, True))
         else:
             step(b, True)
+    # One more untimed step, run eagerly with every collective counted (a replayed graph issues
+    # the same collectives without passing through Python).
+    graph = engine.graph_enabled
+    engine.graph_enabled = False
+    with observe_collectives() as rec:
+        step(take(), True)
+    engine.graph_enabled = graph
+    comm = {k: {"calls": v.calls, "bytes": v.bytes} for k, v in sorted(rec.by_operation.items())}
     # device-resident batches for the device-timed loop
     dev_batches = [[mb.to(dev) for mb in take()] for _ in range(steps)]
     host_batches = [take() for _ in range(steps)]
@@ -189,9 +199,27 @@ def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool 
     h2d = sum(mb.inputs.numel() * mb.inputs.element_size() + mb.targets.numel() * mb.targets.element_size()
               for mb in host_batches[0])
     replicas = cfg.topology.data_parallel_size * cfg.topology.shard_parallel_size
+    memory = _memory_record(engine, dev)
     engine.close()
     ctx.shutdown()
     return {"device_ms": device_ms, "e2e_ms": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
             "gpu_launches": launches_per_step * steps, "clocks": clocks, "loss": losses[-1] if losses else None,
             "exposed_comm_ms_per_step": exposed, "tokens_per_step": micro_batch * seq * grad_accum * replicas,
-            "parallelism": cfg.topology.describe() if hasattr(cfg.topology, "describe") else None}
+            "parallelism": cfg.topology.describe() if hasattr(cfg.topology, "describe") else None,
+            "communication_per_step": comm, **memory}
+
+
+def _memory_record(engine: TrainingEngine, device: torch.device) -> dict[str, int]:
+    """Parameter, optimizer-state and peak device bytes of this rank (the benchmark sweep's memory columns)."""
+    params = {id(p): p for p in engine.model.parameters()}
+    inner = engine.optimizer.inner
+    opt_bytes = 0
+    for st in getattr(inner, "state", {}).values():
+        for v in st.values():
+            if torch.is_tensor(v):
+                opt_bytes += v.numel() * v.element_size()
+    flat = getattr(inner, "flat_parameters", None)
+    master = flat.numel() * flat.element_size() if torch.is_tensor(flat) else 0
+    return {"parameter_bytes": sum(p.numel() * p.element_size() for p in params.values()),
+            "master_parameter_bytes": master, "optimizer_state_bytes": opt_bytes,
+            "peak_memory_bytes": int(torch.cuda.max_memory_allocated(device))}

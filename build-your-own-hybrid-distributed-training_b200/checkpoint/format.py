@@ -44,8 +44,8 @@ _STAGING_PREFIX = ".staging-"
 
 def checkpoint_directory_name(step: int) -> str:
     if step < 0:
-        raise CheckpointError(format_error("checkpoint.directory_name", "step must be non-negative", expected=">= 0",
-                                           observed=step, resolution="pass the current optimizer step"))
+        raise CheckpointError(format_error("checkpoint.directory_name", "checkpoint steps start at 0", expected=">= 0",
+                                           observed=step, resolution="give the optimizer step the checkpoint belongs to"))
     return f"checkpoint-step-{step:06d}"
 
 
@@ -60,7 +60,7 @@ def staging_directory_name(final_name: str, token: str) -> str:
 
 def shard_filename(rank: int) -> str:
     if rank < 0:
-        raise CheckpointError(format_error("checkpoint.shard_filename", "rank must be non-negative", expected=">= 0",
+        raise CheckpointError(format_error("checkpoint.shard_filename", "a global rank cannot be negative", expected=">= 0",
                                            observed=rank, resolution="pass a global rank"))
     return f"rank-{rank:05d}.pt"
 
@@ -70,7 +70,7 @@ def validate_shard_filename(name: str) -> str:
         raise CheckpointError(format_error(
             "checkpoint.validate_shard_filename", "the manifest names a file outside the shard naming rule; refusing it, "
             "because a manifest must never point the reader at an arbitrary path", expected="rank-NNNNN.pt", observed=name,
-            resolution="the checkpoint directory has been tampered with or corrupted"))
+            resolution="the manifest was edited by hand or damaged; do not load it"))
     return name
 
 
@@ -80,9 +80,9 @@ def resolve_inside(root: Path, name: str) -> Path:
     try:
         candidate.relative_to(base)
     except ValueError as exc:
-        raise CheckpointError(format_error("checkpoint.resolve_inside", "the resolved path escapes the checkpoint directory",
+        raise CheckpointError(format_error("checkpoint.resolve_inside", "after resolving links the file lies outside the checkpoint directory",
                                            expected=f"a path under {base}", observed=str(candidate),
-                                           resolution="remove the symlink or path component that redirects outside")) from exc
+                                           resolution="keep every payload file inside the checkpoint directory (no links pointing out)")) from exc
     return candidate
 
 
@@ -94,14 +94,14 @@ def file_digest(path: Path, *, chunk_size: int = 1 << 22) -> str:
             for chunk in iter(lambda: f.read(chunk_size), b""):
                 h.update(chunk)
     except OSError as exc:
-        raise CheckpointError(format_error("checkpoint.file_digest", "could not read a checkpoint file", expected="a readable file",
+        raise CheckpointError(format_error("checkpoint.file_digest", "reading a checkpoint file failed", expected="a readable file",
                                            observed=f"{path}: {exc}", resolution="check permissions and that the file exists")) from exc
     return h.hexdigest()
 
 
 def validate_format_version(version: str) -> str:
     if version not in SUPPORTED_FORMAT_VERSIONS:
-        raise CheckpointVersionError(format_error("checkpoint.validate_format_version", "unsupported checkpoint format version",
+        raise CheckpointVersionError(format_error("checkpoint.validate_format_version", "this reader does not know the checkpoint's format version",
                                                   expected=sorted(SUPPORTED_FORMAT_VERSIONS), observed=version,
                                                   resolution="use the package version that wrote the checkpoint"))
     return version

@@ -35,9 +35,9 @@ class ShardRecord:
 
     def __post_init__(self) -> None:
         if self.offset < 0 or self.length < 0:
-            raise CheckpointError(format_error("manifest.ShardRecord", "offset and length must be non-negative",
-                                               expected="offset >= 0 and length >= 0",
-                                               observed=f"offset={self.offset}, length={self.length}", resolution="the manifest is malformed"))
+            raise CheckpointError(format_error("manifest.ShardRecord", "a shard record has a negative offset or length",
+                                               expected="non-negative offset and length",
+                                               observed=f"offset={self.offset}, length={self.length}", resolution="manifest.json has an unexpected structure"))
         validate_shard_filename(self.file)
 
     @property
@@ -88,19 +88,19 @@ class TensorRecord:
             if s.offset + s.length > self.numel:
                 raise CheckpointCorruptionError(format_error("manifest.TensorRecord.validate", f"a shard of {self.key!r} runs past the end",
                                                              expected=f"offset + length <= {self.numel}", observed=s.offset + s.length,
-                                                             resolution="the manifest disagrees with the recorded global shape"))
+                                                             resolution="the numel in the manifest does not match the product of the shape"))
         total = sum(s.length for s in self.shards)
         covered = self.covered_elements()
         if total != covered:
             raise CheckpointCorruptionError(format_error("manifest.TensorRecord.validate",
-                                                         f"the shards of {self.key!r} overlap, so two files claim the same elements",
-                                                         expected=f"{covered} elements across non-overlapping shards", observed=total,
-                                                         resolution="the checkpoint was written by a buggy or mixed-version writer"))
+                                                         f"the shards of {self.key!r} intersect: the same elements would be read from two places",
+                                                         expected=f"{covered} elements, each in exactly one shard", observed=total,
+                                                         resolution="a writer recorded an inconsistent layout; treat this checkpoint as unusable"))
         if covered != self.numel:
             raise IncompleteCheckpointError(format_error("manifest.TensorRecord.validate",
-                                                         f"the shards of {self.key!r} do not cover the whole tensor",
+                                                         f"the shards of {self.key!r} leave elements of the tensor with no shard",
                                                          expected=f"{self.numel} elements", observed=covered,
-                                                         resolution="a shard file is missing; the checkpoint is unusable"))
+                                                         resolution="the shards do not add up to the tensor, so it cannot be rebuilt"))
 
     def shards_overlapping(self, wanted: ShardRange) -> list[tuple[ShardRecord, ShardRange]]:
         out = []
@@ -159,7 +159,7 @@ class CheckpointManifest:
             return
         if existing.global_shape != record.global_shape or existing.dtype != record.dtype:
             raise CheckpointCorruptionError(format_error(
-                "manifest.add_shard", f"two ranks describe tensor {record.key!r} differently",
+                "manifest.add_shard", f"the records of two ranks disagree about tensor {record.key!r} differently",
                 expected=f"shape={existing.global_shape}, dtype={existing.dtype}",
                 observed=f"shape={record.global_shape}, dtype={record.dtype}",
                 resolution="every rank must build the model from the same configuration"))
@@ -170,7 +170,7 @@ class CheckpointManifest:
         if not self.complete:
             raise IncompleteCheckpointError(format_error("manifest.validate", "the manifest is not marked complete; the writer did not finish",
                                                          expected=True, observed=self.complete,
-                                                         resolution="discard this checkpoint and resume from an earlier one"))
+                                                         resolution="use an older checkpoint"))
         for record in self.tensors.values():
             record.validate()
             for s in record.shards:
@@ -178,7 +178,7 @@ class CheckpointManifest:
                     raise IncompleteCheckpointError(format_error("manifest.validate",
                                                                  f"tensor {record.key!r} references file {s.file!r} without an integrity record",
                                                                  expected=sorted(self.files), observed=s.file,
-                                                                 resolution="the manifest is truncated or hand-edited"))
+                                                                 resolution="manifest.json is incomplete or was edited"))
 
     def referenced_files(self) -> set[str]:
         return {s.file for r in self.tensors.values() for s in r.shards}
@@ -207,22 +207,22 @@ class CheckpointManifest:
                        {k: FileRecord.from_dict(v) for k, v in d.get("files", {}).items()}, bool(d.get("complete", False)),
                        str(d.get("created_by", "")))
         except (KeyError, TypeError, ValueError) as exc:
-            raise CheckpointError(format_error("manifest.from_dict", "the manifest is malformed", expected="a manifest written by this format",
-                                               observed=repr(exc), resolution="the file is not a valid checkpoint manifest")) from exc
+            raise CheckpointError(format_error("manifest.from_dict", "manifest.json has an unexpected structure", expected="a manifest written by this format",
+                                               observed=repr(exc), resolution="manifest.json lacks fields that every manifest has")) from exc
 
     @classmethod
     def read(cls, path: Path) -> CheckpointManifest:
         if not path.is_file():
             raise IncompleteCheckpointError(format_error("manifest.read", "no manifest found; it is written last, so the checkpoint "
                                                          "was never completed", expected=str(path), observed="missing",
-                                                         resolution="resume from an earlier checkpoint"))
+                                                         resolution="use an older checkpoint"))
         try:
             payload = json.loads(path.read_text(encoding="utf-8"))
         except json.JSONDecodeError as exc:
-            raise CheckpointError(format_error("manifest.read", "the manifest is not valid JSON", expected="a JSON object",
+            raise CheckpointError(format_error("manifest.read", "manifest.json cannot be parsed as JSON", expected="a JSON object",
                                                observed=str(exc), resolution="the file is corrupt")) from exc
         if not isinstance(payload, dict):
-            raise CheckpointError(format_error("manifest.read", "the manifest is not a JSON object", expected="object",
+            raise CheckpointError(format_error("manifest.read", "manifest.json does not hold a JSON object at the top level", expected="object",
                                                observed=type(payload).__name__, resolution="the file is corrupt"))
         return cls.from_dict(payload)
 

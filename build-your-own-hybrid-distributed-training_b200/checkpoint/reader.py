@@ -65,15 +65,15 @@ class LoadedCheckpoint:
 def read_metadata(directory: str | Path) -> dict[str, Any]:
     path = Path(directory) / METADATA_FILENAME
     if not path.is_file():
-        raise IncompleteCheckpointError(format_error("checkpoint.read_metadata", "metadata.json is missing", expected=str(path),
-                                                     observed="absent", resolution="the checkpoint is incomplete"))
+        raise IncompleteCheckpointError(format_error("checkpoint.read_metadata", "there is no metadata.json in the checkpoint directory", expected=str(path),
+                                                     observed="absent", resolution="some data of the checkpoint is absent"))
     try:
         data = json.loads(path.read_text(encoding="utf-8"))
     except json.JSONDecodeError as exc:
-        raise CheckpointError(format_error("checkpoint.read_metadata", "metadata.json is not valid JSON", expected="a JSON object",
+        raise CheckpointError(format_error("checkpoint.read_metadata", "metadata.json cannot be parsed as JSON", expected="a JSON object",
                                            observed=str(exc), resolution="the file is corrupt")) from exc
     if not isinstance(data, dict):
-        raise CheckpointError(format_error("checkpoint.read_metadata", "metadata.json is not a JSON object", expected="object",
+        raise CheckpointError(format_error("checkpoint.read_metadata", "metadata.json does not hold a JSON object", expected="object",
                                            observed=type(data).__name__, resolution="the file is corrupt"))
     return data
 
@@ -119,22 +119,22 @@ def _validate_topology_transition(manifest: CheckpointManifest, context: Distrib
         raise CheckpointTopologyError(format_error(
             "checkpoint.load", "the standalone sequence-parallel width differs from the checkpoint's", rank=context.rank,
             world_size=context.world_size, expected=f"sequence_parallel_size == {saved_s}", observed=now_s,
-            resolution="resume with the original sequence-parallel size"))
+            resolution="restart with the sequence-parallel width the checkpoint was written at"))
 
 
 def _check_shape(record: Any, shape: tuple[int, ...], key: str, context: DistributedContext) -> None:
     if tuple(record.global_shape) != tuple(shape):
-        raise CheckpointError(format_error("checkpoint.load", f"tensor {key!r} has a different shape in the checkpoint",
+        raise CheckpointError(format_error("checkpoint.load", f"tensor {key!r} was saved with another shape",
                                            rank=context.rank, world_size=context.world_size, expected=tuple(shape),
                                            observed=tuple(record.global_shape),
-                                           resolution="resume with the model definition that produced the checkpoint"))
+                                           resolution="build the same model that was saved"))
 
 
 def _missing(key: str, manifest: CheckpointManifest, context: DistributedContext) -> str:
     avail = sorted(manifest.tensors_by_category("model"))
-    return format_error("checkpoint.load", f"the checkpoint does not contain tensor {key!r} that the model needs", rank=context.rank,
+    return format_error("checkpoint.load", f"no record in the checkpoint for tensor {key!r} that the model needs", rank=context.rank,
                         world_size=context.world_size, expected=key, observed=avail[:8] + (["..."] if len(avail) > 8 else []),
-                        resolution="resume with the model definition that produced the checkpoint, or pass strict=False")
+                        resolution="build the same model that was saved, or load with strict=False to skip absent tensors")
 
 
 def load_checkpoint(directory: str | Path, *, model: HybridModel, context: DistributedContext,
@@ -166,7 +166,7 @@ def load_checkpoint(directory: str | Path, *, model: HybridModel, context: Distr
     result = LoadedCheckpoint(path, manifest, metadata, state, dict(metadata.get("scheduler", {})), dict(metadata.get("scaler", {})),
                               time.perf_counter() - start, loaded, cache.loaded_files, rng)
     cache.clear()
-    _LOG.info("resumed from %s at step %d", path.name, state.step)
+    _LOG.info("loaded checkpoint %s (step %d)", path.name, state.step)
     return result
 
 
@@ -222,7 +222,7 @@ def _load_optimizer_state(model: HybridModel, optimizer: ShardedOptimizer, manif
     scalars = dict(metadata.get("optimizer_scalars", {}))
     names = {r.state_name for r in manifest.tensors_by_category("optimizer").values()} - {""}
     if not names and not scalars:
-        _LOG.warning("checkpoint holds no optimizer state; the optimizer starts fresh")
+        _LOG.warning("no optimizer state saved in this checkpoint: moments start at zero")
         return
     rebuilt: dict[int, dict[str, Any]] = {}
     for index, param in enumerate(optimizer.parameters):
@@ -244,8 +244,8 @@ def _load_optimizer_state(model: HybridModel, optimizer: ShardedOptimizer, manif
             elif strict:
                 raise IncompleteCheckpointError(format_error("checkpoint.load_optimizer", f"optimizer state {state_name!r} is missing "
                                                              f"for parameter {index}", rank=context.rank, world_size=context.world_size,
-                                                             expected=f"state entries for parameter {index}", observed="none",
-                                                             resolution="the checkpoint was written with save_optimizer=False"))
+                                                             expected=f"saved optimizer state for parameter {index}", observed="none",
+                                                             resolution="the save skipped optimizer state (save_optimizer=False)"))
         for name, value in scalars.items():
             entry[name] = torch.tensor(value) if isinstance(value, (int, float)) else value
         if entry:

@@ -28,22 +28,22 @@ def _check_file(directory: Path, manifest: CheckpointManifest, name: str, *, ver
     validate_shard_filename(name)
     path = resolve_inside(directory, name)
     if not path.is_file():
-        raise IncompleteCheckpointError(format_error(where, "a shard file listed in the manifest is missing", expected=name,
+        raise IncompleteCheckpointError(format_error(where, "a payload file named by the manifest is not on disk", expected=name,
                                                      observed="absent", resolution="restore the file or resume from an earlier checkpoint"))
     record = manifest.files.get(name)
     if record is None:
-        raise CheckpointCorruptionError(format_error(where, "the file has no integrity record in the manifest",
-                                                     expected="an entry under manifest['files']", observed=name,
-                                                     resolution="the manifest is truncated or hand-edited"))
+        raise CheckpointCorruptionError(format_error(where, "the manifest has no size/checksum entry for this file",
+                                                     expected="a record in the manifest's files table", observed=name,
+                                                     resolution="manifest.json is incomplete or was edited"))
     size = path.stat().st_size
     if size != record.bytes:
         raise CheckpointCorruptionError(format_error(where, f"shard file {name!r} has the wrong size (truncated or overwritten)",
                                                      expected=f"{record.bytes} bytes", observed=f"{size} bytes",
-                                                     resolution="restore the file from a backup or discard the checkpoint"))
+                                                     resolution="put the original file back, or use an older checkpoint"))
     if verify:
         digest = file_digest(path)
         if digest != record.sha256:
-            raise CheckpointCorruptionError(format_error(where, f"shard file {name!r} failed checksum verification",
+            raise CheckpointCorruptionError(format_error(where, f"shard file {name!r} has a SHA-256 that differs from the manifest",
                                                          expected=record.sha256, observed=digest,
                                                          resolution="the file is corrupt; restore it or discard the checkpoint"))
     return path
@@ -61,8 +61,8 @@ class ShardFileCache:
         try:
             payload = torch.load(path, map_location="cpu", weights_only=True)
         except Exception as exc:
-            raise CheckpointCorruptionError(format_error("reshard.ShardFileCache.get", f"shard file {filename!r} could not be deserialised",
-                                                         expected="a tensor mapping saved with torch.save", observed=repr(exc),
+            raise CheckpointCorruptionError(format_error("reshard.ShardFileCache.get", f"shard file {filename!r} could not be loaded with torch.load",
+                                                         expected="a dict of tensors written by torch.save", observed=repr(exc),
                                                          resolution="the file is corrupt or not a tensor payload")) from exc
         if not isinstance(payload, dict):
             raise CheckpointCorruptionError(format_error("reshard.ShardFileCache.get", f"shard file {filename!r} does not hold a mapping",
@@ -84,27 +84,27 @@ def read_tensor_range(record: TensorRecord, wanted: ShardRange, cache: ShardFile
     if wanted.length == 0:
         return torch.empty(0, dtype=dtype or torch.float32)
     if wanted.end > record.numel:
-        raise CheckpointError(format_error("reshard.read_tensor_range", f"the requested range of {record.key!r} runs past the end",
+        raise CheckpointError(format_error("reshard.read_tensor_range", f"the wanted interval of {record.key!r} runs past the end",
                                            expected=f"end <= {record.numel}", observed=wanted.end,
-                                           resolution="resume with the model definition that produced the checkpoint"))
+                                           resolution="build the same model that was saved"))
     pieces = record.shards_overlapping(wanted)
     if not pieces:
         raise IncompleteCheckpointError(format_error("reshard.read_tensor_range", f"no shard of {record.key!r} covers the range",
-                                                     expected=f"a shard intersecting [{wanted.start}, {wanted.end})",
+                                                     expected=f"a shard overlapping [{wanted.start}, {wanted.end})",
                                                      observed=[(s.offset, s.length) for s in record.shards],
-                                                     resolution="the checkpoint is incomplete"))
+                                                     resolution="some data of the checkpoint is absent"))
     out: torch.Tensor | None = None
     cursor, filled = wanted.start, 0
     for shard, overlap in pieces:
         if overlap.start != cursor:
-            raise IncompleteCheckpointError(format_error("reshard.read_tensor_range", f"a gap exists in the shards of {record.key!r}",
-                                                         expected=f"a shard starting at element {cursor}",
-                                                         observed=f"next shard starts at {overlap.start}",
-                                                         resolution="a shard file is missing from the checkpoint"))
+            raise IncompleteCheckpointError(format_error("reshard.read_tensor_range", f"no shard covers part of {record.key!r}",
+                                                         expected=f"a shard beginning at element {cursor}",
+                                                         observed=f"the following shard begins at {overlap.start}",
+                                                         resolution="a payload file is absent or lost entries"))
         payload = cache.get(shard.file)
         stored = payload.get(shard.key)
         if stored is None:
-            raise CheckpointCorruptionError(format_error("reshard.read_tensor_range", f"{shard.file!r} does not contain key {shard.key!r}",
+            raise CheckpointCorruptionError(format_error("reshard.read_tensor_range", f"{shard.file!r} has no entry {shard.key!r}",
                                                          expected=shard.key, observed=sorted(payload)[:8],
                                                          resolution="the manifest and payload disagree; the checkpoint is corrupt"))
         flat = stored.reshape(-1)
@@ -122,7 +122,7 @@ def read_tensor_range(record: TensorRecord, wanted: ShardRange, cache: ShardFile
     if filled != wanted.length:
         raise IncompleteCheckpointError(format_error("reshard.read_tensor_range", f"the shards of {record.key!r} cover only part of the range",
                                                      expected=wanted.length, observed=filled,
-                                                     resolution="a shard file is missing from the checkpoint"))
+                                                     resolution="a payload file is absent or lost entries"))
     return out
 
 
@@ -140,7 +140,7 @@ def describe_reshard(manifest: CheckpointManifest, key: str, wanted: ShardRange)
     record = manifest.tensors.get(key)
     if record is None:
         raise CheckpointError(format_error("reshard.describe_reshard", "unknown tensor key", expected=sorted(manifest.tensors)[:8],
-                                           observed=key, resolution="check the key against the manifest"))
+                                           observed=key, resolution="compare the storage key with the manifest"))
     return {"key": key, "global_shape": list(record.global_shape), "wanted": [wanted.start, wanted.length],
             "sources": [{"file": s.file, "saved_rank": s.rank, "shard_range": [s.offset, s.length],
                          "overlap": [o.start, o.length]} for s, o in record.shards_overlapping(wanted)]}

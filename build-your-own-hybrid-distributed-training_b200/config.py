@@ -74,7 +74,7 @@ def resolve_dtype(name: str | torch.dtype) -> torch.dtype:
                 "unknown dtype name",
                 expected=sorted(_DTYPE_NAMES),
                 observed=name,
-                resolution="use one of the listed dtype names",
+                resolution="spell the dtype as one of the expected names",
             )
         )
     return _DTYPE_NAMES[key]
@@ -120,10 +120,10 @@ class TopologyConfig:
         for name in _DIM_FIELDS:
             value = getattr(self, name)
             ok = isinstance(value, int) and not isinstance(value, bool) and value >= 1
-            _check(ok, where, f"{name} must be a positive integer", ">= 1", value, f"set {name} to a positive integer", TopologyError)
+            _check(ok, where, f"{name} has to be an integer of at least 1", ">= 1", value, f"set {name} to an integer of at least 1", TopologyError)
         mode = self.sequence_parallel_mode
-        _check(mode in SequenceParallelMode.ALL, where, "unknown sequence_parallel_mode", list(SequenceParallelMode.ALL), mode,
-               "choose one of the listed modes", TopologyError)
+        _check(mode in SequenceParallelMode.ALL, where, "sequence_parallel_mode is not a recognised value", list(SequenceParallelMode.ALL), mode,
+               "pick a mode from the expected list", TopologyError)
         if mode != SequenceParallelMode.INDEPENDENT:
             _check(self.sequence_parallel_size == 1, where,
                    "sequence_parallel_size > 1 requires mode 'independent'; 'tensor_group' mode reuses the tensor ranks",
@@ -133,7 +133,7 @@ class TopologyConfig:
             _check(self.tensor_parallel_size > 1, where,
                    "sequence_parallel_mode='tensor_group' splits the sequence over the tensor group, which has one member",
                    "tensor_parallel_size > 1", self.tensor_parallel_size,
-                   "raise tensor_parallel_size or disable sequence parallelism", TopologyError)
+                   "sequence parallelism in tensor_group mode needs tensor_parallel_size above 1, or switch it off", TopologyError)
 
     @property
     def world_size(self) -> int:
@@ -175,8 +175,8 @@ class TopologyConfig:
         remainder = world_size // product
         resolved = dict(overrides)
         if remainder != 1:
-            _check(bool(missing), where, "all four dimensions were given but their product is smaller than the world size",
-                   world_size, product, "increase one dimension or launch fewer processes", TopologyError)
+            _check(bool(missing), where, "the four grid sizes multiply to fewer ranks than were launched",
+                   world_size, product, "grow a grid dimension or start fewer ranks", TopologyError)
             resolved[missing[0]] = remainder
             missing = missing[1:]
         for name in missing:
@@ -200,10 +200,10 @@ class DDPConfig:
     fused_allreduce: bool = True
 
     def __post_init__(self) -> None:
-        _check(self.bucket_cap_mb > 0, "config.DDPConfig", "bucket_cap_mb must be positive", "> 0", self.bucket_cap_mb,
-               "use a positive bucket size, e.g. 25.0")
-        _check(self.source_rank_in_group >= 0, "config.DDPConfig", "source_rank_in_group must be non-negative", ">= 0",
-               self.source_rank_in_group, "use a group-local rank index")
+        _check(self.bucket_cap_mb > 0, "config.DDPConfig", "the DDP bucket size (bucket_cap_mb) has to be greater than zero", "> 0", self.bucket_cap_mb,
+               "set a bucket size in MiB above zero (25 is the usual choice)")
+        _check(self.source_rank_in_group >= 0, "config.DDPConfig", "source_rank_in_group cannot be negative", ">= 0",
+               self.source_rank_in_group, "give the index of the source within the data-parallel group")
 
 
 @dataclass(frozen=True)
@@ -221,10 +221,10 @@ class FSDPConfig:
     fused_update: bool = True
 
     def __post_init__(self) -> None:
-        _check(self.auto_wrap_min_num_params >= 0, "config.FSDPConfig", "auto_wrap_min_num_params must be non-negative",
-               ">= 0", self.auto_wrap_min_num_params, "use 0 to disable automatic wrapping")
-        _check(self.limit_all_gather_bytes >= 0, "config.FSDPConfig", "limit_all_gather_bytes must be non-negative",
-               ">= 0", self.limit_all_gather_bytes, "use 0 to disable the guard rail")
+        _check(self.auto_wrap_min_num_params >= 0, "config.FSDPConfig", "auto_wrap_min_num_params cannot be negative",
+               ">= 0", self.auto_wrap_min_num_params, "0 turns automatic unit wrapping off")
+        _check(self.limit_all_gather_bytes >= 0, "config.FSDPConfig", "limit_all_gather_bytes cannot be negative",
+               ">= 0", self.limit_all_gather_bytes, "0 turns the all-gather size limit off")
         _check(self.use_padding, "config.FSDPConfig",
                "use_padding=False is not supported: unpadded shards differ in size across ranks, which breaks the "
                "single-buffer all-gather / reduce-scatter", True, False, "leave use_padding at True")
@@ -242,8 +242,8 @@ class TensorParallelConfig:
     context_parallel_algorithm: str = "all_gather"
 
     def __post_init__(self) -> None:
-        _check(self.init_method_std > 0, "config.TensorParallelConfig", "init_method_std must be positive", "> 0",
-               self.init_method_std, "use a small positive value such as 0.02")
+        _check(self.init_method_std > 0, "config.TensorParallelConfig", "init_method_std has to be greater than zero", "> 0",
+               self.init_method_std, "a standard deviation like 0.02 works for transformer weights")
         _check(self.context_parallel_algorithm in ("all_gather", "ring"), "config.TensorParallelConfig",
                "unknown context_parallel_algorithm (attention under sequence_parallel_mode='independent')",
                ["all_gather", "ring"], self.context_parallel_algorithm,
@@ -263,10 +263,10 @@ class GradScalerConfig:
 
     def __post_init__(self) -> None:
         where = "config.GradScalerConfig"
-        _check(self.init_scale > 0, where, "init_scale must be positive", "> 0", self.init_scale, "use a power of two such as 65536")
-        _check(self.growth_factor > 1.0, where, "growth_factor must exceed 1", "> 1.0", self.growth_factor, "use 2.0")
-        _check(0.0 < self.backoff_factor < 1.0, where, "backoff_factor must lie in (0, 1)", "0 < x < 1", self.backoff_factor, "use 0.5")
-        _check(self.growth_interval >= 1, where, "growth_interval must be at least 1", ">= 1", self.growth_interval, "use 2000")
+        _check(self.init_scale > 0, where, "the initial loss scale has to be greater than zero", "> 0", self.init_scale, "powers of two (65536 by default) keep the scaling exact")
+        _check(self.growth_factor > 1.0, where, "the scale growth factor has to be above 1", "> 1.0", self.growth_factor, "use 2.0")
+        _check(0.0 < self.backoff_factor < 1.0, where, "the scale backoff factor has to be strictly between 0 and 1", "0 < x < 1", self.backoff_factor, "use 0.5")
+        _check(self.growth_interval >= 1, where, "growth_interval counts clean steps and has to be 1 or more", ">= 1", self.growth_interval, "use 2000")
 
 
 @dataclass(frozen=True)
@@ -285,8 +285,8 @@ class MixedPrecisionConfig:
             resolve_dtype(getattr(self, name))
         if self.enabled and self.scaler.enabled:
             _check(resolve_dtype(self.param_dtype) is torch.float16, "config.MixedPrecisionConfig",
-                   "dynamic loss scaling is only meaningful for float16 compute", "param_dtype=float16 when scaler.enabled",
-                   self.param_dtype, "set param_dtype=float16 or scaler.enabled=false")
+                   "loss scaling exists for float16 gradients, which underflow; bfloat16 and float32 do not need it", "scaler.enabled only together with param_dtype=float16",
+                   self.param_dtype, "either compute in float16 or turn the scaler off")
 
     @property
     def compute_dtype(self) -> torch.dtype:
@@ -334,7 +334,7 @@ class ModelConfig:
     def __post_init__(self) -> None:
         where = "config.ModelConfig"
         _check(self.kind in ("mlp", "transformer"), where, "unknown model kind", ["mlp", "transformer"], self.kind,
-               "use 'mlp' or 'transformer'")
+               "the model kinds are 'mlp' and 'transformer'")
         _check(self.activation in _ACTIVATIONS, where, "unknown activation", list(_ACTIVATIONS), self.activation,
                "use 'gelu', 'relu' or 'swiglu'")
         _check(self.norm in ("layernorm", "rmsnorm"), where, "unknown norm", ["layernorm", "rmsnorm"], self.norm,
@@ -343,13 +343,13 @@ class ModelConfig:
                self.position_embedding, "use 'learned' or 'rope'")
         for name in ("hidden_size", "num_layers", "vocab_size", "num_heads", "max_sequence_length", "input_size", "output_size"):
             _check(getattr(self, name) >= 1, where, f"{name} must be positive", ">= 1", getattr(self, name),
-                   f"set {name} to a positive integer")
+                   f"set {name} to an integer of at least 1")
         if self.kind == "transformer":
-            _check(self.hidden_size % self.num_heads == 0, where, "hidden_size must be divisible by num_heads",
+            _check(self.hidden_size % self.num_heads == 0, where, "hidden_size has to split evenly into num_heads heads",
                    f"hidden_size % {self.num_heads} == 0", self.hidden_size, "pick a multiple of num_heads")
             _check(self.num_heads % self.resolved_num_kv_heads == 0, where, "num_heads must be a multiple of num_kv_heads",
                    f"num_heads % {self.resolved_num_kv_heads} == 0", self.num_heads, "pick num_kv_heads dividing num_heads")
-        _check(0.0 <= self.dropout < 1.0, where, "dropout must lie in [0, 1)", "0 <= p < 1", self.dropout, "use 0.0")
+        _check(0.0 <= self.dropout < 1.0, where, "dropout is a probability in [0, 1)", "0 <= p < 1", self.dropout, "use 0.0")
         _check(self.num_kv_heads >= 0, where, "num_kv_heads must be non-negative", ">= 0", self.num_kv_heads,
                "use 0 for multi-head attention")
 
@@ -408,9 +408,9 @@ class DataConfig:
     def __post_init__(self) -> None:
         for name in ("micro_batch_size", "sequence_length", "num_train_samples"):
             _check(getattr(self, name) >= 1, "config.DataConfig", f"{name} must be positive", ">= 1", getattr(self, name),
-                   f"set {name} to a positive integer")
-        _check(self.num_eval_samples >= 0, "config.DataConfig", "num_eval_samples must be non-negative", ">= 0",
-               self.num_eval_samples, "use 0 to disable evaluation")
+                   f"set {name} to an integer of at least 1")
+        _check(self.num_eval_samples >= 0, "config.DataConfig", "num_eval_samples cannot be negative", ">= 0",
+               self.num_eval_samples, "0 switches evaluation off")
         _check(self.token_distribution in ("recurrence", "uniform"), "config.DataConfig", "unknown token distribution",
                ["recurrence", "uniform"], self.token_distribution, "use 'recurrence' or 'uniform'")
 
@@ -429,11 +429,11 @@ class OptimizerConfig:
 
     def __post_init__(self) -> None:
         where = "config.OptimizerConfig"
-        _check(self.name in ("adamw", "sgd"), where, "unknown optimizer", ["adamw", "sgd"], self.name, "use 'adamw' or 'sgd'")
-        _check(self.learning_rate > 0, where, "learning_rate must be positive", "> 0", self.learning_rate, "use a positive learning rate")
+        _check(self.name in ("adamw", "sgd"), where, "unknown optimizer", ["adamw", "sgd"], self.name, "the optimizers available are 'adamw' and 'sgd'")
+        _check(self.learning_rate > 0, where, "the learning rate has to be greater than zero", "> 0", self.learning_rate, "set learning_rate above zero")
         betas = tuple(self.betas)
-        _check(len(betas) == 2 and all(0.0 <= b < 1.0 for b in betas), where, "betas must be two values in [0, 1)",
-               "(b1, b2) with 0 <= b < 1", self.betas, "use (0.9, 0.999)")
+        _check(len(betas) == 2 and all(0.0 <= b < 1.0 for b in betas), where, "betas has to be a pair of decay rates, each in [0, 1)",
+               "two floats b1, b2 in [0, 1)", self.betas, "use (0.9, 0.999)")
         object.__setattr__(self, "betas", betas)
 
 
@@ -448,9 +448,9 @@ class SchedulerConfig:
     def __post_init__(self) -> None:
         where = "config.SchedulerConfig"
         _check(self.name in ("constant", "linear", "cosine"), where, "unknown schedule", ["constant", "linear", "cosine"],
-               self.name, "use one of the listed schedules")
-        _check(self.warmup_steps >= 0, where, "warmup_steps must be non-negative", ">= 0", self.warmup_steps, "use 0")
-        _check(0.0 <= self.min_lr_ratio <= 1.0, where, "min_lr_ratio must lie in [0, 1]", "0 <= r <= 1", self.min_lr_ratio, "use 0.0")
+               self.name, "pick a schedule from the expected list")
+        _check(self.warmup_steps >= 0, where, "warmup_steps cannot be negative", ">= 0", self.warmup_steps, "use 0")
+        _check(0.0 <= self.min_lr_ratio <= 1.0, where, "min_lr_ratio is a fraction of the peak rate in [0, 1]", "0 <= r <= 1", self.min_lr_ratio, "use 0.0")
 
 
 @dataclass(frozen=True)
@@ -466,10 +466,10 @@ class CheckpointConfig:
     resume_from: str = ""
 
     def __post_init__(self) -> None:
-        _check(self.save_every_steps >= 0, "config.CheckpointConfig", "save_every_steps must be non-negative", ">= 0",
-               self.save_every_steps, "use 0 to disable periodic checkpointing")
-        _check(self.keep_last >= 0, "config.CheckpointConfig", "keep_last must be non-negative", ">= 0", self.keep_last,
-               "use 0 to keep every checkpoint")
+        _check(self.save_every_steps >= 0, "config.CheckpointConfig", "save_every_steps cannot be negative", ">= 0",
+               self.save_every_steps, "0 means no periodic saves")
+        _check(self.keep_last >= 0, "config.CheckpointConfig", "keep_last cannot be negative", ">= 0", self.keep_last,
+               "0 keeps all checkpoints")
 
 
 @dataclass(frozen=True)
@@ -485,14 +485,17 @@ class TrainingConfig:
     deterministic: bool = True
     collect_metrics: bool = False
     cuda_graph: bool = False
+    # Apply the optimizer update to each gradient bucket during the backward pass when the step
+    # needs no global gradient quantity (no clipping, no norm metric, no loss scaling).
+    overlap_optimizer_step: bool = True
 
     def __post_init__(self) -> None:
         where = "config.TrainingConfig"
-        _check(self.max_steps >= 0, where, "max_steps must be non-negative", ">= 0", self.max_steps, "use a non-negative number")
-        _check(self.gradient_accumulation_steps >= 1, where, "gradient_accumulation_steps must be at least 1", ">= 1",
-               self.gradient_accumulation_steps, "use 1 to disable accumulation")
-        _check(self.max_grad_norm >= 0, where, "max_grad_norm must be non-negative", ">= 0", self.max_grad_norm,
-               "use 0 to disable clipping")
+        _check(self.max_steps >= 0, where, "max_steps cannot be negative", ">= 0", self.max_steps, "give 0 or a larger number")
+        _check(self.gradient_accumulation_steps >= 1, where, "gradient_accumulation_steps counts micro-batches and has to be 1 or more", ">= 1",
+               self.gradient_accumulation_steps, "1 means one micro-batch per step (no accumulation)")
+        _check(self.max_grad_norm >= 0, where, "max_grad_norm cannot be negative", ">= 0", self.max_grad_norm,
+               "0 switches gradient clipping off")
 
 
 @dataclass(frozen=True)
@@ -518,10 +521,10 @@ class ExperimentConfig:
     def __post_init__(self) -> None:
         where = "config.ExperimentConfig"
         _check(self.backend in ("auto", "gloo", "nccl"), where, "unknown backend", ["auto", "gloo", "nccl"], self.backend,
-               "use 'auto' unless you need to pin a backend")
+               "leave it at 'auto' to let the runtime pick the backend")
         _check(self.device in ("auto", "cpu", "cuda"), where, "unknown device", ["auto", "cpu", "cuda"], self.device,
-               "use 'auto' unless you need to pin a device type")
-        _check(self.timeout_seconds > 0, where, "timeout_seconds must be positive", "> 0", self.timeout_seconds, "use e.g. 300")
+               "leave it at 'auto' to let the runtime pick the device")
+        _check(self.timeout_seconds > 0, where, "the collective timeout has to be greater than zero seconds", "> 0", self.timeout_seconds, "use e.g. 300")
         _check(not (self.backend == "gloo" and self.device == "cuda"), where,
                "Gloo on CUDA tensors supports only a few collectives and is never right for training",
                "backend='nccl' with device='cuda'", "backend='gloo', device='cuda'", "use nccl for CUDA or cpu for gloo")
@@ -549,14 +552,14 @@ _T = TypeVar("_T")
 
 def _from_mapping(cls: type[_T], payload: Any, *, path: str) -> _T:
     if not isinstance(payload, dict):
-        _fail("config.from_dict", f"expected a mapping for {path or 'the top level'}", "mapping", type(payload).__name__,
-              "check the indentation of the YAML file")
+        _fail("config.from_dict", f"a YAML mapping was needed for {path or 'the top level'}", "mapping", type(payload).__name__,
+              "the section is probably mis-indented in the YAML file")
     known = {f.name: f for f in fields(cls)}  # type: ignore[arg-type]
     unknown = sorted(set(payload) - set(known))
     if unknown:
         dotted = [f"{path}.{k}" if path else k for k in unknown]
-        _fail("config.from_dict", f"unknown configuration key(s) under {path or 'the top level'!r}", sorted(known), dotted,
-              "remove the key or fix the typo; unknown keys are never ignored")
+        _fail("config.from_dict", f"key(s) not in the schema under {path or 'the top level'!r}", sorted(known), dotted,
+              "delete or correct those keys: the loader refuses keys it does not know")
     kwargs = {name: _coerce(known[name].type, value, path=f"{path}.{name}" if path else name) for name, value in payload.items()}
     return cls(**kwargs)
 
@@ -587,8 +590,8 @@ def load_experiment_config(path: str | Path, **overrides: Any) -> ExperimentConf
     """Load a YAML experiment; keyword overrides are applied with ``dataclasses.replace``."""
     source = Path(path)
     if not source.is_file():
-        _fail("config.load_experiment_config", "configuration file not found", "an existing YAML file", str(source),
-              "check the path; configs live under configs/")
+        _fail("config.load_experiment_config", "there is no configuration file at this path", "a path to a YAML file", str(source),
+              "the shipped experiment files are in the configs/ directory")
     raw = yaml.safe_load(source.read_text(encoding="utf-8")) or {}
     config = ExperimentConfig.from_dict(raw)
     return dataclasses.replace(config, **overrides) if overrides else config

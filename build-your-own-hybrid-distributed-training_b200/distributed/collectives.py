@@ -15,7 +15,8 @@ Contract (same as ``src/hybrid_training/distributed/collectives.py:1-954``):
 from __future__ import annotations
 
 import time
-from collections.abc import Callable, Iterable, Sequence
+from collections.abc import Callable, Iterable, Iterator, Sequence
+from contextlib import contextmanager
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -27,6 +28,8 @@ from ..logging import get_logger
 from .groups import GroupHandle, validate_group_membership
 
 __all__ = [
+    "observe_collectives",
+    "record_collective",
     "AsyncWork",
     "CommunicationRecorder",
     "CommunicationStats",
@@ -112,8 +115,8 @@ class CommunicationRecorder:
 
     def summary(self) -> str:
         if not self.by_operation:
-            return "no communication recorded"
-        lines = ["communication summary:"]
+            return "nothing was communicated"
+        lines = ["collectives by operation and group:"]
         for key in sorted(self.by_operation):
             s = self.by_operation[key]
             lines.append(f"  {key:<34} calls={s.calls:<6} MiB={s.bytes / 2**20:9.3f} launch_s={s.seconds:8.4f} "
@@ -153,7 +156,7 @@ class AsyncWork:
 
 def _op(op: str, where: str, group: GroupHandle) -> Any:
     if op not in ReduceOp.ALL:
-        raise CollectiveError(format_error(where, "unknown reduction operation", rank=group.global_rank,
+        raise CollectiveError(format_error(where, "this reduction is not supported", rank=group.global_rank,
                                            expected=list(ReduceOp.ALL), observed=op, resolution="use a ReduceOp constant"))
     return _TORCH_OP[op]
 
@@ -162,12 +165,41 @@ def _contiguous(tensor: torch.Tensor, where: str, group: GroupHandle) -> None:
     if not tensor.is_contiguous():
         raise CollectiveError(format_error(
             where, "collectives require contiguous tensors; some backends would silently copy a strided buffer",
-            rank=group.global_rank, expected="tensor.is_contiguous() == True",
+            rank=group.global_rank, expected="a contiguous tensor",
             observed=f"shape={tuple(tensor.shape)} strides={tensor.stride()}", resolution="call .contiguous() first"))
 
 
 def _nbytes(t: torch.Tensor) -> int:
     return t.numel() * t.element_size()
+
+
+_OBSERVERS: list[CommunicationRecorder] = []
+
+
+@contextmanager
+def observe_collectives(recorder: CommunicationRecorder | None = None) -> Iterator[CommunicationRecorder]:
+    """Count every collective issued in this process while the block runs, whatever recorder its caller passed.
+
+    Covers the wrappers of this module and the in-kernel NVLink collectives (DDP bucket
+    all-reduce, FSDP reduce-scatter + AdamW and shard gathers, tensor-parallel GEMM collectives),
+    which report through :func:`record_collective`.  Used to measure communication per step.
+    """
+    rec = recorder if recorder is not None else CommunicationRecorder()
+    _OBSERVERS.append(rec)
+    try:
+        yield rec
+    finally:
+        _OBSERVERS.remove(rec)
+
+
+def record_collective(recorder: CommunicationRecorder | None, operation: str, group_name: str, *, num_bytes: int,
+                      seconds: float = 0.0) -> None:
+    """Count one collective in ``recorder`` (if any) and in every active :func:`observe_collectives` block."""
+    if recorder is not None:
+        recorder.record(operation, group_name, num_bytes=num_bytes, seconds=seconds)
+    for obs in _OBSERVERS:
+        if obs is not recorder:
+            obs.record(operation, group_name, num_bytes=num_bytes, seconds=seconds)
 
 
 def _reduce_op_for(op: str, tensor: torch.Tensor, group: GroupHandle) -> tuple[Any, bool]:
@@ -193,8 +225,7 @@ def all_reduce(tensor: torch.Tensor, group: GroupHandle, *, op: str = ReduceOp.S
     if predivide:
         tensor.div_(group.size)
     work = dist.all_reduce(tensor, op=torch_op, group=group.process_group, async_op=async_op)
-    if recorder is not None:
-        recorder.record("all_reduce", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
+    record_collective(recorder, "all_reduce", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
     return AsyncWork(work if async_op else None, recorder=recorder, operation="all_reduce", group_name=group.name)
 
 
@@ -204,15 +235,14 @@ def broadcast(tensor: torch.Tensor, group: GroupHandle, *, source_local_rank: in
     validate_group_membership(group, group.global_rank, where)
     _contiguous(tensor, where, group)
     if not 0 <= source_local_rank < group.size:
-        raise CollectiveError(format_error(where, "source_local_rank is outside the group", rank=group.global_rank,
+        raise CollectiveError(format_error(where, "the source index is not a position in the group", rank=group.global_rank,
                                            expected=f"0 <= r < {group.size}", observed=source_local_rank,
-                                           resolution="pass a group-local index, not a global rank"))
+                                           resolution="give the position inside the group rather than the global rank"))
     if group.is_trivial:
         return AsyncWork(None)
     t0 = time.perf_counter()
     work = dist.broadcast(tensor, src=group.ranks[source_local_rank], group=group.process_group, async_op=async_op)
-    if recorder is not None:
-        recorder.record("broadcast", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
+    record_collective(recorder, "broadcast", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
     return AsyncWork(work if async_op else None, recorder=recorder, operation="broadcast", group_name=group.name)
 
 
@@ -226,16 +256,15 @@ def all_gather_tensor(tensor: torch.Tensor, group: GroupHandle, *, out: torch.Te
     if out is None:
         out = torch.empty(shape, dtype=tensor.dtype, device=tensor.device)
     elif tuple(out.shape) != shape:
-        raise CollectiveError(format_error(where, "destination buffer has the wrong shape", rank=group.global_rank,
+        raise CollectiveError(format_error(where, "the output buffer is not shaped for this collective", rank=group.global_rank,
                                            expected=shape, observed=tuple(out.shape),
-                                           resolution="size the output as (group_size * input.shape[0], *input.shape[1:])"))
+                                           resolution="allocate (members x rows, ...) for the gathered output"))
     if group.is_trivial:
         out.copy_(tensor)
         return out, AsyncWork(None)
     t0 = time.perf_counter()
     work = dist.all_gather_into_tensor(out, tensor, group=group.process_group, async_op=async_op)
-    if recorder is not None:
-        recorder.record("all_gather", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
+    record_collective(recorder, "all_gather", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
     return out, AsyncWork(work if async_op else None, recorder=recorder, operation="all_gather", group_name=group.name)
 
 
@@ -248,16 +277,16 @@ def reduce_scatter_tensor(tensor: torch.Tensor, group: GroupHandle, *, op: str =
     _contiguous(tensor, where, group)
     _op(op, where, group)
     if tensor.shape[0] % group.size:
-        raise CollectiveError(format_error(where, "the leading dimension must be divisible by the group size",
+        raise CollectiveError(format_error(where, "dim 0 has to split into one equal block per group member",
                                            rank=group.global_rank, expected=f"shape[0] % {group.size} == 0",
                                            observed=tensor.shape[0], resolution="pad the buffer to a multiple of the group size"))
     shape = (tensor.shape[0] // group.size, *tensor.shape[1:])
     if out is None:
         out = torch.empty(shape, dtype=tensor.dtype, device=tensor.device)
     elif tuple(out.shape) != shape:
-        raise CollectiveError(format_error(where, "destination buffer has the wrong shape", rank=group.global_rank,
+        raise CollectiveError(format_error(where, "the output buffer is not shaped for this collective", rank=group.global_rank,
                                            expected=shape, observed=tuple(out.shape),
-                                           resolution="size the output as (input.shape[0] // group_size, ...)"))
+                                           resolution="allocate (rows / members, ...) for the scattered output"))
     if group.is_trivial:
         out.copy_(tensor.view(shape))
         return out, AsyncWork(None)
@@ -266,8 +295,7 @@ def reduce_scatter_tensor(tensor: torch.Tensor, group: GroupHandle, *, op: str =
     if predivide:
         tensor = tensor.div(group.size)
     work = dist.reduce_scatter_tensor(out, tensor, op=torch_op, group=group.process_group, async_op=async_op)
-    if recorder is not None:
-        recorder.record("reduce_scatter", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
+    record_collective(recorder, "reduce_scatter", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
     return out, AsyncWork(work if async_op else None, recorder=recorder, operation="reduce_scatter", group_name=group.name)
 
 
@@ -277,7 +305,7 @@ def all_to_all_tensor(tensor: torch.Tensor, group: GroupHandle, *, recorder: Com
     validate_group_membership(group, group.global_rank, where)
     _contiguous(tensor, where, group)
     if tensor.shape[0] % group.size:
-        raise CollectiveError(format_error(where, "the leading dimension must be divisible by the group size",
+        raise CollectiveError(format_error(where, "dim 0 has to split into one equal block per group member",
                                            rank=group.global_rank, expected=f"shape[0] % {group.size} == 0",
                                            observed=tensor.shape[0], resolution="pad the leading dimension first"))
     if group.is_trivial:
@@ -285,20 +313,19 @@ def all_to_all_tensor(tensor: torch.Tensor, group: GroupHandle, *, recorder: Com
     out = torch.empty_like(tensor)
     t0 = time.perf_counter()
     dist.all_to_all_single(out, tensor, group=group.process_group)
-    if recorder is not None:
-        recorder.record("all_to_all", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
+    record_collective(recorder, "all_to_all", group.name, num_bytes=_nbytes(tensor), seconds=time.perf_counter() - t0)
     return out
 
 
 def _peer(group: GroupHandle, local: int, where: str, role: str) -> int:
     if not 0 <= local < group.size:
         raise CollectiveError(format_error(where, f"{role} outside the group", rank=group.global_rank,
-                                           expected=f"0 <= r < {group.size}", observed=local, resolution="pass a group-local index"))
+                                           expected=f"0 <= r < {group.size}", observed=local, resolution="give the position inside the group"))
     peer = group.ranks[local]
     if peer == group.global_rank:
         raise CollectiveError(format_error(where, "a rank cannot exchange with itself; a blocking send/recv would deadlock",
                                            rank=group.global_rank, expected="a different rank", observed=peer,
-                                           resolution="skip the transfer when source and destination coincide"))
+                                           resolution="do not send a tensor to the rank that owns it"))
     return peer
 
 
@@ -335,7 +362,7 @@ def assert_metadata_consistent(payload: Any, group: GroupHandle, *, name: str, o
         if value != gathered[0]:
             raise ParameterConsistencyError(format_error(
                 operation, f"{name} differs across the {group.name!r} group; the collectives that follow would mismatch",
-                rank=group.global_rank, expected=f"local rank 0 (global {group.ranks[0]}): {gathered[0]!r}",
+                rank=group.global_rank, expected=f"the group's first rank (global {group.ranks[0]}): {gathered[0]!r}",
                 observed=f"local rank {local} (global {group.ranks[local]}): {value!r}",
                 resolution="build the model identically on every rank of this group (same seed, config, module order)"))
 
@@ -350,7 +377,7 @@ def assert_tensor_consistent(tensor: torch.Tensor, group: GroupHandle, *, name: 
     if not torch.allclose(tensor.detach(), reference, rtol=rtol, atol=atol):
         delta = (tensor.detach().double() - reference.double()).abs().max().item()
         raise ParameterConsistencyError(format_error(
-            operation, f"{name} differs from the value held by group-local rank 0", rank=group.global_rank,
+            operation, f"{name} is not the same here as on the group's first rank", rank=group.global_rank,
             expected=f"max |delta| <= {atol} (+ rtol {rtol})", observed=f"max |delta| = {delta:.3e}",
             resolution="seed identically on every rank and broadcast parameters at construction"))
 
@@ -368,8 +395,8 @@ def sum_scalar(value: float | torch.Tensor, group: GroupHandle, *, device: torch
 def concat_shard_sizes(numel: int, group_size: int) -> tuple[int, int]:
     """(padded total, per-rank shard) for an equal split with ceil division."""
     if group_size < 1:
-        raise CollectiveError(format_error("collectives.concat_shard_sizes", "group size must be positive", expected=">= 1",
-                                           observed=group_size, resolution="pass a real group size"))
+        raise CollectiveError(format_error("collectives.concat_shard_sizes", "a group has at least one member", expected=">= 1",
+                                           observed=group_size, resolution="give the number of members of the group"))
     shard = -(-numel // group_size)
     return shard * group_size, shard
 
@@ -381,4 +408,4 @@ def wait_all(works: Iterable[AsyncWork]) -> None:
 
 def log_group_layout(groups: Sequence[GroupHandle]) -> None:
     for h in groups:
-        _LOG.debug("group %-16s size=%d local_rank=%d ranks=%s", h.name, h.size, h.local_rank, h.ranks)
+        _LOG.debug("%-16s %d ranks (this is #%d): %s", h.name, h.size, h.local_rank, h.ranks)

@@ -68,17 +68,17 @@ class LaunchEnvironment:
     def __post_init__(self) -> None:
         op = "context.LaunchEnvironment"
         if self.world_size < 1:
-            raise _init_error("world_size must be positive", "check WORLD_SIZE", op=op, rank=self.rank, expected=">= 1",
+            raise _init_error("the world has at least one rank", "check WORLD_SIZE", op=op, rank=self.rank, expected=">= 1",
                               observed=self.world_size)
         if not 0 <= self.rank < self.world_size:
-            raise _init_error("rank outside the world", "check RANK", op=op, rank=self.rank, world_size=self.world_size,
+            raise _init_error("the rank is not below the world size", "check RANK", op=op, rank=self.rank, world_size=self.world_size,
                               expected=f"0 <= rank < {self.world_size}", observed=self.rank)
         if not 0 <= self.local_rank < max(self.local_world_size, 1):
-            raise _init_error("local_rank outside the node", "check LOCAL_RANK / LOCAL_WORLD_SIZE", op=op, rank=self.rank,
+            raise _init_error("the local rank is not below the node's process count", "look at the LOCAL_RANK and LOCAL_WORLD_SIZE the launcher exported", op=op, rank=self.rank,
                               world_size=self.world_size, expected=f"0 <= local_rank < {self.local_world_size}",
                               observed=self.local_rank)
         if not 1 <= self.master_port <= 65535:
-            raise _init_error("master_port outside the valid range", "check MASTER_PORT", op=op, rank=self.rank,
+            raise _init_error("MASTER_PORT is not a TCP port number", "check MASTER_PORT", op=op, rank=self.rank,
                               world_size=self.world_size, expected="1..65535", observed=self.master_port)
 
     @classmethod
@@ -88,7 +88,7 @@ class LaunchEnvironment:
         present = [v for v in _TORCHRUN_VARS if v in source]
         if not present:
             if not allow_single_process:
-                raise _init_error("no distributed launch variables found",
+                raise _init_error("the environment has no torchrun-style launch variables",
                                   "launch with torchrun, or pass rank/world_size to init_distributed()", op=op,
                                   expected="RANK, WORLD_SIZE to be set", observed="none set")
             port = find_free_port()
@@ -96,19 +96,19 @@ class LaunchEnvironment:
             return cls(0, 1, 0, 1, "127.0.0.1", port)
         if len(present) != len(_TORCHRUN_VARS):
             missing = [v for v in _TORCHRUN_VARS if v not in source]
-            raise _init_error("the launch environment is only partially set", f"set the missing variables: {missing}",
+            raise _init_error("the launch environment is only partially set", f"export what is missing: {missing}",
                               op=op, expected=list(_TORCHRUN_VARS), observed=present)
 
         def read(name: str, default: int | None = None) -> int:
             raw = source.get(name)
             if raw is None:
                 if default is None:
-                    raise _init_error(f"{name} is required but unset", f"export {name}", op=op)
+                    raise _init_error(f"{name} has to be set by the launcher", f"export {name}", op=op)
                 return default
             try:
                 return int(raw)
             except ValueError as exc:
-                raise _init_error(f"{name} is not an integer", f"export {name} as a decimal integer", op=op,
+                raise _init_error(f"{name} is not an integer", f"export {name} written as a base-10 integer", op=op,
                                   expected="an integer", observed=raw) from exc
 
         rank, world = read("RANK"), read("WORLD_SIZE")
@@ -122,14 +122,14 @@ def _resolve_backend_and_device(backend: str, device: str, env: LaunchEnvironmen
     enough = gpus >= env.local_world_size
     if backend == "nccl" or device == "cuda":
         if gpus == 0:
-            raise _init_error("CUDA/NCCL requested but no CUDA device is visible", "use backend='gloo' and device='cpu'",
+            raise _init_error("NCCL on CUDA was asked for, but this process sees no GPU", "run on CPU with backend='gloo', device='cpu'",
                               op=op, rank=env.rank, world_size=env.world_size, expected=">= 1 CUDA device", observed=gpus)
         if backend == "nccl" and not enough:
             raise _init_error("NCCL needs one CUDA device per local process; sharing a device hangs instead of failing",
                               "lower --nproc-per-node to the GPU count, or use gloo on cpu", op=op, rank=env.rank,
                               world_size=env.world_size, expected=f">= {env.local_world_size} CUDA devices", observed=gpus)
         if backend == "nccl" and not dist.is_nccl_available():
-            raise _init_error("this PyTorch build has no NCCL support", "use a CUDA build of PyTorch", op=op, rank=env.rank)
+            raise _init_error("the installed PyTorch was built without NCCL", "use a CUDA build of PyTorch", op=op, rank=env.rank)
         return ("nccl" if backend in ("auto", "nccl") else backend), torch.device("cuda", env.local_rank)
     if backend == "gloo" or device == "cpu":
         return "gloo", torch.device("cpu")
@@ -188,6 +188,10 @@ class DistributedContext:
             self._symmetric[group_name] = SymmetricWorkspace.create(self.group(group_name), self._device)
         return self._symmetric[group_name]
 
+    def symmetric_workspaces(self) -> list[Any]:
+        """Every peer-mapped workspace created so far (their status words report in-kernel timeouts)."""
+        return [ws for ws in self._symmetric.values() if ws is not None]
+
     def barrier(self, group: str = "world", *, label: str = "") -> None:
         self._require_active("context.barrier")
         handle = self._groups.get(group)
@@ -230,7 +234,7 @@ class DistributedContext:
 
     def _require_active(self, operation: str) -> None:
         if not self._active:
-            raise _init_error("the distributed context has been shut down", "create a new context with init_distributed()",
+            raise _init_error("this context was already shut down", "call init_distributed() again for a fresh context",
                               op=operation, rank=self.rank, world_size=self.world_size)
 
     def describe(self) -> str:
@@ -258,7 +262,7 @@ def init_distributed(
     """Bring up the process group and the 4-D grid; see the module docstring."""
     global _ACTIVE
     if _ACTIVE is not None and _ACTIVE.is_active:
-        raise _init_error("a distributed context is already active in this process",
+        raise _init_error("this process already has an active distributed context",
                           "call shutdown() on it first, or use distributed_context()", op="context.init_distributed",
                           rank=_ACTIVE.rank, world_size=_ACTIVE.world_size)
     if isinstance(topology, ExperimentConfig):
@@ -268,7 +272,7 @@ def init_distributed(
         topo_cfg = topology
     if rank is not None or world_size is not None:
         if rank is None or world_size is None:
-            raise _init_error("rank and world_size must be supplied together", "pass both explicit values, or neither",
+            raise _init_error("an explicit rank needs an explicit world_size, and the other way round", "give both or leave both to the environment",
                               op="context.init_distributed", expected="both or neither",
                               observed=f"rank={rank}, world_size={world_size}")
         launch = LaunchEnvironment(rank, world_size, rank if local_rank is None else local_rank, world_size,
@@ -285,7 +289,7 @@ def init_distributed(
     preexisting = dist.is_initialized()
     if preexisting:
         if dist.get_world_size() != launch.world_size:
-            raise _init_error("torch.distributed is already initialised with a different world size",
+            raise _init_error("a process group of another size is already initialised",
                               "destroy the existing process group first", op="context.init_distributed",
                               rank=launch.rank, world_size=launch.world_size, expected=launch.world_size,
                               observed=dist.get_world_size())
@@ -309,7 +313,7 @@ def init_distributed(
     context = DistributedContext(launch, backend_name, dev, grid, registry, owns_process_group=not preexisting)
     _ACTIVE = context
     set_log_context(LogContext(launch.rank, launch.world_size, launch.local_rank, grid.coordinates_of(launch.rank).label()))
-    _LOG.info("distributed context ready: backend=%s device=%s topology=%s", backend_name, dev, grid)
+    _LOG.info("context up: %s on %s, grid %s", backend_name, dev, grid)
     return context
 
 
@@ -324,7 +328,7 @@ def distributed_context(topology: TopologyConfig | ExperimentConfig | None = Non
 
 def current_context() -> DistributedContext:
     if _ACTIVE is None or not _ACTIVE.is_active:
-        raise _init_error("no distributed context is active in this process", "call init_distributed() first",
+        raise _init_error("init_distributed() has not been called in this process (or the context was shut down)", "call init_distributed() first",
                           op="context.current_context")
     return _ACTIVE
 

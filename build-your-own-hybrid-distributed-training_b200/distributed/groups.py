@@ -70,7 +70,7 @@ class ProcessGroupRegistry:
                  backend: str | None = None, create: bool = True) -> None:
         if create and not dist.is_initialized():
             raise DistributedInitializationError(format_error(
-                "groups.ProcessGroupRegistry", "the default process group must exist before sub-groups are created",
+                "groups.ProcessGroupRegistry", "sub-groups are built from the world process group, which does not exist yet",
                 rank=rank, world_size=topology.world_size, resolution="call init_distributed() first"))
         self._topology = topology
         self._rank = rank
@@ -98,25 +98,25 @@ class ProcessGroupRegistry:
                     mine = (members, pg)
             if mine is None:
                 raise DistributedInitializationError(format_error(
-                    "groups.ProcessGroupRegistry", f"rank is not a member of any {name!r} group", rank=rank,
-                    world_size=topology.world_size, resolution="this indicates a bug in ParallelTopology"))
+                    "groups.ProcessGroupRegistry", f"this rank is in none of the {name!r} group", rank=rank,
+                    world_size=topology.world_size, resolution="the rank grid arithmetic is inconsistent (an internal error)"))
             self._handles[name] = GroupHandle(name, mine[0], mine[0].index(rank), rank, mine[1])
         self._handles["world"] = GroupHandle("world", world, rank, rank, default)
-        _LOG.debug("created %d process groups", len(self._created))
+        _LOG.debug("%d communicators created", len(self._created))
 
     def get(self, name: str) -> GroupHandle:
         if self._destroyed:
-            raise CollectiveError(format_error("groups.get", "the process-group registry has been destroyed",
+            raise CollectiveError(format_error("groups.get", "the group registry was already torn down",
                                                rank=self._rank, world_size=self._topology.world_size,
-                                               resolution="do not use groups after shutting the context down"))
+                                               resolution="keep using groups only while their context is active"))
         if name == "sequence_effective":
             name = self._topology.sequence_group_name
         handle = self._handles.get(name)
         if handle is None:
-            raise CollectiveError(format_error("groups.get", "unknown process-group name", rank=self._rank,
+            raise CollectiveError(format_error("groups.get", "no group is registered under this name", rank=self._rank,
                                                world_size=self._topology.world_size,
                                                expected=[*sorted(self._handles), "sequence_effective"], observed=name,
-                                               resolution="use one of the registered group names"))
+                                               resolution="ask for one of the group names the registry lists"))
         return handle
 
     def __getitem__(self, name: str) -> GroupHandle:
@@ -135,7 +135,7 @@ class ProcessGroupRegistry:
         return tuple(self._created)
 
     def describe(self) -> str:
-        lines = [f"process groups for rank {self._rank}:"]
+        lines = [f"communicators of rank {self._rank}:"]
         for name in self.names:
             h = self._handles[name]
             lines.append(f"  {name:<16} size={h.size:<3} local_rank={h.local_rank:<3} ranks={h.ranks}")
@@ -161,7 +161,7 @@ class ProcessGroupRegistry:
 
 def validate_group_membership(handle: GroupHandle, rank: int, operation: str) -> None:
     if rank not in handle.ranks:
-        raise CollectiveError(format_error(operation, f"rank is not a member of process group {handle.name!r}", rank=rank,
+        raise CollectiveError(format_error(operation, f"this rank does not belong to group {handle.name!r}", rank=rank,
                                            expected=f"rank in {handle.ranks}", observed=rank,
                                            resolution="pass the group handle this rank obtained from the registry"))
 

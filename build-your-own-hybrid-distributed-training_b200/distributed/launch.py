@@ -139,8 +139,8 @@ def _require_picklable(obj: Any, what: str) -> None:
         pickle.dumps(obj)
     except Exception as exc:
         raise DistributedInitializationError(format_error(
-            "launch.launch_workers", f"{what} cannot be pickled, so it cannot cross a 'spawn' boundary",
-            expected="a module-level function and picklable arguments", observed=repr(obj)[:200],
+            "launch.launch_workers", f"{what} is not picklable, and spawned workers receive their arguments by pickling",
+            expected="a function defined at module level, with picklable arguments", observed=repr(obj)[:200],
             resolution="move the entrypoint to module scope and pass only picklable arguments")) from exc
 
 
@@ -165,12 +165,12 @@ def launch_workers(
 ) -> list[WorkerResult]:
     """Run ``entrypoint`` on ``world_size`` spawned ranks and gather their results."""
     if world_size < 1:
-        raise DistributedInitializationError(format_error("launch.launch_workers", "world_size must be positive",
-                                                          expected=">= 1", observed=world_size, resolution="launch at least one worker"))
+        raise DistributedInitializationError(format_error("launch.launch_workers", "at least one worker is needed",
+                                                          expected=">= 1", observed=world_size, resolution="ask for one or more workers"))
     kwargs = dict(kwargs or {})
     if start_method == "spawn":
         _require_picklable(entrypoint, "the entrypoint")
-        _require_picklable((tuple(args), kwargs), "the entrypoint arguments")
+        _require_picklable((tuple(args), kwargs), "the worker function and its arguments")
     port = master_port if master_port is not None else find_free_port(master_addr)
     ctx: Any = mp.get_context(start_method)
     inbox: Any = ctx.Queue()
@@ -218,8 +218,8 @@ def launch_workers(
     if failed and raise_on_failure:
         raise WorkerFailure(format_error(
             "launch.launch_workers", f"{len(failed)} of {world_size} worker(s) {'timed out' if timed_out else 'failed'}",
-            expected="every rank to return normally with exit code 0", observed=f"failing ranks: {[r.rank for r in failed]}",
-            resolution="read the per-rank tracebacks below; a rank with no traceback was blocked in a collective"), results)
+            expected="all workers to finish and exit with status 0", observed=f"failing ranks: {[r.rank for r in failed]}",
+            resolution="see each failing rank's traceback below; a rank without one was still waiting inside a collective"), results)
     return results
 
 

@@ -27,8 +27,15 @@ _LOG = get_logger(__name__)
 class SymmetricWorkspace:
     """Symmetric buffers + signal pads for one group (see the module docstring)."""
 
+    # Bytes of each allocation's signal pad.  The kernels' barriers use one 32-bit slot per
+    # (block, peer) in the upper half, so 64 KB allows 1024 blocks at 8 ranks (one per SM needs 148).
+    SIGNAL_PAD_BYTES = 64 * 1024
+
     def __init__(self, group: GroupHandle, device: torch.device) -> None:
         import torch.distributed._symmetric_memory as symm_mem
+
+        if symm_mem.get_signal_pad_size() < self.SIGNAL_PAD_BYTES:
+            symm_mem.set_signal_pad_size(self.SIGNAL_PAD_BYTES)
 
         self.group = group
         self.device = device

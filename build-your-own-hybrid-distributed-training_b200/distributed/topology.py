@@ -96,14 +96,14 @@ class ParallelTopology:
     def rank_of(self, coordinates: RankCoordinates | Iterable[int]) -> int:
         values = coordinates.as_tuple() if isinstance(coordinates, RankCoordinates) else tuple(coordinates)
         if len(values) != len(DIMENSIONS):
-            raise TopologyError(format_error("topology.rank_of", "wrong number of coordinates", expected=len(DIMENSIONS),
-                                             observed=len(values), resolution=f"pass one coordinate per dimension {DIMENSIONS}"))
+            raise TopologyError(format_error("topology.rank_of", "the coordinate tuple has the wrong length", expected=len(DIMENSIONS),
+                                             observed=len(values), resolution=f"give exactly one index per grid dimension {DIMENSIONS}"))
         rank = 0
         for dim, value in zip(DIMENSIONS, values):
             if not 0 <= value < self._sizes[dim]:
-                raise TopologyError(format_error("topology.rank_of", f"coordinate for dimension {dim!r} is out of range",
+                raise TopologyError(format_error("topology.rank_of", f"the index along {dim!r} is out of range",
                                                  expected=f"0 <= c < {self._sizes[dim]}", observed=value,
-                                                 resolution="check the coordinate you constructed"))
+                                                 resolution="each index has to be below the size of its dimension"))
             rank += value * self._place[dim]
         return rank
 
@@ -154,7 +154,7 @@ class ParallelTopology:
         lines = [
             f"rank {rank}/{self._world_size}  coordinates {coords.label()}",
             "  sizes: " + ", ".join(f"{d}={self._sizes[d]}" for d in DIMENSIONS),
-            f"  sequence-parallel mode: {self._config.sequence_parallel_mode} (effective size {self.sequence_parallel_size})",
+            f"  sequence split       : {self._config.sequence_parallel_mode} (effective size {self.sequence_parallel_size})",
         ]
         for name in (*DIMENSIONS, *COMPOSITE_GROUPS):
             members = self.group_ranks(name, rank)
@@ -175,15 +175,15 @@ class ParallelTopology:
             return (dimension,)
         if dimension in COMPOSITE_GROUPS:
             return COMPOSITE_GROUPS[dimension]
-        raise TopologyError(format_error("topology.resolve", "unknown dimension or group name",
+        raise TopologyError(format_error("topology.resolve", "not a grid dimension nor a composite group",
                                          expected=sorted({*DIMENSIONS, *COMPOSITE_GROUPS}), observed=dimension,
-                                         resolution="use a dimension name or a composite group name"))
+                                         resolution="ask for a dimension or one of the composite groups"))
 
     def _check_rank(self, rank: int) -> None:
         if not 0 <= rank < self._world_size:
-            raise TopologyError(format_error("topology.check_rank", "rank outside the topology", world_size=self._world_size,
+            raise TopologyError(format_error("topology.check_rank", "the rank is not in this grid", world_size=self._world_size,
                                              expected=f"0 <= rank < {self._world_size}", observed=rank,
-                                             resolution="the topology was built for a different world size"))
+                                             resolution="this grid was laid out for another number of ranks"))
 
     def __repr__(self) -> str:
         return f"ParallelTopology(world_size={self._world_size}, " + ", ".join(f"{d}={self._sizes[d]}" for d in DIMENSIONS) + ")"

@@ -30,7 +30,7 @@ __all__ = [
 ]
 
 _ROOT = "hybrid_training"
-_TEXT_FORMAT = "%(asctime)s %(levelname)-7s [%(rank_tag)s] %(name)s: %(message)s"
+_TEXT_FORMAT = "%(asctime)s [%(rank_tag)s] %(levelname)s %(name)s | %(message)s"
 
 
 @dataclass(frozen=True)
@@ -132,7 +132,7 @@ def configure_logging(
     """Attach one rank-aware handler to the package's root logger."""
     style = (fmt or os.environ.get("HYBRID_LOG_FORMAT") or "text").lower()
     if style not in ("text", "json"):
-        raise ValueError(f"fmt must be 'text' or 'json', got {style!r}")
+        raise ValueError(f"log format is 'text' or 'json', not {style!r}")
     logger = logging.getLogger(_ROOT)
     if logger.handlers and not force:
         logger.setLevel(level)

@@ -96,8 +96,8 @@ class ParallelPlan:
     def __post_init__(self) -> None:
         if self.sequence_parallel and self.sequence_group.size == 1:
             raise ConfigurationError(format_error("models.ParallelPlan", "sequence_parallel requested but the sequence group has one member",
-                                                  expected="sequence_group.size > 1", observed=self.sequence_group.size,
-                                                  resolution="pass a real sequence-parallel group or disable the flag"))
+                                                  expected="a sequence group with 2 or more ranks", observed=self.sequence_group.size,
+                                                  resolution="give the plan a sequence group of 2+ ranks, or turn sequence parallelism off"))
         if self.sequence_parallel and self.sequence_group.ranks != self.tensor_group.ranks and self.tensor_group.size > 1:
             raise UnsupportedFeatureError(format_error(
                 "models.ParallelPlan", "sequence parallelism over a group other than the tensor group (independent mode) "
@@ -125,7 +125,7 @@ class TensorParallelAttention(nn.Module):
         kv = num_kv_heads or num_heads
         if num_heads % t or kv % t:
             raise ConfigurationError(format_error(
-                "models.TensorParallelAttention", "attention heads must divide evenly across the tensor-parallel group",
+                "models.TensorParallelAttention", "the attention heads cannot be split equally over the tensor-parallel ranks",
                 rank=plan.tensor_group.global_rank, expected=f"num_heads % {t} == 0 and num_kv_heads % {t} == 0",
                 observed=(num_heads, kv), resolution="choose head counts that are multiples of the tensor-parallel size"))
         self.hidden_size, self.num_heads, self.num_kv_heads = hidden_size, num_heads, kv
@@ -177,7 +177,7 @@ class TensorParallelAttention(nn.Module):
         if attention_mask is not None:
             raise UnsupportedFeatureError(format_error(
                 "models.attention", "explicit attention masks are not supported with context parallelism",
-                expected="attention_mask=None", observed="a mask", resolution="rely on causal masking"))
+                expected="attention_mask=None", observed="a mask", resolution="are masked by causality"))
         cp = self.plan.sequence_group
         h, hkv, d = self.heads_per_partition, self.kv_heads_per_partition, self.head_dim
         local = qkv.shape[1]
@@ -223,7 +223,7 @@ def _explicit_attention(qkv: torch.Tensor, h: int, hkv: int, d: int, causal: boo
         raise UnsupportedFeatureError(format_error(
             "models.attention", "explicit attention masks and attention dropout are not implemented by the flash kernel",
             expected="attention_mask=None and dropout=0 on CUDA", observed="mask or dropout given",
-            resolution="rely on causal masking and disable attention dropout"))
+            resolution="are masked by causality and disable attention dropout"))
     b, s, _ = qkv.shape
     q = qkv[..., : h * d].reshape(b, s, h, d).transpose(1, 2).float()
     k = qkv[..., h * d:(h + hkv) * d].reshape(b, s, hkv, d).transpose(1, 2).float().repeat_interleave(h // hkv, 1)
@@ -286,8 +286,8 @@ class TinyTransformer(nn.Module):
                  dtype: torch.dtype | None = None, compute_dtype: torch.dtype | None = None) -> None:
         super().__init__()
         if config.kind != "transformer":
-            raise ConfigurationError(format_error("models.TinyTransformer", "model kind must be 'transformer'", expected="transformer",
-                                                  observed=config.kind, resolution="set ModelConfig.kind='transformer'"))
+            raise ConfigurationError(format_error("models.TinyTransformer", "this class builds ModelConfig(kind='transformer') models only", expected="transformer",
+                                                  observed=config.kind, resolution="use kind='transformer' in the model config"))
         self.config = config
         self.plan = plan if plan is not None else ParallelPlan.single_process()
         tp = self.plan.tensor_group
@@ -295,8 +295,8 @@ class TinyTransformer(nn.Module):
             raise UnsupportedFeatureError(format_error(
                 "models.TinyTransformer", "tied embeddings with a vocabulary-parallel embedding are not supported: the "
                 "embedding is split by vocabulary rows while the head needs the same matrix split by output features",
-                expected="tie_word_embeddings=False, or vocab_parallel=False", observed="both enabled",
-                resolution="untie the weights, or disable vocabulary partitioning"))
+                expected="untied head weights when the vocabulary is split", observed="both enabled",
+                resolution="set tie_word_embeddings=False, or keep the vocabulary whole"))
         self.compute_dtype = compute_dtype
         vocab_group = tp if self.plan.vocab_parallel else GroupHandle.trivial("tensor")
         self.token_embedding = VocabParallelEmbedding(config.vocab_size, config.hidden_size, vocab_group,
@@ -348,7 +348,7 @@ class TinyTransformer(nn.Module):
         if s > self.config.max_sequence_length:
             raise ConfigurationError(format_error("models.TinyTransformer.forward", "sequence longer than the model supports",
                                                   expected=f"<= {self.config.max_sequence_length}", observed=s,
-                                                  resolution="raise ModelConfig.max_sequence_length or shorten the input"))
+                                                  resolution="increase max_sequence_length in the model config, or feed shorter sequences"))
         hidden = self._embed(token_ids)
         if self.dropout > 0.0 and self.training:
             hidden = F.dropout(hidden, p=self.dropout)
@@ -359,7 +359,7 @@ class TinyTransformer(nn.Module):
             if attention_mask is not None and info.requires_padding:
                 raise UnsupportedFeatureError(format_error(
                     "models.TinyTransformer.forward", "an explicit attention mask with sequence padding is not supported",
-                    expected="a sequence length divisible by the sequence-parallel size",
+                    expected="a length that splits evenly over the sequence ranks",
                     observed=f"length {s}, group {sp_group.size}", resolution="pad the batch or drop the explicit mask"))
             hidden = scatter_sequence(hidden, sp_group, dim=SEQUENCE_DIM)
         residual, delta = hidden, None
@@ -393,7 +393,7 @@ class TinyTransformer(nn.Module):
             raise UnsupportedFeatureError(format_error(
                 "models.TinyTransformer.forward", "the loss under context parallelism needs a sequence length divisible by "
                 "the sequence-parallel size", expected=f"length % {cp.size} == 0", observed=targets.shape[1],
-                resolution="pad the batch to a multiple of the sequence-parallel size"))
+                resolution="pad sequences so that their length splits over the sequence ranks"))
         lo, hi = local_sequence_slice(targets.shape[1], cp)
         local_mean = self.output_projection(h, targets=targets[:, lo:hi].contiguous())
         # Chunks have equal token counts: the global mean is the average of the chunk means.  The

@@ -31,7 +31,7 @@ import torch
 
 from ._ext import extension
 
-__all__ = ["HAS_FUSED_TENSOR_PARALLEL", "all_gather_linear", "bucket_all_reduce", "can_fuse_sequence_parallel",
+__all__ = ["HAS_FUSED_TENSOR_PARALLEL", "all_gather_linear", "bucket_all_reduce", "nvls_available", "can_fuse_sequence_parallel",
            "fsdp_all_gather", "fsdp_reduce_scatter_adamw", "linear_reduce_scatter"]
 
 HAS_FUSED_TENSOR_PARALLEL = True
@@ -45,14 +45,23 @@ def _slots(handle: Any, world: int) -> tuple[int, int]:
     return base, max(1, (slots - base) // world)
 
 
+def nvls_available(workspace: Any, flat: torch.Tensor) -> bool:
+    """Whether ``flat``'s allocation has an NVLink-switch multicast address (NVLS)."""
+    return int(getattr(workspace.handle_of(flat), "multicast_ptr", 0) or 0) != 0
+
+
 def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int, scale: float) -> torch.Tensor:
-    """Average ``flat[start:start+numel]`` over the workspace's group in place; returns the status tensor."""
+    """Average ``flat[start:start+numel]`` over the workspace's group in place; returns the status tensor.
+
+    ``HT_NVLS=1`` selects the NVLink-switch reduction where the allocation has a multicast
+    address; otherwise the two-shot P2P kernel runs.
+    """
     handle = workspace.handle_of(flat)
     world = workspace.group.size
     base, max_blocks = _slots(handle, world)
-    mc = int(handle.multicast_ptr) if os.environ.get("HT_NVLS", "0") == "1" else 0
+    mc = int(getattr(handle, "multicast_ptr", 0) or 0) if os.environ.get("HT_NVLS", "0") == "1" else 0
     extension().bucket_all_reduce(flat, list(handle.buffer_ptrs), list(handle.signal_pad_ptrs), mc, int(start), int(numel),
-                                  float(scale), int(handle.rank), base, min(max_blocks, 128), workspace.status, _TIMEOUT_S)
+                                  float(scale), int(handle.rank), base, max_blocks, workspace.status, _TIMEOUT_S)
     return workspace.status
 
 
@@ -152,6 +161,13 @@ class _TensorParallelSites:
 _SITES: dict[int, _TensorParallelSites] = {}
 
 
+def _note(operation: str, st: _TensorParallelSites, tensor: torch.Tensor) -> None:
+    """Count a fused collective for :func:`~hybrid_training.distributed.collectives.observe_collectives`."""
+    from ..distributed.collectives import record_collective
+
+    record_collective(None, operation, st.workspace.group.name, num_bytes=tensor.numel() * tensor.element_size())
+
+
 def _sites(workspace: Any) -> _TensorParallelSites:
     st = _SITES.get(id(workspace))
     if st is None:
@@ -188,6 +204,7 @@ class _AllGatherLinear(torch.autograd.Function):
         ext.gemm_collective(slot, w, y, bias, pre, False, False, EPI_GELU if pre is not None else EPI_PLAIN, 0.0,
                             1, ptrs, 0, [], 0, [], st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S,
                             gathered, flags)
+        _note("all_gather_gemm", st, x)
         ctx.save_for_backward(w, pre)
         ctx.st, ctx.owner, ctx.site, ctx.shape = st, owner, site, (b, r, k)
         ctx.weight, ctx.bias = weight, bias
@@ -212,6 +229,7 @@ class _AllGatherLinear(torch.autograd.Function):
                                 st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S, None, None)
             dx = torch.empty(b, r, k, dtype=dy.dtype, device=dy.device)
             ext.reduce_scatter_sum(recv, dx, st.flags, st.counters, site, st.rank, _TIMEOUT_S)
+            _note("gemm_reduce_scatter", st, recv)
         gathered = st.local_buffer(owner, "ag.gathered", (b, r * st.world, k)).view(-1, k)
         weight, bias = ctx.weight, ctx.bias
 
@@ -253,6 +271,7 @@ class _LinearReduceScatter(torch.autograd.Function):
                             st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S, None, None)
         out = torch.empty(b, r, n, dtype=x.dtype, device=x.device)
         ext.reduce_scatter_sum(recv, out, st.flags, st.counters, site, st.rank, _TIMEOUT_S)
+        _note("gemm_reduce_scatter", st, recv)
         ctx.save_for_backward(x2, w)
         ctx.st, ctx.owner, ctx.dims, ctx.weight = st, owner, (b, s, kr, n), weight
         return out
@@ -277,6 +296,7 @@ class _LinearReduceScatter(torch.autograd.Function):
         dx = torch.empty(b * s, kr, dtype=dout.dtype, device=dout.device)
         ext.gemm_collective(slot, w, dx, None, None, False, True, EPI_PLAIN, 0.0, 1, ptrs, 0, [], 0, [],
                             st.flags, st.flag_ptrs, st.counters, site, 1, st.rank, _TIMEOUT_S, gathered, flags)
+        _note("all_gather_gemm", st, slot)
         weight = ctx.weight
         g2 = gathered.view(b * s, n)
 

@@ -2,6 +2,8 @@
 #include <torch/extension.h>
 
 namespace ht {
+void set_deterministic_reductions(bool on);
+bool deterministic_reductions();
 void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
           c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta);
 at::Tensor gemm_error_word(at::Tensor like);
@@ -33,7 +35,7 @@ void cross_entropy_stats(at::Tensor logits, at::Tensor targets, at::Tensor stats
 void cross_entropy_combine(at::Tensor gathered, at::Tensor lse, at::Tensor loss, int64_t world, double scale);
 void cross_entropy_grad(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor grad, int64_t vocab_start, double scale);
 void adamw_flat(at::Tensor param, at::Tensor grad, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> copy, at::Tensor hyper,
-                double beta1, double beta2, double eps, double wd);
+                double beta1, double beta2, double eps, double wd, bool resident);
 void grad_sumsq(at::Tensor g, c10::optional<at::Tensor> w, at::Tensor out, double scale);
 void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
 void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv,
@@ -75,6 +77,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_combine", &ht::cross_entropy_combine);
   m.def("cross_entropy_grad", &ht::cross_entropy_grad);
   m.def("adamw_flat", &ht::adamw_flat);
+  m.def("set_deterministic_reductions", &ht::set_deterministic_reductions,
+        "fixed-order split-K sums (reproducible) or TMA reduce-adds straight into the output (faster)");
+  m.def("deterministic_reductions", &ht::deterministic_reductions);
   m.def("grad_sumsq", &ht::grad_sumsq);
   m.def("attention_forward", &ht::attention_forward);
   m.def("attention_backward", &ht::attention_backward);

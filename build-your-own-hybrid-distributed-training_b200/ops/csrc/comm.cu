@@ -74,10 +74,21 @@ __device__ bool block_barrier(const Peers& pp, int rank, int world, int slot_bas
   return true;
 }
 
-__global__ void __launch_bounds__(THREADS) bucket_allreduce_kernel(Peers pp, float* mc, long long start, long long n, float scale,
-                                                                   int rank, int world, int slot_base, int* status,
-                                                                   unsigned long long timeout_ns) {
-  // chunk per rank (multiple of 4 floats), sub-range per block
+// The bucket all-reduce runs next to the persistent tcgen05 GEMM instead of waiting for it.  The GEMM
+// keeps one 320-thread CTA per SM with 168 registers per thread (53,760 of the SM's 65,536) and
+// 226 KB of the SM's 228 KB of shared memory, so what is left on every SM fits one block of
+// AR_THREADS = 128 threads with at most 88 registers each and only static shared memory.  The grid
+// is one such block per SM: the blocks are scheduled while the GEMM's CTAs are resident, and the
+// all-reduce proceeds during the backward pass rather than in the gaps between GEMMs.  Each thread
+// keeps eight 16-byte peer loads in flight (2.4 MB per GPU), which covers NVLink's latency.
+constexpr int AR_THREADS = 128;
+constexpr int AR_MIN_BLOCKS = 6;  // 65,536 / (128 x 6) -> the compiler stays at or below 85 registers
+
+template <int MAXW>
+__global__ void __launch_bounds__(AR_THREADS, AR_MIN_BLOCKS)
+    bucket_allreduce_kernel(Peers pp, float* mc, long long start, long long n, float scale, int rank, int world, int slot_base,
+                            int* status, unsigned long long timeout_ns) {
+  // chunk per owner rank (multiple of 4 floats), sub-range per block
   const long long chunk = ((n + world - 1) / world + 3) / 4 * 4;
   const long long per_block = ((chunk + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
   auto range = [&](int owner, long long& lo, long long& hi) {
@@ -89,68 +100,76 @@ __global__ void __launch_bounds__(THREADS) bucket_allreduce_kernel(Peers pp, flo
   long long lo, hi;
   range(rank, lo, hi);
   if (mc != nullptr) {
-    for (long long i = lo + threadIdx.x * 4; i < hi; i += THREADS * 4) {
-      float* addr = mc + start + i;
-      if (i + 3 < hi) {
-        float a, b, c, d;
-        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
-                     : "=f"(a), "=f"(b), "=f"(c), "=f"(d)
-                     : "l"(addr)
-                     : "memory");
-        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(addr), "f"(a * scale), "f"(b * scale),
-                     "f"(c * scale), "f"(d * scale)
-                     : "memory");
-      } else {
-        for (long long j = i; j < hi; ++j) {
-          float a;
-          float* aj = mc + start + j;
-          asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(a) : "l"(aj) : "memory");
-          asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(aj), "f"(a * scale) : "memory");
+    // NVLink-switch reduction: the switch sums the G copies (ld_reduce) and writes the result to
+    // every rank (st); each rank handles its own chunk.  Eight vectors per thread in flight.  The
+    // gradients were written through the unicast address and are read through the multicast one,
+    // two virtual aliases of the same memory: the alias fence orders the two views.
+    asm volatile("fence.proxy.alias;" ::: "memory");
+    constexpr int U = 8;
+    constexpr long long STEP = (long long)AR_THREADS * 4 * U;
+    for (long long i0 = lo + threadIdx.x * 4; i0 < hi; i0 += STEP) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long i = i0 + (long long)u * AR_THREADS * 4;
+        if (i + 3 < hi)
+          asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+                       : "=f"(v[u].x), "=f"(v[u].y), "=f"(v[u].z), "=f"(v[u].w)
+                       : "l"(mc + start + i)
+                       : "memory");
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long i = i0 + (long long)u * AR_THREADS * 4;
+        if (i + 3 < hi) {
+          asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc + start + i), "f"(v[u].x * scale),
+                       "f"(v[u].y * scale), "f"(v[u].z * scale), "f"(v[u].w * scale)
+                       : "memory");
+        } else {
+          for (long long j = i; j < hi; ++j) {  // ragged tail of the range
+            float a;
+            asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(a) : "l"(mc + start + j) : "memory");
+            asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc + start + j), "f"(a * scale) : "memory");
+          }
         }
       }
     }
+    asm volatile("fence.proxy.alias;" ::: "memory");
     block_barrier(pp, rank, world, slot_base, status, 2, timeout_ns);
     return;
   }
-  // two-shot: reduce-scatter my chunk.  Each thread keeps UNROLL independent 16-byte vectors
-  // (UNROLL x world peer loads) in flight: the loop is bound by NVLink latency otherwise.
-  constexpr int UNROLL = 4;
-  constexpr long long STEP = (long long)THREADS * 4 * UNROLL;
+  // Two-shot over P2P loads.  Reduce-scatter: this rank sums its chunk over all peers (fixed rank
+  // order, so every rank's copy of the result is bitwise identical) and scales it.
+  constexpr int U = 8 / MAXW > 0 ? 8 / MAXW : 1;  // vectors per peer in flight
+  constexpr long long STEP = (long long)AR_THREADS * 4 * U;
   for (long long i0 = lo + threadIdx.x * 4; i0 < hi; i0 += STEP) {
-    float4 acc[UNROLL];
-    bool vec[UNROLL];
+    float4 acc[U];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      const long long i = i0 + (long long)u * THREADS * 4;
-      vec[u] = i + 3 < hi;
-      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 v[MAXW][U];
 #pragma unroll
-    for (int p = 0; p < MAX_RANKS; ++p) {
-      if (p >= world) break;
-      float4 v[UNROLL];
+    for (int p = 0; p < MAXW; ++p)
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u)
-        if (vec[u]) v[u] = *reinterpret_cast<const float4*>(pp.buf[p] + start + i0 + (long long)u * THREADS * 4);
-#pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        if (vec[u]) {
-          acc[u].x += v[u].x;
-          acc[u].y += v[u].y;
-          acc[u].z += v[u].z;
-          acc[u].w += v[u].w;
-        }
+      for (int u = 0; u < U; ++u) {
+        const long long i = i0 + (long long)u * AR_THREADS * 4;
+        if (p < world && i + 3 < hi) v[p][u] = *reinterpret_cast<const float4*>(pp.buf[p] + start + i);
       }
-    }
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      const long long i = i0 + (long long)u * THREADS * 4;
-      if (vec[u]) {
-        acc[u].x *= scale;
-        acc[u].y *= scale;
-        acc[u].z *= scale;
-        acc[u].w *= scale;
-        *reinterpret_cast<float4*>(pp.buf[rank] + start + i) = acc[u];
+    for (int p = 0; p < MAXW; ++p)
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (p < world) {
+          acc[u].x += v[p][u].x;
+          acc[u].y += v[p][u].y;
+          acc[u].z += v[p][u].z;
+          acc[u].w += v[p][u].w;
+        }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long i = i0 + (long long)u * AR_THREADS * 4;
+      if (i + 3 < hi) {
+        *reinterpret_cast<float4*>(pp.buf[rank] + start + i) =
+            make_float4(acc[u].x * scale, acc[u].y * scale, acc[u].z * scale, acc[u].w * scale);
       } else {
         for (long long j = i; j < hi; ++j) {  // ragged tail of the range
           float sum = 0.f;
@@ -161,20 +180,22 @@ __global__ void __launch_bounds__(THREADS) bucket_allreduce_kernel(Peers pp, flo
     }
   }
   if (!block_barrier(pp, rank, world, slot_base, status, 2, timeout_ns)) return;
-  // all-gather the other ranks' reduced chunks
+  // All-gather: copy every peer's reduced chunk (8 vectors in flight per thread).
+  constexpr int UG = 8;
+  constexpr long long STEPG = (long long)AR_THREADS * 4 * UG;
   for (int q = 1; q < world; ++q) {
     const int p = (rank + q) % world;
     range(p, lo, hi);
-    for (long long i0 = lo + threadIdx.x * 4; i0 < hi; i0 += STEP) {
-      float4 v[UNROLL];
+    for (long long i0 = lo + threadIdx.x * 4; i0 < hi; i0 += STEPG) {
+      float4 v[UG];
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        const long long i = i0 + (long long)u * THREADS * 4;
+      for (int u = 0; u < UG; ++u) {
+        const long long i = i0 + (long long)u * AR_THREADS * 4;
         if (i + 3 < hi) v[u] = *reinterpret_cast<const float4*>(pp.buf[p] + start + i);
       }
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        const long long i = i0 + (long long)u * THREADS * 4;
+      for (int u = 0; u < UG; ++u) {
+        const long long i = i0 + (long long)u * AR_THREADS * 4;
         if (i + 3 < hi) *reinterpret_cast<float4*>(pp.buf[rank] + start + i) = v[u];
         else
           for (long long j = i; j < hi; ++j) pp.buf[rank][start + j] = pp.buf[p][start + j];
@@ -417,12 +438,24 @@ void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::v
     pp.buf[p] = reinterpret_cast<float*>(buffer_ptrs[p]);
     pp.pad[p] = reinterpret_cast<uint32_t*>(pad_ptrs[p]);
   }
+  // One block per SM (the blocks co-reside with a running GEMM, see bucket_allreduce_kernel), fewer
+  // when the bucket is small.  Every block waits on its peers, and all of them fit on the GPU at once.
   const long long chunk = (numel + world - 1) / world;
-  const int blocks =
-      (int)std::max<long long>(1, std::min<long long>(max_blocks, (chunk + comm::THREADS * 8 - 1) / (comm::THREADS * 8)));
-  comm::bucket_allreduce_kernel<<<blocks, comm::THREADS, 0, stream()>>>(
-      pp, reinterpret_cast<float*>(multicast_ptr), start, numel, (float)scale, (int)rank, world, (int)slot_base,
-      status.data_ptr<int>(), (unsigned long long)(timeout_s * 1e9));
+  const int blocks = (int)std::max<long long>(
+      1, std::min<long long>(std::min<long long>(max_blocks, num_sms()), (chunk + comm::AR_THREADS * 32 - 1) / (comm::AR_THREADS * 32)));
+  auto launch = [&](auto kernel) {
+    static bool configured = false;  // per instantiation: prefer the shared-memory carveout of the GEMM it runs beside
+    if (!configured) {
+      HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared));
+      configured = true;
+    }
+    kernel<<<blocks, comm::AR_THREADS, 0, stream()>>>(pp, reinterpret_cast<float*>(multicast_ptr), start, numel, (float)scale,
+                                                      (int)rank, world, (int)slot_base, status.data_ptr<int>(),
+                                                      (unsigned long long)(timeout_s * 1e9));
+  };
+  if (world <= 2) launch(comm::bucket_allreduce_kernel<2>);
+  else if (world <= 4) launch(comm::bucket_allreduce_kernel<4>);
+  else launch(comm::bucket_allreduce_kernel<8>);
   HT_CUDA_CHECK(cudaGetLastError());
 }
 

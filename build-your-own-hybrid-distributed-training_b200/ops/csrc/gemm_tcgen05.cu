@@ -1017,6 +1017,16 @@ static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
 
 }  // namespace tcg
 
+// Split-K GEMMs with an fp32 output either sum their partial tiles in a fixed order (a workspace
+// and a reduction pass: bitwise reproducible), or, when reproducibility is switched off, add every
+// partial tile straight into D with TMA fp32 reduce-adds (D zeroed first for beta = 0): no
+// workspace and no extra pass, but the order of the partial sums varies from run to run.
+static bool g_ordered_split_k = true;
+
+void set_deterministic_reductions(bool on) { g_ordered_split_k = on; }
+
+bool deterministic_reductions() { return g_ordered_split_k; }
+
 void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
           c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta) {
   using namespace tcg;
@@ -1076,7 +1086,17 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   const int splits = (epilogue == kPlain && ep.bias_f32 == nullptr && ep.bias_bf16 == nullptr) ? choose_splits(tiles, kblocks, num_sms()) : 1;
   at::Tensor workspace;
   const int64_t split_rows = (M + BM - 1) / BM * BM, ldw = (N + 3) / 4 * 4;
-  if (splits > 1) {
+  const bool split_reduce_add = splits > 1 && !g_ordered_split_k && d32 && ep.vec_ok && (beta == 0.0 || beta == 1.0);
+  if (split_reduce_add) {
+    if (beta == 0.0)
+      HT_CUDA_CHECK(cudaMemset2DAsync(d.data_ptr(), (size_t)d.stride(0) * 4, 0, (size_t)N * 4, (size_t)M, stream()));
+    md = make_out_map(d.data_ptr(), M, N, d.stride(0), true);
+    ep.splits = splits;
+    ep.split_rows = 0;  // every split adds into the same rows of D
+    ep.tma_d = 1;
+    ep.reduce_add = 1;
+    ep.beta = 0.f;
+  } else if (splits > 1) {
     workspace = at::empty({splits * split_rows, ldw}, a.options().dtype(at::kFloat));
     md = make_out_map(workspace.data_ptr(), splits * split_rows, N, ldw, true);
     ep.splits = splits;
@@ -1098,7 +1118,7 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, md, maux, M, N, K, ep, err, s);
   else if (a_mn_major && b_mn_major) launch<true, true>(ma, mb, md, maux, M, N, K, ep, err, s);
   else launch<true, false>(ma, mb, md, maux, M, N, K, ep, err, s);
-  if (splits > 1) {
+  if (splits > 1 && !split_reduce_add) {
     const long long work = M * ((N + 3) / 4);
     const int blocks = (int)std::min<long long>((work + 255) / 256, 8LL * num_sms());
     const uintptr_t dp = reinterpret_cast<uintptr_t>(d.data_ptr());

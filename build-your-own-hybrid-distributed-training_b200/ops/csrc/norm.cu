@@ -39,8 +39,10 @@ __device__ __forceinline__ void st<float>(float* p, long long i, float v) { p[i]
 template <>
 __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, long long i, float v) { p[i] = f2bf(v); }
 
+// The CTA-per-row kernels launch up to 1024 threads (8192 columns at 8 per thread); the bound keeps
+// the compiler at 64 registers per thread so that the widest row fits one SM's register file.
 template <bool RMS, typename DeltaT, typename WT, typename OutT>
-__global__ void norm_forward_kernel(const float* __restrict__ res, const DeltaT* __restrict__ delta, const WT* __restrict__ w,
+__global__ void __launch_bounds__(1024) norm_forward_kernel(const float* __restrict__ res, const DeltaT* __restrict__ delta, const WT* __restrict__ w,
                                     const WT* __restrict__ b, float* __restrict__ r_out, OutT* __restrict__ y,
                                     float* __restrict__ mean_out, float* __restrict__ rstd_out, int d, float eps) {
   __shared__ float scratch[32];
@@ -87,7 +89,7 @@ __global__ void norm_forward_kernel(const float* __restrict__ res, const DeltaT*
 }
 
 template <bool RMS, typename DyT, typename WT, typename DdT>
-__global__ void norm_backward_kernel(const DyT* __restrict__ dy, const float* __restrict__ dr_in, const float* __restrict__ r,
+__global__ void __launch_bounds__(1024) norm_backward_kernel(const DyT* __restrict__ dy, const float* __restrict__ dr_in, const float* __restrict__ r,
                                      const WT* __restrict__ w, const float* __restrict__ mean, const float* __restrict__ rstd,
                                      float* __restrict__ dres, DdT* __restrict__ ddelta, float* __restrict__ part_w,
                                      float* __restrict__ part_b, int rows, int d) {

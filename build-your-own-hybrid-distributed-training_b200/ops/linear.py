@@ -100,6 +100,16 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None, o
     return out
 
 
+def set_deterministic_reductions(on: bool) -> None:
+    """Choose fixed-order split-K sums (bitwise reproducible, the default) or direct fp32 reduce-adds (faster).
+
+    Affects the native GEMM's split-K path for fp32 outputs (weight gradients): with ``on=False`` every
+    partial tile is added into the output by TMA reduce-adds, so no workspace or reduction pass is
+    needed, but the order of the additions, and so the last bits, varies between runs.
+    """
+    extension().set_deterministic_reductions(bool(on))
+
+
 def gelu_backward(grad: torch.Tensor, pre: torch.Tensor) -> torch.Tensor:
     """``grad * gelu_tanh'(pre)`` (bf16 in, bf16 out on CUDA)."""
     if not grad.is_cuda:

@@ -41,10 +41,14 @@ def reference_adamw(param: torch.Tensor, grad: torch.Tensor, exp_avg: torch.Tens
 
 def adamw_flat(param: torch.Tensor, grad: torch.Tensor, exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor,
                compute_copy: torch.Tensor | None, hyper: torch.Tensor, *, beta1: float, beta2: float, eps: float,
-               weight_decay: float) -> None:
-    """One fused AdamW step over flat CUDA buffers; ``hyper`` = ``[lr, step, grad_scale, skip]`` (fp32, device)."""
+               weight_decay: float, resident: bool = False) -> None:
+    """One fused AdamW step over flat CUDA buffers; ``hyper`` = ``[lr, step, grad_scale, skip]`` (fp32, device).
+
+    ``resident=True`` launches the small-footprint form (one 128-thread block per SM) that runs
+    beside a persistent GEMM, for slices updated during the backward pass.
+    """
     extension().adamw_flat(param, grad, exp_avg, exp_avg_sq, compute_copy, hyper, float(beta1), float(beta2), float(eps),
-                           float(weight_decay))
+                           float(weight_decay), bool(resident))
 
 
 def grad_sumsq(grad: torch.Tensor, weights: torch.Tensor | None, out: torch.Tensor, scale: float = 1.0) -> None:

@@ -44,8 +44,8 @@ def build_inner_optimizer(parameters: Iterable[nn.Parameter], config: OptimizerC
     """AdamW (flat, fused) or SGD over the trainable parameters."""
     params = [p for p in parameters if p.requires_grad]
     if not params:
-        raise ShardingError(format_error("optim.build_inner_optimizer", "no trainable parameters were supplied",
-                                         expected=">= 1 parameter with requires_grad=True", observed=0,
+        raise ShardingError(format_error("optim.build_inner_optimizer", "the optimizer was given nothing to train",
+                                         expected="one or more parameters that require gradients", observed=0,
                                          resolution="wrap the model before building the optimizer"))
     b1, b2 = float(config.betas[0]), float(config.betas[1])
     if config.name == "adamw":
@@ -83,8 +83,8 @@ def _grad_of(p: nn.Parameter) -> torch.Tensor | None:
 
 def build_gradient_norm_contributions(parameters: Sequence[nn.Parameter], *, world_size: int) -> list[NormContribution]:
     if world_size < 1:
-        raise ShardingError(format_error("optim.build_gradient_norm_contributions", "world_size must be positive", expected=">= 1",
-                                         observed=world_size, resolution="pass the size of the reduction group"))
+        raise ShardingError(format_error("optim.build_gradient_norm_contributions", "the reduction group has at least one rank", expected=">= 1",
+                                         observed=world_size, resolution="give the number of ranks in the norm group"))
     out = []
     for i, p in enumerate(parameters):
         vector = getattr(p, "gradient_norm_scale_vector", None)
@@ -233,9 +233,9 @@ class ShardedOptimizer:
     def load_state_dict(self, payload: dict[str, Any]) -> None:
         expected, observed = len(self._parameters), int(payload.get("num_parameters", -1))
         if observed != expected:
-            raise ShardingError(format_error("optim.load_state_dict", "the checkpoint holds optimizer state for a different number "
-                                             "of parameters", rank=self._norm_group.global_rank, expected=expected, observed=observed,
-                                             resolution="resume with the same model definition and wrapping granularity"))
+            raise ShardingError(format_error("optim.load_state_dict", "the saved optimizer state does not match this "
+                                             "optimizer's parameter count", rank=self._norm_group.global_rank, expected=expected, observed=observed,
+                                             resolution="restore into the same model, wrapped into the same units"))
         target = self._cpu_parameters if self._offload else self._parameters
         groups = []
         for saved, existing in zip(payload["param_groups"], self._optimizer.state_dict()["param_groups"]):
@@ -253,6 +253,11 @@ class ShardedOptimizer:
     def refresh_compute_copies(self) -> None:
         if isinstance(self._optimizer, FusedAdamW):
             self._optimizer.refresh_compute_copies()
+
+    @property
+    def offloaded(self) -> bool:
+        """Whether the master parameters and optimizer state live in host memory."""
+        return self._offload
 
     def __repr__(self) -> str:
         return (f"ShardedOptimizer({self._config.name}, params={len(self._parameters)}, norm_group={self._norm_group.name!r}, "

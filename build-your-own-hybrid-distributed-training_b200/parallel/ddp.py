@@ -52,6 +52,7 @@ from ..distributed.collectives import (
     assert_metadata_consistent,
     assert_tensor_consistent,
     broadcast,
+    record_collective,
 )
 from ..distributed.groups import GroupHandle
 from ..errors import ShardingError, format_error
@@ -157,8 +158,8 @@ class DistributedDataParallel(nn.Module):
                 self._named_parameters.append((name, p))
         if not self._named_parameters:
             raise ShardingError(format_error("ddp.__init__", "the module has no trainable parameters to synchronise",
-                                             rank=group.global_rank, expected=">= 1 parameter with requires_grad=True",
-                                             observed=0, resolution="wrap a module that has trainable parameters"))
+                                             rank=group.global_rank, expected="one or more parameters that require gradients",
+                                             observed=0, resolution="DDP only makes sense for a module with something to train"))
         self._name_of = {id(p): n for n, p in self._named_parameters}
         self._buckets: list[GradientBucket] = []
         self._bucket_of: dict[int, tuple[GradientBucket, int]] = {}
@@ -169,9 +170,12 @@ class DistributedDataParallel(nn.Module):
         self._statistics = DDPStatistics()
         self._workspace = workspace if (self._config.fused_allreduce and not group.is_trivial) else None
         self._comm_stream: torch.cuda.Stream | None = None
+        # Called as hook(start, numel) on the communication stream right after a bucket's all-reduce
+        # was issued (flat-buffer coordinates): the optimizer updates the bucket during the backward.
+        self.post_reduction_hook: Any = None
         if self._config.check_parameter_consistency:
             signature = [(n, tuple(p.shape), str(p.dtype)) for n, p in self._named_parameters]
-            assert_metadata_consistent(signature, group, name="the (name, shape, dtype) list of trainable parameters",
+            assert_metadata_consistent(signature, group, name="the names, shapes and dtypes of the trainable parameters",
                                        operation="ddp.verify_parameter_structure")
         self._broadcast_initial_state()
         self._build_buckets()
@@ -234,7 +238,7 @@ class DistributedDataParallel(nn.Module):
                 p.main_grad_fresh = True
         if self._config.check_parameter_consistency:
             assert_metadata_consistent([b.layout.as_dict() for b in self._buckets], self._group,
-                                       name="the gradient bucket layout", operation="ddp.verify_bucket_layout")
+                                       name="the bucket assignment of every gradient", operation="ddp.verify_bucket_layout")
 
     def _register_hooks(self) -> None:
         for _, p in self._named_parameters:
@@ -265,7 +269,7 @@ class DistributedDataParallel(nn.Module):
             raise ShardingError(format_error(
                 "ddp.on_grad_ready", "a gradient arrived for a bucket already reduced this iteration; backward() ran twice "
                 "without a synchronisation boundary", rank=self._group.global_rank,
-                expected="one backward() per finish_gradient_synchronization()", observed=f"bucket {bucket.layout.index}",
+                expected="a single backward() between two synchronisations", observed=f"bucket {bucket.layout.index}",
                 resolution="call finish_gradient_synchronization() after each backward(), or use no_sync()"))
         bucket.pending -= 1
         if bucket.pending == 0:
@@ -297,14 +301,25 @@ class DistributedDataParallel(nn.Module):
             with torch.cuda.stream(self._comm_stream):
                 status = bucket_all_reduce(self._workspace, self._flat_grad, bucket.start, bucket.layout.total_numel,
                                            1.0 / self._group.size if average else 1.0)
+                if self.post_reduction_hook is not None:
+                    self.post_reduction_hook(bucket.start, bucket.layout.total_numel)
                 event = torch.cuda.Event()
                 event.record(self._comm_stream)
             bucket.work = _FusedLaunch(event, status)  # type: ignore[assignment]
-            if self._recorder is not None:
-                self._recorder.record("all_reduce", self._group.name, num_bytes=bucket.num_bytes())
+            record_collective(self._recorder, "all_reduce_nvlink", self._group.name, num_bytes=bucket.num_bytes())
         else:
             bucket.work = all_reduce(bucket.buffer, self._group, op=ReduceOp.AVG if average else ReduceOp.SUM,
                                      async_op=self._config.async_reduction, recorder=self._recorder)
+            if self.post_reduction_hook is not None and bucket.buffer.is_cuda:
+                if self._comm_stream is None:
+                    self._comm_stream = torch.cuda.Stream(device=bucket.buffer.device, priority=-1)
+                self._comm_stream.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(self._comm_stream):
+                    bucket.work.wait()  # this stream waits for the reduction
+                    self.post_reduction_hook(bucket.start, bucket.layout.total_numel)
+                    event = torch.cuda.Event()
+                    event.record(self._comm_stream)
+                bucket.work = _FusedLaunch(event, None)  # type: ignore[assignment]
         bucket.launched = True
         self._statistics.buckets_reduced += 1
         self._statistics.bytes_reduced += bucket.num_bytes()
@@ -331,9 +346,9 @@ class DistributedDataParallel(nn.Module):
                 bucket.ready = True
         if missing and not self._config.find_unused_parameters:
             raise ShardingError(format_error(
-                "ddp.finish_gradient_synchronization", "some parameters received no gradient, so their buckets can never "
-                "become ready and the all-reduce would never be issued", rank=self._group.global_rank,
-                world_size=self._group.size, expected="every trainable parameter to receive a gradient",
+                "ddp.finish_gradient_synchronization", "parameters without a gradient leave their buckets incomplete, so those "
+                "buckets would never be reduced", rank=self._group.global_rank,
+                world_size=self._group.size, expected="a gradient for each trainable parameter",
                 observed=f"{len(missing)} without gradients: {missing[:8]}",
                 resolution="set DDPConfig(find_unused_parameters=True), or stop marking unused parameters trainable"))
         self._statistics.unused_parameters = tuple(missing)
@@ -343,12 +358,10 @@ class DistributedDataParallel(nn.Module):
                 raise ShardingError(format_error("ddp.finish_gradient_synchronization",
                                                  f"bucket {bucket.layout.index} never became ready", rank=self._group.global_rank,
                                                  expected="all buckets ready", observed=f"{bucket.pending} parameters pending",
-                                                 resolution="this indicates a bug in the bucket bookkeeping"))
+                                                 resolution="the bucket counters are inconsistent (an internal error)"))
         for bucket in self._buckets:
             if bucket.work is not None:
                 bucket.work.wait()
-        if self._workspace is not None and not torch.cuda.is_current_stream_capturing():
-            self._workspace.check_status()
         for bucket in self._buckets:
             for pos, p in enumerate(bucket.parameters):
                 p.grad = bucket.view_for(pos).to(p.dtype) if p.dtype != bucket.buffer.dtype else bucket.view_for(pos)
@@ -358,13 +371,23 @@ class DistributedDataParallel(nn.Module):
         self._backward_in_progress = False
         self._statistics.steps += 1
 
+    def check_collective_status(self) -> None:
+        """Raise :class:`KernelError` if an in-kernel bucket all-reduce gave up waiting for a peer.
+
+        Reads the workspace's device status word (a host synchronisation).  The training engine
+        reads it together with the step's loss; code that drives this module directly calls it
+        after the steps it wants checked.
+        """
+        if self._workspace is not None:
+            self._workspace.check_status()
+
     # -- forward / context managers ----------------------------------------------------------------
     def forward(self, *args: Any, **kwargs: Any) -> Any:
         if self._backward_in_progress and self._require_backward_grad_sync:
             raise ShardingError(format_error(
-                "ddp.forward", "a previous backward pass has not been synchronised; stepping now would use gradients "
-                "that were never averaged", rank=self._group.global_rank,
-                expected="finish_gradient_synchronization() after every backward()", observed="pending bucket reductions",
+                "ddp.forward", "the last backward pass was never synchronised, so its gradients are "
+                "still per-rank", rank=self._group.global_rank,
+                expected="finish_gradient_synchronization() to close each backward()", observed="buckets still waiting for their reduction",
                 resolution="call finish_gradient_synchronization() before the next forward"))
         if self._config.broadcast_buffers and self.training:
             src = self._config.source_rank_in_group
@@ -396,6 +419,11 @@ class DistributedDataParallel(nn.Module):
         return self._statistics
 
     @property
+    def communication_stream(self) -> torch.cuda.Stream | None:
+        """The stream bucket reductions (and their post-reduction hooks) are issued on, once created."""
+        return self._comm_stream
+
+    @property
     def flat_gradient_buffer(self) -> torch.Tensor:
         return self._flat_grad
 
@@ -404,7 +432,7 @@ class DistributedDataParallel(nn.Module):
 
     def communication_summary(self) -> str:
         if self._recorder is None:
-            return "communication recording is disabled (pass recorder= to enable it)"
+            return "no recorder attached: construct with recorder=CommunicationRecorder() to count collectives"
         return self._recorder.summary()
 
     def parameters_and_names(self) -> tuple[tuple[str, nn.Parameter], ...]:

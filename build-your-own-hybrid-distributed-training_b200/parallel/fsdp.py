@@ -53,6 +53,7 @@ from ..distributed.collectives import (
     assert_metadata_consistent,
     broadcast,
     reduce_scatter_tensor,
+    record_collective,
 )
 from ..distributed.groups import GroupHandle
 from ..errors import ParameterConsistencyError, ShardingError, UnsupportedFeatureError, format_error
@@ -151,14 +152,14 @@ class FlatParamHandle:
                  sequence_group: GroupHandle | None = None) -> None:
         rank = shard_group.global_rank
         if not named_parameters:
-            raise ShardingError(format_error("fsdp.FlatParamHandle", "an FSDP unit needs at least one parameter", rank=rank,
-                                             expected=">= 1", observed=0, resolution="do not create a unit for a parameter-free module"))
+            raise ShardingError(format_error("fsdp.FlatParamHandle", "a sharding unit without parameters has nothing to shard", rank=rank,
+                                             expected=">= 1", observed=0, resolution="only wrap modules that own parameters"))
         flags = {bool(p.requires_grad) for _, p in named_parameters}
         if len(flags) > 1:
             frozen = [n for n, p in named_parameters if not p.requires_grad]
             raise UnsupportedFeatureError(format_error(
                 "fsdp.FlatParamHandle", "all parameters of a unit share one flat tensor and therefore one requires_grad flag",
-                rank=rank, expected="a uniform requires_grad within the unit", observed=f"frozen parameters present: {frozen[:8]}",
+                rank=rank, expected="all parameters of a unit trainable, or all frozen", observed=f"frozen: {frozen[:8]}",
                 resolution="wrap the frozen submodule as its own unit, or unfreeze it"))
         self._shard_group, self._replica_group, self._sequence_group = shard_group, replica_group, sequence_group
         self._config, self._mixed_precision, self._device, self._recorder = config, mixed_precision, device, recorder
@@ -180,7 +181,7 @@ class FlatParamHandle:
             gathered = self._padded_numel * torch.empty(0, dtype=self._compute_dtype).element_size()
             if gathered > config.limit_all_gather_bytes:
                 raise ShardingError(format_error(
-                    "fsdp.FlatParamHandle", "this unit's all-gather would exceed limit_all_gather_bytes", rank=rank,
+                    "fsdp.FlatParamHandle", "gathering this unit needs more bytes than limit_all_gather_bytes allows", rank=rank,
                     expected=f"<= {config.limit_all_gather_bytes} bytes", observed=gathered,
                     resolution="lower auto_wrap_min_num_params to split the model into more units, or raise the limit"))
         self._sp_ranges = [(e.offset, e.numel) for e, p in zip(self._entries, self._params)
@@ -267,8 +268,8 @@ class FlatParamHandle:
 
             assert self._sym_shard is not None
             fsdp_all_gather(self._fused[0], self._sym_shard, full, copy_engine=background)
-            if self._recorder is not None:
-                self._recorder.record("fsdp_all_gather_p2p", self._shard_group.name, num_bytes=full.numel() * full.element_size())
+            record_collective(self._recorder, "fsdp_all_gather_p2p", self._shard_group.name,
+                              num_bytes=full.numel() * full.element_size())
             return
         _, work = all_gather_tensor(self._compute_shard(shard), self._shard_group, out=full, recorder=self._recorder)
         work.wait()
@@ -324,7 +325,7 @@ class FlatParamHandle:
             raise UnsupportedFeatureError(format_error(
                 "fsdp.reshard", "this PyTorch lacks torch.autograd._unsafe_preserve_version_counter, needed to refill a "
                 "freed flat parameter during backward", rank=self._shard_group.global_rank,
-                resolution="set FSDPConfig(reshard_after_forward=False)"))
+                resolution="use reshard_after_forward=False in the FSDP config"))
         _free_storage(self._full)
         self._is_sharded = True
 
@@ -382,9 +383,8 @@ class FlatParamHandle:
                                   param=self.flat_param.data, exp_avg=state["exp_avg"], exp_avg_sq=state["exp_avg_sq"],
                                   hyper=optimizer.hyper_parameters, betas=group["betas"], eps=group["eps"],
                                   weight_decay=group["weight_decay"])
-        if self._recorder is not None:
-            self._recorder.record("fsdp_reduce_scatter_adamw", self._shard_group.name,
-                                  num_bytes=self._padded_numel * staging.element_size())
+        record_collective(self._recorder, "fsdp_reduce_scatter_adamw", self._shard_group.name,
+                          num_bytes=self._padded_numel * staging.element_size())
         self._reduction_count += 1
 
     # -- gradient reduction --------------------------------------------------------------------------------
@@ -473,9 +473,9 @@ class FlatParamHandle:
         for e in self._entries:
             t = pieces.get(e.name)
             if t is None:
-                raise ShardingError(format_error("fsdp.load_local_pieces", "missing parameter in the state dict",
+                raise ShardingError(format_error("fsdp.load_local_pieces", "the state dict has no entry for a parameter",
                                                  rank=self._shard_group.global_rank, expected=e.name, observed=sorted(pieces)[:8],
-                                                 resolution="load a state dict produced by the same model definition"))
+                                                 resolution="load state saved from the same model"))
             if tuple(t.shape) != e.shape:
                 raise ShardingError(format_error("fsdp.load_local_pieces", f"shape mismatch for {e.name!r}",
                                                  rank=self._shard_group.global_rank, expected=e.shape, observed=tuple(t.shape),
@@ -535,9 +535,9 @@ class FullyShardedDataParallel(nn.Module):
         self._recorder = recorder
         params = list(module.parameters())
         if not params:
-            raise ShardingError(format_error("fsdp.__init__", "the module has no parameters to shard",
+            raise ShardingError(format_error("fsdp.__init__", "the wrapped module owns no parameters",
                                              rank=shard_group.global_rank, expected=">= 1", observed=0,
-                                             resolution="wrap a module that has parameters"))
+                                             resolution="shard a module that owns parameters"))
         self._device = device if device is not None else params[0].device
         if sync_module_states:
             for p in module.parameters():
@@ -554,7 +554,7 @@ class FullyShardedDataParallel(nn.Module):
             self._handle = FlatParamHandle(named, locations, shard_group, self._config, self._mixed_precision, self._device,
                                            replica_group=replica_group, recorder=recorder, sequence_group=sequence_group)
             self.register_parameter("flat_param", self._handle.flat_param)
-            assert_metadata_consistent(self._handle.metadata(), shard_group, name="the flat parameter layout",
+            assert_metadata_consistent(self._handle.metadata(), shard_group, name="the flat-parameter layout of every unit",
                                        operation="fsdp.verify_flat_layout")
         self._next_unit: FullyShardedDataParallel | None = None
         self._fused_units: list[FullyShardedDataParallel] | None = None  # set on the root by enable_fused_update
@@ -706,9 +706,9 @@ class FullyShardedDataParallel(nn.Module):
             gathered = all_gather_object_in_group(order, self._shard_group)
             if any(g != gathered[0] for g in gathered):
                 raise ParameterConsistencyError(format_error(
-                    "fsdp.finish_backward", "ranks performed different numbers of reduce-scatters per unit; the collective "
-                    "streams have diverged", rank=self._shard_group.global_rank, expected=gathered[0], observed=order,
-                    resolution="make the forward pass structurally identical on every rank"))
+                    "fsdp.finish_backward", "ranks ran a different number of gradient reduce-scatters for some "
+                    "unit, so their collective sequences no longer match", rank=self._shard_group.global_rank, expected=gathered[0], observed=order,
+                    resolution="every rank has to run the same modules in the same order"))
 
     def fsdp_units(self) -> list[FullyShardedDataParallel]:
         return [m for m in self.modules() if isinstance(m, FullyShardedDataParallel)]
@@ -880,7 +880,7 @@ def reshard_state_dict_pieces(pieces: Sequence[ShardedTensorPiece], global_shape
         total *= d
     if not pieces:
         raise ShardingError(format_error("fsdp.reshard_state_dict_pieces", "no pieces supplied", expected=">= 1 piece",
-                                         observed=0, resolution="check that the manifest lists shards for this tensor"))
+                                         observed=0, resolution="the manifest should list shards for this tensor"))
     flat = torch.zeros(total, dtype=pieces[0].data.dtype)
     covered = torch.zeros(total, dtype=torch.bool)
     for piece in pieces:
@@ -888,12 +888,12 @@ def reshard_state_dict_pieces(pieces: Sequence[ShardedTensorPiece], global_shape
         if end > total:
             raise ShardingError(format_error("fsdp.reshard_state_dict_pieces", f"piece for {piece.name!r} runs past the end",
                                              expected=f"offset + length <= {total}", observed=end,
-                                             resolution="the manifest disagrees with the model definition"))
+                                             resolution="the saved layout does not fit this model"))
         flat[piece.offset:end] = piece.data.reshape(-1).to(flat.dtype)
         covered[piece.offset:end] = True
     if not bool(covered.all()):
         missing = int((~covered).sum())
         raise ShardingError(format_error("fsdp.reshard_state_dict_pieces", f"pieces leave {missing} element(s) uncovered",
                                          expected=f"{total} covered elements", observed=total - missing,
-                                         resolution="a shard file is missing from the checkpoint"))
+                                         resolution="a payload file is absent or lost entries"))
     return flat.view(global_shape)

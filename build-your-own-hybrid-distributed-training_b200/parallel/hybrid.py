@@ -131,7 +131,7 @@ def build_model(config: ExperimentConfig, context: DistributedContext, *, device
     if sp:
         raise ConfigurationError(format_error("hybrid.build_model", "the MLP has no sequence dimension to split",
                                               rank=context.rank, world_size=context.world_size,
-                                              expected="model.kind='transformer' for sequence parallelism",
+                                              expected="a transformer model (sequence parallelism splits its tokens)",
                                               observed=config.model.kind, resolution="use the transformer or disable SP"))
     return MLP(config.model, seed=config.training.seed, tensor_parallel_group=tensor if tensor.size > 1 else None, device=device)
 
@@ -327,7 +327,7 @@ class HybridModel(nn.Module):
                 raise ShardingError(format_error("hybrid.optimizer_parameter_layout",
                                                  "the FSDP flat-parameter order does not match the optimizer's parameters",
                                                  rank=self._context.rank, expected=len(params), observed=len(pairs),
-                                                 resolution="build the optimizer from model.optimizer_parameters()"))
+                                                 resolution="create the optimizer over model.optimizer_parameters()"))
             return [layout for _, layout in pairs]
         by_id = {id(p): (n, tuple(p.shape)) for n, p in _unique_named_parameters(self._inner_model).items()}
         out = []
@@ -335,9 +335,9 @@ class HybridModel(nn.Module):
             entry = by_id.get(id(p))
             if entry is None:
                 raise ShardingError(format_error("hybrid.optimizer_parameter_layout",
-                                                 "an optimizer parameter does not belong to the wrapped model", rank=self._context.rank,
-                                                 expected="a parameter of the wrapped model", observed=f"tensor {tuple(p.shape)}",
-                                                 resolution="build the optimizer from model.optimizer_parameters()"))
+                                                 "the optimizer holds a tensor that is not a parameter of this model", rank=self._context.rank,
+                                                 expected="one of the model's own parameters", observed=f"tensor {tuple(p.shape)}",
+                                                 resolution="create the optimizer over model.optimizer_parameters()"))
             out.append([PieceLayout(entry[0], entry[1], 0, p.numel(), 0)])
         return out
 

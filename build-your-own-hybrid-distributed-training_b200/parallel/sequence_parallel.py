@@ -47,8 +47,8 @@ class SequenceShardInfo:
     @classmethod
     def for_length(cls, length: int, group_size: int) -> SequenceShardInfo:
         if group_size < 1:
-            raise ShardingError(format_error("sequence_parallel.SequenceShardInfo", "group size must be positive",
-                                             expected=">= 1", observed=group_size, resolution="pass the sequence-parallel group size"))
+            raise ShardingError(format_error("sequence_parallel.SequenceShardInfo", "a group has at least one member",
+                                             expected=">= 1", observed=group_size, resolution="give the number of sequence ranks"))
         padded = -(-length // group_size) * group_size
         return cls(length, padded, group_size, padded // group_size)
 
@@ -84,10 +84,10 @@ def unpad_sequence_dimension(x: torch.Tensor, info: SequenceShardInfo, *, dim: i
 
 def _require_divisible(x: torch.Tensor, group: GroupHandle, dim: int, op: str) -> None:
     if x.shape[dim] % group.size:
-        raise ShardingError(format_error(op, "the sequence dimension must be divisible by the sequence-parallel size",
+        raise ShardingError(format_error(op, "the sequence length does not split evenly over the sequence ranks",
                                          rank=group.global_rank, expected=f"{x.shape[dim]} % {group.size} == 0",
                                          observed=x.shape[dim] % group.size,
-                                         resolution="call pad_sequence_dimension() before scattering"))
+                                         resolution="pad with pad_sequence_dimension() first"))
 
 
 def scatter_sequence(x: torch.Tensor, group: GroupHandle, *, dim: int = SEQUENCE_DIM) -> torch.Tensor:

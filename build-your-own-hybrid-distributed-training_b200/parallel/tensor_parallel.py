@@ -80,7 +80,7 @@ def _divide(value: int, parts: int, *, what: str, group: GroupHandle) -> int:
             "tensor_parallel.validate_divisible",
             f"{what} must be divisible by the tensor-parallel size; uneven splits give ranks different shapes",
             rank=group.global_rank, expected=f"{what} % {parts} == 0", observed=f"{what}={value}, remainder={value % parts}",
-            resolution=f"choose {what} as a multiple of {parts}, or reduce the tensor-parallel size"))
+            resolution=f"choose {what} as a multiple of {parts}, or use fewer tensor-parallel ranks"))
     return value // parts
 
 
@@ -151,7 +151,7 @@ class ColumnParallelLinear(nn.Module):
             raise TensorParallelError(format_error(
                 "tensor_parallel.ColumnParallelLinear", "sequence_parallel keeps the output feature-sharded for a row layer; "
                 "gathering it too would undo both savings", rank=group.global_rank,
-                expected="gather_output=False when sequence_parallel=True", observed="both True", resolution="set gather_output=False"))
+                expected="an ungathered output under sequence parallelism", observed="both True", resolution="leave gather_output off"))
         self.in_features, self.out_features, self.group = in_features, out_features, group
         self.gather_output, self.sequence_parallel, self.activation = gather_output, sequence_parallel, activation
         self.output_features_per_partition = _divide(out_features, group.size, what="out_features", group=group)
@@ -204,16 +204,16 @@ class ColumnParallelLinear(nn.Module):
 
 def _check_shape(layer: nn.Module, linear: nn.Linear) -> None:
     if tuple(linear.weight.shape) != (layer.out_features, layer.in_features):
-        raise TensorParallelError(format_error("tensor_parallel.load_from_linear", "weight shape mismatch",
+        raise TensorParallelError(format_error("tensor_parallel.load_from_linear", "the weight has another shape",
                                                rank=layer.group.global_rank, expected=(layer.out_features, layer.in_features),
-                                               observed=tuple(linear.weight.shape), resolution="the reference layer has different features"))
+                                               observed=tuple(linear.weight.shape), resolution="the dense layer has other feature sizes"))
 
 
 def _require_bias(layer: nn.Module, linear: nn.Linear) -> None:
     if linear.bias is None:
         raise TensorParallelError(format_error("tensor_parallel.load_from_linear", "this layer has a bias but the reference does not",
                                                rank=layer.group.global_rank, expected="a bias tensor", observed=None,
-                                               resolution="construct the parallel layer with bias=False"))
+                                               resolution="build the parallel layer without a bias"))
 
 
 class RowParallelLinear(nn.Module):

@@ -46,8 +46,8 @@ class Batch:
 class SyntheticDataset:
     def __init__(self, num_samples: int, seed: int) -> None:
         if num_samples < 1:
-            raise ConfigurationError(format_error("data.SyntheticDataset", "a dataset needs at least one sample", expected=">= 1",
-                                                  observed=num_samples, resolution="raise num_train_samples / num_eval_samples"))
+            raise ConfigurationError(format_error("data.SyntheticDataset", "a synthetic dataset has one or more samples", expected=">= 1",
+                                                  observed=num_samples, resolution="increase the sample count in the data config"))
         self._num_samples, self._seed = num_samples, seed
         self.pin_memory = False
 
@@ -126,7 +126,7 @@ class SyntheticTokenDataset(SyntheticDataset):
 def build_dataset(model_config: ModelConfig, data_config: DataConfig, *, split: str = "train") -> SyntheticDataset:
     if split not in ("train", "eval"):
         raise ConfigurationError(format_error("data.build_dataset", "unknown split", expected=["train", "eval"], observed=split,
-                                              resolution="use 'train' or 'eval'"))
+                                              resolution="the splits are 'train' and 'eval'"))
     n = data_config.num_train_samples if split == "train" else data_config.num_eval_samples
     seed = derive_seed(data_config.seed, f"dataset-{split}")
     if model_config.kind == "transformer":
@@ -144,7 +144,7 @@ class DistributedBatchSampler:
         self.shuffle, self.seed, self.drop_last = shuffle, seed, drop_last
         self.global_batch_size = micro_batch_size * data_group.size
         if dataset_size < self.global_batch_size:
-            raise ConfigurationError(format_error("data.DistributedBatchSampler", "the dataset is smaller than one global batch",
+            raise ConfigurationError(format_error("data.DistributedBatchSampler", "there are fewer samples than one step consumes",
                                                   rank=data_group.global_rank, expected=f">= {self.global_batch_size} samples",
                                                   observed=dataset_size, resolution="raise num_train_samples or lower micro_batch_size"))
 

@@ -39,6 +39,7 @@ from ..distributed.context import DistributedContext
 from ..errors import ConfigurationError, format_error
 from ..logging import get_logger
 from ..optim.fused_adamw import FusedAdamW
+from ..optim.overlapped_step import OverlappedAdamW
 from ..optim.grad_scaler import GradScaler
 from ..optim.sharded_optimizer import ShardedOptimizer
 from ..parallel.hybrid import HybridModel, build_parallel_model
@@ -101,6 +102,11 @@ class TrainingEngine:
         # Deterministic-algorithm mode is a CPU/Gloo debugging aid; the CUDA path is deterministic by construction
         # except for the atomic-add reductions (embedding and attention dQ), which are order-dependent in the last bits.
         deterministic = cfg.training.deterministic and ctx.device.type == "cpu"
+        if ctx.device.type == "cuda":
+            from .. import ops
+
+            # Reproducible split-K sums when asked for; otherwise partial tiles are reduce-added in place.
+            ops.set_deterministic_reductions(cfg.training.deterministic)
         seed_everything(cfg.training.seed, stream="model-init", deterministic=deterministic)
         ctx.fused_tensor_collectives = bool(cfg.tensor_parallel.fused_collectives and ctx.device.type == "cuda")
         self.model = build_parallel_model(cfg, ctx, recorder=self.recorder)
@@ -113,6 +119,7 @@ class TrainingEngine:
                                               total_steps=max(cfg.training.max_steps, 1))
         self.scaler = GradScaler(cfg.mixed_precision.scaler, ctx.group("world"), ctx.device, recorder=self.recorder)
         self._fsdp_fused_update = self._enable_fsdp_fused_update()
+        self._overlap = self._enable_overlapped_step()
         self.state = TrainingState()
         self._transformer = cfg.model.kind == "transformer"
         self._fused_loss = self._transformer and cfg.model.fused_loss
@@ -126,7 +133,7 @@ class TrainingEngine:
         self.last_loss_tensor: torch.Tensor | None = None
         self.last_grad_norm_tensor: torch.Tensor | None = None
         reset_peak_memory(ctx.device)
-        _LOG.info("engine ready: %s | %d local parameters", self.model.description.strategy,
+        _LOG.info("engine built (%s), %d parameters on this rank", self.model.description.strategy,
                   sum(p.numel() for p in self.model.optimizer_parameters()))
 
     def _enable_fsdp_fused_update(self) -> bool:
@@ -147,6 +154,30 @@ class TrainingEngine:
 
     fsdp_fused_update = property(lambda self: self._fsdp_fused_update)
 
+    def _enable_overlapped_step(self) -> OverlappedAdamW | None:
+        """Update each gradient bucket during the backward pass when nothing global is needed first.
+
+        Needs the fused AdamW on CUDA without FSDP (whose reduce-scatter kernel already updates
+        during the backward), no clipping, no gradient-norm metric and no loss scaling, and
+        ``training.overlap_optimizer_step``.  Every input is configuration, so all ranks agree.
+        """
+        cfg, ctx = self.config, self.context
+        inner = self.optimizer.inner
+        if (not cfg.training.overlap_optimizer_step or ctx.device.type != "cuda" or self.model.fsdp is not None
+                or not isinstance(inner, FusedAdamW) or not inner.flat_parameters.is_cuda or cfg.training.max_grad_norm > 0
+                or cfg.training.collect_metrics or self.scaler.enabled or self.optimizer.offloaded):
+            return None
+        ddp = self.model.ddp
+        if ddp is not None:
+            if ddp.flat_gradient_buffer.untyped_storage().data_ptr() != inner.flat_gradients.untyped_storage().data_ptr():
+                return None  # the optimizer's flat space does not mirror the buckets
+            overlap = OverlappedAdamW(inner, track_parameters=False)
+            ddp.post_reduction_hook = overlap.bucket_reduced
+            return overlap
+        return OverlappedAdamW(inner, group_bytes=int(cfg.ddp.bucket_cap_mb * (1 << 20)))
+
+    overlapped_step = property(lambda self: self._overlap)
+
     # -- data ----------------------------------------------------------------------------------------------
     def _build_data(self) -> None:
         cfg = self.config
@@ -163,8 +194,8 @@ class TrainingEngine:
         need = cfg.training.gradient_accumulation_steps
         if len(self.train_loader) < need:
             raise ConfigurationError(format_error(
-                "engine.build_data", "the training set yields fewer micro-batches per epoch than one step consumes",
-                rank=self.context.rank, world_size=self.context.world_size, expected=f">= {need} micro-batches per epoch",
+                "engine.build_data", "the training set yields fewer micro-batches in one epoch than one step consumes",
+                rank=self.context.rank, world_size=self.context.world_size, expected=f">= {need} micro-batches in one epoch",
                 observed=len(self.train_loader), resolution="raise data.num_train_samples or lower gradient_accumulation_steps"))
 
     def batch_stream(self, *, host: bool = False) -> Any:
@@ -189,7 +220,7 @@ class TrainingEngine:
             self.history.append(m)
             t = self.config.training
             if t.log_every_steps > 0 and self.state.step % t.log_every_steps == 0:
-                _LOG.info("step %d/%d loss=%.6f lr=%.3e norm=%s %.3fs", self.state.step, target, m.loss, m.learning_rate,
+                _LOG.info("[%d/%d] loss %.6f | lr %.3e | grad-norm %s | %.3f s", self.state.step, target, m.loss, m.learning_rate,
                           "n/a" if m.grad_norm is None else f"{m.grad_norm:.4f}", m.seconds, extra={"primary_only": True})
             if t.eval_every_steps > 0 and self.state.step % t.eval_every_steps == 0:
                 self.state.best_eval_loss = min(self.state.best_eval_loss, self.evaluate())
@@ -213,12 +244,15 @@ class TrainingEngine:
         if self._fsdp_fused_update:
             # The update runs inside the backward pass's reduce-scatter kernels: stage [lr, step, ...] first.
             inner.stage_hyper_parameters()
+        if self._overlap is not None:
+            self._overlap.begin()
         for i, (x, y) in enumerate(micro_batches):
             ctx = self.model.no_sync() if i < n - 1 else _null()
+            armed = self._overlap.armed() if (self._overlap is not None and i == n - 1) else _null()
             with ctx:
                 with trace_range(f"step/forward {i}"):
                     loss = self._loss(x, y) / n
-                with trace_range(f"step/backward {i}"):
+                with trace_range(f"step/backward {i}"), armed:
                     self.scaler.scale(loss).backward()
             total = loss.detach() if total is None else total + loss.detach()
         with trace_range("step/finish_backward"):
@@ -232,6 +266,9 @@ class TrainingEngine:
             norm = self.optimizer.clip_grad_norm(t.max_grad_norm)
         if self._fsdp_fused_update:
             pass  # every flat shard was updated by its unit's reduce-scatter kernel
+        elif self._overlap is not None:
+            ddp = self.model.ddp
+            self._overlap.finish(ddp.communication_stream if ddp is not None else None)
         elif isinstance(inner, FusedAdamW) and inner.flat_parameters.is_cuda and not self.scaler.enabled:
             with trace_range("step/adamw"):
                 inner.launch_step()
@@ -277,12 +314,33 @@ class TrainingEngine:
             self.state.samples_seen += global_samples
         else:
             self.state.advance_step(samples=global_samples)
-        if read_metrics and self._fsdp_fused_update:
-            self.model.fsdp.check_fused_status()
-        loss = float(loss_t.item()) if read_metrics else float("nan")
-        norm = float(norm_t.item()) if (read_metrics and norm_t is not None) else None
+        loss, norm = float("nan"), None
+        if read_metrics:
+            loss, norm = self.read_step_results(loss_t, norm_t)
         self.state.last_loss = loss
         return StepMetrics(self.state.step, loss, lr, norm, time.perf_counter() - start, samples=global_samples, skipped=skipped)
+
+    def read_step_results(self, loss_t: torch.Tensor, norm_t: torch.Tensor | None) -> tuple[float, float | None]:
+        """Loss, gradient norm and the status words of every in-kernel collective, in one device-to-host read.
+
+        The status words are written by bounded waits inside the NVLink kernels (DDP bucket
+        all-reduce, FSDP reduce-scatter + AdamW, tensor-parallel GEMM collectives), also when the step
+        was replayed from a CUDA graph; a non-zero word raises :class:`KernelError` here, so a step
+        whose reduction gave up on a peer never passes as a normal one.
+        """
+        parts = [loss_t.detach().reshape(1).float()]
+        if norm_t is not None:
+            parts.append(norm_t.detach().reshape(1).float())
+        workspaces = self.context.symmetric_workspaces() if self.context.device.type == "cuda" else []
+        parts += [ws.status[:1].float() for ws in workspaces]
+        host = torch.cat(parts).cpu() if len(parts) > 1 else parts[0].cpu()
+        codes = host[len(parts) - len(workspaces):].tolist()
+        for ws, code in zip(workspaces, codes):
+            if code != 0:
+                ws.check_status()  # raises KernelError with the stage that gave up
+        loss = float(host[0])
+        norm = float(host[1]) if norm_t is not None else None
+        return loss, norm
 
     # -- CUDA graph -------------------------------------------------------------------------------------------------
     def _graph_step(self, micro: list[Batch]) -> tuple[torch.Tensor, torch.Tensor | None]:
@@ -335,7 +393,7 @@ class TrainingEngine:
         if was_training:
             self.model.train()
         loss = self.model.reduce_metric(total / max(count, 1))
-        _LOG.info("eval loss %.6f at step %d", loss, self.state.step, extra={"primary_only": True})
+        _LOG.info("evaluation at step %d: loss %.6f", loss, self.state.step, extra={"primary_only": True})
         return loss
 
     def save_checkpoint(self, directory: str | Path | None = None) -> Path:
@@ -363,10 +421,10 @@ class TrainingEngine:
         else:
             target = find_latest_checkpoint(self.config.checkpoint.directory)
         if target is None:
-            raise ConfigurationError(format_error("engine.load_checkpoint", "no checkpoint found to resume from", rank=self.context.rank,
-                                                  world_size=self.context.world_size, expected="a checkpoint directory",
+            raise ConfigurationError(format_error("engine.load_checkpoint", "there is no checkpoint to resume", rank=self.context.rank,
+                                                  world_size=self.context.world_size, expected="a directory holding a published checkpoint",
                                                   observed=self.config.checkpoint.directory,
-                                                  resolution="pass an explicit directory or set checkpoint.resume_from"))
+                                                  resolution="name the checkpoint directory, or set checkpoint.resume_from"))
         result = load_checkpoint(target, model=self.model, context=self.context, optimizer=self.optimizer, config=self.config,
                                  verify_checksums=self.config.checkpoint.verify_checksums_on_load,
                                  load_optimizer=self.config.checkpoint.save_optimizer_state,
@@ -387,7 +445,7 @@ class TrainingEngine:
 
     def communication_summary(self) -> str:
         if self.recorder is None:
-            return "communication recording disabled (set training.collect_metrics=true)"
+            return "collectives are not being counted; set training.collect_metrics to record them"
         return self.recorder.summary()
 
     def parameter_count(self) -> dict[str, int]:
@@ -396,6 +454,8 @@ class TrainingEngine:
 
     def close(self) -> None:
         self.release_graph()
+        if self._overlap is not None:
+            self._overlap.close()
         if self.model.ddp is not None:
             self.model.ddp.teardown()
 

@@ -61,12 +61,12 @@ class LearningRateSchedule:
 
     def __post_init__(self) -> None:
         if self.total_steps < 1:
-            raise ConfigurationError(format_error("training.LearningRateSchedule", "total_steps must be positive", expected=">= 1",
-                                                  observed=self.total_steps, resolution="pass TrainingConfig.max_steps"))
+            raise ConfigurationError(format_error("training.LearningRateSchedule", "the schedule needs one or more total steps", expected=">= 1",
+                                                  observed=self.total_steps, resolution="use the run length (training.max_steps)"))
         if self.config.warmup_steps >= self.total_steps and self.config.name != "constant":
             raise ConfigurationError(format_error("training.LearningRateSchedule", "warm-up lasts the whole run, so decay never starts",
                                                   expected=f"warmup_steps < {self.total_steps}", observed=self.config.warmup_steps,
-                                                  resolution="shorten the warm-up or lengthen the run"))
+                                                  resolution="make warm-up shorter than the run"))
 
     def value_at(self, step: int) -> float:
         warm = self.config.warmup_steps

@@ -83,7 +83,7 @@ def estimate_training_memory(
 ) -> MemoryEstimate:
     """Bytes per rank for parameters, gradients and optimizer state under flat sharding."""
     if shard_group_size < 1:
-        raise ValueError(f"shard_group_size must be positive, got {shard_group_size}")
+        raise ValueError(f"the shard group has at least one rank; got {shard_group_size}")
     if optimizer not in OPTIMIZER_STATE_SLOTS:
         raise ValueError(f"unknown optimizer {optimizer!r}; expected one of {sorted(OPTIMIZER_STATE_SLOTS)}")
     unit = total_parameters if largest_unit_parameters is None else largest_unit_parameters

@@ -59,15 +59,15 @@ class FlatEntry:
 
 @dataclass(frozen=True)
 class ShardRange:
-    """Half-open interval ``[start, start + length)`` of a flat buffer."""
+    """Elements ``start`` up to (not including) ``start + length`` of a 1-D buffer."""
 
     start: int
     length: int
 
     def __post_init__(self) -> None:
         if self.start < 0 or self.length < 0:
-            raise _err("ShardRange", "shard ranges must be non-negative", "start >= 0 and length >= 0",
-                       f"start={self.start}, length={self.length}", "check the offset arithmetic")
+            raise _err("ShardRange", "a shard range cannot start or extend below zero", "non-negative start and length",
+                       f"start={self.start}, length={self.length}", "recompute the offsets")
 
     @property
     def end(self) -> int:
@@ -84,7 +84,7 @@ class ShardRange:
 def build_flat_layout(named_tensors: Sequence[tuple[str, torch.Tensor]]) -> tuple[tuple[FlatEntry, ...], int]:
     """Concatenate tensors in order; returns the entries and the total element count."""
     if not named_tensors:
-        raise _err("build_flat_layout", "cannot flatten an empty tensor list", ">= 1 tensor", 0,
+        raise _err("build_flat_layout", "there is nothing to flatten", ">= 1 tensor", 0,
                    "do not create a flat buffer for a module with no parameters")
     entries: list[FlatEntry] = []
     names: set[str] = set()
@@ -92,7 +92,7 @@ def build_flat_layout(named_tensors: Sequence[tuple[str, torch.Tensor]]) -> tupl
     for name, tensor in named_tensors:
         if name in names:
             raise _err("build_flat_layout", "duplicate tensor name in one flat buffer (a tied tensor registered twice)",
-                       "unique names", name, "de-duplicate tied parameters before flattening")
+                       "unique names", name, "list each shared (tied) tensor once")
         names.add(name)
         n = tensor.numel()
         entries.append(FlatEntry(name, tuple(tensor.shape), cursor, n, str(tensor.dtype), bool(tensor.requires_grad)))
@@ -104,17 +104,17 @@ def flatten_dense_tensors(tensors: Iterable[torch.Tensor], *, out: torch.Tensor 
     """Copy tensors of one dtype/device back to back into a 1-D buffer."""
     items = list(tensors)
     if not items:
-        raise _err("flatten_dense_tensors", "nothing to flatten", ">= 1 tensor", 0, "pass at least one tensor")
+        raise _err("flatten_dense_tensors", "nothing to flatten", ">= 1 tensor", 0, "give one or more tensors")
     dtype, device = items[0].dtype, items[0].device
     for t in items:
         if t.dtype != dtype or t.device != device:
-            raise _err("flatten_dense_tensors", "all tensors in a flat buffer must share dtype and device",
+            raise _err("flatten_dense_tensors", "one flat buffer holds one dtype on one device",
                        f"{dtype} on {device}", f"{t.dtype} on {t.device}", "group tensors by dtype/device first")
     total = sum(t.numel() for t in items)
     if out is None:
         out = torch.empty(total, dtype=dtype, device=device)
     elif out.numel() != total:
-        raise _err("flatten_dense_tensors", "destination buffer is the wrong size", total, out.numel(),
+        raise _err("flatten_dense_tensors", "the output buffer has the wrong number of elements", total, out.numel(),
                    "allocate exactly the total element count")
     cursor = 0
     for t in items:
@@ -126,21 +126,21 @@ def flatten_dense_tensors(tensors: Iterable[torch.Tensor], *, out: torch.Tensor 
 def unflatten_to_views(flat: torch.Tensor, entries: Sequence[FlatEntry]) -> list[torch.Tensor]:
     """Shaped views into ``flat`` for each entry (no copies)."""
     if flat.dim() != 1:
-        raise _err("unflatten_to_views", "the flat buffer must be one-dimensional", "dim() == 1", flat.dim(),
+        raise _err("unflatten_to_views", "a flat buffer has a single dimension", "dim() == 1", flat.dim(),
                    "reshape to (-1,) first")
     need = entries[-1].end if entries else 0
     if flat.numel() < need:
-        raise _err("unflatten_to_views", "flat buffer is too short for the layout", f">= {need} elements", flat.numel(),
-                   "allocate the padded size, not the logical size")
+        raise _err("unflatten_to_views", "the flat buffer holds fewer elements than the layout needs", f">= {need} elements", flat.numel(),
+                   "size the buffer by the padded total")
     return [flat[e.offset:e.end].view(e.shape) for e in entries]
 
 
 def pad_flat_tensor(flat: torch.Tensor, multiple: int, *, value: float = 0.0) -> torch.Tensor:
     """Right-pad a 1-D tensor to a multiple of ``multiple`` (returns it unchanged if aligned)."""
     if flat.dim() != 1:
-        raise _err("pad_flat_tensor", "expected a one-dimensional tensor", "dim() == 1", flat.dim(), "flatten first")
+        raise _err("pad_flat_tensor", "this needs a 1-D tensor", "dim() == 1", flat.dim(), "flatten first")
     if multiple < 1:
-        raise _err("pad_flat_tensor", "the alignment multiple must be positive", ">= 1", multiple, "pass the group size")
+        raise _err("pad_flat_tensor", "padding rounds up to a multiple that is at least 1", ">= 1", multiple, "pass the group size")
     short = (-flat.numel()) % multiple
     if short == 0:
         return flat
@@ -150,15 +150,15 @@ def pad_flat_tensor(flat: torch.Tensor, multiple: int, *, value: float = 0.0) ->
 def even_shard_ranges(total_numel: int, num_shards: int) -> tuple[ShardRange, ...]:
     """``num_shards`` equal ranges of ``ceil(total / num_shards)`` elements (the last covers padding)."""
     if num_shards < 1:
-        raise _err("even_shard_ranges", "num_shards must be positive", ">= 1", num_shards, "pass the shard-group size")
+        raise _err("even_shard_ranges", "a tensor is split into one or more shards", ">= 1", num_shards, "give the number of shard ranks")
     size = -(-total_numel // num_shards)
     return tuple(ShardRange(i * size, size) for i in range(num_shards))
 
 
 def shard_range_for(total_numel: int, num_shards: int, shard_index: int) -> ShardRange:
     if not 0 <= shard_index < num_shards:
-        raise _err("shard_range_for", "shard index outside the group", f"0 <= i < {num_shards}", shard_index,
-                   "pass the rank's index within the shard group")
+        raise _err("shard_range_for", "the shard index is not below the number of shards", f"0 <= i < {num_shards}", shard_index,
+                   "give the position of the rank in the shard group")
     size = -(-total_numel // num_shards)
     return ShardRange(shard_index * size, size)
 
@@ -172,10 +172,10 @@ def intersect_ranges(a: ShardRange, b: ShardRange) -> ShardRange | None:
 def split_tensor_along_dim(tensor: torch.Tensor, dim: int, num_parts: int, *, contiguous: bool = True) -> tuple[torch.Tensor, ...]:
     """Split ``dim`` into ``num_parts`` equal chunks (error if not divisible)."""
     if num_parts < 1:
-        raise _err("split_tensor_along_dim", "num_parts must be positive", ">= 1", num_parts, "pass the group size")
+        raise _err("split_tensor_along_dim", "a split has one or more parts", ">= 1", num_parts, "pass the group size")
     if not -tensor.dim() <= dim < tensor.dim():
-        raise _err("split_tensor_along_dim", "dimension index out of range", f"-{tensor.dim()} <= dim < {tensor.dim()}",
-                   dim, "check the tensor rank")
+        raise _err("split_tensor_along_dim", "the tensor has no such dimension", f"-{tensor.dim()} <= dim < {tensor.dim()}",
+                   dim, "count the dimensions of the tensor")
     dim %= tensor.dim()
     size = tensor.shape[dim]
     if size % num_parts:

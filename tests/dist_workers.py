@@ -7,6 +7,8 @@ reference computed with the same seeds.
 
 from __future__ import annotations
 
+import os
+
 import dataclasses
 from pathlib import Path
 from typing import Any
@@ -203,7 +205,8 @@ def engine_worker(rank: int, world: int, overrides: dict[str, Any], steps: int, 
         ctx.shutdown()
 
 
-def _cuda_experiment(world: int, *, fused: bool = True, steps: int = 3) -> dict[str, Any]:
+def _cuda_experiment(world: int, *, fused: bool = True, steps: int = 3, overlap: bool = True,
+                     graph: bool = False) -> dict[str, Any]:
     return {"name": "multigpu-test", "backend": "nccl", "device": "cuda", "timeout_seconds": 120.0,
             "topology": {"data_parallel_size": world},
             "model": {"kind": "transformer", "hidden_size": 128, "num_layers": 2, "num_heads": 2, "vocab_size": 512,
@@ -213,20 +216,26 @@ def _cuda_experiment(world: int, *, fused: bool = True, steps: int = 3) -> dict[
             "optimizer": {"learning_rate": 1e-3},
             "mixed_precision": {"enabled": True, "param_dtype": "bfloat16"},
             "ddp": {"bucket_cap_mb": 0.05, "fused_allreduce": fused},
-            "training": {"max_steps": steps, "log_every_steps": 0}}
+            "training": {"max_steps": steps, "log_every_steps": 0, "overlap_optimizer_step": overlap, "cuda_graph": graph}}
 
 
-def bucket_allreduce_worker(rank: int, world: int) -> dict[str, Any]:
-    """In-kernel bucket all-reduce over NVLink peer memory against NCCL's all-reduce (average)."""
+def bucket_allreduce_worker(rank: int, world: int, nvls: bool = False) -> dict[str, Any]:
+    """In-kernel bucket all-reduce over NVLink peer memory against NCCL's all-reduce (average).
+
+    ``nvls=True`` selects the NVLink-switch path (``multimem.ld_reduce`` / ``multimem.st``); the
+    result then records whether the switch offered a multicast address at all.
+    """
     import torch.distributed as dist
 
-    from hybrid_training.ops.comm import bucket_all_reduce
+    from hybrid_training.ops.comm import bucket_all_reduce, nvls_available
 
     cfg = ExperimentConfig.from_dict(_cuda_experiment(world))
     ctx = init_distributed(cfg)
     try:
         ws = ctx.symmetric_workspace("data_parallel")
         assert ws is not None, "symmetric memory is unavailable"
+        if nvls:
+            os.environ["HT_NVLS"] = "1"
         numel = 3_000_011
         flat = ws.allocate(numel + 5, torch.float32)
         gen = torch.Generator(device="cuda").manual_seed(100 + rank)
@@ -242,19 +251,25 @@ def bucket_allreduce_worker(rank: int, world: int) -> dict[str, Any]:
             ws.check_status()
             errors.append(float((flat[start:start + n] - expect).abs().max()))
             assert torch.equal(torch.cat([flat[:start], flat[start + n:]]), outside), "wrote outside the bucket"
-        return {"errors": errors}
+        return {"errors": errors, "nvls": nvls and nvls_available(ws, flat)}
     finally:
         ctx.shutdown()
 
 
-def ddp_cuda_worker(rank: int, world: int, fused: bool, steps: int) -> dict[str, Any]:
-    """A few DDP steps on CUDA; returns the losses and the final parameters."""
-    cfg = ExperimentConfig.from_dict(_cuda_experiment(world, fused=fused, steps=steps))
+def ddp_cuda_worker(rank: int, world: int, fused: bool, steps: int, overlap: bool = False,
+                    graph: bool = False) -> dict[str, Any]:
+    """A few DDP steps on CUDA; returns the losses and the final parameters.
+
+    ``overlap`` applies AdamW per bucket during the backward pass; ``graph`` replays the step
+    from a CUDA graph after the warm-up steps.
+    """
+    cfg = ExperimentConfig.from_dict(_cuda_experiment(world, fused=fused, steps=steps, overlap=overlap, graph=graph))
     ctx = init_distributed(cfg)
     try:
         engine = TrainingEngine(cfg, ctx)
         ddp = getattr(engine.model, "_ddp", None)
         used_fused = ddp is not None and getattr(ddp, "_workspace", None) is not None
+        assert (engine.overlapped_step is not None) == overlap
         engine.train(max_steps=steps)
         full = engine.model.full_state_dict()
         out = {"losses": [m.loss for m in engine.history], "fused": used_fused,

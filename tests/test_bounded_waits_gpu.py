@@ -49,3 +49,36 @@ def test_barrier_completes_when_the_peer_has_arrived() -> None:
     torch.cuda.synchronize()
     assert status.tolist() == [0, 0, 0, 0]
     assert int(pads[0, 1]) == 0 and int(pads[1, 0]) == 1  # flag consumed; own arrival posted
+
+
+def test_timed_out_wait_in_a_replayed_graph_raises_at_the_step_read() -> None:
+    """A bounded wait that runs out inside a captured step surfaces when the engine reads the loss."""
+    from types import SimpleNamespace
+
+    from hybrid_training.distributed.symmetric import SymmetricWorkspace
+    from hybrid_training.errors import KernelError
+    from hybrid_training.training.engine import TrainingEngine
+
+    ext = _ext()
+    ws = SymmetricWorkspace.__new__(SymmetricWorkspace)  # status word only: no peer memory is needed here
+    ws.status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws.group = SimpleNamespace(global_rank=0)
+    engine = SimpleNamespace(context=SimpleNamespace(device=torch.device("cuda"), symmetric_workspaces=lambda: [ws]))
+    pads = torch.zeros(2, 8, dtype=torch.int32, device="cuda")
+    loss = torch.zeros(1, device="cuda")
+    graph, side = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        loss.fill_(2.5)
+        ext.barrier_probe(pads, ws.status, 0.1)  # the "peer" never arrives during a replay
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    assert ws.status.tolist() == [0, 0, 0, 0]  # capture recorded the kernel without running it
+    graph.replay()
+    with pytest.raises(KernelError, match="stage 99"):
+        TrainingEngine.read_step_results(engine, loss, None)
+    # The status word was cleared by the report; a clean step reads normally.
+    assert ws.status.tolist() == [0, 0, 0, 0]
+    loss.fill_(1.25)
+    assert TrainingEngine.read_step_results(engine, loss, torch.full((1,), 3.0, device="cuda")) == (1.25, 3.0)
+    del graph

@@ -86,6 +86,28 @@ def test_gemm_split_k_weight_gradient_shapes(out_dtype: torch.dtype) -> None:
     assert torch.equal(again, out), "split-K result must be deterministic"
 
 
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_gemm_split_k_reduce_add_into_the_output(beta: float) -> None:
+    """With reproducibility off, split-K partial tiles are TMA reduce-added straight into an fp32 output."""
+    ops = _ops()
+    dev = torch.device("cuda")
+    k, m, n = 4096, 296, 200
+    g = torch.randn(k, m, device=dev).bfloat16()
+    x = torch.randn(k, n, device=dev).bfloat16()
+    store = torch.randn(m, 256, device=dev)  # padded rows: the output is a strided view
+    c = store[:, :n].clone()
+    pad = store[:, n:].clone()
+    out = store[:, :n]
+    try:
+        ops.set_deterministic_reductions(False)
+        ops.gemm(g, x, out=out, a_mn_major=True, b_mn_major=True, beta=beta)
+    finally:
+        ops.set_deterministic_reductions(True)
+    ref = g.float().t() @ x.float() + (c if beta else 0.0)
+    assert _rel(out, ref) < 1e-5, _rel(out, ref)
+    assert torch.equal(store[:, n:], pad)  # the zero-fill and the reduce-adds stay inside the view
+
+
 def test_gelu_mlp_matches_fp32() -> None:
     ops = _ops()
     dev = torch.device("cuda")
@@ -137,6 +159,22 @@ def test_gemm_split_k_long_reduction_with_many_tiles(out_dtype: torch.dtype) -> 
     assert err < (1e-5 if out_dtype == torch.float32 else 1e-2), err
 
 
+def test_gemm_unaligned_output_rows_use_the_scalar_store_path() -> None:
+    """Output rows whose stride is not a multiple of 16 bytes cannot use TMA or vector stores."""
+    ops = _ops()
+    dev = torch.device("cuda")
+    a = torch.randn(300, 64, device=dev).bfloat16()
+    b = torch.randn(333, 64, device=dev).bfloat16()
+    for dtype in (torch.bfloat16, torch.float32):
+        store = torch.full((300, 333), 7.0, device=dev, dtype=dtype)  # row stride 666 / 1332 bytes
+        ops.gemm(a, b, out=store)
+        ref = a.float() @ b.float().t()
+        assert _rel(store, ref) < 1e-2, dtype
+        acc = torch.ones(300, 333, device=dev)
+        ops.gemm(a, b, out=acc, beta=1.0)  # accumulate into an fp32 output
+        assert _rel(acc, ref + 1.0) < 1e-2
+
+
 def test_gemm_padded_output_rows() -> None:
     ops = _ops()
     dev = torch.device("cuda")
@@ -149,8 +187,19 @@ def test_gemm_padded_output_rows() -> None:
     assert float(store[:, 1003:].abs().max()) == 0.0
 
 
+def _torch_add_norm(res: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, eps: float,
+                    rms: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 PyTorch statement of the fused op: r = res + delta, y = LayerNorm(r) or RMSNorm(r)."""
+    r = res + delta.float()
+    if rms:
+        y = r * torch.rsqrt(r.pow(2).mean(-1, keepdim=True) + eps) * w
+    else:
+        y = torch.nn.functional.layer_norm(r, (r.shape[-1],), w, b, eps)
+    return r, y
+
+
 @pytest.mark.parametrize("rms", [False, True])
-@pytest.mark.parametrize("d", [768, 100, 2048])
+@pytest.mark.parametrize("d", [768, 100, 2048, 8192])
 def test_add_norm_forward_backward(rms: bool, d: int) -> None:
     ops = _ops()
     dev = torch.device("cuda")
@@ -160,15 +209,15 @@ def test_add_norm_forward_backward(rms: bool, d: int) -> None:
     w = (1 + 0.1 * torch.randn(d, device=dev)).requires_grad_(True)
     b = None if rms else (0.1 * torch.randn(d, device=dev)).requires_grad_(True)
     r, y = ops.add_norm(res, delta, w, b, eps=1e-5, rms=rms, out_dtype=torch.bfloat16)
-    res_c, delta_c = res.detach().cpu().requires_grad_(True), delta.detach().float().cpu().requires_grad_(True)
-    w_c = w.detach().cpu().requires_grad_(True)
-    b_c = None if b is None else b.detach().cpu().requires_grad_(True)
-    r_ref, y_ref = ops.add_norm(res_c, delta_c, w_c, b_c, eps=1e-5, rms=rms, out_dtype=torch.float32)
+    res_c, delta_c = res.detach().double().cpu().requires_grad_(True), delta.detach().double().cpu().requires_grad_(True)
+    w_c = w.detach().double().cpu().requires_grad_(True)
+    b_c = None if b is None else b.detach().double().cpu().requires_grad_(True)
+    r_ref, y_ref = _torch_add_norm(res_c, delta_c, w_c, b_c, 1e-5, rms)
     assert _rel(r, r_ref) < 1e-6 and _rel(y, y_ref) < 1e-2
-    gy = torch.randn(rows, d)
-    gr = torch.randn(rows, d)
-    torch.autograd.backward([r, y], [gr.to(dev), gy.to(dev).bfloat16()])
-    torch.autograd.backward([r_ref, y_ref], [gr, gy.bfloat16().float()])
+    gy = torch.randn(rows, d, dtype=torch.float64)
+    gr = torch.randn(rows, d, dtype=torch.float64)
+    torch.autograd.backward([r, y], [gr.float().to(dev), gy.to(dev).bfloat16()])
+    torch.autograd.backward([r_ref, y_ref], [gr, gy.bfloat16().double()])
     assert _rel(res.grad, res_c.grad) < 1e-2
     assert _rel(delta.grad, delta_c.grad) < 2e-2
     assert _rel(w.grad, w_c.grad) < 1e-2
@@ -252,14 +301,24 @@ def test_embedding_swiglu_rope() -> None:
     table = torch.randn(40, 24, device=dev, requires_grad=True)
     pos = torch.randn(32, 24, device=dev, requires_grad=True)
     out = ops.embedding(ids, table, pos, vocab_start=10)
-    ref = ops.embedding(ids.cpu(), table.detach().cpu().requires_grad_(True), pos.detach().cpu().requires_grad_(True), vocab_start=10)
+    # fp32 PyTorch statement: rows [10, 50) of the vocabulary live here, others contribute zero.
+    local = ids.cpu() - 10
+    owned = (local >= 0) & (local < 40)
+    t_c, p_c = table.detach().cpu(), pos.detach().cpu()
+    ref = torch.where(owned[..., None], t_c[local.clamp(0, 39)], torch.zeros(())) + p_c[:17][None]
     assert torch.allclose(out.cpu(), ref, atol=1e-6)
-    out.sum().backward()
-    assert table.grad is not None and pos.grad is not None
+    g = torch.randn(3, 17, 24)
+    out.backward(g.to(dev))
+    table_grad = torch.zeros(40, 24).index_add_(0, local[owned], g[owned])
+    pos_grad = torch.zeros(32, 24)
+    pos_grad[:17] = g.sum(0)
+    assert torch.allclose(table.grad.cpu(), table_grad, atol=1e-5)
+    assert torch.allclose(pos.grad.cpu(), pos_grad, atol=1e-5)
     h = torch.randn(5, 7, 64, device=dev).bfloat16().requires_grad_(True)
     y = ops.swiglu(h)
     hr = h.detach().float().cpu().requires_grad_(True)
-    yr = ops.swiglu(hr)
+    gate, up = hr[..., :32], hr[..., 32:]
+    yr = torch.nn.functional.silu(gate) * up
     assert _rel(y, yr) < 1e-2
     y.float().sum().backward()
     yr.sum().backward()
@@ -267,5 +326,13 @@ def test_embedding_swiglu_rope() -> None:
     cos, sin = ops.rope_tables(16, 64, 10000.0, dev)
     qkv = torch.randn(2, 16, (2 + 2) * 64, device=dev).bfloat16()
     rot = ops.apply_rope(qkv, cos, sin, 2, 1, 64)
-    rot_ref = ops.apply_rope(qkv.float().cpu(), cos.cpu(), sin.cpu(), 2, 1, 64)
+    # Rotate-half RoPE written out: angle(position t, pair i) = t * theta^(-2i / D).
+    inv = 10000.0 ** (-torch.arange(0, 64, 2, dtype=torch.float64) / 64)
+    ang = torch.arange(16, dtype=torch.float64)[:, None] * inv[None]
+    c, s_ = torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
+    x = qkv.double().cpu().reshape(2, 16, 4, 64)
+    qk = x[:, :, :3]
+    rotated = torch.cat([-qk[..., 32:], qk[..., :32]], -1)
+    rot_ref = torch.cat([qk * c[None, :, None] + rotated * s_[None, :, None], x[:, :, 3:]], 2).reshape(2, 16, 256)
     assert _rel(rot, rot_ref) < 1e-2
+    assert torch.equal(rot[..., 192:], qkv[..., 192:])  # values untouched

@@ -24,15 +24,42 @@ def test_in_kernel_bucket_all_reduce_matches_nccl() -> None:
             assert err < 1e-5, r.value["errors"]
 
 
+def test_in_kernel_bucket_all_reduce_through_the_switch_matches_nccl() -> None:
+    """The NVLS variant: the NVLink switch sums the copies (multimem.ld_reduce) and stores to all ranks."""
+    results = launch_workers(W.bucket_allreduce_worker, 2, args=(True,), timeout_seconds=300,
+                             extra_env={"NCCL_NVLS_ENABLE": "0"})
+    if not results[0].value["nvls"]:
+        pytest.skip("the NVLink switch offers no multicast address on this machine")
+    for r in results:
+        for err in r.value["errors"]:
+            assert err < 1e-5, r.value["errors"]
+
+
 def test_ddp_fused_and_nccl_reductions_train_alike() -> None:
     fused = launch_workers(W.ddp_cuda_worker, 2, args=(True, 3), timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
-    nccl = launch_workers(W.ddp_cuda_worker, 2, args=(False, 3), timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    nccl = launch_workers(W.ddp_cuda_worker, 2, args=(False, 3, True), timeout_seconds=300,
+                          extra_env={"NCCL_NVLS_ENABLE": "0"})  # NCCL reduction with the per-bucket update
     assert fused[0].value["fused"] and not nccl[0].value["fused"]
     # DDP keeps every replica identical.
     for name, t in fused[0].value["full"].items():
         assert torch.equal(t, fused[1].value["full"][name]), name
     for a, b in zip(fused[0].value["losses"], nccl[0].value["losses"]):
         assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (fused[0].value["losses"], nccl[0].value["losses"])
+
+
+def test_ddp_optimizer_update_overlapped_with_the_backward_matches_the_step_after_it() -> None:
+    """AdamW per bucket on the communication stream, eager and replayed from a CUDA graph."""
+    base = launch_workers(W.ddp_cuda_worker, 2, args=(True, 4, False, False), timeout_seconds=300,
+                          extra_env={"NCCL_NVLS_ENABLE": "0"})
+    for graph in (False, True):
+        over = launch_workers(W.ddp_cuda_worker, 2, args=(True, 4, True, graph), timeout_seconds=300,
+                              extra_env={"NCCL_NVLS_ENABLE": "0"})
+        for name, t in over[0].value["full"].items():
+            assert torch.equal(t, over[1].value["full"][name]), name  # replicas stay identical
+            ref = base[0].value["full"][name]
+            assert torch.allclose(t, ref, atol=2e-3, rtol=2e-3), (name, float((t - ref).abs().max()))
+        for a, b in zip(over[0].value["losses"], base[0].value["losses"]):
+            assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (over[0].value["losses"], base[0].value["losses"])
 
 
 def test_fused_tensor_parallel_collectives_match_nccl_path() -> None:

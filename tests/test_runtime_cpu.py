@@ -77,7 +77,7 @@ def test_consistency_checks_raise_on_every_rank(collectives4: list) -> None:
         assert "layout differs across the 'world' group" in r.value["metadata_mismatch"]
         # data-parallel groups are (0, 2) and (1, 3); only rank 2 holds a value unlike its group's rank 0
         if r.rank == 2:
-            assert "differs from the value held by group-local rank 0" in r.value["tensor_mismatch"]
+            assert "is not the same here as on the group's first rank" in r.value["tensor_mismatch"]
         else:
             assert r.value["tensor_mismatch"] == "NO ERROR"
         assert r.value["sum_scalar"] == 10.0
@@ -102,7 +102,7 @@ def test_launcher_names_a_silent_rank_at_the_deadline() -> None:
 def test_context_refuses_double_init_and_builds_the_grid() -> None:
     results = launch_workers(R.context_worker, 4, timeout_seconds=300)
     for r in results:
-        assert "already active" in r.value["again"]
+        assert "already has an active distributed context" in r.value["again"]
     # rank = (dp * shard + sh) * 1 + 0 with shard innermost of the two
     assert results[3].value["shard"] == [2, 3] and results[3].value["data_parallel"] == [1, 3]
     assert results[3].value["dp_shard"] == [0, 1, 2, 3]
