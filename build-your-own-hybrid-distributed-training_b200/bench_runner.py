@@ -73,7 +73,7 @@ CONFIGS = ("gpt2_ddp", "llama_fsdp", "llama_tp_sp", "llama_hybrid")
 
 
 def experiment(world: int, *, micro_batch: int, seq: int, samples: int, use_graph: bool, config: str = "gpt2_ddp",
-               grad_accum: int = 1) -> ExperimentConfig:
+               grad_accum: int = 1, overlap_step: bool = True) -> ExperimentConfig:
     """The ExperimentConfig of one benchmark configuration on ``world`` GPUs."""
     common = dict(backend="nccl", device="cuda", timeout_seconds=600.0,
                   data=DataConfig(micro_batch_size=micro_batch, sequence_length=seq, num_train_samples=samples,
@@ -82,7 +82,8 @@ def experiment(world: int, *, micro_batch: int, seq: int, samples: int, use_grap
     # CUDA-graph replay is used for the data-parallel step; the sharded / tensor-parallel
     # configurations run eagerly.
     training = TrainingConfig(max_steps=1_000_000, log_every_steps=0, deterministic=False,
-                              cuda_graph=use_graph and config == "gpt2_ddp", gradient_accumulation_steps=grad_accum)
+                              cuda_graph=use_graph and config == "gpt2_ddp", gradient_accumulation_steps=grad_accum,
+                              overlap_optimizer_step=overlap_step)
     if config == "gpt2_ddp":
         return ExperimentConfig(name="bench-gpt2-124m-ddp", topology=TopologyConfig(data_parallel_size=world),
                                 model=ModelConfig.gpt2_124m(),
@@ -143,11 +144,11 @@ def _exposed_communication_ms(engine: TrainingEngine, stream: Any, take: Callabl
 
 def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool = True,
         clock_start: Callable[[], None] | None = None, clock_stop: Callable[[], dict] | None = None,
-        config: str = "gpt2_ddp", grad_accum: int = 1) -> dict:
+        config: str = "gpt2_ddp", grad_accum: int = 1, overlap_step: bool = True) -> dict:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     cfg = experiment(world, micro_batch=micro_batch, seq=seq,
                      samples=micro_batch * world * grad_accum * (2 * steps + warmup + 9), use_graph=use_graph,
-                     config=config, grad_accum=grad_accum)
+                     config=config, grad_accum=grad_accum, overlap_step=overlap_step)
     ctx = init_distributed(cfg)
     engine = TrainingEngine(cfg, ctx)
     stream = engine.batch_stream(host=True)

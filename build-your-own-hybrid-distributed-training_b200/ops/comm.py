@@ -50,18 +50,22 @@ def nvls_available(workspace: Any, flat: torch.Tensor) -> bool:
     return int(getattr(workspace.handle_of(flat), "multicast_ptr", 0) or 0) != 0
 
 
-def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int, scale: float) -> torch.Tensor:
+def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int, scale: float, *,
+                      wide: bool = True) -> torch.Tensor:
     """Average ``flat[start:start+numel]`` over the workspace's group in place; returns the status tensor.
 
-    ``HT_NVLS=1`` selects the NVLink-switch reduction where the allocation has a multicast
-    address; otherwise the two-shot P2P kernel runs.
+    ``wide=False`` launches the narrow shape that runs beside a persistent GEMM (for buckets
+    reduced while the backward pass is still computing); ``wide=True`` the full-width shape for a
+    reduction that has the GPU to itself.  ``HT_NVLS=1`` selects the NVLink-switch reduction where
+    the allocation has a multicast address; otherwise the two-shot P2P kernel runs.
     """
     handle = workspace.handle_of(flat)
     world = workspace.group.size
     base, max_blocks = _slots(handle, world)
     mc = int(getattr(handle, "multicast_ptr", 0) or 0) if os.environ.get("HT_NVLS", "0") == "1" else 0
     extension().bucket_all_reduce(flat, list(handle.buffer_ptrs), list(handle.signal_pad_ptrs), mc, int(start), int(numel),
-                                  float(scale), int(handle.rank), base, max_blocks, workspace.status, _TIMEOUT_S)
+                                  float(scale), int(handle.rank), base, max_blocks, workspace.status, _TIMEOUT_S,
+                                  bool(wide))
     return workspace.status
 
 

@@ -74,20 +74,29 @@ __device__ bool block_barrier(const Peers& pp, int rank, int world, int slot_bas
   return true;
 }
 
-// The bucket all-reduce runs next to the persistent tcgen05 GEMM instead of waiting for it.  The GEMM
-// keeps one 320-thread CTA per SM with 168 registers per thread (53,760 of the SM's 65,536) and
-// 226 KB of the SM's 228 KB of shared memory, so what is left on every SM fits one block of
-// AR_THREADS = 128 threads with at most 88 registers each and only static shared memory.  The grid
-// is one such block per SM: the blocks are scheduled while the GEMM's CTAs are resident, and the
-// all-reduce proceeds during the backward pass rather than in the gaps between GEMMs.  Each thread
-// keeps eight 16-byte peer loads in flight (2.4 MB per GPU), which covers NVLink's latency.
-constexpr int AR_THREADS = 128;
-constexpr int AR_MIN_BLOCKS = 6;  // 65,536 / (128 x 6) -> the compiler stays at or below 85 registers
+// Two shapes of the same kernel:
+//
+// * narrow (buckets reduced while the backward pass still runs): it runs next to the persistent
+//   tcgen05 GEMM instead of waiting for it.  The GEMM keeps one 320-thread CTA per SM with 168
+//   registers per thread (53,760 of the SM's 65,536) and 226 KB of the SM's 228 KB of shared
+//   memory, so what is left on every SM fits one block of 128 threads with at most 88 registers
+//   each and only static shared memory.  The grid is one such block per SM, so the all-reduce
+//   proceeds during the backward pass rather than in the gaps between GEMMs;
+// * wide (the last bucket, reduced when the backward pass has finished and the GPU is otherwise
+//   idle): 512 threads per block, four times the loads in flight, for NVLink bandwidth.
+//
+// Every thread issues all of its peer loads (peers x vectors, 8 vectors of 16 bytes) before it
+// uses any: the loop is bound by NVLink latency (a few microseconds), so bytes in flight decide
+// the rate.
+constexpr int AR_THREADS = 128;       // narrow
+constexpr int AR_MIN_BLOCKS = 6;      // 65,536 / (128 x 6) -> the compiler stays at or below 85 registers
+constexpr int AR_WIDE_THREADS = 512;  // wide
 
-template <int MAXW>
-__global__ void __launch_bounds__(AR_THREADS, AR_MIN_BLOCKS)
+template <int MAXW, int AR_THREADS_, int MINB>
+__global__ void __launch_bounds__(AR_THREADS_, MINB)
     bucket_allreduce_kernel(Peers pp, float* mc, long long start, long long n, float scale, int rank, int world, int slot_base,
                             int* status, unsigned long long timeout_ns) {
+  constexpr int AR_THREADS = AR_THREADS_;
   // chunk per owner rank (multiple of 4 floats), sub-range per block
   const long long chunk = ((n + world - 1) / world + 3) / 4 * 4;
   const long long per_block = ((chunk + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
@@ -425,7 +434,7 @@ __global__ void __launch_bounds__(THREADS) barrier_probe_kernel(uint32_t* pad0, 
 
 void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
                        int64_t start, int64_t numel, double scale, int64_t rank, int64_t slot_base, int64_t max_blocks,
-                       at::Tensor status, double timeout_s) {
+                       at::Tensor status, double timeout_s, bool wide) {
   const c10::cuda::CUDAGuard guard(flat.device());
   const int world = (int)buffer_ptrs.size();
   HT_CHECK(world >= 2 && world <= comm::MAX_RANKS, "bucket_all_reduce supports 2..8 ranks");
@@ -442,20 +451,28 @@ void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::v
   // when the bucket is small.  Every block waits on its peers, and all of them fit on the GPU at once.
   const long long chunk = (numel + world - 1) / world;
   const int blocks = (int)std::max<long long>(
-      1, std::min<long long>(std::min<long long>(max_blocks, num_sms()), (chunk + comm::AR_THREADS * 32 - 1) / (comm::AR_THREADS * 32)));
-  auto launch = [&](auto kernel) {
+      1, std::min<long long>(std::min<long long>(max_blocks, num_sms()),
+                             (chunk + (wide ? comm::AR_WIDE_THREADS : comm::AR_THREADS) * 32 - 1) /
+                                 ((wide ? comm::AR_WIDE_THREADS : comm::AR_THREADS) * 32)));
+  auto launch = [&](auto kernel, int threads) {
     static bool configured = false;  // per instantiation: prefer the shared-memory carveout of the GEMM it runs beside
     if (!configured) {
       HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared));
       configured = true;
     }
-    kernel<<<blocks, comm::AR_THREADS, 0, stream()>>>(pp, reinterpret_cast<float*>(multicast_ptr), start, numel, (float)scale,
-                                                      (int)rank, world, (int)slot_base, status.data_ptr<int>(),
-                                                      (unsigned long long)(timeout_s * 1e9));
+    kernel<<<blocks, threads, 0, stream()>>>(pp, reinterpret_cast<float*>(multicast_ptr), start, numel, (float)scale, (int)rank,
+                                             world, (int)slot_base, status.data_ptr<int>(), (unsigned long long)(timeout_s * 1e9));
   };
-  if (world <= 2) launch(comm::bucket_allreduce_kernel<2>);
-  else if (world <= 4) launch(comm::bucket_allreduce_kernel<4>);
-  else launch(comm::bucket_allreduce_kernel<8>);
+  constexpr int NT = comm::AR_THREADS, WT = comm::AR_WIDE_THREADS, NB = comm::AR_MIN_BLOCKS;
+  if (wide) {
+    if (world <= 2) launch(comm::bucket_allreduce_kernel<2, WT, 1>, WT);
+    else if (world <= 4) launch(comm::bucket_allreduce_kernel<4, WT, 1>, WT);
+    else launch(comm::bucket_allreduce_kernel<8, WT, 1>, WT);
+  } else {
+    if (world <= 2) launch(comm::bucket_allreduce_kernel<2, NT, NB>, NT);
+    else if (world <= 4) launch(comm::bucket_allreduce_kernel<4, NT, NB>, NT);
+    else launch(comm::bucket_allreduce_kernel<8, NT, NB>, NT);
+  }
   HT_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -216,12 +216,14 @@ def bench_allreduce(mb: float) -> None:
         flat = ws.allocate(n, torch.float32)
         flat.normal_()
         pg = ctx.group("data_parallel").process_group
-        ours = _max_over_ranks(_time(lambda: bucket_all_reduce(ws, flat, 0, n, 1.0 / world), 10))
+        wide = _max_over_ranks(_time(lambda: bucket_all_reduce(ws, flat, 0, n, 1.0 / world, wide=True), 10))
+        narrow = _max_over_ranks(_time(lambda: bucket_all_reduce(ws, flat, 0, n, 1.0 / world, wide=False), 10))
         nccl = _max_over_ranks(_time(lambda: dist.all_reduce(flat, group=pg), 10))
         ws.check_status()
         bus = 2.0 * (world - 1) / world * n * 4  # bytes each rank moves in a ring all-reduce
         if ctx.rank == 0:
-            print(f"allreduce {world} ranks {mb:.0f} MB fp32: in-kernel {ours * 1e3:.1f} us ({bus / ours / 1e6:.0f} GB/s bus), "
+            print(f"allreduce {world} ranks {mb:.0f} MB fp32: in-kernel wide {wide * 1e3:.1f} us ({bus / wide / 1e6:.0f} GB/s bus), "
+                  f"narrow (co-resident shape) {narrow * 1e3:.1f} us ({bus / narrow / 1e6:.0f} GB/s bus), "
                   f"NCCL {nccl * 1e3:.1f} us ({bus / nccl / 1e6:.0f} GB/s bus)", flush=True)
     finally:
         ctx.shutdown()

@@ -173,6 +173,7 @@ class DistributedDataParallel(nn.Module):
         # Called as hook(start, numel) on the communication stream right after a bucket's all-reduce
         # was issued (flat-buffer coordinates): the optimizer updates the bucket during the backward.
         self.post_reduction_hook: Any = None
+        self._draining = False  # True while finish_gradient_synchronization launches what is left
         if self._config.check_parameter_consistency:
             signature = [(n, tuple(p.shape), str(p.dtype)) for n, p in self._named_parameters]
             assert_metadata_consistent(signature, group, name="the names, shapes and dtypes of the trainable parameters",
@@ -299,8 +300,11 @@ class DistributedDataParallel(nn.Module):
                 self._comm_stream = torch.cuda.Stream(device=bucket.buffer.device, priority=-1)
             self._comm_stream.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(self._comm_stream):
+                # Buckets reduced during the backward pass share the GPU with its GEMMs (narrow
+                # kernel); the last bucket is reduced when the backward has finished (wide kernel).
+                last = bucket.layout.index == len(self._buckets) - 1 or self._draining
                 status = bucket_all_reduce(self._workspace, self._flat_grad, bucket.start, bucket.layout.total_numel,
-                                           1.0 / self._group.size if average else 1.0)
+                                           1.0 / self._group.size if average else 1.0, wide=last)
                 if self.post_reduction_hook is not None:
                     self.post_reduction_hook(bucket.start, bucket.layout.total_numel)
                 event = torch.cuda.Event()
@@ -352,7 +356,11 @@ class DistributedDataParallel(nn.Module):
                 observed=f"{len(missing)} without gradients: {missing[:8]}",
                 resolution="set DDPConfig(find_unused_parameters=True), or stop marking unused parameters trainable"))
         self._statistics.unused_parameters = tuple(missing)
-        self._launch_ready_buckets()
+        self._draining = True
+        try:
+            self._launch_ready_buckets()
+        finally:
+            self._draining = False
         for bucket in self._buckets:
             if not bucket.launched:
                 raise ShardingError(format_error("ddp.finish_gradient_synchronization",

@@ -240,13 +240,14 @@ def bucket_allreduce_worker(rank: int, world: int, nvls: bool = False) -> dict[s
         flat = ws.allocate(numel + 5, torch.float32)
         gen = torch.Generator(device="cuda").manual_seed(100 + rank)
         errors = []
-        for start, n in ((0, numel), (4, 1001), (1024, 17), (8, 2_000_000)):
+        for (start, n), wide in zip(((0, numel), (4, 1001), (1024, 17), (8, 2_000_000), (0, numel), (8, 999_999)),
+                                    (True, True, False, False, False, True)):
             flat.normal_(generator=gen)
             expect = flat[start:start + n].clone()
             dist.all_reduce(expect, op=dist.ReduceOp.SUM, group=ctx.group("data_parallel").process_group)
             expect /= world
             outside = torch.cat([flat[:start], flat[start + n:]]).clone()
-            bucket_all_reduce(ws, flat, start, n, 1.0 / world)
+            bucket_all_reduce(ws, flat, start, n, 1.0 / world, wide=wide)
             torch.cuda.synchronize()
             ws.check_status()
             errors.append(float((flat[start:start + n] - expect).abs().max()))
