@@ -187,6 +187,31 @@ def transformer_forward_worker(rank: int, world: int, tp: int, sp: bool, kind: s
         ctx.shutdown()
 
 
+def _tensor_parallel_full(engine: Any, ctx: Any) -> dict[str, torch.Tensor]:
+    """The model's full state with tensor-parallel slices gathered back into whole tensors."""
+    full = engine.model.full_state_dict()
+    tensor = ctx.group("tensor")
+    if tensor.size == 1:
+        return full
+    from hybrid_training.autograd import all_gather_along_dim
+
+    info = engine.model.parameter_parallel_info()
+    inner = getattr(engine.model, "_inner_model", engine.model)
+    out = {}
+    for name, t in full.items():
+        i = info.get(name)
+        if i is not None and i.partition_dim is not None and i.tensor_parallel_size > 1:
+            t = all_gather_along_dim(t.contiguous(), tensor, i.partition_dim)
+            try:
+                owner = inner.get_submodule(name.rsplit(".", 1)[0])
+            except AttributeError:
+                owner = None
+            if owner is not None and hasattr(owner, "canonical"):
+                t = owner.canonical(t)
+        out[name] = t
+    return out
+
+
 def engine_worker(rank: int, world: int, overrides: dict[str, Any], steps: int, ckpt: str | None, resume: str | None) -> dict[str, Any]:
     cfg = ExperimentConfig.from_dict(overrides)
     ctx = init_distributed(cfg)
@@ -196,7 +221,7 @@ def engine_worker(rank: int, world: int, overrides: dict[str, Any], steps: int, 
             engine.load_checkpoint(resume)
         engine.train(max_steps=steps)
         path = str(engine.save_checkpoint(ckpt)) if ckpt else None
-        full = engine.model.full_state_dict()
+        full = _tensor_parallel_full(engine, ctx)
         out = {"losses": [m.loss for m in engine.history], "path": path,
                "full": {k: v.detach().clone() for k, v in full.items()}, "step": engine.state.step}
         engine.close()
@@ -441,6 +466,39 @@ def fsdp_fused_update_worker(rank: int, world: int, fused: bool, steps: int, acc
         full = engine.model.full_state_dict()
         out = {"fused": engine.fsdp_fused_update, "losses": [m.loss for m in engine.history],
                "full": {k: v.detach().float().cpu().clone() for k, v in full.items()}}
+        engine.close()
+        return out
+    finally:
+        ctx.shutdown()
+
+
+def instrumented_engine_worker(rank: int, world: int, overrides: dict[str, Any], steps: int) -> dict[str, Any]:
+    """Train ``steps`` steps through the engine and count every collective of the last one.
+
+    Returns per-step ``{op/group: (calls, bytes)}``, the FSDP memory summary (or ``None``), the
+    local parameter / gradient / optimizer-state element counts and the losses.
+    """
+    from hybrid_training.distributed.collectives import observe_collectives
+
+    cfg = ExperimentConfig.from_dict(overrides)
+    ctx = init_distributed(cfg)
+    try:
+        engine = TrainingEngine(cfg, ctx)
+        engine.train(max_steps=steps - 1)
+        batches = engine.batch_stream()
+        with observe_collectives() as rec:
+            engine.history.append(engine.train_step(batches))
+        comm = {k: (v.calls, v.bytes) for k, v in rec.by_operation.items()}
+        fsdp = engine.model.fsdp
+        params = list(engine.model.optimizer_parameters())
+        state = engine.optimizer.inner.state
+        opt_elems = sum(t.numel() for p in params for t in state.get(p, {}).values() if torch.is_tensor(t) and t.dim() > 0)
+        out = {"comm": comm, "memory": fsdp.memory_summary() if fsdp is not None else None,
+               "local_params": sum(p.numel() for p in params), "optimizer_elements": opt_elems,
+               "grad_elements": sum(p.grad.numel() for p in params if p.grad is not None),
+               "losses": [m.loss for m in engine.history],
+               "largest_unit": max((u.handle.total_numel for u in fsdp.fsdp_units() if u.handle is not None), default=0)
+               if fsdp is not None else 0}
         engine.close()
         return out
     finally:
