@@ -503,3 +503,33 @@ def instrumented_engine_worker(rank: int, world: int, overrides: dict[str, Any],
         return out
     finally:
         ctx.shutdown()
+
+
+def checkpoint_write_failure_worker(rank: int, world: int, root: str) -> dict[str, Any]:
+    """Rank 1's payload write fails (its torch.save raises); every rank must raise the same voted error."""
+    from hybrid_training.checkpoint import writer
+    from hybrid_training.errors import CheckpointError
+
+    cfg = ExperimentConfig.from_dict({"backend": "gloo", "device": "cpu", "topology": {"shard_parallel_size": world},
+                                      "model": {"kind": "mlp", "input_size": 16, "hidden_size": 32, "num_layers": 2,
+                                                "output_size": 1},
+                                      "data": {"micro_batch_size": 4, "num_train_samples": 64, "num_eval_samples": 0},
+                                      "training": {"max_steps": 1, "log_every_steps": 0}})
+    ctx = init_distributed(cfg)
+    try:
+        engine = TrainingEngine(cfg, ctx)
+        engine.train(max_steps=1)
+        if rank == 1:
+            def broken_save(obj: Any, f: Any) -> None:
+                raise OSError("no space left on device (injected)")
+
+            writer.torch.save = broken_save  # type: ignore[assignment]
+        try:
+            engine.save_checkpoint(root)
+            return {"raised": False, "message": ""}
+        except CheckpointError as exc:
+            return {"raised": True, "message": str(exc)}
+        finally:
+            engine.close()
+    finally:
+        ctx.shutdown()

@@ -229,3 +229,62 @@ def test_verify_files_returns_the_recorded_digests(fsdp_checkpoint: Path) -> Non
     digests = verify_files(fsdp_checkpoint, manifest)
     assert set(digests) == {"rank-00000.pt", "rank-00001.pt"}
     assert all(digests[name] == record.sha256 for name, record in manifest.files.items())
+
+
+def test_metadata_is_plain_json_with_the_training_state(fsdp_checkpoint: Path) -> None:
+    from hybrid_training.checkpoint import read_metadata
+
+    meta = read_metadata(fsdp_checkpoint)
+    json.dumps(meta, allow_nan=False)  # no tensors, no NaN
+    assert meta["training_state"]["step"] == 1 and meta["world_size"] == 2
+    assert meta["rng"]["saved"] and meta["rng"]["ranks"] == [0, 1]
+
+
+def test_manifest_describes_global_tensors_split_in_flat_intervals(fsdp_checkpoint: Path) -> None:
+    manifest = CheckpointManifest.read(fsdp_checkpoint / "manifest.json")
+    model = {k: r for k, r in manifest.tensors.items() if r.category == "model"}
+    assert model and all(r.covered_elements() == r.numel for r in model.values())
+    # full-shard over 2 ranks: some tensor is split between the two payload files
+    assert any(len({s.file for s in r.shards}) == 2 for r in model.values())
+    optimizer = {k: r for k, r in manifest.tensors.items() if r.category == "optimizer"}
+    assert {r.state_name for r in optimizer.values()} == {"exp_avg", "exp_avg_sq"}
+
+
+def test_swapped_payload_files_fail_verification(fsdp_checkpoint: Path, tmp_path: Path) -> None:
+    bad = _copy(fsdp_checkpoint, tmp_path, "swapped")
+    a, b = (bad / "rank-00000.pt").read_bytes(), (bad / "rank-00001.pt").read_bytes()
+    (bad / "rank-00000.pt").write_bytes(b)
+    (bad / "rank-00001.pt").write_bytes(a)
+    with pytest.raises(CheckpointCorruptionError):
+        inspect_checkpoint(bad)
+
+
+def test_a_link_that_leaves_the_directory_is_rejected(fsdp_checkpoint: Path, tmp_path: Path) -> None:
+    bad = _copy(fsdp_checkpoint, tmp_path, "symlink")
+    outside = tmp_path / "elsewhere.pt"
+    outside.write_bytes((bad / "rank-00001.pt").read_bytes())
+    (bad / "rank-00001.pt").unlink()
+    (bad / "rank-00001.pt").symlink_to(outside)
+    with pytest.raises(CheckpointError):
+        inspect_checkpoint(bad)
+
+
+def test_saving_twice_at_one_step_fails_on_every_rank(tmp_path: Path) -> None:
+    root = tmp_path / "twice"
+    launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 1, str(root), None), timeout_seconds=600)
+    again = launch_workers(W.engine_worker, 2, args=(_cfg(2, 2), 1, str(root), None), timeout_seconds=600,
+                           raise_on_failure=False)
+    for r in again:
+        assert "CheckpointError" in (r.traceback_text or "") and "reserve" in (r.traceback_text or ""), r.traceback_text
+    assert len([p for p in root.iterdir() if p.name.startswith("checkpoint-step-")]) == 1
+    assert not [p for p in root.iterdir() if p.name.startswith(".staging-")]
+
+
+def test_a_rank_that_cannot_write_makes_every_rank_fail(tmp_path: Path) -> None:
+    """A write failure on one rank (not the coordinator) is voted on: all ranks raise, nothing is published."""
+    results = launch_workers(W.checkpoint_write_failure_worker, 2, args=(str(tmp_path / "voted"),), timeout_seconds=600,
+                             raise_on_failure=False)
+    for r in results:
+        assert r.value is not None and r.value["raised"], r.traceback_text
+        assert "rank 1" in r.value["message"] and "write" in r.value["message"]
+    assert not [p for p in (tmp_path / "voted").iterdir() if p.name.startswith("checkpoint-step-")]
