@@ -370,8 +370,8 @@ __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CU
   }
 }
 
-// All output tiles of one epilogue warp.  CW = output columns per 128-byte piece.
-template <int CW, int KIND>
+// All output tiles of one epilogue warp.  CW = output columns per 128-byte piece; TN = tile width.
+template <int CW, int KIND, int TN = BN>
 __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
                                               uint8_t* tile, uint32_t tmem_base, uint64_t* tfull_bar, uint64_t* tempty_bar,
                                               int M, int N, int num_m, int num_n, int num_tiles, int warp, int lane, int* err,
@@ -380,7 +380,7 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
   const int half = (warp - 2) >> 2;
   const int row_in_tile = quarter * 32 + lane;
   const float alpha = ep.alpha != nullptr ? *ep.alpha : 1.f;
-  constexpr int PIECES = BN / CW;
+  constexpr int PIECES = TN / CW;
   int acc = 0;
   uint32_t acc_phase = 0;
   const int num_units = num_tiles * ep.splits;
@@ -403,7 +403,7 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
     const int row = mb * BM + row_in_tile;
 #pragma unroll 1
     for (int c = half; c < PIECES; c += 2) {
-      const int col0 = nb * BN + c * CW;
+      const int col0 = nb * TN + c * CW;
       if (col0 >= N) break;
       float v[CW];
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * CW;
@@ -497,16 +497,17 @@ __device__ __noinline__ void coll_copy_warp(const CollParams& c, uint32_t epoch,
   }
 }
 
-template <bool A_MN, bool B_MN, bool COLL, int KIND>
+template <bool A_MN, bool B_MN, bool COLL, int KIND, int TN = BN>
 __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtensorMap& tma_b, const CUtensorMap& tma_d,
                                           const CUtensorMap& tma_aux, int M, int N, int K, const EpiParams& ep, int* err,
                                           const CollParams* coll) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  constexpr int TB_BYTES = TN * BK * 2;  // one stage of the B tile
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sEpi = smem + STAGES * (A_BYTES + B_BYTES);  // 1024-byte aligned staging tiles
+  uint8_t* sEpi = smem + STAGES * (A_BYTES + TB_BYTES);  // 1024-byte aligned staging tiles
 
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -517,7 +518,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + BN - 1) / BN;
+  const int num_n = (N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
   const int num_units = num_tiles * ep.splits;
   const int kblocks = (K + BK - 1) / BK;
@@ -569,7 +570,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
       tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
       if (COLL && coll->a_mode == 1) mb = coll_phys_mblock(*coll, mb);
       split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
-      const int m0 = mb * BM, n0 = nb * BN;
+      const int m0 = mb * BM, n0 = nb * TN;
       int tile_src = 0, tile_lrow = 0, tile_b = 0;  // A source of this tile: 0 local map, 1 own shard, 2 gathered copy
       if (COLL && c_amode == 1) {
         // A tile of a remote block: the whole warp polls the block's slice flags in parallel
@@ -604,7 +605,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
         }
         if (COLL && lane == 0) {
           uint8_t* a_dst = sA + stage * A_BYTES;
-          uint8_t* b_dst = sB + stage * B_BYTES;
+          uint8_t* b_dst = sB + stage * TB_BYTES;
           const int k0 = kb * BK;
           int b_owner = c_rank, b_row = 0, b_b = 0, a_owner2 = c_rank, a_row2 = 0, a_b2 = 0;
           if (c_amode == 2) seq_owner(*coll, k0, a_owner2, a_row2, a_b2);
@@ -617,7 +618,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
             ok = wait_published(*coll, b_owner, epoch, err);
             ready_mask |= 1u << b_owner;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
+          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + TB_BYTES);
           if (tile_src == 1) {
             tma_load_3d(a_dst, own_map, &full_bar[stage], k0, tile_lrow, tile_b);
           } else if (tile_src == 2) {
@@ -633,19 +634,19 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
           }
           if (c_bmode == 2) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
+            for (int j = 0; j < TN / 64; ++j)
               tma_load_3d(b_dst + j * BK * 128, &coll->b[b_owner], &full_bar[stage], n0 + 64 * j, b_row, b_b);
           } else if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], n0 + 64 * j, k0);
+            for (int j = 0; j < TN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], n0 + 64 * j, k0);
           } else {
             tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, n0);
           }
         } else if (lane == 0) {
           uint8_t* a_dst = sA + stage * A_BYTES;
-          uint8_t* b_dst = sB + stage * B_BYTES;
+          uint8_t* b_dst = sB + stage * TB_BYTES;
           const int k0 = kb * BK;
-          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
+          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + TB_BYTES);
           if (A_MN) {
             tma_load_2d(a_dst, &tma_a, &full_bar[stage], m0, k0);
             tma_load_2d(a_dst + BK * 128, &tma_a, &full_bar[stage], m0 + 64, k0);
@@ -654,7 +655,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
           }
           if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], n0 + 64 * j, k0);
+            for (int j = 0; j < TN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], n0 + 64 * j, k0);
           } else {
             tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, n0);
           }
@@ -670,7 +671,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+    constexpr uint32_t idesc = umma_idesc_bf16(BM, TN, A_MN, B_MN);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -681,7 +682,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
       split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
       if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, err, 2)) break;
       tc_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * BN;
+      const uint32_t d_tmem = tmem_base + acc * BN;  // accumulator buffers 256 columns apart for every tile width
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full_bar[stage], phase, err, 3)) {
           ok = false;
@@ -690,7 +691,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
         tc_fence_after();
         if (lane == 0) {
           const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * TB_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t adesc = A_MN ? umma_desc_sw128(a_addr + k * 2048, BK * 128, 1024)
@@ -723,13 +724,13 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
     uint8_t* tile = sEpi + (warp - 2) * EPI_STAGE_BYTES;
     if constexpr (KIND == kKindGeneric) {
       if (ep.d_fp32)
-        epilogue_loop<32, KIND>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp,
+        epilogue_loop<32, KIND, TN>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp,
                                 lane, err, COLL ? coll : nullptr);
       else
-        epilogue_loop<64, KIND>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp,
+        epilogue_loop<64, KIND, TN>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp,
                                 lane, err, COLL ? coll : nullptr);
     } else {
-      epilogue_loop<KIND == kKindF32 ? 32 : 64, KIND>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m,
+      epilogue_loop<KIND == kKindF32 ? 32 : 64, KIND, TN>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m,
                                                       num_n, num_tiles, warp, lane, err, nullptr);
     }
   }
@@ -754,12 +755,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
   }
 }
 
-template <bool A_MN, bool B_MN, int KIND>
+template <bool A_MN, bool B_MN, int KIND, int TN = BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
                 EpiParams ep, int* err) {
-  gemm_body<A_MN, B_MN, false, KIND>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, nullptr);
+  gemm_body<A_MN, B_MN, false, KIND, TN>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, nullptr);
 }
 
 template <bool A_MN, bool B_MN>
@@ -978,19 +979,36 @@ static void check_operand(const at::Tensor& t, const char* name) {
   HT_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
 }
 
-template <bool A_MN, bool B_MN, int KIND>
+template <bool A_MN, bool B_MN, int KIND, int TN = BN>
 static void launch_kind(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
                         int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
-  auto kernel = gemm_kernel<A_MN, B_MN, KIND>;
+  auto kernel = gemm_kernel<A_MN, B_MN, KIND, TN>;
+  constexpr int smem = STAGES * (A_BYTES + TN * BK * 2) + EPI_WARPS * EPI_STAGE_BYTES + 1024;
   static bool configured = false;
   if (!configured) {
-    HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * ep.splits;
+  const int units = ((M + BM - 1) / BM) * ((N + TN - 1) / TN) * ep.splits;
   const int grid = std::min(units, num_sms());
-  kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, md, maux, M, N, K, ep, err);
+  kernel<<<grid, THREADS, smem, s>>>(ma, mb, md, maux, M, N, K, ep, err);
   HT_CUDA_CHECK(cudaGetLastError());
+}
+
+// Output-tile width: 256 columns, or 192 when it packs the tiles into fewer full waves over the
+// SMs (N = 768: 192 tiles of 128 x 256 fill 148 SMs 1.3 times, 256 tiles of 128 x 192 fill them
+// 1.7 times, so the last wave idles less).  Cost model: waves x tile width (per-tile time grows
+// with its width); the narrow tile must win by 10 % to be used.
+static constexpr int NARROW_TN = 192;
+
+static int choose_tile_n(int64_t M, int64_t N, int splits) {
+  if (splits > 1 || N % 64 != 0) return BN;
+  const int sms = num_sms();
+  auto cost = [&](int tn) {
+    const long long tiles = ((M + BM - 1) / BM) * ((N + tn - 1) / tn);
+    return (double)((tiles + sms - 1) / sms) * tn;
+  };
+  return cost(NARROW_TN) < 0.9 * cost(BN) ? NARROW_TN : BN;
 }
 
 // The epilogue kind that covers `ep` with the least code.
@@ -1005,7 +1023,17 @@ static int epilogue_kind(const EpiParams& ep) {
 
 template <bool A_MN, bool B_MN>
 static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
-                   int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
+                   int N, int K, const EpiParams& ep, int* err, cudaStream_t s, int tn = BN) {
+  if constexpr (!A_MN) {  // the narrow tile exists for the forward and data-gradient products (A K-major)
+    if (tn == NARROW_TN) {
+      switch (epilogue_kind(ep)) {
+        case kKindBf16: launch_kind<A_MN, B_MN, kKindBf16, NARROW_TN>(ma, mb, md, maux, M, N, K, ep, err, s); return;
+        case kKindGelu: launch_kind<A_MN, B_MN, kKindGelu, NARROW_TN>(ma, mb, md, maux, M, N, K, ep, err, s); return;
+        case kKindGeluBwd: launch_kind<A_MN, B_MN, kKindGeluBwd, NARROW_TN>(ma, mb, md, maux, M, N, K, ep, err, s); return;
+        default: break;
+      }
+    }
+  }
   switch (epilogue_kind(ep)) {
     case kKindBf16: launch_kind<A_MN, B_MN, kKindBf16>(ma, mb, md, maux, M, N, K, ep, err, s); break;
     case kKindF32: launch_kind<A_MN, B_MN, kKindF32>(ma, mb, md, maux, M, N, K, ep, err, s); break;
@@ -1073,8 +1101,6 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   }
   const CUtensorMap ma = a_mn_major ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64)
                                     : make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
-  const CUtensorMap mb = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64)
-                                    : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
   // TMA output path: aligned rows, and a store or an fp32 accumulate (beta = 1); the GELU
   // pre-activation is written through its own map when D is bf16.  GEMMs with too few output
   // tiles to fill the GPU (weight gradients: small M x N, long K) split K over several CTAs
@@ -1112,10 +1138,17 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
     ep.tma_aux = epilogue == kGelu ? 1 : 0;
     ep.reduce_add = beta == 1.0 ? 1 : 0;
   }
+  // The narrow tile is compiled for A K-major products with the bf16 / GELU / GELU' epilogues; the
+  // K-major B map's box must match the tile width the kernel expects.
+  const int kind = epilogue_kind(ep);
+  const bool narrow_ok = !a_mn_major && (kind == kKindBf16 || kind == kKindGelu || kind == kKindGeluBwd);
+  const int tn = narrow_ok ? choose_tile_n(M, N, ep.splits) : BN;
+  const CUtensorMap mb = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64)
+                                    : make_map(b.data_ptr(), N, K, b.stride(0), 64, tn);
   int* err = error_word(a.device());
   cudaStream_t s = stream();
-  if (!a_mn_major && !b_mn_major) launch<false, false>(ma, mb, md, maux, M, N, K, ep, err, s);
-  else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, md, maux, M, N, K, ep, err, s);
+  if (!a_mn_major && !b_mn_major) launch<false, false>(ma, mb, md, maux, M, N, K, ep, err, s, tn);
+  else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, md, maux, M, N, K, ep, err, s, tn);
   else if (a_mn_major && b_mn_major) launch<true, true>(ma, mb, md, maux, M, N, K, ep, err, s);
   else launch<true, false>(ma, mb, md, maux, M, N, K, ep, err, s);
   if (splits > 1 && !split_reduce_add) {

@@ -66,6 +66,33 @@ def test_gemm_epilogues() -> None:
     assert _rel(out, ref_acc) < 1e-5
 
 
+@pytest.mark.parametrize("m,n,k", [(8192, 768, 256), (2048, 3072, 128), (4096, 768, 192), (8192, 2304, 64)])
+def test_gemm_tile_widths_on_model_shapes(m: int, n: int, k: int) -> None:
+    """N = 768 / 3072 outputs run 128 x 192 tiles (fewer idle SMs in the last wave), N = 2304 runs 128 x 256:
+    plain, GELU and GELU' epilogues, B K-major (forward) and MN-major (data gradient), against fp32 PyTorch."""
+    ops = _ops()
+    dev = torch.device("cuda")
+    a = torch.randn(m, k, device=dev).bfloat16()
+    w = (torch.randn(n, k, device=dev) * 0.05).bfloat16()
+    bias = torch.randn(n, device=dev)
+    ref = a.float() @ w.float().t() + bias
+    y = ops.gemm(a, w, bias=bias)
+    assert _rel(y, ref) < 1e-2
+    pre = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    h = ops.gemm(a, w, bias=bias, aux=pre, epilogue=ops.EPI_GELU)
+    assert _rel(pre, ref) < 1e-2
+    assert _rel(h, torch.nn.functional.gelu(ref, approximate="tanh")) < 1e-2
+    wt = (torch.randn(k, n, device=dev) * 0.05).bfloat16()  # [K, N] read MN-major
+    ref_mn = a.float() @ wt.float()
+    assert _rel(ops.gemm(a, wt, b_mn_major=True), ref_mn) < 1e-2
+    dpre = torch.randn(m, n, device=dev).bfloat16()
+    dx = ops.gemm(a, wt, b_mn_major=True, aux=dpre, epilogue=ops.EPI_GELU_BWD)
+    x = dpre.float()
+    t = torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))
+    dgelu = 0.5 * (1 + t) + 0.5 * x * (1 - t * t) * 0.7978845608028654 * (1 + 3 * 0.044715 * x * x)
+    assert _rel(dx, ref_mn * dgelu) < 2e-2
+
+
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 def test_gemm_split_k_weight_gradient_shapes(out_dtype: torch.dtype) -> None:
     """Few output tiles and a long K: the K loop is split and the partials are summed in order."""
