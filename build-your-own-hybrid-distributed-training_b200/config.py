@@ -244,10 +244,11 @@ class TensorParallelConfig:
     def __post_init__(self) -> None:
         _check(self.init_method_std > 0, "config.TensorParallelConfig", "init_method_std has to be greater than zero", "> 0",
                self.init_method_std, "a standard deviation like 0.02 works for transformer weights")
-        _check(self.context_parallel_algorithm in ("all_gather", "ring"), "config.TensorParallelConfig",
+        _check(self.context_parallel_algorithm in ("all_gather", "ring", "ulysses"), "config.TensorParallelConfig",
                "unknown context_parallel_algorithm (attention under sequence_parallel_mode='independent')",
-               ["all_gather", "ring"], self.context_parallel_algorithm,
-               "use 'all_gather' (fewer transfers) or 'ring' (memory per rank independent of the sequence length)")
+               ["all_gather", "ring", "ulysses"], self.context_parallel_algorithm,
+               "use 'all_gather' (fewer transfers), 'ring' (memory per rank independent of the sequence length) or "
+               "'ulysses' (all-to-all to head groups; the flash kernel runs on the whole sequence)")
 
 
 @dataclass(frozen=True)

@@ -78,6 +78,7 @@ class ParallelPlan:
     sequence_parallel: bool = False
     vocab_parallel: bool = True
     ring_attention: bool = False  # context parallelism: pass keys/values around the ring instead of all-gathering
+    ulysses_attention: bool = False  # context parallelism: all-to-all from sequence chunks to head groups and back
 
     @property
     def context_parallel(self) -> bool:
@@ -171,8 +172,9 @@ class TensorParallelAttention(nn.Module):
         positions.  Scores are materialised per chunk (``S / C x S``): this is the all-gather
         form of context parallelism, which the reference describes but does not implement
         (``docs/06_sequence_parallelism.md:234-256``; its ``independent`` mode gives
-        attention only the local chunk).  A ring with online softmax is the form that also
-        bounds memory; it is not built.
+        attention only the local chunk).  ``context_parallel_algorithm`` selects instead the ring
+        with online softmax (memory per rank independent of the sequence) or Ulysses (all-to-all
+        to head groups, then the flash kernel over the whole sequence).
         """
         if attention_mask is not None:
             raise UnsupportedFeatureError(format_error(
@@ -185,6 +187,19 @@ class TensorParallelAttention(nn.Module):
         if self.rope_theta is not None:
             cos, sin = self._rope(local * cp.size, qkv.device)
             qkv = ops.apply_rope(qkv, cos[offset:offset + local].contiguous(), sin[offset:offset + local].contiguous(), h, hkv, d)
+        if self.plan.ulysses_attention:
+            from ..parallel.context_parallel import ulysses_attention
+
+            if self.dropout > 0.0 and self.training:
+                raise UnsupportedFeatureError(format_error(
+                    "models.attention", "attention dropout is not implemented by Ulysses attention", expected="dropout=0",
+                    observed=self.dropout, resolution="disable attention dropout or use context_parallel_algorithm='all_gather'"))
+            if h % cp.size or hkv % cp.size:
+                raise UnsupportedFeatureError(format_error(
+                    "models.attention", "Ulysses attention gives every rank of the sequence group an equal share of the heads",
+                    expected=f"query and key/value head counts divisible by {cp.size}", observed=f"{h} and {hkv}",
+                    resolution="use context_parallel_algorithm='ring' or 'all_gather' for this head count"))
+            return ulysses_attention(qkv.contiguous(), h, hkv, d, cp, causal=self.causal).to(qkv.dtype)
         q = qkv[..., : h * d]
         if self.plan.ring_attention:
             from ..parallel.context_parallel import ring_attention

@@ -453,6 +453,347 @@ __global__ void __launch_bounds__(THREADS, DkvCfg<D>::MIN_BLOCKS)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ------------------------------------------------------------------------------------------------
+// Fused dK, dV and dQ for D = 64 (used when bitwise reproducibility is not required).
+//
+// One CTA per (128-key tile, kv head, batch), 14 warps, one CTA per SM.  For each query head of
+// the group and each 128-query tile at or after the key tile:
+//   S^T = K Q^T and dP^T = V dO^T into TMEM (M = 128 keys, N = 128 queries);
+//   eight element-wise warps (two per TMEM lane quarter, 64 queries each) form P^T and
+//   dS^T = P^T (dP^T - delta) and write them as bf16 into shared memory, 128-byte swizzled;
+//   dV += P^T dO and dK += dS^T Q read them there as K-major A operands, and dQ_tile = dS K reads
+//   the same dS^T bytes as an MN-major A operand;
+//   four epilogue warps add dQ_tile (fp32, double-buffered in TMEM) into a global fp32 dQ
+//   accumulator with TMA reduce-adds, whose order across key tiles is not fixed.
+// The MMA of the next tile's S^T / dP^T starts as soon as the element-wise warps have read the
+// current one, so the tensor cores and the exponentials overlap.  S and dP are computed once per
+// (key tile, query tile), against twice in the reproducible two-kernel path.
+// TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ [384,448) and [448,512).
+// ------------------------------------------------------------------------------------------------
+struct FusedCfg {
+  static constexpr int D = 64, BKV = 128, BQ = 128;
+  static constexpr int TILE = 128 * 64 * 2;  // one 128-row x 64-column bf16 tile (16 KB)
+  static constexpr int STAGES = 2;
+  static constexpr int OFF_K = 0, OFF_V = TILE, OFF_Q = 2 * TILE;  // stage s: Q at OFF_Q + 2 s TILE, dO next to it
+  static constexpr int OFF_P = OFF_Q + STAGES * 2 * TILE;          // P^T: two 64-query chunks of 128 key rows
+  static constexpr int OFF_DS = OFF_P + 2 * TILE;                  // dS^T: same layout
+  static constexpr int OFF_DQ = OFF_DS + 2 * TILE;                 // dQ staging: 4 warps x 2 pieces x 4 KB
+  static constexpr int PIECE = 32 * 128;
+  static constexpr int SMEM = OFF_DQ + 4 * 2 * PIECE + 1024;
+  static constexpr uint32_t ST_COL = 0, DPT_COL = 128, DV_COL = 256, DK_COL = 320, DQ_COL = 384;
+  static constexpr int THREADS = 448;  // warp 0 TMA, warp 1 MMA, warps 2..9 element-wise, warps 10..13 dQ
+};
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(FusedCfg::THREADS, 1)
+    fused_bwd_kernel(const __grid_constant__ CUtensorMap map_qkv128, const __grid_constant__ CUtensorMap map_do128,
+                     const __grid_constant__ CUtensorMap map_dqkv128, const __grid_constant__ CUtensorMap map_dq_acc,
+                     const float* __restrict__ lse, const float* __restrict__ delta, int S, int H, int HKV, int causal,
+                     float scale, int* err) {
+  using C = FusedCfg;
+  constexpr int D = C::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sP = smem + C::OFF_P;
+  uint8_t* sDS = smem + C::OFF_DS;
+
+  __shared__ __align__(8) uint64_t kv_ready, s_full, st_free, p_ready, pd_free, acc_full, kv_staged;
+  __shared__ __align__(8) uint64_t q_full[C::STAGES], q_empty[C::STAGES], dq_full[2], dq_free[2];
+  __shared__ uint32_t tmem_slot;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkt = (S + C::BKV - 1) / C::BKV;
+  const int kt = nkt - 1 - (int)blockIdx.x;  // causal: early key tiles see the most queries; launch them first
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int group = H / HKV;
+  const int kv0 = kt * C::BKV;
+  const int nqt = (S + C::BQ - 1) / C::BQ;
+  const int first_qt = causal ? kv0 / C::BQ : 0;
+  const int per_head = nqt - first_qt;
+  const int n_steps = per_head * group;
+  const float scale_log2 = scale * LOG2E;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&kv_ready, 1);
+    mbar_init(&s_full, 1);
+    mbar_init(&st_free, 8);
+    mbar_init(&p_ready, 8);
+    mbar_init(&pd_free, 1);
+    mbar_init(&acc_full, 1);
+    mbar_init(&kv_staged, 256);
+    for (int i = 0; i < C::STAGES; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_free[i], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  auto step_head = [&](int t) { return hk * group + t / per_head; };
+  auto step_q0 = [&](int t) { return (first_qt + t % per_head) * C::BQ; };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&kv_ready, 2 * C::TILE);
+      tma_load_3d(sK, &map_qkv128, &kv_ready, (H + hk) * D, kv0, b);
+      tma_load_3d(sV, &map_qkv128, &kv_ready, (H + HKV + hk) * D, kv0, b);
+      for (int t = 0; t < n_steps; ++t) {
+        const int st = t % C::STAGES;
+        if (!mbar_wait(&q_empty[st], ((t / C::STAGES) & 1) ^ 1u, err, 51)) break;
+        mbar_arrive_expect_tx(&q_full[st], 2 * C::TILE);
+        uint8_t* q_dst = smem + C::OFF_Q + st * 2 * C::TILE;
+        tma_load_3d(q_dst, &map_qkv128, &q_full[st], step_head(t) * D, step_q0(t), b);
+        tma_load_3d(q_dst + C::TILE, &map_do128, &q_full[st], step_head(t) * D, step_q0(t), b);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);   // S^T, dP^T
+    constexpr uint32_t idesc_kv = umma_idesc_bf16(128, D, false, true);    // dV, dK: A K-major (smem), B MN-major
+    constexpr uint32_t idesc_q = umma_idesc_bf16(128, D, true, true);      // dQ: A = dS MN-major, B = K MN-major
+    const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sP), dsa = smem_u32(sDS);
+    bool ok = mbar_wait(&kv_ready, 0, err, 52);
+    for (int j = 0; j <= n_steps && ok; ++j) {
+      if (j < n_steps) {
+        const int st = j % C::STAGES;
+        if (!mbar_wait(&q_full[st], (j / C::STAGES) & 1, err, 53)) break;
+        if (j > 0 && !mbar_wait(&st_free, (j - 1) & 1, err, 54)) break;  // S^T / dP^T of step j-1 read
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qa = smem_u32(smem + C::OFF_Q + st * 2 * C::TILE), da = qa + C::TILE;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            tc_mma_f16(tmem + C::ST_COL, umma_desc_sw128(ka + k * 32, 16, 1024), umma_desc_sw128(qa + k * 32, 16, 1024),
+                       idesc_s, k != 0 ? 1u : 0u);
+            tc_mma_f16(tmem + C::DPT_COL, umma_desc_sw128(va + k * 32, 16, 1024), umma_desc_sw128(da + k * 32, 16, 1024),
+                       idesc_s, k != 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full);
+        }
+        __syncwarp();
+      }
+      if (j > 0) {
+        const int i = j - 1, sti = i % C::STAGES, buf = i & 1;
+        if (!mbar_wait(&p_ready, i & 1, err, 55)) break;              // P^T / dS^T of step i in shared memory
+        if (i >= 2 && !mbar_wait(&dq_free[buf], ((i >> 1) - 1) & 1, err, 56)) break;  // dQ buffer drained
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qa = smem_u32(smem + C::OFF_Q + sti * 2 * C::TILE), da = qa + C::TILE;
+#pragma unroll
+          for (int kk = 0; kk < C::BQ / 16; ++kk) {
+            const uint32_t aoff = (kk >> 2) * C::TILE + (kk & 3) * 32;
+            tc_mma_f16(tmem + C::DV_COL, umma_desc_sw128(pa + aoff, 16, 1024), umma_desc_sw128(da + kk * 2048, C::TILE, 1024),
+                       idesc_kv, (i > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16(tmem + C::DK_COL, umma_desc_sw128(dsa + aoff, 16, 1024), umma_desc_sw128(qa + kk * 2048, C::TILE, 1024),
+                       idesc_kv, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < C::BKV / 16; ++kk)
+            tc_mma_f16(tmem + C::DQ_COL + buf * D, umma_desc_sw128(dsa + kk * 2048, C::TILE, 1024),
+                       umma_desc_sw128(ka + kk * 2048, C::TILE, 1024), idesc_q, kk > 0 ? 1u : 0u);
+          tc_commit(&pd_free);
+          tc_commit(&q_empty[sti]);
+          tc_commit(&dq_full[buf]);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) tc_commit(&acc_full);
+    __syncwarp();
+  } else if (warp < 10) {
+    // ---------------- element-wise: P^T and dS^T ----------------
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;  // key row within the tile
+    const int kv = kv0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    for (int t = 0; t < n_steps; ++t) {
+      const int h = step_head(t), qb = step_q0(t);
+      // Per-query statistics come straight from global memory (every lane of a warp reads the
+      // same addresses, so each is one broadcast load); no barrier among the warps is needed.
+      const long long row0 = ((long long)b * H + h) * S;
+      const int qh = qb + half * 64;  // first query of this thread's 64
+      if (!mbar_wait(&s_full, t & 1, err, 57)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool edge = (qb + C::BQ > S) || (causal && qb < kv0 + C::BKV);
+      uint32_t pp[32], pd[32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {  // 16 queries per chunk
+        float ls[16], dl[16];
+        const int qc = qh + c * 16;
+        if (qc + 16 <= S && ((row0 + qc) & 3) == 0) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 l4 = __ldg(reinterpret_cast<const float4*>(lse + row0 + qc) + u);
+            const float4 d4 = __ldg(reinterpret_cast<const float4*>(delta + row0 + qc) + u);
+            ls[4 * u] = l4.x; ls[4 * u + 1] = l4.y; ls[4 * u + 2] = l4.z; ls[4 * u + 3] = l4.w;
+            dl[4 * u] = d4.x; dl[4 * u + 1] = d4.y; dl[4 * u + 2] = d4.z; dl[4 * u + 3] = d4.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const long long qi = row0 + min(qc + e, S - 1);
+            ls[e] = __ldg(lse + qi);
+            dl[e] = __ldg(delta + qi);
+          }
+        }
+        float sv[16], dp[16];
+        tmem_ld_32x32b_x16(tmem + lane_off + C::ST_COL + half * 64 + c * 16, sv);
+        tmem_ld_32x32b_x16(tmem + lane_off + C::DPT_COL + half * 64 + c * 16, dp);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const float2 l2 = make_float2(ls[e] * LOG2E, ls[e + 1] * LOG2E);
+          const float2 d2 = make_float2(dl[e], dl[e + 1]);
+          float p0 = fast_exp2(fmaf(sv[e], scale_log2, -l2.x));
+          float p1 = fast_exp2(fmaf(sv[e + 1], scale_log2, -l2.y));
+          if (edge) {
+            const int qa = qc + e;
+            if (qa >= S || (causal && qa < kv)) p0 = 0.f;
+            if (qa + 1 >= S || (causal && qa + 1 < kv)) p1 = 0.f;
+          }
+          pp[c * 8 + e / 2] = pack2(p0, p1);
+          pd[c * 8 + e / 2] = pack2(p0 * (dp[e] - d2.x), p1 * (dp[e + 1] - d2.y));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st_free);  // TMEM S^T / dP^T may be overwritten by the next tile
+      if (t > 0 && !mbar_wait(&pd_free, (t - 1) & 1, err, 58)) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = sP + half * C::TILE + r * 128;
+      uint8_t* drow = sDS + half * C::TILE + r * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int off = (u ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + off) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+        *reinterpret_cast<uint4*>(drow + off) = make_uint4(pd[4 * u], pd[4 * u + 1], pd[4 * u + 2], pd[4 * u + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_ready);
+    }
+    // ---------------- dV / dK epilogue ----------------
+    if (ok && mbar_wait(&acc_full, 0, err, 59)) {
+      tc_fence_after();
+      uint8_t* buf = half == 0 ? sV : sK;  // no MMA reads K or V any more
+      const uint32_t col = half == 0 ? C::DV_COL : C::DK_COL;
+      const float f = half == 0 ? 1.f : scale;
+      uint8_t* row = buf + r * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+        if (n_steps > 0) {
+          tmem_ld_32x32b_x32(tmem + lane_off + col + c * 32, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 pkd;
+          pkd.x = pack2(v[u * 8 + 0] * f, v[u * 8 + 1] * f);
+          pkd.y = pack2(v[u * 8 + 2] * f, v[u * 8 + 3] * f);
+          pkd.z = pack2(v[u * 8 + 4] * f, v[u * 8 + 5] * f);
+          pkd.w = pack2(v[u * 8 + 6] * f, v[u * 8 + 7] * f);
+          const int unit = c * 4 + u;
+          *reinterpret_cast<uint4*>(row + ((unit ^ (r & 7)) << 4)) = pkd;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&kv_staged);  // every element-wise thread; the storing thread waits (bounded)
+      if (threadIdx.x == 64 && mbar_wait(&kv_staged, 0, err, 61)) {
+        tma_store_3d(&map_dqkv128, sK, (H + hk) * D, kv0, b);
+        tma_store_3d(&map_dqkv128, sV, (H + HKV + hk) * D, kv0, b);
+        bulk_commit();
+        bulk_wait_all();
+      }
+    }
+  } else {
+    // ---------------- dQ: TMEM -> fp32 reduce-add into the global accumulator ----------------
+    const int quarter = warp & 3;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint8_t* stage = smem + C::OFF_DQ + (warp - 10) * 2 * C::PIECE;
+    for (int i = 0; i < n_steps; ++i) {
+      const int buf = i & 1;
+      if (!mbar_wait(&dq_full[buf], (i >> 1) & 1, err, 60)) break;
+      tc_fence_after();
+      const int h = step_head(i), qb = step_q0(i);
+#pragma unroll
+      for (int piece = 0; piece < 2; ++piece) {
+        float v[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + C::DQ_COL + buf * D + piece * 32, v);
+        uint4 units[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          units[j] = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                                __float_as_uint(v[4 * j + 3]));
+        uint8_t* tile = stage + piece * C::PIECE;
+        if (lane == 0) bulk_wait_read_all();  // the previous reduce-add from this staging tile has read it
+        __syncwarp();
+        uint8_t* row = tile + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = units[j];
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&map_dq_acc, tile, h * D + piece * 32, b * S + qb + quarter * 32);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_free[buf]);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// dqkv[b, s, h*D + d] = bf16(scale * acc[(b*S + s), h*D + d]) for the query columns of dqkv.
+__global__ void __launch_bounds__(256) dq_finish_kernel(const float4* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv,
+                                                        long long rows, int hd4, long long row_stride, float scale) {
+  const long long n = rows * hd4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / hd4;
+    const int c = (int)(i - row * hd4);
+    const float4 v = acc[i];
+    __align__(8) __nv_bfloat16 o[4] = {f2bf(v.x * scale), f2bf(v.y * scale), f2bf(v.z * scale), f2bf(v.w * scale)};
+    *reinterpret_cast<uint2*>(dqkv + row * row_stride + 4 * c) = *reinterpret_cast<const uint2*>(o);
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
                                    const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -511,9 +852,50 @@ static void launch(const at::Tensor& qkv, const at::Tensor& dout, const at::Tens
                                                    (int)S, H, HKV, causal ? 1 : 0, scale, err);
 }
 
+// fp32 [rows][cols] map with 32-column x 32-row boxes and the 128-byte swizzle (dQ accumulator).
+static CUtensorMap make_acc_map(void* base, int64_t rows, int64_t cols) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 4)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult res = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  HT_CHECK(res == CUDA_SUCCESS, "cuTensorMapEncodeTiled (dQ accumulator) failed with code ", (int)res);
+  return map;
+}
+
+static void launch_fused(const at::Tensor& qkv, const at::Tensor& dout, const at::Tensor& lse, const at::Tensor& delta,
+                         at::Tensor& dqkv, int H, int HKV, bool causal, float scale, int* err, cudaStream_t s) {
+  constexpr int D = FusedCfg::D;
+  const int64_t B = qkv.size(0), S = qkv.size(1), W = qkv.size(2);
+  at::Tensor acc = at::zeros({B * S, (int64_t)H * D}, qkv.options().dtype(at::kFloat));
+  const CUtensorMap q128 = make_map(qkv.data_ptr(), B, S, W, 128);
+  const CUtensorMap do128 = make_map(dout.data_ptr(), B, S, (int64_t)H * D, 128);
+  const CUtensorMap dqkv128 = make_map(dqkv.data_ptr(), B, S, W, 128);
+  const CUtensorMap macc = make_acc_map(acc.data_ptr(), B * S, (int64_t)H * D);
+  static bool once = [] {
+    set_smem(fused_bwd_kernel, FusedCfg::SMEM);
+    return true;
+  }();
+  (void)once;
+  const dim3 grid((unsigned)((S + 127) / 128), (unsigned)HKV, (unsigned)B);
+  fused_bwd_kernel<<<grid, FusedCfg::THREADS, FusedCfg::SMEM, s>>>(q128, do128, dqkv128, macc, lse.data_ptr<float>(),
+                                                                   delta.data_ptr<float>(), (int)S, H, HKV, causal ? 1 : 0,
+                                                                   scale, err);
+  HT_CUDA_CHECK(cudaGetLastError());
+  const long long rows = B * S;
+  const int hd4 = H * D / 4;
+  const int blocks = (int)std::min<long long>((rows * hd4 + 255) / 256, 8LL * num_sms());
+  dq_finish_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(acc.data_ptr<float>()),
+                                          reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), rows, hd4, W, scale);
+}
+
 }  // namespace attn_bwd
 
 int* attention_error_word(const at::Device& dev);
+bool deterministic_reductions();
 
 // Runs both backward kernels after the caller has filled `delta`; returns false (nothing
 // launched) when the tensor-core path does not apply.
@@ -525,7 +907,10 @@ bool attention_backward_tcgen05(at::Tensor qkv, at::Tensor dout, at::Tensor lse,
   bind_context(qkv.device().index());
   int* err = attention_error_word(qkv.device());
   cudaStream_t s = stream();
-  if (D == 64) attn_bwd::launch<64>(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, err, s);
+  // D = 64 without the reproducibility requirement: one fused kernel (dQ summed by reduce-adds).
+  if (D == 64 && !deterministic_reductions() && (H * D) % 32 == 0)
+    attn_bwd::launch_fused(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, err, s);
+  else if (D == 64) attn_bwd::launch<64>(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, err, s);
   else attn_bwd::launch<128>(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, err, s);
   HT_CUDA_CHECK(cudaGetLastError());
   return true;

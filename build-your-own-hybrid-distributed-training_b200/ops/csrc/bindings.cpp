@@ -21,6 +21,7 @@ void norm_backward(c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dr, a
                    at::Tensor rstd, at::Tensor dres, c10::optional<at::Tensor> ddelta, at::Tensor part_w,
                    c10::optional<at::Tensor> part_b, bool rms);
 int64_t norm_backward_blocks(int64_t rows);
+void sum_rows_pair(at::Tensor part_a, at::Tensor out_a, double beta_a, at::Tensor part_b, at::Tensor out_b, double beta_b);
 void sum_rows(at::Tensor part, at::Tensor out, double beta);
 void gelu_backward(at::Tensor g, at::Tensor pre, at::Tensor out);
 void swiglu_forward(at::Tensor h, at::Tensor out);
@@ -63,6 +64,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_forward", &ht::norm_forward);
   m.def("norm_backward", &ht::norm_backward);
   m.def("norm_backward_blocks", &ht::norm_backward_blocks);
+  m.def("sum_rows_pair", &ht::sum_rows_pair, "two column reductions (a norm's weight and bias gradients) in one launch");
   m.def("sum_rows", &ht::sum_rows);
   m.def("gelu_backward", &ht::gelu_backward);
   m.def("swiglu_forward", &ht::swiglu_forward);

@@ -371,6 +371,41 @@ __global__ void __launch_bounds__(SR_WARPS * 32) sum_rows_kernel(const float* __
   }
 }
 
+// Two independent column reductions in one launch (the weight and bias gradients of a norm):
+// blocks [0, strips) reduce `part_a` into `out_a`, the rest `part_b` into `out_b`, each exactly as
+// sum_rows_kernel does (same order, same result).
+__global__ void __launch_bounds__(SR_WARPS * 32) sum_rows_pair_kernel(const float* __restrict__ part_a, float* __restrict__ out_a,
+                                                                       float beta_a, const float* __restrict__ part_b,
+                                                                       float* __restrict__ out_b, float beta_b, int nrows, int d,
+                                                                       int strips) {
+  __shared__ float red[SR_WARPS][33];
+  const bool second = (int)blockIdx.x >= strips;
+  const float* part = second ? part_b : part_a;
+  float* out = second ? out_b : out_a;
+  const float beta = second ? beta_b : beta_a;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = (second ? blockIdx.x - strips : blockIdx.x) * 32 + tx;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (c < d) {
+    int r = ty;
+    for (; r + 3 * SR_WARPS < nrows; r += 4 * SR_WARPS) {
+      s0 += part[(long long)r * d + c];
+      s1 += part[(long long)(r + SR_WARPS) * d + c];
+      s2 += part[(long long)(r + 2 * SR_WARPS) * d + c];
+      s3 += part[(long long)(r + 3 * SR_WARPS) * d + c];
+    }
+    for (; r < nrows; r += SR_WARPS) s0 += part[(long long)r * d + c];
+  }
+  red[ty][tx] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (ty == 0 && c < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < SR_WARPS; ++k) t += red[k][tx];
+    out[c] = t + (beta != 0.f ? beta * out[c] : 0.f);
+  }
+}
+
 // Vectors of 4 per lane for the warp-per-row kernels (2, 4, 6 or 8), or 0 when d does not fit.
 inline int warp_vectors(int d) {
   if (d % 4 != 0 || d > 32 * 4 * 8) return 0;
@@ -544,6 +579,21 @@ void norm_backward(c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dr, a
   };
   if (rms) with_dy(std::true_type{});
   else with_dy(std::false_type{});
+  HT_CUDA_CHECK(cudaGetLastError());
+}
+
+void sum_rows_pair(at::Tensor part_a, at::Tensor out_a, double beta_a, at::Tensor part_b, at::Tensor out_b, double beta_b) {
+  const c10::cuda::CUDAGuard guard(part_a.device());
+  for (const at::Tensor* t : {&part_a, &out_a, &part_b, &out_b})
+    HT_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous(), "sum_rows_pair takes contiguous fp32 tensors");
+  HT_CHECK(part_a.dim() == 2 && part_b.sizes() == part_a.sizes(), "sum_rows_pair: the two partial blocks must have one shape");
+  const int nrows = part_a.size(0), d = part_a.size(1);
+  HT_CHECK(out_a.numel() == d && out_b.numel() == d, "sum_rows_pair output size mismatch");
+  if (d == 0) return;
+  const int strips = (d + 31) / 32;
+  norm::sum_rows_pair_kernel<<<2 * strips, norm::SR_WARPS * 32, 0, stream()>>>(
+      part_a.data_ptr<float>(), out_a.data_ptr<float>(), (float)beta_a, part_b.data_ptr<float>(), out_b.data_ptr<float>(),
+      (float)beta_b, nrows, d, strips);
   HT_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -21,7 +21,7 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import extension
-from .grads import deliver_grad
+from .grads import adopt_exposed_gradient, deliver_grad, has_main_grad, main_grad_beta
 
 __all__ = ["add_norm", "layer_norm", "rms_norm"]
 
@@ -72,6 +72,15 @@ class _AddNormFunction(torch.autograd.Function):
         part_b = torch.empty(blocks, d, dtype=torch.float32, device=r.device) if ctx.has_bias else None
         ext.norm_backward(dy2, dr2, r, weight, mean, rstd, dres, ddelta, part_w, part_b, bool(ctx.rms))
         dw = db = None
+        w, bp = ctx.weight_param, ctx.bias_param
+        if ctx.has_bias and ctx.needs_input_grad[2] and ctx.needs_input_grad[3] and has_main_grad(w) and has_main_grad(bp):
+            # Both reductions in one launch, straight into the two main_grad slices.
+            adopt_exposed_gradient(w, from_autograd=False)
+            adopt_exposed_gradient(bp, from_autograd=False)
+            ext.sum_rows_pair(part_w, w.main_grad, main_grad_beta(w), part_b, bp.main_grad, main_grad_beta(bp))
+            deliver_grad(w, compute=_written)
+            deliver_grad(bp, compute=_written)
+            return (dres.view(ctx.shape), None if ddelta is None else ddelta.view(ctx.shape), None, None, None, None, None)
         if ctx.needs_input_grad[2]:
             dw = deliver_grad(ctx.weight_param, compute=lambda out, beta: ext.sum_rows(part_w, out, beta),
                               value=None if getattr(ctx.weight_param, "main_grad", None) is not None else part_w.sum(0).to(ctx.weight_param.dtype))
@@ -79,6 +88,10 @@ class _AddNormFunction(torch.autograd.Function):
             db = deliver_grad(ctx.bias_param, compute=lambda out, beta: ext.sum_rows(part_b, out, beta),
                               value=None if getattr(ctx.bias_param, "main_grad", None) is not None else part_b.sum(0).to(ctx.bias_param.dtype))
         return (dres.view(ctx.shape), None if ddelta is None else ddelta.view(ctx.shape), dw, db, None, None, None)
+
+
+def _written(out: torch.Tensor, beta: float) -> None:
+    """Delivery of a gradient that a combined launch has already written into ``main_grad``."""
 
 
 def add_norm(residual: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, bias: torch.Tensor | None = None,

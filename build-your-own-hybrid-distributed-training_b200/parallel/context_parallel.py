@@ -1,4 +1,6 @@
-"""Ring attention: context parallelism whose memory per rank does not grow with the sequence.
+"""Context parallelism: ring attention and Ulysses all-to-all attention.
+
+Ring attention is the form whose memory per rank does not grow with the sequence.
 
 The ranks of a sequence group hold consecutive chunks of the sequence.  Each rank keeps its
 query chunk and passes key/value chunks around the ring (send to ``r + 1``, receive from
@@ -28,7 +30,7 @@ import torch
 from ..distributed.collectives import recv_tensor, send_tensor
 from ..distributed.groups import GroupHandle
 
-__all__ = ["ring_attention"]
+__all__ = ["ring_attention", "ulysses_attention"]
 
 
 def _ring_pass(tensors: list[torch.Tensor], group: GroupHandle) -> list[torch.Tensor]:
@@ -126,3 +128,58 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group: Gro
         s = _scores(q.float(), k.float(), 1.0 / math.sqrt(q.shape[-1]), causal)
         return (torch.softmax(s, -1) @ v.float()).to(dtype)
     return _RingAttention.apply(q.float().contiguous(), k.float().contiguous(), v.float().contiguous(), group, causal).to(dtype)
+
+
+# ------------------------------------------------------------------------------------------------
+# Ulysses: all-to-all between sequence chunks and head groups.
+# ------------------------------------------------------------------------------------------------
+class _AllToAll(torch.autograd.Function):
+    """Equal-split all-to-all along dim 0; its adjoint is the same exchange applied to the gradient."""
+
+    @staticmethod
+    def forward(ctx: Any, x: torch.Tensor, group: GroupHandle) -> torch.Tensor:
+        from ..distributed.collectives import all_to_all_tensor
+
+        ctx.group = group
+        return all_to_all_tensor(x.contiguous(), group)
+
+    @staticmethod
+    def backward(ctx: Any, grad: torch.Tensor) -> tuple[Any, ...]:
+        from ..distributed.collectives import all_to_all_tensor
+
+        return all_to_all_tensor(grad.contiguous(), ctx.group), None
+
+
+def ulysses_attention(qkv: torch.Tensor, num_heads: int, num_kv_heads: int, head_dim: int, group: GroupHandle, *,
+                      causal: bool = True) -> torch.Tensor:
+    """Context-parallel attention by re-sharding from sequence chunks to head groups and back.
+
+    ``qkv``: ``[B, L, (H + 2 Hkv) * D]``, this rank's chunk of ``L = S / C`` consecutive positions
+    (rotary positions already applied with the global offset).  One all-to-all gives every rank
+    the whole sequence for ``H / C`` query heads and ``Hkv / C`` key/value heads; ordinary causal
+    attention runs on that (the native flash kernel on CUDA, so context parallelism uses the same
+    tensor-core kernel as the single-GPU path); a second all-to-all returns each rank's positions
+    for all heads.  Returns ``[B, L, H * D]``.  Needs ``H`` and ``Hkv`` divisible by ``C``.
+
+    The reference describes this scheme (``docs/06_sequence_parallelism.md:247-251``) and
+    provides ``all_to_all_tensor`` (``distributed/collectives.py:614-666``) without using it.
+    """
+    from .. import ops
+
+    c = group.size
+    b, length, _ = qkv.shape
+    h, hkv, d = num_heads, num_kv_heads, head_dim
+    hl, hkvl = h // c, hkv // c
+    if c == 1:
+        return ops.attention(qkv, h, hkv, d, causal=causal)
+    q = qkv[..., : h * d].reshape(b, length, c, hl * d)
+    k = qkv[..., h * d:(h + hkv) * d].reshape(b, length, c, hkvl * d)
+    v = qkv[..., (h + hkv) * d:].reshape(b, length, c, hkvl * d)
+    # [C (destination head group), B, L, local packed qkv] -> exchange -> [C (source chunk), B, L, ...]
+    send = torch.cat([q, k, v], dim=-1).permute(2, 0, 1, 3)
+    recv = _AllToAll.apply(send, group)
+    full = recv.permute(1, 0, 2, 3).reshape(b, c * length, (hl + 2 * hkvl) * d)  # the whole sequence, local heads
+    context = ops.attention(full.contiguous(), hl, hkvl, d, causal=causal)      # [B, S, hl * d]
+    back = context.reshape(b, c, length, hl * d).permute(1, 0, 2, 3)          # [C (destination chunk), B, L, hl*d]
+    mine = _AllToAll.apply(back, group)                                        # [C (source head group), B, L, hl*d]
+    return mine.permute(1, 2, 0, 3).reshape(b, length, h * d)

@@ -125,7 +125,8 @@ def build_model(config: ExperimentConfig, context: DistributedContext, *, device
                 observed=str(config.mixed_precision.compute_dtype),
                 resolution="enable bf16 mixed precision (fp32 compute is available on the CPU path)"))
         plan = ParallelPlan(tensor_group=tensor, sequence_group=sequence, sequence_parallel=sp, vocab_parallel=tensor.size > 1,
-                            ring_attention=config.tensor_parallel.context_parallel_algorithm == "ring")
+                            ring_attention=config.tensor_parallel.context_parallel_algorithm == "ring",
+                            ulysses_attention=config.tensor_parallel.context_parallel_algorithm == "ulysses")
         return TinyTransformer(config.model, plan, seed=config.training.seed, device=device,
                                compute_dtype=config.mixed_precision.compute_dtype)
     if sp:
@@ -180,9 +181,12 @@ def describe_parallel_plan(config: ExperimentConfig, context: DistributedContext
                      ("reduce-scatter in the data-gradient GEMM epilogue" if fused_tp else f"{library} reduce-scatter")
                      if sp else f"{library} all-reduce"))
     if independent:
-        ring = config.tensor_parallel.context_parallel_algorithm == "ring"
-        add(PlanStep("forward", "attention keys / values", topo.sequence_group_name,
-                     f"{library} send/recv ring with online-softmax merge" if ring else f"{library} all-gather"))
+        algorithm = config.tensor_parallel.context_parallel_algorithm
+        add(PlanStep("forward", "attention keys / values" if algorithm != "ulysses" else "attention sequence <-> head re-shard",
+                     topo.sequence_group_name,
+                     {"ring": f"{library} send/recv ring with online-softmax merge",
+                      "ulysses": f"{library} all-to-all to head groups, flash attention over the whole sequence, all-to-all back"}
+                     .get(algorithm, f"{library} all-gather")))
     if shard > 1:
         fused_fsdp = cuda and config.fsdp.fused_update
         add(PlanStep("forward", "flat-parameter all-gather per unit", "shard",

@@ -270,6 +270,35 @@ def test_attention_forward_backward(d: int, h: int, hkv: int, s: int, causal: bo
     assert _rel(qkv.grad, ref_in.grad) < 3e-2, _rel(qkv.grad, ref_in.grad)
 
 
+@pytest.mark.parametrize("h,hkv,s,causal", [(4, 4, 128, True), (4, 2, 100, True), (2, 1, 700, True), (2, 2, 300, False),
+                                             (12, 12, 1024, True), (3, 3, 260, False)])
+def test_attention_backward_fused_kernel(h: int, hkv: int, s: int, causal: bool) -> None:
+    """D = 64 backward as one kernel (dQ summed by reduce-adds) against fp32 PyTorch and the two-kernel path."""
+    ops = _ops()
+    dev = torch.device("cuda")
+    d, bsz = 64, 2
+    qkv0 = (torch.randn(bsz, s, (h + 2 * hkv) * d, device=dev) * 0.5).bfloat16()
+    g = torch.randn(bsz, s, h * d, device=dev).bfloat16()
+    grads = {}
+    for deterministic in (True, False):
+        qkv = qkv0.clone().requires_grad_(True)
+        try:
+            ops.set_deterministic_reductions(deterministic)
+            out = ops.attention(qkv, h, hkv, d, causal=causal)
+            out.backward(g)
+        finally:
+            ops.set_deterministic_reductions(True)
+        grads[deterministic] = qkv.grad.float()
+    ref_in = qkv0.float().cpu().requires_grad_(True)
+    ref = ops.reference_attention(ref_in, h, hkv, d, causal=causal)
+    ref.backward(g.float().cpu())
+    q_cols, kv_cols = h * d, hkv * d
+    for name, sl in (("dq", slice(0, q_cols)), ("dk", slice(q_cols, q_cols + kv_cols)), ("dv", slice(q_cols + kv_cols, None))):
+        fused, ordered, want = grads[False][..., sl], grads[True][..., sl], ref_in.grad[..., sl]
+        assert _rel(fused, want) < 3e-2, (name, _rel(fused, want))
+        assert _rel(fused, ordered) < 2e-2, (name, _rel(fused, ordered))
+
+
 def test_attention_lse_and_error_word() -> None:
     """The forward's log-sum-exp (used by the backward) and the kernel's timeout word."""
     ops = _ops()

@@ -173,9 +173,10 @@ def test_launcher_exports_the_rendezvous_environment() -> None:
 
 
 @pytest.mark.parametrize("kind,algorithm,world", [("gpt2", "all_gather", 2), ("llama", "all_gather", 2), ("gpt2", "ring", 2),
-                                                  ("llama", "ring", 4)])
+                                                  ("llama", "ring", 4), ("gpt2", "ulysses", 2), ("llama", "ulysses", 2),
+                                                  ("gpt2", "ulysses", 4)])
 def test_independent_sequence_parallel_matches_single_process(kind: str, algorithm: str, world: int) -> None:
-    """``independent`` mode is context parallelism: every chunk attends to the whole prefix (all-gather or ring)."""
+    """``independent`` mode is context parallelism: every chunk attends to the whole prefix (all-gather, ring or Ulysses)."""
     ref = launch_workers(W.transformer_forward_worker, 1, args=(1, False, kind), timeout_seconds=300)[0].value
     for r in launch_workers(R.independent_sp_worker, world, args=(kind, algorithm), timeout_seconds=300):
         assert abs(r.value["loss"] - ref["loss"]) < 1e-5
