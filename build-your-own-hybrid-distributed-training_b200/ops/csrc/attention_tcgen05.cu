@@ -167,9 +167,13 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
         for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e]);
       }
-      const float m_new = fmaxf(m, mx * scale_log2);
+      // Lazy rescaling: the running maximum moves only when the tile's maximum exceeds it by more
+      // than 8 (a factor of 256 in the exponentials, harmless in fp32 sums and bf16 probabilities),
+      // so the O rows are rarely rescaled after the first tiles.
+      const float m_cand = fmaxf(m, mx * scale_log2);
+      const float m_new = (m_cand > m + 8.f) ? m_cand : m;
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = fast_exp2(m - m_use);
+      const float alpha = m_new == m ? 1.f : fast_exp2(m - m_use);
       // Pass 2: p = 2^(s * scale - m), row sum, P as bf16 pairs into TMEM.
       float rs = 0.f;
 #pragma unroll 1
@@ -180,7 +184,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = fast_exp2(fmaf(v[e], scale_log2, -m_use)), p1 = fast_exp2(fmaf(v[e + 1], scale_log2, -m_use));
+          // Half of the exponentials on the MUFU unit, half on the FMA pipe (exp2_poly).
+          const float p0 = fast_exp2(fmaf(v[e], scale_log2, -m_use)), p1 = exp2_poly(fmaf(v[e + 1], scale_log2, -m_use));
           rs += p0 + p1;
           __nv_bfloat162 pr = __floats2bfloat162_rn(p0, p1);
           pk[e / 2] = *reinterpret_cast<uint32_t*>(&pr);

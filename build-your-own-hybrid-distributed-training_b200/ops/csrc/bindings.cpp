@@ -22,6 +22,7 @@ void norm_backward(c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dr, a
                    c10::optional<at::Tensor> part_b, bool rms);
 int64_t norm_backward_blocks(int64_t rows);
 void sum_rows_pair(at::Tensor part_a, at::Tensor out_a, double beta_a, at::Tensor part_b, at::Tensor out_b, double beta_b);
+void exp2_poly_eval(at::Tensor x, at::Tensor poly, at::Tensor mufu);
 void sum_rows(at::Tensor part, at::Tensor out, double beta);
 void gelu_backward(at::Tensor g, at::Tensor pre, at::Tensor out);
 void swiglu_forward(at::Tensor h, at::Tensor out);
@@ -65,6 +66,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_backward", &ht::norm_backward);
   m.def("norm_backward_blocks", &ht::norm_backward_blocks);
   m.def("sum_rows_pair", &ht::sum_rows_pair, "two column reductions (a norm's weight and bias gradients) in one launch");
+  m.def("exp2_poly_eval", &ht::exp2_poly_eval, "the FMA-pipe 2^x of the attention softmax next to exp2f (tests)");
   m.def("sum_rows", &ht::sum_rows);
   m.def("gelu_backward", &ht::gelu_backward);
   m.def("swiglu_forward", &ht::swiglu_forward);

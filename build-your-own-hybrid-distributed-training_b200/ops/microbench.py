@@ -90,10 +90,12 @@ def bench_gemm(only: str | None, iters: int) -> None:
 ATTN_SHAPES = {"gpt2": (8, 1024, 12, 12, 64), "llama8b": (1, 4096, 32, 8, 128)}
 
 
-def bench_attention(shape: str, once: bool) -> None:
+def bench_attention(shape: str, once: bool, fast: bool = False) -> None:
+    """``fast``: the backward without the reproducibility requirement (one fused kernel at D = 64)."""
     from ._ext import extension
 
     ext = extension()
+    ext.set_deterministic_reductions(not fast)
     dev = torch.device("cuda")
     b, s, h, hkv, d = ATTN_SHAPES[shape]
     scale = 1.0 / math.sqrt(d)
@@ -112,7 +114,7 @@ def bench_attention(shape: str, once: bool) -> None:
         return
     flops = 4.0 * b * h * s * s * d / 2  # causal
     tf, tb = _time(fwd, 10), _time(bwd, 10)
-    print(f"attention {shape} B={b} S={s} H={h} Hkv={hkv} D={d}: forward {tf * 1e3:.1f} us ({flops / tf / 1e9:.0f} TFLOP/s), "
+    print(f"attention {shape}{' (fast backward)' if fast else ''} B={b} S={s} H={h} Hkv={hkv} D={d}: forward {tf * 1e3:.1f} us ({flops / tf / 1e9:.0f} TFLOP/s), "
           f"backward {tb * 1e3:.1f} us ({2.5 * flops / tb / 1e9:.0f} TFLOP/s)", flush=True)
 
 
@@ -300,6 +302,7 @@ def main(argv: list[str] | None = None) -> None:
     a = sub.add_parser("attention")
     a.add_argument("--shape", choices=list(ATTN_SHAPES), default="gpt2")
     a.add_argument("--once", action="store_true")
+    a.add_argument("--fast", action="store_true", help="backward without the reproducibility requirement")
     n = sub.add_parser("norm")
     n.add_argument("--once", action="store_true")
     t = sub.add_parser("tp-layer")
@@ -312,7 +315,7 @@ def main(argv: list[str] | None = None) -> None:
     if args.what == "gemm":
         bench_gemm(args.only, args.iters)
     elif args.what == "attention":
-        bench_attention(args.shape, args.once)
+        bench_attention(args.shape, args.once, args.fast)
     elif args.what == "norm":
         bench_norm(args.once)
     elif args.what == "tp-layer":

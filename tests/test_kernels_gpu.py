@@ -392,3 +392,21 @@ def test_embedding_swiglu_rope() -> None:
     rot_ref = torch.cat([qk * c[None, :, None] + rotated * s_[None, :, None], x[:, :, 3:]], 2).reshape(2, 16, 256)
     assert _rel(rot, rot_ref) < 1e-2
     assert torch.equal(rot[..., 192:], qkv[..., 192:])  # values untouched
+
+
+def test_fma_pipe_exp2_is_within_its_error_bound() -> None:
+    """The polynomial 2^x that shares the softmax exponentials with the MUFU unit, against exp2f."""
+    ops = _ops()
+    ext = ops.extension()
+    dev = torch.device("cuda")
+    x = torch.cat([torch.linspace(-126.0, 0.0, 1 << 20, device=dev), -torch.rand(1 << 20, device=dev) * 40,
+                   torch.tensor([0.0, -0.5, -0.49999997, -1.0, -125.5, -126.0, -200.0, float("-inf")], device=dev)])
+    poly, mufu = torch.empty_like(x), torch.empty_like(x)
+    ext.exp2_poly_eval(x, poly, mufu)
+    exact = torch.exp2(x.double())
+    normal = exact > 2.0 ** -125
+    rel = ((poly.double() - exact).abs() / exact)[normal]
+    assert float(rel.max()) < 1.1e-4, float(rel.max())  # the fitted bound is 1.0e-4
+    assert float(((mufu.double() - exact).abs() / exact)[normal].max()) < 1e-5
+    assert float(poly[~normal].abs().max()) < 2.0 ** -124  # clamped inputs underflow towards zero
+    assert torch.isfinite(poly).all() and (poly >= 0).all()
