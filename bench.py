@@ -57,8 +57,8 @@ def _args() -> argparse.Namespace:
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["native", "reference"], default="native")
     p.add_argument("--no-graph", action="store_true", help="native arm: run eagerly instead of replaying a CUDA graph")
-    p.add_argument("--no-overlap-step", action="store_true",
-                   help="native arm: run the optimizer update after the backward pass instead of bucket by bucket during it")
+    p.add_argument("--overlap-step", action="store_true",
+                   help="native arm: run the optimizer update bucket by bucket during the backward pass (default: after it)")
     p.add_argument("--config", choices=list(CONFIGS), default="gpt2_ddp",
                    help="gpt2_ddp (the headline, default); llama_fsdp (1.3B full shard, S2048, 4/GPU); llama_tp_sp "
                         "(Llama-3-8B, TP=N with SP, S4096, micro-batch 1); llama_hybrid (Llama-3-8B, DP2 x TP N/2 with SP, "
@@ -177,7 +177,7 @@ def main() -> None:
     model_name, micro_batch, seq, accum = CONFIGS[args.config]
     extra = {"config": args.config, "grad_accum": accum}
     if args.impl == "native":
-        extra["overlap_step"] = not args.no_overlap_step
+        extra["overlap_step"] = args.overlap_step
     result = runner(steps=args.steps, warmup=args.warmup, micro_batch=micro_batch, seq=seq,
                     use_graph=not args.no_graph, clock_start=(sampler.start if sampler else None),
                     clock_stop=(sampler.stop if sampler else None), **extra)
@@ -205,7 +205,7 @@ def main() -> None:
                        "grad_accum": accum, "bucket_cap_mb": 25, "optimizer": "AdamW fp32 master",
                        "l2": "no flush: per-step working set of several GB exceeds the 126 MB L2",
                        "cuda_graph": (not args.no_graph) if args.impl == "native" else False,
-                       "optimizer_update": ("bucket by bucket during the backward" if not args.no_overlap_step
+                       "optimizer_update": ("bucket by bucket during the backward" if args.overlap_step
                                             else "after the backward") if args.impl == "native" else "after the backward"},
             "clocks": result.get("clocks", {}),
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": result["h2d_bytes_per_step"],

@@ -73,7 +73,7 @@ CONFIGS = ("gpt2_ddp", "llama_fsdp", "llama_tp_sp", "llama_hybrid")
 
 
 def experiment(world: int, *, micro_batch: int, seq: int, samples: int, use_graph: bool, config: str = "gpt2_ddp",
-               grad_accum: int = 1, overlap_step: bool = True) -> ExperimentConfig:
+               grad_accum: int = 1, overlap_step: bool = False) -> ExperimentConfig:
     """The ExperimentConfig of one benchmark configuration on ``world`` GPUs."""
     common = dict(backend="nccl", device="cuda", timeout_seconds=600.0,
                   data=DataConfig(micro_batch_size=micro_batch, sequence_length=seq, num_train_samples=samples,
@@ -144,7 +144,7 @@ def _exposed_communication_ms(engine: TrainingEngine, stream: Any, take: Callabl
 
 def run(*, steps: int, warmup: int, micro_batch: int, seq: int, use_graph: bool = True,
         clock_start: Callable[[], None] | None = None, clock_stop: Callable[[], dict] | None = None,
-        config: str = "gpt2_ddp", grad_accum: int = 1, overlap_step: bool = True) -> dict:
+        config: str = "gpt2_ddp", grad_accum: int = 1, overlap_step: bool = False) -> dict:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     cfg = experiment(world, micro_batch=micro_batch, seq=seq,
                      samples=micro_batch * world * grad_accum * (2 * steps + warmup + 9), use_graph=use_graph,

@@ -6,7 +6,7 @@ as the numerical oracle) and CUDA tensors (the native kernels in
 :class:`~hybrid_training.errors.KernelError`).
 """
 
-from ._ext import build_extension, extension, extension_path, has_extension
+from ._ext import build_checked_extension, build_extension, checked_extension, extension, extension_path, has_extension
 from .attention import apply_rope, attention, reference_attention, rope_tables
 from .embedding import embedding
 from .grads import deliver_grad, has_main_grad, reset_main_grad_state
@@ -25,7 +25,9 @@ __all__ = [
     "add_norm",
     "apply_rope",
     "attention",
+    "build_checked_extension",
     "build_extension",
+    "checked_extension",
     "compute_weight",
     "cross_entropy",
     "deliver_grad",

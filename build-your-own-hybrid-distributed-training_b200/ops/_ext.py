@@ -24,7 +24,8 @@ from types import ModuleType
 
 from ..errors import KernelError, format_error
 
-__all__ = ["ARCH_FLAGS", "build_extension", "extension", "extension_path", "has_extension"]
+__all__ = ["ARCH_FLAGS", "build_checked_extension", "build_extension", "checked_extension", "checked_extension_path",
+           "extension", "extension_path", "has_extension"]
 
 _HERE = Path(__file__).resolve().parent
 _CSRC = _HERE / "csrc"
@@ -93,6 +94,54 @@ def build_extension(verbose: bool = False, jobs: int | None = None) -> Path:
         tmp.write_bytes(built.read_bytes())
         tmp.replace(target)
     return target
+
+
+_CHECKED_NAME = "_C_checked"
+_checked_module: ModuleType | None = None
+
+
+def checked_extension_path() -> Path:
+    suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
+    return _HERE / f"{_CHECKED_NAME}{suffix}"
+
+
+def build_checked_extension(verbose: bool = False) -> Path:
+    """Compile the bounds-checked module (``csrc/checked``, ``-DHT_BOUNDS_CHECK``) next to the regular one."""
+    from torch.utils import cpp_extension
+
+    build_dir = _HERE / "_build_checked"
+    build_dir.mkdir(exist_ok=True)
+    cuda_flags = [*ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "--use_fast_math", "--expt-relaxed-constexpr", "-DNDEBUG",
+                  f"-I{_CSRC}"]
+    cpp_extension.load(name=_CHECKED_NAME, sources=[str(_CSRC / "checked" / "checked_ops.cu")], build_directory=str(build_dir),
+                       extra_cflags=["-O3", "-std=c++17", f"-I{_CSRC}"], extra_cuda_cflags=cuda_flags,
+                       extra_ldflags=_libstdcxx_link_flags(), verbose=verbose, is_python_module=True, with_cuda=True)
+    built = build_dir / f"{_CHECKED_NAME}.so"
+    target = checked_extension_path()
+    if built.exists():
+        tmp = target.with_suffix(".tmp")
+        tmp.write_bytes(built.read_bytes())
+        tmp.replace(target)
+    return target
+
+
+def checked_extension() -> ModuleType:
+    """The bounds-checked module (built by :func:`build_checked_extension`); raises if it is missing."""
+    global _checked_module
+    if _checked_module is None:
+        path = checked_extension_path()
+        if not path.exists():
+            raise KernelError(format_error("ops.checked_extension", "the bounds-checked module has not been built",
+                                           expected=str(path), observed="missing",
+                                           resolution="run hybrid_training.ops.build_checked_extension()"))
+        import torch  # noqa: F401
+
+        spec = importlib.util.spec_from_file_location(f"hybrid_training.ops.{_CHECKED_NAME}", path)
+        assert spec is not None and spec.loader is not None
+        module = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(module)
+        _checked_module = module
+    return _checked_module
 
 
 def extension() -> ModuleType:

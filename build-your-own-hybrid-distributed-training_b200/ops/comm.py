@@ -51,13 +51,14 @@ def nvls_available(workspace: Any, flat: torch.Tensor) -> bool:
 
 
 def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int, scale: float, *,
-                      wide: bool = True) -> torch.Tensor:
+                      wide: bool = True, peer_slots: int = 0) -> torch.Tensor:
     """Average ``flat[start:start+numel]`` over the workspace's group in place; returns the status tensor.
 
     ``wide=False`` launches the narrow shape that runs beside a persistent GEMM (for buckets
     reduced while the backward pass is still computing); ``wide=True`` the full-width shape for a
     reduction that has the GPU to itself.  ``HT_NVLS=1`` selects the NVLink-switch reduction where
-    the allocation has a multicast address; otherwise the two-shot P2P kernel runs.
+    the allocation has a multicast address; otherwise the two-shot P2P kernel runs.  ``peer_slots``
+    (2, 4 or 8) selects a kernel instantiation for at least that many peers (tests only).
     """
     handle = workspace.handle_of(flat)
     world = workspace.group.size
@@ -65,7 +66,7 @@ def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int
     mc = int(getattr(handle, "multicast_ptr", 0) or 0) if os.environ.get("HT_NVLS", "0") == "1" else 0
     extension().bucket_all_reduce(flat, list(handle.buffer_ptrs), list(handle.signal_pad_ptrs), mc, int(start), int(numel),
                                   float(scale), int(handle.rank), base, max_blocks, workspace.status, _TIMEOUT_S,
-                                  bool(wide))
+                                  bool(wide), int(peer_slots))
     return workspace.status
 
 

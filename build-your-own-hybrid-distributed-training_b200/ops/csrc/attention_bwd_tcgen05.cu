@@ -513,6 +513,8 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
   __shared__ __align__(8) uint64_t kv_ready, s_full, st_free, p_ready, pd_free, acc_full, kv_staged;
   __shared__ __align__(8) uint64_t q_full[C::STAGES], q_empty[C::STAGES], dq_full[2], dq_free[2];
   __shared__ uint32_t tmem_slot;
+  // Per stage: lse and delta of the step's 128 queries, bulk-copied with the Q / dO tiles.
+  __shared__ __align__(16) float s_stats[C::STAGES][2][C::BQ];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkt = (S + C::BKV - 1) / C::BKV;
@@ -562,10 +564,19 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
       for (int t = 0; t < n_steps; ++t) {
         const int st = t % C::STAGES;
         if (!mbar_wait(&q_empty[st], ((t / C::STAGES) & 1) ^ 1u, err, 51)) break;
-        mbar_arrive_expect_tx(&q_full[st], 2 * C::TILE);
+        // The statistics of queries qb .. qb + n - 1 (n rounded down to a multiple of 4 floats; the
+        // element-wise warps read the ragged tail from global memory).
+        const int qb = step_q0(t);
+        const int nstat = (min(C::BQ, S - qb) / 4) * 4;
+        const long long row0 = ((long long)b * H + step_head(t)) * S + qb;
+        mbar_arrive_expect_tx(&q_full[st], 2 * C::TILE + 2 * nstat * 4);
         uint8_t* q_dst = smem + C::OFF_Q + st * 2 * C::TILE;
-        tma_load_3d(q_dst, &map_qkv128, &q_full[st], step_head(t) * D, step_q0(t), b);
-        tma_load_3d(q_dst + C::TILE, &map_do128, &q_full[st], step_head(t) * D, step_q0(t), b);
+        tma_load_3d(q_dst, &map_qkv128, &q_full[st], step_head(t) * D, qb, b);
+        tma_load_3d(q_dst + C::TILE, &map_do128, &q_full[st], step_head(t) * D, qb, b);
+        if (nstat > 0) {
+          bulk_load(s_stats[st][0], lse + row0, nstat * 4, &q_full[st]);
+          bulk_load(s_stats[st][1], delta + row0, nstat * 4, &q_full[st]);
+        }
       }
     }
     __syncwarp();
@@ -632,10 +643,19 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
     bool ok = true;
     for (int t = 0; t < n_steps; ++t) {
       const int h = step_head(t), qb = step_q0(t);
-      // Per-query statistics come straight from global memory (every lane of a warp reads the
-      // same addresses, so each is one broadcast load); no barrier among the warps is needed.
+      // Per-query statistics: in shared memory, bulk-copied with this step's Q / dO tiles (the
+      // q_full phase of the stage covers them); the ragged tail beyond a multiple of 4 comes from
+      // global memory.
       const long long row0 = ((long long)b * H + h) * S;
       const int qh = qb + half * 64;  // first query of this thread's 64
+      const int st = t % C::STAGES;
+      const int nstat = (min(C::BQ, S - qb) / 4) * 4;
+      if (!mbar_wait(&q_full[st], (t / C::STAGES) & 1, err, 62)) {
+        ok = false;
+        break;
+      }
+      const float* sl = s_stats[st][0] + half * 64;
+      const float* sd = s_stats[st][1] + half * 64;
       if (!mbar_wait(&s_full, t & 1, err, 57)) {
         ok = false;
         break;
@@ -647,20 +667,21 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
       for (int c = 0; c < 4; ++c) {  // 16 queries per chunk
         float ls[16], dl[16];
         const int qc = qh + c * 16;
-        if (qc + 16 <= S && ((row0 + qc) & 3) == 0) {
+        if (qc + 16 - qb <= nstat) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const float4 l4 = __ldg(reinterpret_cast<const float4*>(lse + row0 + qc) + u);
-            const float4 d4 = __ldg(reinterpret_cast<const float4*>(delta + row0 + qc) + u);
+            const float4 l4 = reinterpret_cast<const float4*>(sl + c * 16)[u];
+            const float4 d4 = reinterpret_cast<const float4*>(sd + c * 16)[u];
             ls[4 * u] = l4.x; ls[4 * u + 1] = l4.y; ls[4 * u + 2] = l4.z; ls[4 * u + 3] = l4.w;
             dl[4 * u] = d4.x; dl[4 * u + 1] = d4.y; dl[4 * u + 2] = d4.z; dl[4 * u + 3] = d4.w;
           }
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const long long qi = row0 + min(qc + e, S - 1);
-            ls[e] = __ldg(lse + qi);
-            dl[e] = __ldg(delta + qi);
+            const int q = min(qc + e, S - 1);  // queries past the end reuse the last one's (finite) statistics
+            const int k = q - qb;
+            ls[e] = k < nstat ? s_stats[st][0][k] : __ldg(lse + row0 + q);
+            dl[e] = k < nstat ? s_stats[st][1][k] : __ldg(delta + row0 + q);
           }
         }
         float sv[16], dp[16];

@@ -44,7 +44,7 @@ void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Ten
                         int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
 void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
                        int64_t start, int64_t numel, double scale, int64_t rank, int64_t slot_base, int64_t max_blocks,
-                       at::Tensor status, double timeout_s, bool wide);
+                       at::Tensor status, double timeout_s, bool wide, int64_t min_peer_slots);
 void fsdp_reduce_scatter_adamw(at::Tensor staging, std::vector<int64_t> grad_ptrs, std::vector<int64_t> pad_ptrs, int64_t rank,
                                int64_t shard, int64_t valid, double scale, at::Tensor param, at::Tensor exp_avg,
                                at::Tensor exp_avg_sq, at::Tensor shard16, c10::optional<at::Tensor> grad_out, at::Tensor hyper,

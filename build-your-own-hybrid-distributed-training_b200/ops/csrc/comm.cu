@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(THREADS) barrier_probe_kernel(uint32_t* pad0, 
 
 void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
                        int64_t start, int64_t numel, double scale, int64_t rank, int64_t slot_base, int64_t max_blocks,
-                       at::Tensor status, double timeout_s, bool wide) {
+                       at::Tensor status, double timeout_s, bool wide, int64_t min_peer_slots) {
   const c10::cuda::CUDAGuard guard(flat.device());
   const int world = (int)buffer_ptrs.size();
   HT_CHECK(world >= 2 && world <= comm::MAX_RANKS, "bucket_all_reduce supports 2..8 ranks");
@@ -464,13 +464,16 @@ void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::v
                                              world, (int)slot_base, status.data_ptr<int>(), (unsigned long long)(timeout_s * 1e9));
   };
   constexpr int NT = comm::AR_THREADS, WT = comm::AR_WIDE_THREADS, NB = comm::AR_MIN_BLOCKS;
+  // The instantiation for up to `slots` peers (2, 4 or 8); `min_peer_slots` can ask for a wider one
+  // than the group needs (tests run the 8-peer code on two GPUs that way).
+  const int slots = std::max<int>(world, (int)min_peer_slots);
   if (wide) {
-    if (world <= 2) launch(comm::bucket_allreduce_kernel<2, WT, 1>, WT);
-    else if (world <= 4) launch(comm::bucket_allreduce_kernel<4, WT, 1>, WT);
+    if (slots <= 2) launch(comm::bucket_allreduce_kernel<2, WT, 1>, WT);
+    else if (slots <= 4) launch(comm::bucket_allreduce_kernel<4, WT, 1>, WT);
     else launch(comm::bucket_allreduce_kernel<8, WT, 1>, WT);
   } else {
-    if (world <= 2) launch(comm::bucket_allreduce_kernel<2, NT, NB>, NT);
-    else if (world <= 4) launch(comm::bucket_allreduce_kernel<4, NT, NB>, NT);
+    if (slots <= 2) launch(comm::bucket_allreduce_kernel<2, NT, NB>, NT);
+    else if (slots <= 4) launch(comm::bucket_allreduce_kernel<4, NT, NB>, NT);
     else launch(comm::bucket_allreduce_kernel<8, NT, NB>, NT);
   }
   HT_CUDA_CHECK(cudaGetLastError());

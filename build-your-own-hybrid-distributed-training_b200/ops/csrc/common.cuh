@@ -21,6 +21,28 @@
 
 namespace ht {
 
+// Index checks of the bounds-checked build (`-DHT_BOUNDS_CHECK`, compiled as the separate module
+// `_C_checked` from csrc/checked/): HT_IN_BOUNDS(i, n, code) is true when 0 <= i < n; otherwise it
+// records (1, code, i, n) in the module's error word -- the first failure wins -- and the caller
+// skips the access.  In the regular build it is the constant `true` and costs nothing.  This is
+// the stand-in for a memory checker where compute-sanitizer is not available: the checked kernels
+// run the same tests and must leave the word at zero.
+#ifdef HT_BOUNDS_CHECK
+static __device__ long long ht_bounds_word[4];
+__device__ __forceinline__ bool ht_in_bounds(long long i, long long n, int code) {
+  if (i >= 0 && i < n) return true;
+  if (atomicCAS(reinterpret_cast<unsigned long long*>(&ht_bounds_word[0]), 0ull, 1ull) == 0ull) {
+    ht_bounds_word[1] = code;
+    ht_bounds_word[2] = i;
+    ht_bounds_word[3] = n;
+  }
+  return false;
+}
+#define HT_IN_BOUNDS(i, n, code) ::ht::ht_in_bounds((long long)(i), (long long)(n), (code))
+#else
+#define HT_IN_BOUNDS(i, n, code) true
+#endif
+
 // Upper bound on polls of any spin-wait inside a kernel; past it the kernel records
 // an error code and stops waiting instead of hanging the GPU.
 constexpr long long kSpinLimit = 1ll << 22;
@@ -149,6 +171,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
           smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
+}
+// Untiled bulk copy global -> shared (both addresses and the size multiples of 16 bytes),
+// completing on `bar` with its byte count.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 // Shared -> global tile store / fp32 reduce-add through the tensor map (bulk-group completion).
 // Rows and columns outside the map's extents are clipped by the hardware.

@@ -10,6 +10,7 @@ namespace ew {
 __global__ void gelu_backward_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ pre,
                                      __nv_bfloat16* __restrict__ out, long long n8) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    if (!HT_IN_BOUNDS(i, n8, 1)) continue;
     uint4 gv = reinterpret_cast<const uint4*>(g)[i];
     uint4 pv = reinterpret_cast<const uint4*>(pre)[i];
     const __nv_bfloat16* ga = reinterpret_cast<const __nv_bfloat16*>(&gv);
@@ -29,6 +30,7 @@ __global__ void swiglu_forward_kernel(const __nv_bfloat16* __restrict__ h, __nv_
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / f;
     const int c = i - r * f;
+    if (!HT_IN_BOUNDS(r * 2 * f + f + c, total * 2, 2)) continue;
     const float gt = bf2f(h[r * 2 * f + c]);
     const float up = bf2f(h[r * 2 * f + f + c]);
     out[i] = f2bf(silu(gt) * up);
@@ -41,6 +43,7 @@ __global__ void swiglu_backward_kernel(const __nv_bfloat16* __restrict__ h, cons
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / f;
     const int c = i - r * f;
+    if (!HT_IN_BOUNDS(r * 2 * f + f + c, total * 2, 3)) continue;
     const float gt = bf2f(h[r * 2 * f + c]);
     const float up = bf2f(h[r * 2 * f + f + c]);
     const float go = bf2f(g[i]);
@@ -105,7 +108,7 @@ __global__ void __launch_bounds__(256) column_partial_kernel(const T* __restrict
       float t = 0.f;
 #pragma unroll
       for (int k = 0; k < 8; ++k) t += red[k][i];
-      part[(long long)blockIdx.y * cols + c] = t;
+      if (HT_IN_BOUNDS((long long)blockIdx.y * cols + c, (long long)gridDim.y * cols, 8)) part[(long long)blockIdx.y * cols + c] = t;
     }
   }
 }
@@ -120,7 +123,7 @@ __global__ void embedding_forward_kernel(const int* __restrict__ ids, const WT* 
     const int s = t % seq;
     for (int c = threadIdx.x; c < d; c += blockDim.x) {
       float v = 0.f;
-      if (own) {
+      if (own && HT_IN_BOUNDS((long long)id * d + c, (long long)rows * d, 4)) {
         if constexpr (std::is_same<WT, float>::value) v = table[(long long)id * d + c];
         else v = bf2f(table[(long long)id * d + c]);
       }
@@ -128,7 +131,7 @@ __global__ void embedding_forward_kernel(const int* __restrict__ ids, const WT* 
         if constexpr (std::is_same<WT, float>::value) v += pos[(long long)s * d + c];
         else v += bf2f(pos[(long long)s * d + c]);
       }
-      out[t * d + c] = v;
+      if (HT_IN_BOUNDS(t * d + c, tokens * d, 5)) out[t * d + c] = v;
     }
   }
 }
@@ -139,7 +142,8 @@ __global__ void embedding_backward_kernel(const int* __restrict__ ids, const flo
   for (long long t = blockIdx.x; t < tokens; t += gridDim.x) {
     const int id = ids[t] - vocab_start;
     if (id < 0 || id >= rows) continue;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) atomicAdd(dtable + (long long)id * d + c, grad[t * d + c]);
+    for (int c = threadIdx.x; c < d; c += blockDim.x)
+      if (HT_IN_BOUNDS((long long)id * d + c, (long long)rows * d, 6)) atomicAdd(dtable + (long long)id * d + c, grad[t * d + c]);
   }
 }
 
@@ -163,6 +167,7 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, const float* __restri
     const int h = th % heads;
     const long long t = th / heads;
     const int s = t % seq;
+    if (!HT_IN_BOUNDS(t * row_width + (long long)h * hd + j + half, tokens * row_width, 7)) continue;
     const float c = cosv[s * half + j];
     const float sn = inverse ? -sinv[s * half + j] : sinv[s * half + j];
     __nv_bfloat16* p = x + t * row_width + (long long)h * hd;

@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(1024) norm_forward_kernel(const float* __restr
   for (int i = 0; i < VPT; ++i) {
     const int c = c0 + i;
     float v = 0.f;
-    if (c < d) {
+    if (c < d && HT_IN_BOUNDS(base + c, (long long)gridDim.x * d, 30)) {
       v = res[base + c];
       if (delta != nullptr) v += ld(delta, base + c);
       r_out[base + c] = v;
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(SR_WARPS * 32) sum_rows_kernel(const float* __
   }
   red[ty][tx] = (s0 + s1) + (s2 + s3);
   __syncthreads();
-  if (ty == 0 && c < d) {
+  if (ty == 0 && c < d && HT_IN_BOUNDS(c, d, 31)) {
     float t = 0.f;
 #pragma unroll
     for (int k = 0; k < SR_WARPS; ++k) t += red[k][tx];

@@ -23,6 +23,7 @@ __global__ void adamw_kernel(float4* __restrict__ param, const float4* __restric
   const float step = lr / bc1;
   const float decay = 1.f - lr * wd;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    if (!HT_IN_BOUNDS(i, n4, 20)) continue;
     float4 p = param[i], g = grad[i], mm = m[i], vv = v[i];
     float* pp = reinterpret_cast<float*>(&p);
     const float* gg = reinterpret_cast<const float*>(&g);
@@ -69,7 +70,7 @@ __global__ void __launch_bounds__(RESIDENT_THREADS, 6)
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const long long i = i0 + u * stride;
-      if (i < n4) {
+      if (i < n4 && HT_IN_BOUNDS(i, n4, 21)) {
         p[u] = param[i];
         g[u] = grad[i];
         mm[u] = m[i];

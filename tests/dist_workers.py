@@ -230,7 +230,7 @@ def engine_worker(rank: int, world: int, overrides: dict[str, Any], steps: int, 
         ctx.shutdown()
 
 
-def _cuda_experiment(world: int, *, fused: bool = True, steps: int = 3, overlap: bool = True,
+def _cuda_experiment(world: int, *, fused: bool = True, steps: int = 3, overlap: bool = False,
                      graph: bool = False) -> dict[str, Any]:
     return {"name": "multigpu-test", "backend": "nccl", "device": "cuda", "timeout_seconds": 120.0,
             "topology": {"data_parallel_size": world},
@@ -265,14 +265,15 @@ def bucket_allreduce_worker(rank: int, world: int, nvls: bool = False) -> dict[s
         flat = ws.allocate(numel + 5, torch.float32)
         gen = torch.Generator(device="cuda").manual_seed(100 + rank)
         errors = []
-        for (start, n), wide in zip(((0, numel), (4, 1001), (1024, 17), (8, 2_000_000), (0, numel), (8, 999_999)),
-                                    (True, True, False, False, False, True)):
+        cases = zip(((0, numel), (4, 1001), (1024, 17), (8, 2_000_000), (0, numel), (8, 999_999), (0, numel), (12, 777_777)),
+                    (True, True, False, False, False, True, False, True), (0, 0, 0, 0, 0, 0, 8, 8))
+        for (start, n), wide, slots in cases:  # slots 8: the 8-peer instantiation run by two ranks
             flat.normal_(generator=gen)
             expect = flat[start:start + n].clone()
             dist.all_reduce(expect, op=dist.ReduceOp.SUM, group=ctx.group("data_parallel").process_group)
             expect /= world
             outside = torch.cat([flat[:start], flat[start + n:]]).clone()
-            bucket_all_reduce(ws, flat, start, n, 1.0 / world, wide=wide)
+            bucket_all_reduce(ws, flat, start, n, 1.0 / world, wide=wide, peer_slots=slots)
             torch.cuda.synchronize()
             ws.check_status()
             errors.append(float((flat[start:start + n] - expect).abs().max()))
