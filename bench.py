@@ -80,7 +80,7 @@ class ClockSampler:
 
     def start(self) -> None:
         try:
-            self._proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+            self._proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"],
                                           stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self._proc = None
@@ -95,6 +95,10 @@ class ClockSampler:
 
         self._thread = threading.Thread(target=pump, daemon=True)
         self._thread.start()
+        deadline = time.monotonic() + 3.0  # nvidia-smi takes a moment to start: let it begin sampling first
+        while not self.rows and time.monotonic() < deadline:
+            time.sleep(0.01)
+        self.rows.clear()
 
     def stop(self) -> dict:
         if self._proc is not None:

@@ -438,6 +438,11 @@ class DistributedDataParallel(nn.Module):
     def bucket_layouts(self) -> tuple[BucketLayout, ...]:
         return tuple(b.layout for b in self._buckets)
 
+    @property
+    def reduction_path(self) -> str:
+        """``"in-kernel"`` when buckets are reduced by the symmetric-memory kernel, else ``"process-group"``."""
+        return "in-kernel" if self._workspace is not None else "process-group"
+
     def communication_summary(self) -> str:
         if self._recorder is None:
             return "no recorder attached: construct with recorder=CommunicationRecorder() to count collectives"

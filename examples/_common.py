@@ -6,6 +6,7 @@ import argparse
 import dataclasses
 import sys
 from pathlib import Path
+from collections.abc import Callable
 from typing import Any
 
 ROOT = Path(__file__).resolve().parent.parent
@@ -77,7 +78,22 @@ def report_result(context: DistributedContext, engine: Any) -> None:
     print("=" * 72)
 
 
-def run_training(description: str, default_config: str) -> None:
+Hook = Callable[[DistributedContext, Any], None]
+
+
+def primary_print(context: DistributedContext, *lines: str) -> None:
+    if context.is_primary:
+        for line in lines:
+            print(line)
+
+
+def run_training(description: str, default_config: str, *, before: Hook | None = None, after: Hook | None = None) -> None:
+    """Build the engine for ``--config``, run it, report.
+
+    ``before`` runs on every rank once the model is wrapped (before the first step) and ``after``
+    once training has finished; the example programs use them to show what their strategy does.
+    Both may call collectives: every rank runs them.
+    """
     from hybrid_training.distributed import distributed_context
     from hybrid_training.training import TrainingEngine
 
@@ -88,6 +104,10 @@ def run_training(description: str, default_config: str) -> None:
         engine = TrainingEngine(cfg, ctx)
         if ctx.is_primary:
             print(engine.model.description.render())
+        if before is not None:
+            before(ctx, engine)
         engine.train()
+        if after is not None:
+            after(ctx, engine)
         report_result(ctx, engine)
         engine.close()
