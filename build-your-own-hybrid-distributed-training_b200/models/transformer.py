@@ -169,8 +169,11 @@ class TensorParallelAttention(nn.Module):
         positions are offset by the chunk start; keys and values are all-gathered along the
         sequence (the gather's adjoint reduce-scatters their gradients, so each rank's
         contribution to every key reaches its owner); causal masking compares global
-        positions.  Scores are materialised per chunk (``S / C x S``): this is the all-gather
-        form of context parallelism, which the reference describes but does not implement
+        positions.  On CUDA (chunks of a multiple of 128 positions) the native flash kernels run
+        over the rank's query window of a full-sequence packed tensor
+        (:func:`~hybrid_training.parallel.context_parallel.gathered_attention`); elsewhere the
+        scores are materialised per chunk (``S / C x S``).  This is the all-gather form of context
+        parallelism, which the reference describes but does not implement
         (``docs/06_sequence_parallelism.md:234-256``; its ``independent`` mode gives
         attention only the local chunk).  ``context_parallel_algorithm`` selects instead the ring
         with online softmax (memory per rank independent of the sequence) or Ulysses (all-to-all
@@ -215,6 +218,11 @@ class TensorParallelAttention(nn.Module):
             vh = qkv[..., (h + hkv) * d:].reshape(b, local, hkv, d).transpose(1, 2).repeat_interleave(h // hkv, 1)
             out = ring_attention(qh, kh, vh, cp, causal=self.causal)
             return out.transpose(1, 2).reshape(b, local, h * d).to(qkv.dtype)
+        if qkv.is_cuda and not (self.dropout > 0.0 and self.training):
+            from ..parallel.context_parallel import gathered_attention, gathered_attention_supported
+
+            if gathered_attention_supported(local, d):
+                return gathered_attention(qkv.contiguous(), h, hkv, d, cp, causal=self.causal).to(qkv.dtype)
         kv = gather_from_sequence_parallel_region(qkv[..., h * d:].contiguous(), cp, dim=SEQUENCE_DIM)
         b, total = q.shape[0], kv.shape[1]
         qf = q.reshape(b, local, h, d).transpose(1, 2).float()

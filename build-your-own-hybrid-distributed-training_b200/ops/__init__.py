@@ -11,7 +11,7 @@ from .attention import apply_rope, attention, reference_attention, rope_tables
 from .embedding import embedding
 from .grads import deliver_grad, has_main_grad, reset_main_grad_state
 from .linear import (EPI_GELU, EPI_GELU_BWD, EPI_PLAIN, compute_weight, gelu_backward, gelu_mlp, gemm, linear, reference_gemm,
-                     set_deterministic_reductions, swiglu)
+                     set_deterministic_reductions, swiglu, swiglu_gemm, swiglu_mlp, swiglu_mlp_supported)
 from .loss import cross_entropy, lm_head_cross_entropy, reference_vocab_parallel_cross_entropy
 from .norm import add_norm, layer_norm, rms_norm
 from .optim import HYPER_SLOTS, adamw_flat, grad_sumsq, reference_adamw
@@ -52,4 +52,7 @@ __all__ = [
     "rope_tables",
     "set_deterministic_reductions",
     "swiglu",
+    "swiglu_gemm",
+    "swiglu_mlp",
+    "swiglu_mlp_supported",
 ]

@@ -92,6 +92,35 @@ class _AttentionFunction(torch.autograd.Function):
         return dqkv, None, None, None, None
 
 
+def attention_window_forward(full: torch.Tensor, h: int, hkv: int, d: int, q_begin: int, q_len: int,
+                             causal: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Attention of the queries ``[q_begin, q_begin + q_len)`` of a packed ``full`` tensor against all its keys.
+
+    Returns ``(out_full, lse)``: ``out_full`` is ``[B, S, H*D]`` with the window's rows written and
+    every other row zero; ``lse`` is ``[B, H, S]`` (meaningful inside the window).  The query
+    columns of ``full`` outside the window are never read.  ``q_begin`` is a multiple of 128.
+    """
+    b, s, _ = full.shape
+    out = torch.zeros(b, s, h * d, dtype=full.dtype, device=full.device)
+    lse = torch.empty(b, h, s, dtype=torch.float32, device=full.device)
+    extension().attention_forward(full, out, lse, h, hkv, d, bool(causal), 1.0 / math.sqrt(d), int(q_begin), int(q_len))
+    return out, lse
+
+
+def attention_window_backward(full: torch.Tensor, out: torch.Tensor, lse: torch.Tensor, dout_window: torch.Tensor, h: int,
+                              hkv: int, d: int, q_begin: int, q_len: int, causal: bool) -> torch.Tensor:
+    """Gradient of :func:`attention_window_forward`: ``dqkv`` ``[B, S, W]`` with dQ in the window's rows and
+    dK / dV for every key (summed over the window's queries).  dQ rows outside the window are undefined."""
+    b, s, _ = full.shape
+    dout = torch.zeros(b, s, h * d, dtype=full.dtype, device=full.device)
+    dout[:, q_begin:q_begin + q_len] = dout_window
+    dqkv = torch.empty_like(full)
+    delta = torch.empty(b, h, s, dtype=torch.float32, device=full.device)
+    extension().attention_backward(full, out, dout, lse, delta, dqkv, h, hkv, d, bool(causal), 1.0 / math.sqrt(d),
+                                   int(q_begin), int(q_len))
+    return dqkv
+
+
 def attention(qkv: torch.Tensor, num_heads: int, num_kv_heads: int, head_dim: int, *, causal: bool = True) -> torch.Tensor:
     """Attention over a packed ``[B, S, (H + 2*Hkv) * D]`` tensor; returns ``[B, S, H*D]``."""
     if not qkv.is_cuda:

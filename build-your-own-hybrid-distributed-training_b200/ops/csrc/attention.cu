@@ -537,16 +537,24 @@ static void attn_check(const at::Tensor& qkv, int64_t H, int64_t HKV, int64_t D)
 }
 
 bool attention_forward_tcgen05(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal,
-                               double scale);
+                               double scale, int64_t q_begin, int64_t q_len);
 
-void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale) {
+// `q_begin` / `q_len` (q_len < 0: every query) restrict the queries to one window of the sequence
+// (context parallelism: a rank's own positions against the gathered keys); windows run on the
+// tcgen05 kernels only.
+void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale,
+                       int64_t q_begin, int64_t q_len) {
   attn_check(qkv, H, HKV, D);
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int B = qkv.size(0), S = qkv.size(1);
   if (B == 0 || S == 0) return;
+  const bool window = q_len >= 0 && !(q_begin == 0 && q_len == S);
   // The tcgen05 kernel (attention_tcgen05.cu) covers contiguous, 16-byte aligned tensors; the
   // mma.sync kernel below remains for any other layout.
-  if (std::getenv("HT_ATTN_MMA_SYNC") == nullptr && attention_forward_tcgen05(qkv, out, lse, H, HKV, D, causal, scale)) return;
+  if ((window || std::getenv("HT_ATTN_MMA_SYNC") == nullptr) &&
+      attention_forward_tcgen05(qkv, out, lse, H, HKV, D, causal, scale, q_begin, q_len))
+    return;
+  HT_CHECK(!window, "a query window needs contiguous, 16-byte aligned tensors and D of 64 or 128");
   dim3 grid((S + attn::BQ - 1) / attn::BQ, H, B);
   const float sl2 = (float)scale * attn::LOG2E;
   const auto* q = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
@@ -566,10 +574,12 @@ void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H
 }
 
 bool attention_backward_tcgen05(at::Tensor qkv, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv, int64_t H,
-                                int64_t HKV, int64_t D, bool causal, double scale);
+                                int64_t HKV, int64_t D, bool causal, double scale, int64_t q_begin, int64_t q_len);
 
+// With a query window the rows of `out` and `dout` outside it must be zero (their delta is then
+// zero and they contribute nothing to dK / dV).
 void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv,
-                        int64_t H, int64_t HKV, int64_t D, bool causal, double scale) {
+                        int64_t H, int64_t HKV, int64_t D, bool causal, double scale, int64_t q_begin, int64_t q_len) {
   attn_check(qkv, H, HKV, D);
   const c10::cuda::CUDAGuard guard(qkv.device());
   HT_CHECK(dout.is_contiguous() && dqkv.is_contiguous() && dqkv.sizes() == qkv.sizes(), "attention backward buffers");
@@ -597,11 +607,13 @@ void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Ten
     attn::delta_kernel<128><<<dgrid, dthreads, 0, s>>>(o, d, delta.data_ptr<float>(), S, H, rows);
   }
   // The tcgen05 kernels (attention_bwd_tcgen05.cu) cover contiguous, 16-byte aligned tensors.
-  if (std::getenv("HT_ATTN_MMA_SYNC") == nullptr &&
-      attention_backward_tcgen05(qkv, dout, lse, delta, dqkv, H, HKV, D, causal, scale)) {
+  const bool window = q_len >= 0 && !(q_begin == 0 && q_len == S);
+  if ((window || std::getenv("HT_ATTN_MMA_SYNC") == nullptr) &&
+      attention_backward_tcgen05(qkv, dout, lse, delta, dqkv, H, HKV, D, causal, scale, q_begin, q_len)) {
     HT_CUDA_CHECK(cudaGetLastError());
     return;
   }
+  HT_CHECK(!window, "a query window needs contiguous, 16-byte aligned tensors and D of 64 or 128");
   if (D == 64) {
     constexpr int smem_q = 6 * attn::BQ * 64 * 2;
     constexpr int smem_k = 6 * attn::BQ * 64 * 2 + 4 * attn::BQ * 4;

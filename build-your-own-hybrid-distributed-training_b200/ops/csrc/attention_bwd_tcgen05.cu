@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     dq_kernel(const __grid_constant__ CUtensorMap map_q128, const __grid_constant__ CUtensorMap map_kv64,
               const __grid_constant__ CUtensorMap map_do128, const __grid_constant__ CUtensorMap map_dqkv128,
               const float* __restrict__ lse, const float* __restrict__ delta, int S, int H, int HKV, int causal, float scale,
-              int* err) {
+              int qt0, int nqt_w, int* err) {
   using C = DqCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -64,9 +64,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   __shared__ uint32_t tmem_slot;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqt = (S + C::BQ - 1) / C::BQ;
-  const int qt = nqt - 1 - (int)blockIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z;
+  int qt, h, b;  // query tiles qt0 .. qt0 + nqt_w - 1
+  tile_major_block(nqt_w, H, qt, h, b);
+  qt = qt0 + nqt_w - 1 - qt;  // causal: the last query tiles see the most keys; they start first
   const int hk = h / (H / HKV);
   const int q0 = qt * C::BQ;
   const int nkt = (S + C::BKV - 1) / C::BKV;
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(THREADS, DkvCfg<D>::MIN_BLOCKS)
     dkdv_kernel(const __grid_constant__ CUtensorMap map_kv128, const __grid_constant__ CUtensorMap map_q64,
                 const __grid_constant__ CUtensorMap map_do64, const __grid_constant__ CUtensorMap map_dqkv128,
                 const float* __restrict__ lse, const float* __restrict__ delta, int S, int H, int HKV, int causal, float scale,
-                int* err) {
+                int qt0, int nqt_w, int* err) {
   using C = DkvCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -259,13 +259,14 @@ __global__ void __launch_bounds__(THREADS, DkvCfg<D>::MIN_BLOCKS)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkt = (S + C::BKV - 1) / C::BKV;
-  const int kt = nkt - 1 - (int)blockIdx.x;  // causal: early key tiles see the most queries
-  const int hk = blockIdx.y, b = blockIdx.z;
+  int kt, hk, b;  // causal: key tile kt sees nqt - kt query tiles, so tile 0 is the heaviest
+  tile_major_block(nkt, HKV, kt, hk, b);
   const int group = H / HKV;
   const int kv0 = kt * C::BKV;
   const int nqt = (S + C::BQ - 1) / C::BQ;
-  const int first_qt = causal ? kv0 / C::BQ : 0;
-  const int per_head = nqt - first_qt;
+  // Query tiles that can see this key tile, inside the window qt0 .. qt0 + nqt_w - 1.
+  const int first_qt = max(causal ? kv0 / C::BQ : 0, qt0);
+  const int per_head = max(0, min(nqt, qt0 + nqt_w) - first_qt);
   const int n_steps = per_head * group;
   const float scale_log2 = scale * LOG2E;
 
@@ -500,7 +501,7 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
     fused_bwd_kernel(const __grid_constant__ CUtensorMap map_qkv128, const __grid_constant__ CUtensorMap map_do128,
                      const __grid_constant__ CUtensorMap map_dqkv128, const __grid_constant__ CUtensorMap map_dq_acc,
                      const float* __restrict__ lse, const float* __restrict__ delta, int S, int H, int HKV, int causal,
-                     float scale, int* err) {
+                     float scale, int qt0, int nqt_w, int* err) {
   using C = FusedCfg;
   constexpr int D = C::D;
   extern __shared__ uint8_t smem_raw[];
@@ -518,13 +519,14 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkt = (S + C::BKV - 1) / C::BKV;
-  const int kt = nkt - 1 - (int)blockIdx.x;  // causal: early key tiles see the most queries; launch them first
-  const int hk = blockIdx.y, b = blockIdx.z;
+  int kt, hk, b;  // causal: key tile kt sees nqt - kt query tiles, so tile 0 is the heaviest
+  tile_major_block(nkt, HKV, kt, hk, b);
   const int group = H / HKV;
   const int kv0 = kt * C::BKV;
   const int nqt = (S + C::BQ - 1) / C::BQ;
-  const int first_qt = causal ? kv0 / C::BQ : 0;
-  const int per_head = nqt - first_qt;
+  // Query tiles that can see this key tile, inside the window qt0 .. qt0 + nqt_w - 1.
+  const int first_qt = max(causal ? kv0 / C::BQ : 0, qt0);
+  const int per_head = max(0, min(nqt, qt0 + nqt_w) - first_qt);
   const int n_steps = per_head * group;
   const float scale_log2 = scale * LOG2E;
 
@@ -662,9 +664,12 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
       }
       tc_fence_after();
       const bool edge = (qb + C::BQ > S) || (causal && qb < kv0 + C::BKV);
-      uint32_t pp[32], pd[32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 16 queries per chunk
+      uint8_t* prow = sP + half * C::TILE + r * 128;
+      uint8_t* drow = sDS + half * C::TILE + r * 128;
+      // One chunk of 16 queries at a time, written to shared memory as soon as it is computed: a
+      // rolled loop keeps the instruction footprint and the live registers small.
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
         float ls[16], dl[16];
         const int qc = qh + c * 16;
         if (qc + 16 - qb <= nstat) {
@@ -687,6 +692,12 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
         float sv[16], dp[16];
         tmem_ld_32x32b_x16(tmem + lane_off + C::ST_COL + half * 64 + c * 16, sv);
         tmem_ld_32x32b_x16(tmem + lane_off + C::DPT_COL + half * 64 + c * 16, dp);
+        if (c == 3) {  // last TMEM read of this tile: S^T / dP^T may be overwritten by the next one
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&st_free);
+        }
+        uint32_t pp[8], pd[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
           const float2 l2 = make_float2(ls[e] * LOG2E, ls[e + 1] * LOG2E);
@@ -698,25 +709,22 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
             if (qa >= S || (causal && qa < kv)) p0 = 0.f;
             if (qa + 1 >= S || (causal && qa + 1 < kv)) p1 = 0.f;
           }
-          pp[c * 8 + e / 2] = pack2(p0, p1);
-          pd[c * 8 + e / 2] = pack2(p0 * (dp[e] - d2.x), p1 * (dp[e + 1] - d2.y));
+          pp[e / 2] = pack2(p0, p1);
+          pd[e / 2] = pack2(p0 * (dp[e] - d2.x), p1 * (dp[e + 1] - d2.y));
+        }
+        // The previous step's dV / dK MMAs read sP / sDS: wait for them before the first store.
+        if (c == 0 && t > 0 && !mbar_wait(&pd_free, (t - 1) & 1, err, 58)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int off = ((2 * c + j) ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pp[4 * j], pp[4 * j + 1], pp[4 * j + 2], pp[4 * j + 3]);
+          *reinterpret_cast<uint4*>(drow + off) = make_uint4(pd[4 * j], pd[4 * j + 1], pd[4 * j + 2], pd[4 * j + 3]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&st_free);  // TMEM S^T / dP^T may be overwritten by the next tile
-      if (t > 0 && !mbar_wait(&pd_free, (t - 1) & 1, err, 58)) {
-        ok = false;
-        break;
-      }
-      uint8_t* prow = sP + half * C::TILE + r * 128;
-      uint8_t* drow = sDS + half * C::TILE + r * 128;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int off = (u ^ (r & 7)) << 4;
-        *reinterpret_cast<uint4*>(prow + off) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
-        *reinterpret_cast<uint4*>(drow + off) = make_uint4(pd[4 * u], pd[4 * u + 1], pd[4 * u + 2], pd[4 * u + 3]);
-      }
+      if (!ok) break;
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready);
@@ -852,7 +860,7 @@ static void set_smem(K kernel, int bytes) {
 
 template <int D>
 static void launch(const at::Tensor& qkv, const at::Tensor& dout, const at::Tensor& lse, const at::Tensor& delta,
-                   at::Tensor& dqkv, int H, int HKV, bool causal, float scale, int* err, cudaStream_t s) {
+                   at::Tensor& dqkv, int H, int HKV, bool causal, float scale, int qt0, int nqt_w, int* err, cudaStream_t s) {
   const int64_t B = qkv.size(0), S = qkv.size(1), W = qkv.size(2);
   const CUtensorMap q128 = make_map(qkv.data_ptr(), B, S, W, 128);
   const CUtensorMap q64 = make_map(qkv.data_ptr(), B, S, W, 64);
@@ -865,12 +873,12 @@ static void launch(const at::Tensor& qkv, const at::Tensor& dout, const at::Tens
     return true;
   }();
   (void)once;
-  const dim3 gq((unsigned)((S + 127) / 128), (unsigned)H, (unsigned)B);
-  const dim3 gk((unsigned)((S + 127) / 128), (unsigned)HKV, (unsigned)B);
+  const dim3 gq((unsigned)(nqt_w * H * B));
+  const dim3 gk((unsigned)(((S + 127) / 128) * HKV * B));
   dkdv_kernel<D><<<gk, THREADS, DkvCfg<D>::SMEM, s>>>(q128, q64, do64, dqkv128, lse.data_ptr<float>(), delta.data_ptr<float>(),
-                                                       (int)S, H, HKV, causal ? 1 : 0, scale, err);
+                                                       (int)S, H, HKV, causal ? 1 : 0, scale, qt0, nqt_w, err);
   dq_kernel<D><<<gq, THREADS, DqCfg<D>::SMEM, s>>>(q128, q64, do128, dqkv128, lse.data_ptr<float>(), delta.data_ptr<float>(),
-                                                   (int)S, H, HKV, causal ? 1 : 0, scale, err);
+                                                   (int)S, H, HKV, causal ? 1 : 0, scale, qt0, nqt_w, err);
 }
 
 // fp32 [rows][cols] map with 32-column x 32-row boxes and the 128-byte swizzle (dQ accumulator).
@@ -888,7 +896,8 @@ static CUtensorMap make_acc_map(void* base, int64_t rows, int64_t cols) {
 }
 
 static void launch_fused(const at::Tensor& qkv, const at::Tensor& dout, const at::Tensor& lse, const at::Tensor& delta,
-                         at::Tensor& dqkv, int H, int HKV, bool causal, float scale, int* err, cudaStream_t s) {
+                         at::Tensor& dqkv, int H, int HKV, bool causal, float scale, int qt0, int nqt_w, int* err,
+                         cudaStream_t s) {
   constexpr int D = FusedCfg::D;
   const int64_t B = qkv.size(0), S = qkv.size(1), W = qkv.size(2);
   at::Tensor acc = at::zeros({B * S, (int64_t)H * D}, qkv.options().dtype(at::kFloat));
@@ -901,10 +910,10 @@ static void launch_fused(const at::Tensor& qkv, const at::Tensor& dout, const at
     return true;
   }();
   (void)once;
-  const dim3 grid((unsigned)((S + 127) / 128), (unsigned)HKV, (unsigned)B);
+  const dim3 grid((unsigned)(((S + 127) / 128) * HKV * B));
   fused_bwd_kernel<<<grid, FusedCfg::THREADS, FusedCfg::SMEM, s>>>(q128, do128, dqkv128, macc, lse.data_ptr<float>(),
                                                                    delta.data_ptr<float>(), (int)S, H, HKV, causal ? 1 : 0,
-                                                                   scale, err);
+                                                                   scale, qt0, nqt_w, err);
   HT_CUDA_CHECK(cudaGetLastError());
   const long long rows = B * S;
   const int hd4 = H * D / 4;
@@ -920,9 +929,16 @@ bool deterministic_reductions();
 
 // Runs both backward kernels after the caller has filled `delta`; returns false (nothing
 // launched) when the tensor-core path does not apply.
+// Queries [q_begin, q_begin + q_len) only (q_len < 0: all): dQ rows of that window, and dK / dV
+// summed over those queries (rows of dQ outside the window are not written).
 bool attention_backward_tcgen05(at::Tensor qkv, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv, int64_t H,
-                                int64_t HKV, int64_t D, bool causal, double scale) {
+                                int64_t HKV, int64_t D, bool causal, double scale, int64_t q_begin, int64_t q_len) {
   if (!(D == 64 || D == 128) || !qkv.is_contiguous() || !dout.is_contiguous() || !dqkv.is_contiguous()) return false;
+  const int64_t S = qkv.size(1);
+  if (q_len < 0) q_begin = 0, q_len = S;
+  HT_CHECK(q_begin % 128 == 0 && q_begin >= 0 && q_len > 0 && q_begin + q_len <= S,
+           "attention query window must start at a multiple of 128 inside the sequence");
+  const int qt0 = (int)(q_begin / 128), nqt_w = (int)((q_len + 127) / 128);
   for (const at::Tensor* t : {&qkv, &dout, &dqkv})
     if (reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) return false;
   bind_context(qkv.device().index());
@@ -930,9 +946,9 @@ bool attention_backward_tcgen05(at::Tensor qkv, at::Tensor dout, at::Tensor lse,
   cudaStream_t s = stream();
   // D = 64 without the reproducibility requirement: one fused kernel (dQ summed by reduce-adds).
   if (D == 64 && !deterministic_reductions() && (H * D) % 32 == 0)
-    attn_bwd::launch_fused(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, err, s);
-  else if (D == 64) attn_bwd::launch<64>(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, err, s);
-  else attn_bwd::launch<128>(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, err, s);
+    attn_bwd::launch_fused(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, qt0, nqt_w, err, s);
+  else if (D == 64) attn_bwd::launch<64>(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, qt0, nqt_w, err, s);
+  else attn_bwd::launch<128>(qkv, dout, lse, delta, dqkv, (int)H, (int)HKV, causal, (float)scale, qt0, nqt_w, err, s);
   HT_CUDA_CHECK(cudaGetLastError());
   return true;
 }

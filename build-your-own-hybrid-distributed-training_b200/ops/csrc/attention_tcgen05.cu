@@ -49,7 +49,7 @@ __device__ __forceinline__ void mask_chunk(float* v, int kv0, int q, int S, int 
 template <int D>
 __global__ void __launch_bounds__(THREADS, 2)
     fwd_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_out, float* __restrict__ lse,
-               int S, int H, int HKV, int causal, float scale_log2, int* err) {
+               int S, int H, int HKV, int causal, float scale_log2, int qt0, int nqt_w, int* err) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -62,9 +62,11 @@ __global__ void __launch_bounds__(THREADS, 2)
   __shared__ uint32_t tmem_slot;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqt = (S + BQ - 1) / BQ;
-  const int qt = nqt - 1 - (int)blockIdx.x;  // heaviest causal tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Query tiles qt0 .. qt0 + nqt_w - 1 (the whole sequence, or one rank's window of it under
+  // context parallelism); keys always cover the whole sequence.
+  int qt, h, b;
+  tile_major_block(nqt_w, H, qt, h, b);
+  qt = qt0 + nqt_w - 1 - qt;  // causal: the last query tiles see the most keys; they start first
   const int hk = h / (H / HKV);
   const int q0 = qt * BQ;
   const int nkt = (S + BKV - 1) / BKV;
@@ -292,9 +294,14 @@ int* attention_error_word(const at::Device& dev) {
 }
 
 // Returns false (nothing launched) when the tensor-core path does not apply to these tensors.
+// Queries [q_begin, q_begin + q_len) only (q_len < 0: all); q_begin a multiple of 128.
 bool attention_forward_tcgen05(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal,
-                               double scale) {
+                               double scale, int64_t q_begin, int64_t q_len) {
   const int64_t B = qkv.size(0), S = qkv.size(1), W = qkv.size(2);
+  if (q_len < 0) q_begin = 0, q_len = S;
+  HT_CHECK(q_begin % attn_tc::BQ == 0 && q_begin >= 0 && q_len > 0 && q_begin + q_len <= S,
+           "attention query window must start at a multiple of 128 inside the sequence");
+  const int qt0 = (int)(q_begin / attn_tc::BQ), nqt_w = (int)((q_len + attn_tc::BQ - 1) / attn_tc::BQ);
   if (!(D == 64 || D == 128) || !qkv.is_contiguous() || !out.is_contiguous() || out.size(2) != H * D) return false;
   if ((reinterpret_cast<uintptr_t>(qkv.data_ptr()) & 15) || (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15)) return false;
   bind_context(qkv.device().index());
@@ -302,7 +309,7 @@ bool attention_forward_tcgen05(at::Tensor qkv, at::Tensor out, at::Tensor lse, i
   const CUtensorMap mo = attn_tc::make_map_3d(out.data_ptr(), B, S, H * D);
   int* err = attention_error_word(qkv.device());
   const float sl2 = (float)(scale * 1.4426950408889634);
-  const dim3 grid((unsigned)((S + attn_tc::BQ - 1) / attn_tc::BQ), (unsigned)H, (unsigned)B);
+  const dim3 grid((unsigned)(nqt_w * H * B));
   cudaStream_t s = stream();
   if (D == 64) {
     constexpr int smem = attn_tc::Cfg<64>::SMEM;
@@ -312,7 +319,7 @@ bool attention_forward_tcgen05(at::Tensor qkv, at::Tensor out, at::Tensor lse, i
     }();
     (void)once;
     attn_tc::fwd_kernel<64><<<grid, attn_tc::THREADS, smem, s>>>(mq, mo, lse.data_ptr<float>(), (int)S, (int)H, (int)HKV,
-                                                                 causal ? 1 : 0, sl2, err);
+                                                                 causal ? 1 : 0, sl2, qt0, nqt_w, err);
   } else {
     constexpr int smem = attn_tc::Cfg<128>::SMEM;
     static bool once = [] {
@@ -321,7 +328,7 @@ bool attention_forward_tcgen05(at::Tensor qkv, at::Tensor out, at::Tensor lse, i
     }();
     (void)once;
     attn_tc::fwd_kernel<128><<<grid, attn_tc::THREADS, smem, s>>>(mq, mo, lse.data_ptr<float>(), (int)S, (int)H, (int)HKV,
-                                                                  causal ? 1 : 0, sl2, err);
+                                                                  causal ? 1 : 0, sl2, qt0, nqt_w, err);
   }
   HT_CUDA_CHECK(cudaGetLastError());
   return true;

@@ -6,6 +6,7 @@ void set_deterministic_reductions(bool on);
 bool deterministic_reductions();
 void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
           c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta);
+void gemm_swiglu(at::Tensor a, at::Tensor b, at::Tensor h, at::Tensor out, c10::optional<at::Tensor> bias, bool backward);
 at::Tensor gemm_error_word(at::Tensor like);
 void gemm_collective(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
                      bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta, int64_t a_mode, std::vector<int64_t> a_ptrs,
@@ -39,9 +40,10 @@ void cross_entropy_grad(at::Tensor logits, at::Tensor targets, at::Tensor lse, a
 void adamw_flat(at::Tensor param, at::Tensor grad, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> copy, at::Tensor hyper,
                 double beta1, double beta2, double eps, double wd, bool resident);
 void grad_sumsq(at::Tensor g, c10::optional<at::Tensor> w, at::Tensor out, double scale);
-void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
+void attention_forward(at::Tensor qkv, at::Tensor out, at::Tensor lse, int64_t H, int64_t HKV, int64_t D, bool causal, double scale,
+                       int64_t q_begin, int64_t q_len);
 void attention_backward(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor delta, at::Tensor dqkv,
-                        int64_t H, int64_t HKV, int64_t D, bool causal, double scale);
+                        int64_t H, int64_t HKV, int64_t D, bool causal, double scale, int64_t q_begin, int64_t q_len);
 void bucket_all_reduce(at::Tensor flat, std::vector<int64_t> buffer_ptrs, std::vector<int64_t> pad_ptrs, int64_t multicast_ptr,
                        int64_t start, int64_t numel, double scale, int64_t rank, int64_t slot_base, int64_t max_blocks,
                        at::Tensor status, double timeout_s, bool wide, int64_t min_peer_slots);
@@ -58,6 +60,7 @@ void fsdp_all_gather_copy_engine(std::vector<int64_t> shard_ptrs, at::Tensor out
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hybrid_training native kernels (sm_100a)";
   m.def("gemm", &ht::gemm, "tcgen05 GEMM with fused epilogue");
+  m.def("gemm_swiglu", &ht::gemm_swiglu, "tcgen05 GEMM with the SwiGLU activation (or its gradient) in the epilogue");
   m.def("gemm_error_word", &ht::gemm_error_word, "device error word written by timed-out GEMM waits");
   m.def("gemm_collective", &ht::gemm_collective, "GEMM with peer-sharded operands or a reduce-scatter epilogue");
   m.def("reduce_scatter_sum", &ht::reduce_scatter_sum, "sum of the reduce-scatter receive slots");
@@ -85,8 +88,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "fixed-order split-K sums (reproducible) or TMA reduce-adds straight into the output (faster)");
   m.def("deterministic_reductions", &ht::deterministic_reductions);
   m.def("grad_sumsq", &ht::grad_sumsq);
-  m.def("attention_forward", &ht::attention_forward);
-  m.def("attention_backward", &ht::attention_backward);
+  m.def("attention_forward", &ht::attention_forward, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("H"), py::arg("HKV"),
+        py::arg("D"), py::arg("causal"), py::arg("scale"), py::arg("q_begin") = 0, py::arg("q_len") = -1);
+  m.def("attention_backward", &ht::attention_backward, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
+        py::arg("delta"), py::arg("dqkv"), py::arg("H"), py::arg("HKV"), py::arg("D"), py::arg("causal"), py::arg("scale"),
+        py::arg("q_begin") = 0, py::arg("q_len") = -1);
   m.def("bucket_all_reduce", &ht::bucket_all_reduce, "in-kernel NVLink all-reduce of one DDP bucket");
   m.def("fsdp_reduce_scatter_adamw", &ht::fsdp_reduce_scatter_adamw,
         "FSDP gradient reduce-scatter fused with the cast and the sharded AdamW update (NVLink peer memory)");

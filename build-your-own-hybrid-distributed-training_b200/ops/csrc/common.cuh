@@ -295,6 +295,18 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Block coordinates of a flattened (tile, head, batch) grid with the tile as the slowest index.
+// Blocks are dispatched in index order, so every block of tile 0 starts before any block of tile 1:
+// with causal attention, where the work per block falls (or rises) with the tile index, ordering
+// the tiles heaviest first keeps the light blocks for the last wave.
+__device__ __forceinline__ void tile_major_block(int ntiles, int heads, int& tile, int& head, int& batch) {
+  const int per_tile = (int)gridDim.x / ntiles;
+  const int bid = (int)blockIdx.x;
+  tile = bid / per_tile;
+  head = (bid % per_tile) % heads;
+  batch = (bid % per_tile) / heads;
+}
+
 // 2^x on the FMA pipe, for softmax arguments x <= 0, so that part of the exponentials can leave
 // the MUFU unit.  Method: Cody-Waite range reduction x = n + f with n = round(x) and f in
 // [-1/2, 1/2], where the rounding adds and subtracts 1.5 * 2^23 (the float's mantissa then holds

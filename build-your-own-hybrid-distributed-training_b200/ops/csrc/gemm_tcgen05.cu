@@ -42,13 +42,14 @@ constexpr int EPI_STAGE_BYTES = 32 * 128;  // one 32-row x 128-byte output piece
 constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * EPI_STAGE_BYTES + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA exceeded");
 
-enum Epilogue : int { kPlain = 0, kGelu = 1, kGeluBwd = 2 };
+enum Epilogue : int { kPlain = 0, kGelu = 1, kGeluBwd = 2, kSwiGLU = 3, kSwiGLUBwd = 4 };
 
 // Compile-time epilogue kind of a kernel instance.  Each instance carries only its own epilogue
 // code, which keeps the kernel small enough that the epilogue warps do not evict the MMA
 // issue loop from the instruction cache.  kKindGeneric decides everything at run time (the
 // fallback for unaligned outputs and the collective kernels).
-enum EpiKind : int { kKindGeneric = 0, kKindBf16 = 1, kKindF32 = 2, kKindGelu = 3, kKindGeluBwd = 4 };
+enum EpiKind : int { kKindGeneric = 0, kKindBf16 = 1, kKindF32 = 2, kKindGelu = 3, kKindGeluBwd = 4, kKindSwiGLU = 5,
+                     kKindSwiGLUBwd = 6 };
 
 struct EpiParams {
   void* d;
@@ -67,6 +68,7 @@ struct EpiParams {
   int reduce_add;  // D (fp32) += result through TMA reduce-add (beta == 1)
   int splits;      // split-K factor: work unit u covers tile u / splits, K-range u % splits
   int split_rows;  // rows per split slice of the fp32 workspace (split-K only)
+  int half_n;      // SwiGLU kinds: F, the column of the first `up` feature in the [gate | up] tensors
 };
 
 // ------------------------------------------------------------------------------------------------
@@ -437,6 +439,134 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
   __syncwarp();
 }
 
+// ---------------- SwiGLU epilogues ----------------
+// Output pieces here are 32 bf16 columns (64 bytes): the staging tile of each epilogue warp holds
+// two 32-row x 64-byte slots used alternately, written with the 64-byte swizzle their tensor maps
+// expect (16-byte unit j of row r at unit j ^ ((r / 2) % 4)).  Before a slot is rewritten, every
+// bulk store but the most recent one (which read the other slot) must have read its source.
+__device__ __forceinline__ void bulk_wait_read_allbut1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+__device__ __forceinline__ void pack_bf16x32(const float* v, uint4* units) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    units[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                          pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+
+// Stages one 32-column piece of this lane's row in `slot` and stores it at (col, row0) of `map`.
+__device__ __forceinline__ void store_piece64(const CUtensorMap* map, uint8_t* slot, int lane, const float* v, int col, int row0) {
+  uint4 units[4];
+  pack_bf16x32(v, units);
+  if (lane == 0) bulk_wait_read_allbut1();
+  __syncwarp();
+  uint8_t* row = slot + lane * 64;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(row + ((j ^ ((lane >> 1) & 3)) << 4)) = units[j];
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, slot, col, row0);
+    bulk_commit();
+  }
+}
+
+__device__ __forceinline__ float swiglu_bias(const EpiParams& ep, int c) {
+  if (ep.bias_f32 != nullptr) return __ldg(ep.bias_f32 + c);
+  if (ep.bias_bf16 != nullptr) return bf2f(ep.bias_bf16[c]);
+  return 0.f;
+}
+
+// BWD = false (forward, tiles of TN/2 output columns): h[:, n] = gate + bias, h[:, F + n] = up +
+//   bias through `map_aux`, and D[:, n] = silu(gate) * up through `map_d`.
+// BWD = true (the down projection's data gradient, tiles of TN columns of dA): with gate and up
+//   read back from h (`ep.aux`), D[:, n] = dA * up * silu'(gate) and D[:, F + n] = dA * silu(gate).
+template <bool BWD, int TN>
+__device__ __forceinline__ void epilogue_loop_swiglu(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
+                                                     uint8_t* tile, uint32_t tmem_base, uint64_t* tfull_bar,
+                                                     uint64_t* tempty_bar, int M, int N, int num_m, int num_n, int num_tiles,
+                                                     int warp, int lane, int* err) {
+  const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
+  const float alpha = ep.alpha != nullptr ? *ep.alpha : 1.f;
+  constexpr int TN_OUT = BWD ? TN : TN / 2;
+  int acc = 0, slot = 0;
+  uint32_t acc_phase = 0;
+  for (int unit = blockIdx.x; unit < num_tiles; unit += gridDim.x) {
+    int mb, nb;
+    tile_coords(unit, num_m, num_n, mb, nb);
+    const int row0 = mb * BM + quarter * 32;
+    const int row = row0 + lane;
+    if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 4)) break;
+    tc_fence_after();
+    const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+    // The two warpgroups take alternate 32-column pieces of the tile's output columns.
+#pragma unroll 1
+    for (int c = half * 32; c < TN_OUT; c += 64) {
+      const int col = nb * TN_OUT + c;
+      if (col >= N) break;
+      float x[32], y[32];
+      tmem_ld_32x32b_x32(tbase + c, x);
+      if constexpr (!BWD) {
+        tmem_ld_32x32b_x32(tbase + TN / 2 + c, y);  // up features sit TN / 2 accumulator columns further on
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x[i] = x[i] * alpha + swiglu_bias(ep, col + i);
+          y[i] = y[i] * alpha + swiglu_bias(ep, ep.half_n + col + i);
+        }
+        store_piece64(map_aux, tile + slot * 2048, lane, x, col, row0);
+        slot ^= 1;
+        store_piece64(map_aux, tile + slot * 2048, lane, y, ep.half_n + col, row0);
+        slot ^= 1;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = x[i] / (1.f + __expf(-x[i])) * y[i];
+        store_piece64(map_d, tile + slot * 2048, lane, x, col, row0);
+        slot ^= 1;
+      } else {
+        float g[32];
+        if (row < M) {
+          const __nv_bfloat16* hp = ep.aux + (long long)row * ep.ldaux + col;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 gr = *reinterpret_cast<const uint4*>(hp + q * 8);
+            const uint4 ur = *reinterpret_cast<const uint4*>(hp + ep.half_n + q * 8);
+            const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gr);
+            const __nv_bfloat16* up = reinterpret_cast<const __nv_bfloat16*>(&ur);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              g[q * 8 + j] = bf2f(gp[j]);
+              y[q * 8 + j] = bf2f(up[j]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) g[i] = y[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float da = x[i] * alpha;
+          const float sig = 1.f / (1.f + __expf(-g[i]));
+          const float sl = g[i] * sig;
+          x[i] = da * y[i] * sig * (1.f + g[i] * (1.f - sig));  // d gate
+          y[i] = da * sl;                                         // d up
+        }
+        store_piece64(map_d, tile + slot * 2048, lane, x, col, row0);
+        slot ^= 1;
+        store_piece64(map_d, tile + slot * 2048, lane, y, ep.half_n + col, row0);
+        slot ^= 1;
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    if (++acc == 2) {
+      acc = 0;
+      acc_phase ^= 1u;
+    }
+  }
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -517,8 +647,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // SwiGLU forward: a tile's TN accumulator columns are TN / 2 gate features and the same TN / 2
+  // up features, so it covers TN / 2 output columns.
+  constexpr bool SWI = KIND == kKindSwiGLU;
+  constexpr int TN_OUT = SWI ? TN / 2 : TN;
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + TN - 1) / TN;
+  const int num_n = (N + TN_OUT - 1) / TN_OUT;
   const int num_tiles = num_m * num_n;
   const int num_units = num_tiles * ep.splits;
   const int kblocks = (K + BK - 1) / BK;
@@ -570,7 +704,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
       tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
       if (COLL && coll->a_mode == 1) mb = coll_phys_mblock(*coll, mb);
       split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
-      const int m0 = mb * BM, n0 = nb * TN;
+      const int m0 = mb * BM, n0 = nb * TN_OUT;
       int tile_src = 0, tile_lrow = 0, tile_b = 0;  // A source of this tile: 0 local map, 1 own shard, 2 gathered copy
       if (COLL && c_amode == 1) {
         // A tile of a remote block: the whole warp polls the block's slice flags in parallel
@@ -656,6 +790,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < TN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], n0 + 64 * j, k0);
+          } else if (SWI) {  // gate rows n0.., then up rows F + n0.. (two boxes of TN / 2 rows)
+            tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, n0);
+            tma_load_2d(b_dst + (TN / 2) * 128, &tma_b, &full_bar[stage], k0, ep.half_n + n0);
           } else {
             tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, n0);
           }
@@ -729,6 +866,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tma_a, const CUtens
       else
         epilogue_loop<64, KIND, TN>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m, num_n, num_tiles, warp,
                                 lane, err, COLL ? coll : nullptr);
+    } else if constexpr (KIND == kKindSwiGLU || KIND == kKindSwiGLUBwd) {
+      epilogue_loop_swiglu<KIND == kKindSwiGLUBwd, TN>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m,
+                                                       num_n, num_tiles, warp, lane, err);
     } else {
       epilogue_loop<KIND == kKindF32 ? 32 : 64, KIND, TN>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N, num_m,
                                                       num_n, num_tiles, warp, lane, err, nullptr);
@@ -964,6 +1104,20 @@ static CUtensorMap make_out_map(void* base, int64_t rows, int64_t cols, int64_t 
   return map;
 }
 
+// bf16 [rows][cols] map with 32-column x 32-row boxes and the 64-byte swizzle (SwiGLU epilogues).
+static CUtensorMap make_out_map64(void* base, int64_t rows, int64_t cols, int64_t ld) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  HT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (SwiGLU output) failed with code ", (int)r);
+  return map;
+}
+
 int* error_word(const at::Device& dev) {
   // Intentionally leaked: a static tensor destroyed after the CUDA context would fault at exit.
   static at::Tensor* words = new at::Tensor[64];
@@ -989,7 +1143,8 @@ static void launch_kind(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
     HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  const int units = ((M + BM - 1) / BM) * ((N + TN - 1) / TN) * ep.splits;
+  constexpr int TN_OUT = KIND == kKindSwiGLU ? TN / 2 : TN;
+  const int units = ((M + BM - 1) / BM) * ((N + TN_OUT - 1) / TN_OUT) * ep.splits;
   const int grid = std::min(units, num_sms());
   kernel<<<grid, THREADS, smem, s>>>(ma, mb, md, maux, M, N, K, ep, err);
   HT_CUDA_CHECK(cudaGetLastError());
@@ -1164,6 +1319,62 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
                                                                 reinterpret_cast<__nv_bfloat16*>(d.data_ptr()), (int)M, (int)N,
                                                                 d.stride(0), (int)ldw, splits, split_rows * ldw, (float)beta, vec_d);
     HT_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+// SwiGLU fused into GEMM epilogues (see epilogue_loop_swiglu).
+//   backward == false: a = X [M, K], b = W [2F, K] (F gate rows, then F up rows), bias [2F] or none;
+//     writes h = X W^T + bias as [M, 2F] (gate | up) and out = silu(gate) * up as [M, F].
+//   backward == true: a = dY [M, K], b = W2 [K, F] (the down projection's weight, read MN-major),
+//     h from the forward; writes out = dH [M, 2F] = (dA * up * silu'(gate) | dA * silu(gate)) with
+//     dA = dY W2, so neither dA nor a separate element-wise pass is needed.
+// F must be a multiple of 128 (a forward tile holds 128 gate and 128 up features).
+void gemm_swiglu(at::Tensor a, at::Tensor b, at::Tensor h, at::Tensor out, c10::optional<at::Tensor> bias, bool backward) {
+  using namespace tcg;
+  check_operand(a, "A");
+  check_operand(b, "B");
+  check_operand(h, "h");
+  check_operand(out, "out");
+  const c10::cuda::CUDAGuard guard(a.device());
+  bind_context(a.device().index());
+  const int64_t M = a.size(0), K = a.size(1);
+  const int64_t F = backward ? b.size(1) : b.size(0) / 2;
+  HT_CHECK(F > 0 && F % 128 == 0, "SwiGLU GEMM: the feature count F must be a positive multiple of 128, got ", F);
+  HT_CHECK((backward ? b.size(0) : b.size(1)) == K, "SwiGLU GEMM: reduction sizes differ");
+  HT_CHECK(backward || b.size(0) == 2 * F, "SwiGLU GEMM: W must have 2F rows");
+  HT_CHECK(h.size(0) == M && h.size(1) == 2 * F, "SwiGLU GEMM: h must be [M, 2F]");
+  HT_CHECK(out.size(0) == M && out.size(1) == (backward ? 2 * F : F), "SwiGLU GEMM: out must be [M, ", backward ? "2F" : "F",
+           "]");
+  if (M == 0) return;
+  EpiParams ep{};
+  ep.d = out.data_ptr();
+  ep.ldd = out.stride(0);
+  ep.beta = 0.f;
+  ep.epi = backward ? kSwiGLUBwd : kSwiGLU;
+  ep.vec_ok = 1;
+  ep.tma_d = 1;
+  ep.splits = 1;
+  ep.half_n = (int)F;
+  ep.aux = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
+  ep.ldaux = h.stride(0);
+  if (!backward && bias.has_value() && bias->defined()) {
+    HT_CHECK(bias->is_contiguous() && bias->numel() == 2 * F, "SwiGLU GEMM: bias must be a contiguous [2F] tensor");
+    if (bias->scalar_type() == at::kFloat) ep.bias_f32 = bias->data_ptr<float>();
+    else if (bias->scalar_type() == at::kBFloat16) ep.bias_bf16 = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+    else HT_CHECK(false, "bias must be fp32 or bf16");
+  }
+  const CUtensorMap ma = make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
+  const CUtensorMap md = make_out_map64(out.data_ptr(), M, out.size(1), out.stride(0));
+  int* err = error_word(a.device());
+  cudaStream_t s = stream();
+  if (!backward) {
+    const CUtensorMap mb = make_map(b.data_ptr(), 2 * F, K, b.stride(0), 64, BN / 2);
+    const CUtensorMap maux = make_out_map64(h.data_ptr(), M, 2 * F, h.stride(0));
+    ep.tma_aux = 1;
+    launch_kind<false, false, kKindSwiGLU>(ma, mb, md, maux, (int)M, (int)F, (int)K, ep, err, s);
+  } else {
+    const CUtensorMap mb = make_map(b.data_ptr(), K, F, b.stride(0), 64, 64);
+    launch_kind<false, true, kKindSwiGLUBwd>(ma, mb, md, md, (int)M, (int)F, (int)K, ep, err, s);
   }
 }
 

@@ -5,6 +5,7 @@ Single GPU::
     python -m hybrid_training.ops.microbench gemm [--only NAME] [--iters N]
     python -m hybrid_training.ops.microbench attention [--shape gpt2|llama8b] [--once]
     python -m hybrid_training.ops.microbench norm [--once]
+    python -m hybrid_training.ops.microbench mlp [--rows 8192 --hidden 2048 --ffn 5504]
 
 Several GPUs (one process per GPU, e.g. ``torchrun --nproc-per-node 2 --master-addr 127.0.0.1``)::
 
@@ -145,6 +146,38 @@ def bench_norm(once: bool) -> None:
     bwd_bytes = rows * d * (2 + 4 + 4 + 4 + 2)
     print(f"layernorm rows={rows} d={d}: forward {tf * 1e3:.1f} us ({fwd_bytes / tf / 1e6:.0f} GB/s), "
           f"backward {tb * 1e3:.1f} us ({bwd_bytes / tb / 1e6:.0f} GB/s)", flush=True)
+
+
+def bench_mlp(rows: int, hidden: int, ffn: int) -> None:
+    """SwiGLU MLP forward + backward: activation in the GEMM epilogues vs GEMMs plus element-wise kernels."""
+    from .linear import gemm, swiglu, swiglu_mlp
+
+    dev = torch.device("cuda")
+    x = torch.randn(rows, hidden, device=dev).bfloat16().requires_grad_(True)
+    w1 = (torch.randn(2 * ffn, hidden, device=dev) * 0.02).bfloat16().requires_grad_(True)
+    w2 = (torch.randn(hidden, ffn, device=dev) * 0.02).bfloat16().requires_grad_(True)
+    g = torch.randn(rows, hidden, device=dev).bfloat16()
+
+    def fused() -> None:
+        swiglu_mlp(x, w1, None, w2, None).backward(g)
+
+    def unfused() -> None:
+        h = gemm(x.detach(), w1.detach())
+        hh = h.requires_grad_(True)
+        a = swiglu(hh)
+        y = gemm(a.detach(), w2.detach())
+        da = gemm(g, w2.detach(), b_mn_major=True)
+        a.backward(da)
+        dh = hh.grad
+        gemm(dh, w1.detach(), b_mn_major=True)
+        gemm(dh, x.detach(), a_mn_major=True, b_mn_major=True)
+        gemm(g, a.detach(), a_mn_major=True, b_mn_major=True)
+        del y
+
+    flops = 2 * rows * hidden * 3 * ffn * 3  # three GEMMs of the forward, twice that in the backward
+    tf, tu = _time(fused, 10), _time(unfused, 10)
+    print(f"swiglu mlp rows={rows} hidden={hidden} ffn={ffn}: fused {tf * 1e3:.0f} us ({flops / tf / 1e9:.0f} TFLOP/s), "
+          f"GEMMs + element-wise {tu * 1e3:.0f} us ({flops / tu / 1e9:.0f} TFLOP/s)", flush=True)
 
 
 def _init_group(kind: str, hidden: int, seq: int):  # noqa: ANN202
@@ -305,6 +338,10 @@ def main(argv: list[str] | None = None) -> None:
     a.add_argument("--fast", action="store_true", help="backward without the reproducibility requirement")
     n = sub.add_parser("norm")
     n.add_argument("--once", action="store_true")
+    ml = sub.add_parser("mlp")
+    ml.add_argument("--rows", type=int, default=8192)
+    ml.add_argument("--hidden", type=int, default=2048)
+    ml.add_argument("--ffn", type=int, default=5504)
     t = sub.add_parser("tp-layer")
     t.add_argument("--seq", type=int, default=4096)
     r = sub.add_parser("allreduce")
@@ -318,6 +355,8 @@ def main(argv: list[str] | None = None) -> None:
         bench_attention(args.shape, args.once, args.fast)
     elif args.what == "norm":
         bench_norm(args.once)
+    elif args.what == "mlp":
+        bench_mlp(args.rows, args.hidden, args.ffn)
     elif args.what == "tp-layer":
         bench_tp_layer(args.seq)
     elif args.what == "fsdp":

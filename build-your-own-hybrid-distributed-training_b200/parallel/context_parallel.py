@@ -1,4 +1,12 @@
-"""Context parallelism: ring attention and Ulysses all-to-all attention.
+"""Context parallelism: all-gather attention on the native kernel, ring attention and Ulysses
+all-to-all attention.
+
+All-gather form (:func:`gathered_attention`, CUDA): every rank gathers the keys and values of the
+whole sequence, places its own queries at their positions in a packed full-sequence tensor, and
+runs the tcgen05 flash kernel over its query window only (the window's rows against every key,
+causal by global position); the backward kernels produce dQ for the window and dK / dV for every
+key from the window's queries, and a reduce-scatter returns each key chunk's gradient sum to its
+owner.
 
 Ring attention is the form whose memory per rank does not grow with the sequence.
 
@@ -27,10 +35,11 @@ from typing import Any
 
 import torch
 
-from ..distributed.collectives import recv_tensor, send_tensor
+from ..autograd.collectives import all_gather_along_dim, reduce_scatter_along_dim
+from ..distributed.collectives import ReduceOp, recv_tensor, send_tensor
 from ..distributed.groups import GroupHandle
 
-__all__ = ["ring_attention", "ulysses_attention"]
+__all__ = ["gathered_attention", "gathered_attention_supported", "ring_attention", "ulysses_attention"]
 
 
 def _ring_pass(tensors: list[torch.Tensor], group: GroupHandle) -> list[torch.Tensor]:
@@ -183,3 +192,43 @@ def ulysses_attention(qkv: torch.Tensor, num_heads: int, num_kv_heads: int, head
     back = context.reshape(b, c, length, hl * d).permute(1, 0, 2, 3)          # [C (destination chunk), B, L, hl*d]
     mine = _AllToAll.apply(back, group)                                        # [C (source head group), B, L, hl*d]
     return mine.permute(1, 2, 0, 3).reshape(b, length, h * d)
+
+
+def gathered_attention_supported(local_len: int, head_dim: int) -> bool:
+    """Whether :func:`gathered_attention` applies: windows start on 128-row tiles, D is 64 or 128."""
+    return local_len % 128 == 0 and head_dim in (64, 128)
+
+
+class _GatheredAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx: Any, qkv: torch.Tensor, h: int, hkv: int, d: int, group: GroupHandle, causal: bool) -> torch.Tensor:
+        from ..ops.attention import attention_window_forward
+
+        b, local, width = qkv.shape
+        begin, total = group.local_rank * local, local * group.size
+        kv = all_gather_along_dim(qkv[..., h * d:].contiguous(), group, 1)  # [B, S, 2 * Hkv * D]
+        full = torch.empty(b, total, width, dtype=qkv.dtype, device=qkv.device)
+        full[..., h * d:] = kv
+        full[:, begin:begin + local, : h * d] = qkv[..., : h * d]  # other ranks' query columns stay unread
+        out_full, lse = attention_window_forward(full, h, hkv, d, begin, local, causal)
+        ctx.save_for_backward(full, out_full, lse)
+        ctx.dims = (h, hkv, d, causal, begin, local, group)
+        return out_full[:, begin:begin + local].contiguous()
+
+    @staticmethod
+    def backward(ctx: Any, dout: torch.Tensor) -> tuple[Any, ...]:
+        from ..ops.attention import attention_window_backward
+
+        full, out_full, lse = ctx.saved_tensors
+        h, hkv, d, causal, begin, local, group = ctx.dims
+        dqkv = attention_window_backward(full, out_full, lse, dout.contiguous(), h, hkv, d, begin, local, causal)
+        dkv = reduce_scatter_along_dim(dqkv[..., h * d:].contiguous(), group, 1, op=ReduceOp.SUM)  # this rank's keys
+        dq = dqkv[:, begin:begin + local, : h * d]
+        return torch.cat([dq, dkv], dim=-1), None, None, None, None, None
+
+
+def gathered_attention(qkv: torch.Tensor, num_heads: int, num_kv_heads: int, head_dim: int, group: GroupHandle, *,
+                       causal: bool = True) -> torch.Tensor:
+    """Context-parallel attention of this rank's chunk ``qkv`` ``[B, S/C, W]`` (positions ``r S/C ..``)
+    against the keys of the whole sequence, on the native flash kernels (see the module docstring)."""
+    return _GatheredAttention.apply(qkv, num_heads, num_kv_heads, head_dim, group, causal)

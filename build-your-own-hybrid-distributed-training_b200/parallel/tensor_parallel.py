@@ -376,7 +376,8 @@ class TensorParallelFeedForward(nn.Module):
 
     ``activation='swiglu'`` makes fc1 produce ``[gate; up]`` per rank (width
     ``2 * ffn / T``) and applies ``silu(gate) * up``.  GELU is fused into the
-    fc1 GEMM epilogue.
+    fc1 GEMM epilogue; with a width-1 tensor group both activations, and their
+    gradients, run inside the two GEMMs' epilogues.
     """
 
     def __init__(self, hidden_size: int, ffn_hidden_size: int, group: GroupHandle, *, activation: str = "gelu",
@@ -405,6 +406,11 @@ class TensorParallelFeedForward(nn.Module):
         if self.activation_name == "gelu" and self.fc1.group.is_trivial and x.is_cuda:
             # Width-1 group: both linears and the GELU as one fused op (GELU' in fc2's dgrad epilogue).
             return ops.gelu_mlp(x, self.fc1.weight, self.fc1.bias, self.fc2.weight, self.fc2.bias)
+        if (self.activation_name == "swiglu" and self.fc1.group.is_trivial and x.is_cuda
+                and ops.swiglu_mlp_supported(self.fc1.output_features_per_partition // 2)):
+            # Width-1 group: SwiGLU in fc1's epilogue (gate and up rows in one tile) and its
+            # gradient in fc2's data-gradient epilogue.
+            return ops.swiglu_mlp(x, self.fc1.weight, self.fc1.bias, self.fc2.weight, self.fc2.bias)
         h = self.fc1(x)
         if self.activation_name == "swiglu":
             h = ops.swiglu(h)

@@ -244,6 +244,37 @@ def _cuda_experiment(world: int, *, fused: bool = True, steps: int = 3, overlap:
             "training": {"max_steps": steps, "log_every_steps": 0, "overlap_optimizer_step": overlap, "cuda_graph": graph}}
 
 
+def gathered_attention_worker(rank: int, world: int) -> dict[str, float]:
+    """Native all-gather context-parallel attention of one chunk per rank against the single-GPU kernel
+    over the whole sequence (output, and the gradient of this rank's chunk of the packed input)."""
+    from hybrid_training import ops
+    from hybrid_training.parallel.context_parallel import gathered_attention
+
+    cfg = ExperimentConfig.from_dict(_cuda_experiment(world))
+    ctx = init_distributed(cfg)
+    try:
+        torch.manual_seed(0)
+        b, s, h, hkv, d = 2, 512 * world, 8, 4, 64
+        qkv = (torch.randn(b, s, (h + 2 * hkv) * d, device=ctx.device) * 0.5).bfloat16()
+        dout = torch.randn(b, s, h * d, device=ctx.device).bfloat16()
+        local = s // world
+        win = slice(rank * local, (rank + 1) * local)
+        mine = qkv[:, win].clone().requires_grad_(True)
+        out = gathered_attention(mine, h, hkv, d, ctx.group("data_parallel"), causal=True)
+        out.backward(dout[:, win])
+        full = qkv.clone().requires_grad_(True)
+        ref = ops.attention(full, h, hkv, d, causal=True)
+        ref.backward(dout)
+
+        def rel(a: torch.Tensor, r: torch.Tensor) -> float:
+            return float((a.float() - r.float()).norm() / r.float().norm())
+
+        return {"out": rel(out, ref[:, win]), "dq": rel(mine.grad[..., : h * d], full.grad[:, win, : h * d]),
+                "dkv": rel(mine.grad[..., h * d:], full.grad[:, win, h * d:])}
+    finally:
+        ctx.shutdown()
+
+
 def bucket_allreduce_worker(rank: int, world: int, nvls: bool = False) -> dict[str, Any]:
     """In-kernel bucket all-reduce over NVLink peer memory against NCCL's all-reduce (average).
 

@@ -156,6 +156,71 @@ def test_gelu_mlp_matches_fp32() -> None:
         assert _rel(got.grad, want.grad) < 3e-2, _rel(got.grad, want.grad)
 
 
+@pytest.mark.parametrize("rows,k,f,bias", [(300, 256, 256, True), (1024, 512, 384, False), (77, 64, 128, True)])
+def test_swiglu_mlp_matches_fp32(rows: int, k: int, f: int, bias: bool) -> None:
+    """SwiGLU inside fc1's epilogue and its gradient inside fc2's data-gradient epilogue, against fp32 torch."""
+    ops = _ops()
+    dev = torch.device("cuda")
+    x = torch.randn(rows, k, device=dev).bfloat16().requires_grad_(True)
+    w1 = (torch.randn(2 * f, k, device=dev) * 0.08).requires_grad_(True)
+    b1 = (torch.randn(2 * f, device=dev) * 0.1).requires_grad_(True) if bias else None
+    w2 = (torch.randn(k, f, device=dev) * 0.08).requires_grad_(True)
+    b2 = (torch.randn(k, device=dev) * 0.1).requires_grad_(True) if bias else None
+    params = [t for t in (x, w1, b1, w2, b2) if t is not None]
+    y = ops.swiglu_mlp(x, w1, b1, w2, b2)
+    ref_in = [t.detach().float().cpu().requires_grad_(True) for t in params]
+    xr, w1r, w2r = ref_in[0], ref_in[1], ref_in[3 if bias else 2]
+    b1r, b2r = (ref_in[2], ref_in[4]) if bias else (None, None)
+    h = xr @ w1r.bfloat16().float().t() + (b1r if bias else 0.0)
+    gate, up = h[:, :f], h[:, f:]
+    ref = (F.silu(gate) * up) @ w2r.bfloat16().float().t() + (b2r if bias else 0.0)
+    assert _rel(y, ref) < 2e-2, _rel(y, ref)
+    # the saved pre-activations are exactly the fused GEMM's h
+    hh, a = ops.swiglu_gemm(x.detach(), w1.detach().bfloat16(), None if b1 is None else b1.detach())
+    assert _rel(hh, h.detach()) < 1e-2 and _rel(a, F.silu(gate) * up) < 2e-2
+    g = torch.randn_like(ref)
+    y.backward(g.to(dev).bfloat16())
+    ref.backward(g.bfloat16().float())
+    for got, want in zip(params, ref_in):
+        assert _rel(got.grad, want.grad) < 3e-2, _rel(got.grad, want.grad)
+
+
+@pytest.mark.parametrize("d,hkv,causal,fast", [(64, 4, True, False), (64, 4, True, True), (128, 2, True, False),
+                                               (64, 4, False, True)])
+def test_attention_query_windows_compose_the_full_attention(d: int, hkv: int, causal: bool, fast: bool) -> None:
+    """Query windows (one context-parallel rank each) reproduce the full kernel: outputs of the window
+    rows, dQ of the window rows, and dK / dV summed over the windows, against an fp32 torch oracle."""
+    from hybrid_training.ops.attention import attention_window_backward, attention_window_forward, reference_attention
+
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    b, s, h = 2, 512, 8
+    w = (h + 2 * hkv) * d
+    qkv = (torch.randn(b, s, w, device=dev) * 0.5).bfloat16()
+    dout = torch.randn(b, s, h * d, device=dev).bfloat16()
+    ref_in = qkv.float().cpu().requires_grad_(True)
+    ref = reference_attention(ref_in, h, hkv, d, causal=causal)
+    ref.float().backward(dout.float().cpu())
+    out = torch.zeros(b, s, h * d)
+    dq = torch.zeros(b, s, h * d)
+    dkv = torch.zeros(b, s, w - h * d)
+    ops = _ops()
+    ops.set_deterministic_reductions(not fast)  # fast: the fused D = 64 backward kernel
+    try:
+        for begin, length in ((0, 128), (128, 256), (384, 128)):
+            o_full, lse = attention_window_forward(qkv, h, hkv, d, begin, length, causal)
+            assert torch.count_nonzero(o_full[:, :begin]) == 0 and torch.count_nonzero(o_full[:, begin + length:]) == 0
+            out[:, begin:begin + length] = o_full[:, begin:begin + length].float().cpu()
+            g = attention_window_backward(qkv, o_full, lse, dout[:, begin:begin + length], h, hkv, d, begin, length, causal)
+            dq[:, begin:begin + length] = g[:, begin:begin + length, : h * d].float().cpu()
+            dkv += g[..., h * d:].float().cpu()
+    finally:
+        ops.set_deterministic_reductions(True)
+    assert _rel(out, ref) < 2e-2, _rel(out, ref)
+    assert _rel(dq, ref_in.grad[..., : h * d]) < 3e-2
+    assert _rel(dkv, ref_in.grad[..., h * d:]) < 3e-2
+
+
 def test_column_sum_and_sum_rows() -> None:
     ops = _ops()
     ext = ops.extension()

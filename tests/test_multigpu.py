@@ -16,6 +16,12 @@ from . import dist_workers as W
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
+def test_native_all_gather_context_parallel_attention_matches_the_whole_sequence() -> None:
+    results = launch_workers(W.gathered_attention_worker, 2, timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+    for r in results:
+        assert r["out"] < 1e-2 and r["dq"] < 1e-2 and r["dkv"] < 2e-2, r
+
+
 def test_in_kernel_bucket_all_reduce_matches_nccl() -> None:
     results = launch_workers(W.bucket_allreduce_worker, 2, timeout_seconds=300,
                              extra_env={"NCCL_NVLS_ENABLE": "0"})
