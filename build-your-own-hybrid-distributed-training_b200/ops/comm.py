@@ -73,11 +73,14 @@ def bucket_all_reduce(workspace: Any, flat: torch.Tensor, start: int, numel: int
 def fsdp_reduce_scatter_adamw(workspace: Any, staging: torch.Tensor, shard16: torch.Tensor, *, shard: int, valid: int,
                               scale: float, param: torch.Tensor, exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor,
                               hyper: torch.Tensor, betas: tuple[float, float], eps: float, weight_decay: float,
-                              grad_out: torch.Tensor | None = None) -> torch.Tensor:
+                              grad_out: torch.Tensor | None = None, slice_index: int | None = None) -> torch.Tensor:
     """Reduce-scatter the unit gradient in every peer's ``staging`` and apply AdamW to this rank's shard.
 
-    ``staging`` (bf16 or fp32, at least ``world * shard`` elements) and ``shard16`` (bf16,
-    ``shard`` elements) must be allocations of ``workspace``; ``param`` / ``exp_avg`` /
+    ``staging`` (bf16 or fp32, the unit's padded gradient) must be an allocation of ``workspace``,
+    whose group is the set of ranks whose gradients are summed: the shard group, or under hybrid
+    sharding the data-parallel x shard group, with ``slice_index`` this rank's index in the shard
+    group (default: its rank in ``workspace``).  ``shard16`` (bf16, ``shard`` elements) receives
+    the updated shard for the next all-gather; ``param`` / ``exp_avg`` /
     ``exp_avg_sq`` are this rank's fp32 master shard and moments; ``hyper`` is the optimizer's
     device vector ``[lr, step, grad_scale, skip]``.  Elements at local index ``>= valid`` are
     padding and get a zero gradient.  ``grad_out`` (fp32, optional) receives the reduced shard
@@ -89,7 +92,7 @@ def fsdp_reduce_scatter_adamw(workspace: Any, staging: torch.Tensor, shard16: to
     extension().fsdp_reduce_scatter_adamw(staging, list(handle.buffer_ptrs), list(handle.signal_pad_ptrs), int(handle.rank),
                                           int(shard), int(valid), float(scale), param, exp_avg, exp_avg_sq, shard16, grad_out,
                                           hyper, float(betas[0]), float(betas[1]), float(eps), float(weight_decay), base,
-                                          max_blocks, workspace.status, _TIMEOUT_S)
+                                          max_blocks, workspace.status, _TIMEOUT_S, -1 if slice_index is None else int(slice_index))
     return workspace.status
 
 

@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 // ------------------------------------------------------------------------------------------------
 template <int D>
 struct DkvCfg {
-  static constexpr int BKV = 128, BQ = 64;
+  static constexpr int BKV = 128, BQ = 64;  // BQ divides 128 (query windows are given in 128-row tiles)
   static constexpr int KV_BYTES = BKV * D * 2;  // K and V tiles (resident)
   static constexpr int Q_BYTES = BQ * D * 2;    // Q and dO tiles (streamed)
   static constexpr int STAGES = 2;
@@ -264,9 +264,11 @@ __global__ void __launch_bounds__(THREADS, DkvCfg<D>::MIN_BLOCKS)
   const int group = H / HKV;
   const int kv0 = kt * C::BKV;
   const int nqt = (S + C::BQ - 1) / C::BQ;
-  // Query tiles that can see this key tile, inside the window qt0 .. qt0 + nqt_w - 1.
-  const int first_qt = max(causal ? kv0 / C::BQ : 0, qt0);
-  const int per_head = max(0, min(nqt, qt0 + nqt_w) - first_qt);
+  // Query tiles (of BQ rows) that can see this key tile, inside the window of 128-row tiles
+  // qt0 .. qt0 + nqt_w - 1.
+  const int win_lo = qt0 * 128 / C::BQ, win_hi = (qt0 + nqt_w) * 128 / C::BQ;
+  const int first_qt = max(causal ? kv0 / C::BQ : 0, win_lo);
+  const int per_head = max(0, min(nqt, win_hi) - first_qt);
   const int n_steps = per_head * group;
   const float scale_log2 = scale * LOG2E;
 
@@ -405,7 +407,9 @@ __global__ void __launch_bounds__(THREADS, DkvCfg<D>::MIN_BLOCKS)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full);
     }
-    if (ok && (n_steps == 0 || mbar_wait(&o_full, (n_steps - 1) & 1, err, 37))) {
+    // With no query step (a key tile outside a query window) the K / V loads may still be in
+    // flight: wait for them before the zeros below overwrite the same buffers.
+    if (ok && (n_steps == 0 ? mbar_wait(&kv_ready, 0, err, 38) : mbar_wait(&o_full, (n_steps - 1) & 1, err, 37))) {
       tc_fence_after();
       // dV (unscaled) into the V buffer, dK * scale into the K buffer (both no longer read).
 #pragma unroll 1
@@ -524,9 +528,11 @@ __global__ void __launch_bounds__(FusedCfg::THREADS, 1)
   const int group = H / HKV;
   const int kv0 = kt * C::BKV;
   const int nqt = (S + C::BQ - 1) / C::BQ;
-  // Query tiles that can see this key tile, inside the window qt0 .. qt0 + nqt_w - 1.
-  const int first_qt = max(causal ? kv0 / C::BQ : 0, qt0);
-  const int per_head = max(0, min(nqt, qt0 + nqt_w) - first_qt);
+  // Query tiles (of BQ rows) that can see this key tile, inside the window of 128-row tiles
+  // qt0 .. qt0 + nqt_w - 1.
+  const int win_lo = qt0 * 128 / C::BQ, win_hi = (qt0 + nqt_w) * 128 / C::BQ;
+  const int first_qt = max(causal ? kv0 / C::BQ : 0, win_lo);
+  const int per_head = max(0, min(nqt, win_hi) - first_qt);
   const int n_steps = per_head * group;
   const float scale_log2 = scale * LOG2E;
 

@@ -51,7 +51,7 @@ void fsdp_reduce_scatter_adamw(at::Tensor staging, std::vector<int64_t> grad_ptr
                                int64_t shard, int64_t valid, double scale, at::Tensor param, at::Tensor exp_avg,
                                at::Tensor exp_avg_sq, at::Tensor shard16, c10::optional<at::Tensor> grad_out, at::Tensor hyper,
                                double beta1, double beta2, double eps, double wd, int64_t slot_base, int64_t max_blocks,
-                               at::Tensor status, double timeout_s);
+                               at::Tensor status, double timeout_s, int64_t slice);
 void fsdp_all_gather(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t shard, int64_t rank);
 void barrier_probe(at::Tensor pads, at::Tensor status, double timeout_s);
 void fsdp_all_gather_copy_engine(std::vector<int64_t> shard_ptrs, at::Tensor out, int64_t shard, int64_t rank);

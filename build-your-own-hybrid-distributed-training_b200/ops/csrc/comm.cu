@@ -300,7 +300,8 @@ __global__ void __launch_bounds__(THREADS) fsdp_rs_adamw_kernel(ShardPeers sp, l
                                                                 float* __restrict__ mom2, __nv_bfloat16* __restrict__ out16,
                                                                 float* __restrict__ grad_out, const float* __restrict__ hyper,
                                                                 float beta1, float beta2, float eps, float wd, int rank, int world,
-                                                                int slot_base, int* status, unsigned long long timeout_ns) {
+                                                                int slot_base, int* status, unsigned long long timeout_ns,
+                                                                int slice) {
   Peers pp{};
 #pragma unroll
   for (int p = 0; p < MAX_RANKS; ++p) pp.pad[p] = sp.pad[p];
@@ -317,7 +318,10 @@ __global__ void __launch_bounds__(THREADS) fsdp_rs_adamw_kernel(ShardPeers sp, l
   a.step = a.lr / (1.f - powf(beta1, t));
   a.bc2_sqrt = sqrtf(1.f - powf(beta2, t));
   a.decay = 1.f - a.lr * wd;
-  const long long base = (long long)rank * shard;  // this rank's shard inside every staging buffer
+  // This rank's shard inside every staging buffer: slice `slice` (its index in the shard group;
+  // under hybrid sharding the peers are every rank of the data-parallel x shard group, and the
+  // replicas of a shard sum the same slice of each other's buffers).
+  const long long base = (long long)slice * shard;
   const long long per_block = ((shard + gridDim.x - 1) / gridDim.x + 7) / 8 * 8;
   const long long lo = (long long)blockIdx.x * per_block;
   const long long hi = min(lo + per_block, shard);
@@ -488,14 +492,16 @@ void fsdp_reduce_scatter_adamw(at::Tensor staging, std::vector<int64_t> grad_ptr
                                int64_t shard, int64_t valid, double scale, at::Tensor param, at::Tensor exp_avg,
                                at::Tensor exp_avg_sq, at::Tensor shard16, c10::optional<at::Tensor> grad_out, at::Tensor hyper,
                                double beta1, double beta2, double eps, double wd, int64_t slot_base, int64_t max_blocks,
-                               at::Tensor status, double timeout_s) {
+                               at::Tensor status, double timeout_s, int64_t slice) {
   const c10::cuda::CUDAGuard guard(param.device());
   const int world = (int)grad_ptrs.size();
   HT_CHECK(world >= 2 && world <= comm::MAX_RANKS, "fsdp_reduce_scatter_adamw supports 2..8 ranks");
   HT_CHECK((int)pad_ptrs.size() == world, "one signal pad per rank expected");
   HT_CHECK(rank >= 0 && rank < world, "rank out of range");
+  if (slice < 0) slice = rank;
+  HT_CHECK(slice < world, "shard slice out of range");
   HT_CHECK(staging.scalar_type() == at::kBFloat16 || staging.scalar_type() == at::kFloat, "bf16 or fp32 gradient staging expected");
-  HT_CHECK(staging.numel() >= shard * world, "the staging buffer must hold the unit's padded gradient");
+  HT_CHECK(staging.numel() >= shard * (slice + 1), "the staging buffer must hold the unit's padded gradient");
   HT_CHECK(valid >= 0 && valid <= shard, "valid must lie in [0, shard]");
   for (const at::Tensor* t : {&param, &exp_avg, &exp_avg_sq})
     HT_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == shard, "fp32 shard, moments of the shard size");
@@ -527,7 +533,7 @@ void fsdp_reduce_scatter_adamw(at::Tensor staging, std::vector<int64_t> grad_ptr
   comm::fsdp_rs_adamw_kernel<T, V><<<blocks, comm::THREADS, 0, stream()>>>(                                                \
       sp, shard, valid, (float)scale, param.data_ptr<float>(), exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(), out16, \
       gout, hyper.data_ptr<float>(), (float)beta1, (float)beta2, (float)eps, (float)wd, (int)rank, world, (int)slot_base,      \
-      status.data_ptr<int>(), tns)
+      status.data_ptr<int>(), tns, (int)slice)
   if (staging.scalar_type() == at::kBFloat16) {
     if (vec) HT_FSDP_RS(__nv_bfloat16, true); else HT_FSDP_RS(__nv_bfloat16, false);
   } else {

@@ -198,6 +198,7 @@ class FlatParamHandle:
         # fused reduce-scatter + AdamW state (attach_fused_update): (workspace, optimizer, staging)
         self._fused: tuple[Any, Any, torch.Tensor] | None = None
         self._sym_shard: torch.Tensor | None = None
+        self._gather_workspace: Any = None
         self._sym_stale = True
         self._detach_originals()
 
@@ -267,7 +268,7 @@ class FlatParamHandle:
             from ..ops.comm import fsdp_all_gather
 
             assert self._sym_shard is not None
-            fsdp_all_gather(self._fused[0], self._sym_shard, full, copy_engine=background)
+            fsdp_all_gather(self._gather_workspace, self._sym_shard, full, copy_engine=background)
             record_collective(self._recorder, "fsdp_all_gather_p2p", self._shard_group.name,
                               num_bytes=full.numel() * full.element_size())
             return
@@ -343,15 +344,21 @@ class FlatParamHandle:
     def fused_update_supported(self) -> bool:
         """Whether this unit can take the fused path (CUDA, bf16 compute, fp32 master, plain shard group)."""
         sp_partial = bool(self._sp_ranges) and self._sequence_group is not None and self._sequence_group.size > 1
-        return (self.flat_param.is_cuda and not self._shard_group.is_trivial and self._shard_group.size <= 8
-                and (self._replica_group is None or self._replica_group.size == 1)
+        replicas = 1 if self._replica_group is None else self._replica_group.size
+        return (self.flat_param.is_cuda and not self._shard_group.is_trivial and self._shard_group.size * replicas <= 8
                 and not self._config.cpu_offload_params and self._compute_dtype == torch.bfloat16
                 and self._master_dtype == torch.float32 and self._requires_grad and not sp_partial)
 
-    def attach_fused_update(self, workspace: Any, optimizer: Any, staging: torch.Tensor) -> None:
-        """Route this unit's gradient through the fused kernel (collective: allocates a peer-mapped shard)."""
+    def attach_fused_update(self, workspace: Any, optimizer: Any, staging: torch.Tensor, reduce_workspace: Any = None) -> None:
+        """Route this unit's gradient through the fused kernel (collective: allocates a peer-mapped shard).
+
+        ``workspace`` spans the shard group (the bf16 shards that the all-gathers read);
+        ``reduce_workspace`` (hybrid sharding) spans the data-parallel x shard group and holds
+        ``staging``, so one kernel sums every replica's gradient of this rank's slice.
+        """
         self._sym_shard = workspace.allocate(self._shard_numel, torch.bfloat16)
-        self._fused = (workspace, optimizer, staging)
+        self._gather_workspace = workspace
+        self._fused = (workspace if reduce_workspace is None else reduce_workspace, optimizer, staging)
         self._sym_stale = True
 
     def sync_fused_shard(self) -> None:
@@ -378,12 +385,13 @@ class FlatParamHandle:
         group = optimizer.param_groups[0]
         local = self.local_shard_range()
         valid = max(0, min(self._shard_numel, self._total_numel - local.start))
-        scale = 1.0 / self._shard_group.size if self._config.average_gradients else 1.0
+        summed = workspace.group.size  # shard ranks, times the replicas under hybrid sharding
+        scale = 1.0 / summed if self._config.average_gradients else 1.0
         fsdp_reduce_scatter_adamw(workspace, staging, self._sym_shard, shard=self._shard_numel, valid=valid, scale=scale,
                                   param=self.flat_param.data, exp_avg=state["exp_avg"], exp_avg_sq=state["exp_avg_sq"],
                                   hyper=optimizer.hyper_parameters, betas=group["betas"], eps=group["eps"],
-                                  weight_decay=group["weight_decay"])
-        record_collective(self._recorder, "fsdp_reduce_scatter_adamw", self._shard_group.name,
+                                  weight_decay=group["weight_decay"], slice_index=self._shard_group.local_rank)
+        record_collective(self._recorder, "fsdp_reduce_scatter_adamw", workspace.group.name,
                           num_bytes=self._padded_numel * staging.element_size())
         self._reduction_count += 1
 
@@ -611,13 +619,16 @@ class FullyShardedDataParallel(nn.Module):
             return getattr(inner, name)
 
     # -- fused reduce-scatter + AdamW ------------------------------------------------------------------------
-    def enable_fused_update(self, workspace: Any, optimizer: Any, *, accumulate: bool = False) -> bool:
+    def enable_fused_update(self, workspace: Any, optimizer: Any, *, accumulate: bool = False,
+                            reduce_workspace: Any = None) -> bool:
         """Update every unit inside its gradient reduce-scatter kernel; returns whether the path is on.
 
         Requirements (decided from configuration only, so every rank decides alike): a peer-mapped
         ``workspace`` for the shard group, ``optimizer`` a CUDA ``FusedAdamW`` whose parameters are
-        exactly the units' flat shards, bf16 compute with fp32 master shards, no replica group, no
-        CPU offload.  The caller must not need the gradient afterwards (no clipping, no norm, no
+        exactly the units' flat shards, bf16 compute with fp32 master shards, no CPU offload, at
+        most 8 ranks summed.  With a replica group (hybrid sharding) ``reduce_workspace`` must span
+        the data-parallel x shard group: the kernel then sums the gradients of every replica of
+        the shard in the same pass (the reduce-scatter and the replica all-reduce in one).  The caller must not need the gradient afterwards (no clipping, no norm, no
         loss scaling): the optimizer step happens during the backward pass, unit by unit, and
         ``optimizer.step()`` must be skipped.  ``accumulate`` stages fp32 gradients (exact sums
         of accumulated micro-batches) instead of bf16 ones.  Collective over the shard group.
@@ -627,6 +638,9 @@ class FullyShardedDataParallel(nn.Module):
         units = [u for u in self.fsdp_units() if u._handle is not None]
         if workspace is None or not units or not isinstance(optimizer, FusedAdamW) or not optimizer.flat_parameters.is_cuda:
             return False
+        hybrid = self._replica_group is not None and self._replica_group.size > 1
+        if hybrid and reduce_workspace is None:
+            return False
         owned = {id(p) for p in optimizer.param_groups[0]["params"]}
         shards = {id(u._handle.flat_param) for u in units}
         if owned != shards or len(optimizer.param_groups) != 1:
@@ -634,11 +648,12 @@ class FullyShardedDataParallel(nn.Module):
         if not all(u._handle.fused_update_supported() for u in units):
             return False
         dtype = torch.float32 if accumulate else torch.bfloat16
-        staging = workspace.allocate(max(u._handle.padded_numel for u in units), dtype)
+        staging_ws = reduce_workspace if hybrid else workspace
+        staging = staging_ws.allocate(max(u._handle.padded_numel for u in units), dtype)
         for u in units:
-            u._handle.attach_fused_update(workspace, optimizer, staging)
+            u._handle.attach_fused_update(workspace, optimizer, staging, reduce_workspace if hybrid else None)
         self._fused_units = units
-        self._fused_workspace = workspace
+        self._fused_workspace = staging_ws
         _LOG.info("fsdp: fused reduce-scatter + AdamW over NVLink for %d units (%s gradient staging)", len(units),
                   str(dtype).replace("torch.", ""))
         return True

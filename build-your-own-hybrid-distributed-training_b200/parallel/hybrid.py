@@ -195,11 +195,17 @@ def describe_parallel_plan(config: ExperimentConfig, context: DistributedContext
         if config.fsdp.reshard_after_forward:
             add(PlanStep("backward", "flat-parameter re-gather per unit", "shard",
                          "peer copies of bf16 shards" if fused_fsdp else f"{library} all-gather"))
-        add(PlanStep("backward", "flat-gradient reduce-scatter per unit", "shard",
-                     "one kernel: reduce-scatter over peer memory + 1/G + AdamW on the shard, when the step needs no "
-                     "global gradient norm or loss scaling; otherwise " + library if fused_fsdp else f"{library} reduce-scatter"))
-        if dp > 1:
-            add(PlanStep("backward", "sharded-gradient all-reduce across replicas", "data_parallel", f"{library} all-reduce"))
+        if dp > 1 and fused_fsdp and shard * dp <= 8:
+            add(PlanStep("backward", "flat-gradient reduce-scatter per unit, summed across replicas", "dp_shard",
+                         "one kernel over the replicas x shards: every replica's slice summed over peer memory + 1/(G R) + "
+                         "AdamW on the shard, when the step needs no global gradient norm or loss scaling; otherwise "
+                         f"{library} reduce-scatter, then {library} all-reduce across replicas"))
+        else:
+            add(PlanStep("backward", "flat-gradient reduce-scatter per unit", "shard",
+                         "one kernel: reduce-scatter over peer memory + 1/G + AdamW on the shard, when the step needs no "
+                         "global gradient norm or loss scaling; otherwise " + library if fused_fsdp else f"{library} reduce-scatter"))
+            if dp > 1:
+                add(PlanStep("backward", "sharded-gradient all-reduce across replicas", "data_parallel", f"{library} all-reduce"))
     elif dp > 1:
         add(PlanStep("backward", f"gradient buckets of {config.ddp.bucket_cap_mb:g} MiB, launched in bucket order",
                      "data_parallel",

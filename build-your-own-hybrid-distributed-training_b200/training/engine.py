@@ -150,7 +150,11 @@ class TrainingEngine:
                 or cfg.training.max_grad_norm > 0 or cfg.training.collect_metrics or self.scaler.enabled):
             return False
         workspace = ctx.symmetric_workspace("shard")
-        return fsdp.enable_fused_update(workspace, inner, accumulate=cfg.training.gradient_accumulation_steps > 1)
+        # Hybrid sharding: the replicas' gradients are summed by the same kernel over the
+        # data-parallel x shard group.
+        reduce_ws = ctx.symmetric_workspace("dp_shard") if ctx.group("data_parallel").size > 1 else None
+        return fsdp.enable_fused_update(workspace, inner, accumulate=cfg.training.gradient_accumulation_steps > 1,
+                                        reduce_workspace=reduce_ws)
 
     fsdp_fused_update = property(lambda self: self._fsdp_fused_update)
 

@@ -415,8 +415,12 @@ def llama_cuda_worker(rank: int, world: int, topology: dict[str, Any], fused_tp:
         ctx.shutdown()
 
 
-def _fsdp_experiment(world: int, *, fused_update: bool, steps: int = 3, accumulation: int = 1) -> dict[str, Any]:
-    cfg = _llama_experiment(world, {"shard_parallel_size": world}, steps=steps)
+def _fsdp_experiment(world: int, *, fused_update: bool, steps: int = 3, accumulation: int = 1,
+                     replicas: int = 1) -> dict[str, Any]:
+    topology = {"shard_parallel_size": world // replicas}
+    if replicas > 1:
+        topology["data_parallel_size"] = replicas  # hybrid sharding
+    cfg = _llama_experiment(world, topology, steps=steps)
     cfg["fsdp"] = {"auto_wrap_min_num_params": 10000, "fused_update": fused_update}
     cfg["training"] = {"max_steps": steps, "log_every_steps": 0, "gradient_accumulation_steps": accumulation}
     cfg["optimizer"] = {"learning_rate": 1e-3, "weight_decay": 0.1}
@@ -488,9 +492,12 @@ def fsdp_fused_kernels_worker(rank: int, world: int) -> dict[str, Any]:
         ctx.shutdown()
 
 
-def fsdp_fused_update_worker(rank: int, world: int, fused: bool, steps: int, accumulation: int) -> dict[str, Any]:
-    """Engine steps of a Llama-style decoder under FSDP with or without the fused reduce-scatter + AdamW."""
-    cfg = ExperimentConfig.from_dict(_fsdp_experiment(world, fused_update=fused, steps=steps, accumulation=accumulation))
+def fsdp_fused_update_worker(rank: int, world: int, fused: bool, steps: int, accumulation: int,
+                             replicas: int = 1) -> dict[str, Any]:
+    """Engine steps of a Llama-style decoder under FSDP (``replicas`` > 1: hybrid sharding) with or without
+    the fused reduce-scatter + AdamW."""
+    cfg = ExperimentConfig.from_dict(_fsdp_experiment(world, fused_update=fused, steps=steps, accumulation=accumulation,
+                                                      replicas=replicas))
     ctx = init_distributed(cfg)
     try:
         engine = TrainingEngine(cfg, ctx)

@@ -138,7 +138,11 @@ def test_parallel_plan_names_each_collective_and_its_implementation(sizes: dict,
         ctx = SimpleNamespace(topology=ParallelTopology(topo_cfg, world), device=device)
         plan = describe_parallel_plan(cfg, ctx)
         seen = {(s.phase, s.group) for s in plan.steps}
-        assert expect_ops <= seen, (expect_ops, seen)
+        want = set(expect_ops)
+        if device.type == "cuda" and sizes.get("shard_parallel_size", 1) > 1 and sizes.get("data_parallel_size", 1) > 1:
+            # hybrid sharding on CUDA: one fused kernel sums every replica's slice over the replicas x shards
+            want = {("backward", "dp_shard")} | {op for op in want if op[1] not in ("shard", "data_parallel")}
+        assert want <= seen, (want, seen)
         text = plan.render()
         assert plan.strategy in text and "metrics:" in text
         for s in plan.steps:

@@ -57,13 +57,50 @@ def test_reduce_scatter_adamw_arithmetic(rank: int, shard: int, pad: int, dtype:
     hyper = torch.tensor([lr, float(step), 1.0, 0.0], device=dev)
     ext.fsdp_reduce_scatter_adamw(staging[rank], [s.data_ptr() for s in staging], [pads[0].data_ptr(), pads[1].data_ptr()],
                                   rank, shard, valid, 1.0 / world, param, m, v, shard16, grad_out, hyper, b1, b2, eps, wd, 0,
-                                  _BLOCKS, status, 0.1)
+                                  _BLOCKS, status, 0.1, -1)
     torch.cuda.synchronize()
     assert status[:2].tolist() == [1, 12], status.tolist()  # only the closing barrier (no live peer) ran out
     scale = float(expect.abs().max())
     assert float((grad_out - expect).abs().max()) <= 2e-6 * scale
     assert float((param - ref_p).abs().max()) < 2e-6
     assert float((m - ref_m).abs().max()) < 2e-6 and float((v - ref_v).abs().max()) < 2e-6
+    assert torch.equal(shard16, param.bfloat16())
+
+
+@pytest.mark.parametrize("rank", [0, 3])
+def test_hybrid_shard_reduction_sums_every_replica_of_the_slice(rank: int) -> None:
+    """Hybrid sharding: 2 replicas x 2 shards.  The kernel runs as rank ``rank`` of the 4-rank
+    data-parallel x shard group and reduces slice ``rank % 2`` (its shard index) of all four ranks'
+    staging buffers, which equals the reduce-scatter over the shard group followed by the
+    all-reduce over the replicas."""
+    ext = _ext()
+    dev = torch.device("cuda")
+    world, shards, shard = 4, 2, 65_536
+    slice_index = rank % shards
+    gen = torch.Generator(device="cuda").manual_seed(11 + rank)
+    staging = [torch.randn(shards * shard, device=dev, generator=gen).bfloat16() for _ in range(world)]
+    lo, hi = slice_index * shard, (slice_index + 1) * shard
+    expect = sum(st[lo:hi].float() for st in staging) / world
+    param = torch.randn(shard, device=dev, generator=gen)
+    m, v = torch.zeros(shard, device=dev), torch.zeros(shard, device=dev)
+    lr, b1, b2, eps, wd, step = 1e-3, 0.9, 0.95, 1e-8, 0.0, 1
+    ref_p, ref_m, ref_v = param.clone(), m.clone(), v.clone()
+    reference_adamw(ref_p, expect, ref_m, ref_v, lr=lr, beta1=b1, beta2=b2, eps=eps, weight_decay=wd, step=step)
+    pads = torch.zeros(world, 2 * _BLOCKS * world, dtype=torch.int32, device=dev)
+    for sender in range(world):
+        if sender != rank:
+            pads[rank, sender::world] = 1  # every peer's arrival at the opening barrier
+    shard16 = torch.empty(shard, device=dev, dtype=torch.bfloat16)
+    grad_out = torch.full((shard,), float("nan"), device=dev)
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    hyper = torch.tensor([lr, float(step), 1.0, 0.0], device=dev)
+    ext.fsdp_reduce_scatter_adamw(staging[rank], [t.data_ptr() for t in staging], [pads[q].data_ptr() for q in range(world)],
+                                  rank, shard, shard, 1.0 / world, param, m, v, shard16, grad_out, hyper, b1, b2, eps, wd, 0,
+                                  _BLOCKS, status, 0.1, slice_index)
+    torch.cuda.synchronize()
+    assert status[:2].tolist() == [1, 12], status.tolist()  # only the closing barrier (no live peers) ran out
+    assert float((grad_out - expect).abs().max()) <= 2e-6 * float(expect.abs().max())
+    assert float((param - ref_p).abs().max()) < 2e-6
     assert torch.equal(shard16, param.bfloat16())
 
 

@@ -116,3 +116,25 @@ def test_fsdp_fused_update_trains_like_nccl_path(accumulation: int) -> None:
         ref = nccl[0].value["full"][name]
         err = float((t - ref).abs().max())
         assert err < 5e-3 * max(1.0, float(ref.abs().max())), (name, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="hybrid sharding (2 replicas x 2 shards) needs 4 GPUs")
+def test_hybrid_sharding_fused_update_trains_like_nccl_path() -> None:
+    """HSDP: one kernel sums every replica's slice over the 4 ranks and updates the shard, against
+    NCCL reduce-scatter + replica all-reduce + the separate optimizer step."""
+    fused = launch_workers(W.fsdp_fused_update_worker, 4, args=(True, 3, 1, 2), timeout_seconds=300,
+                           extra_env={"NCCL_NVLS_ENABLE": "0"})
+    nccl = launch_workers(W.fsdp_fused_update_worker, 4, args=(False, 3, 1, 2), timeout_seconds=300,
+                          extra_env={"NCCL_NVLS_ENABLE": "0"})
+    assert all(r.value["fused"] for r in fused) and not nccl[0].value["fused"]
+    for a, b in zip(fused[0].value["losses"], nccl[0].value["losses"]):
+        assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (fused[0].value["losses"], nccl[0].value["losses"])
+    for r in fused[1:]:
+        assert r.value["losses"] == fused[0].value["losses"]
+    for name, t in fused[0].value["full"].items():
+        ref = nccl[0].value["full"][name]
+        err = float((t - ref).abs().max())
+        assert err < 5e-3 * max(1.0, float(ref.abs().max())), (name, err)
+    # the replicas of a shard hold bitwise-identical parameters
+    for name, t in fused[0].value["full"].items():
+        assert torch.equal(t, fused[2].value["full"][name]), name
