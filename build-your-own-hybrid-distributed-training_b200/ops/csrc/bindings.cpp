@@ -3,6 +3,7 @@
 
 namespace ht {
 void set_deterministic_reductions(bool on);
+void set_gemm_pair(int64_t mode);
 bool deterministic_reductions();
 void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bias, c10::optional<at::Tensor> aux,
           c10::optional<at::Tensor> alpha, bool a_mn_major, bool b_mn_major, int64_t epilogue, double beta);
@@ -60,6 +61,7 @@ void fsdp_all_gather_copy_engine(std::vector<int64_t> shard_ptrs, at::Tensor out
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hybrid_training native kernels (sm_100a)";
   m.def("gemm", &ht::gemm, "tcgen05 GEMM with fused epilogue");
+  m.def("set_gemm_pair", &ht::set_gemm_pair, "1: CTA-pair (cta_group::2) tiles for eligible GEMMs, 0: single-CTA tiles only");
   m.def("gemm_swiglu", &ht::gemm_swiglu, "tcgen05 GEMM with the SwiGLU activation (or its gradient) in the epilogue");
   m.def("gemm_error_word", &ht::gemm_error_word, "device error word written by timed-out GEMM waits");
   m.def("gemm_collective", &ht::gemm_collective, "GEMM with peer-sharded operands or a reduce-scatter epilogue");

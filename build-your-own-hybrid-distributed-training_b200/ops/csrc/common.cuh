@@ -229,6 +229,59 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                : "memory");
 }
 
+// ---- CTA pairs (clusters of two CTAs sharing one tcgen05.mma.cta_group::2) ----
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t smem_in_cta(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+// Arrive on an mbarrier of another CTA of the cluster.  The default (CTA-scope) semantics: what
+// the barrier orders here is the completion of asynchronous copies and tensor-core reads, not
+// generic memory, so no cluster-wide fence is needed (a `.release.cluster` arrive measured as a
+// membar stall on every pipeline stage).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Bounded wait on a local mbarrier whose arrivals may come from the other CTA of the pair.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait(bar, parity, err, code);
+}
+// Every thread of both CTAs: arrive, then wait (orders shared-memory accesses across the pair).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMEM of a CTA pair: the same columns in both CTAs, allocated by the same warp of each.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+// D (rows 0-127 in this CTA's TMEM, rows 128-255 in the peer's) (+)= A * B over both CTAs' shared
+// memory: A rows and B columns are split between the CTAs at the same addresses.  Issued by CTA 0.
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive on `bar` (same offset) in both CTAs of the pair once the pair's issued MMAs complete.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"((uint16_t)3)
+               : "memory");
+}
+
 // Each thread of the warp reads 32 consecutive fp32 columns of its own TMEM lane.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float* v) {
   uint32_t r[32];

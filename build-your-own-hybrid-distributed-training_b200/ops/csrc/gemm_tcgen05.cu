@@ -373,7 +373,9 @@ __device__ __forceinline__ void epilogue_piece_tma(const EpiParams& ep, const CU
 }
 
 // All output tiles of one epilogue warp.  CW = output columns per 128-byte piece; TN = tile width.
-template <int CW, int KIND, int TN = BN>
+// PAIR: a CTA of a pair kernel (tiles of 256 rows, this CTA's 128 rows in its own TMEM; the
+// accumulator-free signal goes to the pair's first CTA, which issues the MMAs).
+template <int CW, int KIND, int TN = BN, bool PAIR = false>
 __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtensorMap* map_d, const CUtensorMap* map_aux,
                                               uint8_t* tile, uint32_t tmem_base, uint64_t* tfull_bar, uint64_t* tempty_bar,
                                               int M, int N, int num_m, int num_n, int num_tiles, int warp, int lane, int* err,
@@ -386,9 +388,13 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
   int acc = 0;
   uint32_t acc_phase = 0;
   const int num_units = num_tiles * ep.splits;
-  for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+  const int first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int stride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int crank = PAIR ? (int)cluster_ctarank() : 0;
+  for (int unit = first; unit < num_units; unit += stride) {
     int mb, nb;
     tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
+    if (PAIR) mb = mb * 2 + crank;  // this CTA's 128-row half of the pair tile
     if (coll != nullptr && coll->a_mode == 1) mb = coll_phys_mblock(*coll, mb);
     int out_row0 = (unit % ep.splits) * ep.split_rows + mb * BM + quarter * 32;
     const CUtensorMap* dmap = map_d;
@@ -400,7 +406,7 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
       out_row0 = lrow + quarter * 32;
       z = coll->rank * coll->batch + bidx;
     }
-    if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 4)) break;
+    if (!(PAIR ? mbar_wait_cluster(&tfull_bar[acc], acc_phase, err, 4) : mbar_wait(&tfull_bar[acc], acc_phase, err, 4))) break;
     tc_fence_after();
     const int row = mb * BM + row_in_tile;
 #pragma unroll 1
@@ -421,7 +427,10 @@ __device__ __forceinline__ void epilogue_loop(const EpiParams& ep, const CUtenso
     }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    if (lane == 0) {
+      if (PAIR) mbar_arrive_cluster(smem_in_cta(&tempty_bar[acc], 0));
+      else mbar_arrive(&tempty_bar[acc]);
+    }
     if (++acc == 2) {
       acc = 0;
       acc_phase ^= 1u;
@@ -903,6 +912,223 @@ __global__ void __launch_bounds__(THREADS, 1)
   gemm_body<A_MN, B_MN, false, KIND, TN>(tma_a, tma_b, tma_d, tma_aux, M, N, K, ep, err, nullptr);
 }
 
+// ------------------------------------------------------------------------------------------------
+// CTA-pair GEMM (cluster of two CTAs, tcgen05.mma.cta_group::2): 256 x TN output tiles.  Each CTA
+// loads its own 128 rows of A and its half (TN / 2 rows or columns) of B into its own shared
+// memory, so a stage holds 16 KB + TN * 64 bytes per CTA instead of 16 KB + TN * 128: six stages
+// fit where the single-CTA kernel holds four, and every CTA reads a third fewer operand bytes per
+// multiply-add from L2.  CTA 0 issues the MMAs for the pair (rows 0-127 accumulate in its TMEM,
+// rows 128-255 in CTA 1's) and its commits arrive on both CTAs' barriers.  Every TMA load
+// completes on a barrier of the CTA that issued it; CTA 1's MMA warp relays "stage full" to CTA 0
+// with a cluster-scope arrive, so no asynchronous copy ever targets the other CTA's memory and no
+// CTA can leave while its partner still uses its shared memory (a cluster barrier closes the
+// kernel, after every issued MMA has completed).  No load is multicast.
+// ------------------------------------------------------------------------------------------------
+constexpr int PAIR_STAGES = 6;
+
+template <int TN>
+struct PairCfg {
+  static constexpr int TB_BYTES = (TN / 2) * BK * 2;  // this CTA's half of a B stage
+  static constexpr int STAGE_BYTES = A_BYTES + TB_BYTES;
+  static constexpr int SMEM = PAIR_STAGES * STAGE_BYTES + EPI_WARPS * EPI_STAGE_BYTES + 1024;
+  static_assert(SMEM <= 232448, "shared memory budget of one sm_100 CTA exceeded");
+};
+
+__device__ __forceinline__ void tc_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <bool A_MN, bool B_MN, int KIND, int TN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_aux, int M, int N, int K,
+                     EpiParams ep, int* err) {
+  using P = PairCfg<TN>;
+  static_assert(!B_MN || (TN / 2) % 64 == 0, "an MN-major B half is loaded in 64-column boxes");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PAIR_STAGES * A_BYTES;
+  uint8_t* sEpi = smem + PAIR_STAGES * P::STAGE_BYTES;
+
+  __shared__ __align__(8) uint64_t full_bar[PAIR_STAGES];   // this CTA's stage landed (its own loads)
+  __shared__ __align__(8) uint64_t peer_full[PAIR_STAGES];  // CTA 0 only: CTA 1's stage landed (relayed)
+  __shared__ __align__(8) uint64_t empty_bar[PAIR_STAGES];  // the pair's MMAs have read the stage
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], mma_done;
+  __shared__ uint32_t tmem_base_slot;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+  const int num_m = (M + 2 * BM - 1) / (2 * BM);
+  const int num_n = (N + TN - 1) / TN;
+  const int num_tiles = num_m * num_n;
+  const int num_units = num_tiles * ep.splits;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&peer_full[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2 * EPI_WARPS);  // every epilogue warp of both CTAs (used in CTA 0)
+    }
+    mbar_init(&mma_done, 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+    if (ep.tma_d) prefetch_tensormap(&tma_d);
+    if (ep.tma_aux) prefetch_tensormap(&tma_aux);
+  }
+  if (warp == 1) tmem_alloc_pair(&tmem_base_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any arrive crosses the pair
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs): this CTA's A rows and B half ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int unit = pair; unit < num_units && ok; unit += npairs) {
+        int mb, nb, kb0, kb1;
+        tile_coords(unit / ep.splits, num_m, num_n, mb, nb);
+        split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
+        const int m0 = mb * 2 * BM + (int)crank * BM;
+        const int nh = nb * TN + (int)crank * (TN / 2);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, err, 61)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * P::TB_BYTES;
+          const int k0 = kb * BK;
+          mbar_arrive_expect_tx(&full_bar[stage], P::STAGE_BYTES);
+          if (A_MN) {
+            tma_load_2d(a_dst, &tma_a, &full_bar[stage], m0, k0);
+            tma_load_2d(a_dst + BK * 128, &tma_a, &full_bar[stage], m0 + 64, k0);
+          } else {
+            tma_load_2d(a_dst, &tma_a, &full_bar[stage], k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < TN / 128; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, &full_bar[stage], nh + 64 * j, k0);
+          } else {
+            tma_load_2d(b_dst, &tma_b, &full_bar[stage], k0, nh);
+          }
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: every filled stage has been read by the pair's MMAs (all their commits have
+      // arrived here) before this CTA may reach the closing cluster barrier.
+      for (int i = 0; i < PAIR_STAGES; ++i) {
+        if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, err, 62)) break;
+        if (++stage == PAIR_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1 && crank == 1) {
+    // ---------------- relay (CTA 1): "my half of the stage landed" -> CTA 0 ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int unit = pair; unit < num_units && ok; unit += npairs) {
+        int kb0, kb1;
+        split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, err, 63)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_cluster(smem_in_cta(&peer_full[stage], 0));
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (CTA 0) for the pair ----------------
+    constexpr uint32_t idesc = umma_idesc_bf16(2 * BM, TN, A_MN, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int unit = pair; unit < num_units && ok; unit += npairs) {
+      int kb0, kb1;
+      split_range(kblocks, ep.splits, unit % ep.splits, kb0, kb1);
+      if (!mbar_wait_cluster(&tempty_bar[acc], acc_phase ^ 1u, err, 64)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, err, 65) || !mbar_wait_cluster(&peer_full[stage], phase, err, 66)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * P::TB_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a_addr + k * 2048, BK * 128, 1024)
+                                        : umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + k * 2048, BK * 128, 1024)
+                                        : umma_desc_sw128(b_addr + k * 32, 16, 1024);
+            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+          }
+          tc_commit_pair(&empty_bar[stage]);
+        }
+        __syncwarp();
+        if (++stage == PAIR_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit_pair(&tfull_bar[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    // Every MMA issued above has completed (it reads both CTAs' shared memory and writes both
+    // TMEMs) before the pair may leave.
+    if (lane == 0) tc_commit_pair_local(&mma_done);
+    __syncwarp();
+    mbar_wait(&mma_done, 0, err, 67);
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows ----------------
+    uint8_t* tile = sEpi + (warp - 2) * EPI_STAGE_BYTES;
+    epilogue_loop<KIND == kKindF32 ? 32 : 64, KIND, TN, true>(ep, &tma_d, &tma_aux, tile, tmem_base, tfull_bar, tempty_bar, M, N,
+                                                              num_m, num_n, num_tiles, warp, lane, err, nullptr);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(COLL_THREADS, 1)
     gemm_coll_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -1198,7 +1424,56 @@ static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   }
 }
 
+// CTA-pair launch (256-row tiles, 74 pairs); returns false when this combination has no pair instance.
+template <bool A_MN, bool B_MN, int KIND>
+static void launch_pair_kind(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux, int M,
+                             int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
+  auto kernel = gemm_pair_kernel<A_MN, B_MN, KIND, BN>;
+  constexpr int smem = PairCfg<BN>::SMEM;
+  static bool configured = false;
+  if (!configured) {
+    HT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  const int units = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * ep.splits;
+  const int pairs = std::min(units, num_sms() / 2);
+  kernel<<<2 * pairs, THREADS, smem, s>>>(ma, mb, md, maux, M, N, K, ep, err);
+  HT_CUDA_CHECK(cudaGetLastError());
+}
+
+template <bool A_MN, bool B_MN>
+static bool launch_pair(int kind, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& maux,
+                        int M, int N, int K, const EpiParams& ep, int* err, cudaStream_t s) {
+  if constexpr (!A_MN && !B_MN) {  // forward
+    if (kind == kKindBf16) return launch_pair_kind<false, false, kKindBf16>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+    if (kind == kKindGelu) return launch_pair_kind<false, false, kKindGelu>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+    if (kind == kKindF32) return launch_pair_kind<false, false, kKindF32>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+  } else if constexpr (!A_MN && B_MN) {  // data gradient
+    if (kind == kKindBf16) return launch_pair_kind<false, true, kKindBf16>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+    if (kind == kKindGeluBwd) return launch_pair_kind<false, true, kKindGeluBwd>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+    if (kind == kKindF32) return launch_pair_kind<false, true, kKindF32>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+  } else if constexpr (A_MN && B_MN) {  // weight gradient
+    if (kind == kKindF32) return launch_pair_kind<true, true, kKindF32>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+    if (kind == kKindBf16) return launch_pair_kind<true, true, kKindBf16>(ma, mb, md, maux, M, N, K, ep, err, s), true;
+  }
+  return false;
+}
+
+// CTA pairs for every eligible GEMM (1), or never (0, the default); HT_GEMM_PAIR=1 in the
+// environment sets 1.
+static int g_pair_mode = -1;
+
+static bool pair_enabled() {
+  if (g_pair_mode < 0) {
+    const char* e = std::getenv("HT_GEMM_PAIR");
+    g_pair_mode = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return g_pair_mode == 1;
+}
+
 }  // namespace tcg
+
+void set_gemm_pair(int64_t mode) { tcg::g_pair_mode = mode ? 1 : 0; }
 
 // Split-K GEMMs with an fp32 output either sum their partial tiles in a fixed order (a workspace
 // and a reduction pass: bitwise reproducible), or, when reproducibility is switched off, add every
@@ -1262,11 +1537,17 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   // that store fp32 partial tiles into a workspace, summed in a fixed order afterwards.
   CUtensorMap md{}, maux{};
   ep.splits = 1;
-  const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
+  // CTA pairs (256-row tiles) for the epilogues they carry; the kind is confirmed below.
+  const bool pair_shape = pair_enabled() && M > BM && (epilogue == kPlain || epilogue == kGelu || epilogue == kGeluBwd) &&
+                          !(a_mn_major && !b_mn_major);
+  const int tile_rows = pair_shape ? 2 * BM : BM;
+  const int tiles = (int)(((M + tile_rows - 1) / tile_rows) * ((N + BN - 1) / BN));
   const int kblocks = (int)((K + BK - 1) / BK);
-  const int splits = (epilogue == kPlain && ep.bias_f32 == nullptr && ep.bias_bf16 == nullptr) ? choose_splits(tiles, kblocks, num_sms()) : 1;
+  const int splits = (epilogue == kPlain && ep.bias_f32 == nullptr && ep.bias_bf16 == nullptr)
+                         ? choose_splits(tiles, kblocks, pair_shape ? num_sms() / 2 : num_sms())
+                         : 1;
   at::Tensor workspace;
-  const int64_t split_rows = (M + BM - 1) / BM * BM, ldw = (N + 3) / 4 * 4;
+  const int64_t split_rows = (M + tile_rows - 1) / tile_rows * tile_rows, ldw = (N + 3) / 4 * 4;
   const bool split_reduce_add = splits > 1 && !g_ordered_split_k && d32 && ep.vec_ok && (beta == 0.0 || beta == 1.0);
   if (split_reduce_add) {
     if (beta == 0.0)
@@ -1296,13 +1577,26 @@ void gemm(at::Tensor a, at::Tensor b, at::Tensor d, c10::optional<at::Tensor> bi
   // The narrow tile is compiled for A K-major products with the bf16 / GELU / GELU' epilogues; the
   // K-major B map's box must match the tile width the kernel expects.
   const int kind = epilogue_kind(ep);
+  int* err = error_word(a.device());
+  cudaStream_t s = stream();
+  const bool pair = pair_shape && (kind == kKindBf16 || kind == kKindF32 || kind == kKindGelu || kind == kKindGeluBwd);
+  if (pair) {
+    // Each CTA of a pair loads half of the B tile: K-major boxes of BN / 2 rows.
+    const CUtensorMap mbp = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64)
+                                       : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN / 2);
+    bool done = false;
+    if (!a_mn_major && !b_mn_major) done = launch_pair<false, false>(kind, ma, mbp, md, maux, M, N, K, ep, err, s);
+    else if (!a_mn_major && b_mn_major) done = launch_pair<false, true>(kind, ma, mbp, md, maux, M, N, K, ep, err, s);
+    else if (a_mn_major && b_mn_major) done = launch_pair<true, true>(kind, ma, mbp, md, maux, M, N, K, ep, err, s);
+    HT_CHECK(done, "no CTA-pair GEMM instance for this operand layout and epilogue");
+  }
   const bool narrow_ok = !a_mn_major && (kind == kKindBf16 || kind == kKindGelu || kind == kKindGeluBwd);
   const int tn = narrow_ok ? choose_tile_n(M, N, ep.splits) : BN;
   const CUtensorMap mb = b_mn_major ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64)
                                     : make_map(b.data_ptr(), N, K, b.stride(0), 64, tn);
-  int* err = error_word(a.device());
-  cudaStream_t s = stream();
-  if (!a_mn_major && !b_mn_major) launch<false, false>(ma, mb, md, maux, M, N, K, ep, err, s, tn);
+  if (pair) {
+    // launched above
+  } else if (!a_mn_major && !b_mn_major) launch<false, false>(ma, mb, md, maux, M, N, K, ep, err, s, tn);
   else if (!a_mn_major && b_mn_major) launch<false, true>(ma, mb, md, maux, M, N, K, ep, err, s, tn);
   else if (a_mn_major && b_mn_major) launch<true, true>(ma, mb, md, maux, M, N, K, ep, err, s);
   else launch<true, false>(ma, mb, md, maux, M, N, K, ep, err, s);

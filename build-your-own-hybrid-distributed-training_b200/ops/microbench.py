@@ -80,11 +80,17 @@ def bench_gemm(only: str | None, iters: int) -> None:
         a = _padded(torch.randn((k, m) if amn else (m, k), device=dev).bfloat16())
         b = _padded(torch.randn((k, n) if bmn else (n, k), device=dev).bfloat16())
         out = torch.zeros(m, (n + 63) // 64 * 64, device=dev, dtype=torch.float32 if f32 else torch.bfloat16)[:, :n]
+        from ._ext import extension
+
+        extension().set_gemm_pair(1)
+        pair = _time(lambda: gemm(a, b, out=out, a_mn_major=amn, b_mn_major=bmn, beta=1.0 if f32 else 0.0), iters, flush)
+        extension().set_gemm_pair(0)
         ours = _time(lambda: gemm(a, b, out=out, a_mn_major=amn, b_mn_major=bmn, beta=1.0 if f32 else 0.0), iters, flush)
         aa, bb = (a.t() if amn else a), (b if bmn else b.t())
         lib = _time(lambda: torch.matmul(aa, bb), iters, flush)
         flops = 2.0 * m * n * k
-        print(f"gemm {name:11s} M={m} N={n} K={k}: {ours * 1e3:8.1f} us {flops / ours / 1e9:7.1f} TFLOP/s | "
+        print(f"gemm {name:11s} M={m} N={n} K={k}: {ours * 1e3:8.1f} us {flops / ours / 1e9:7.1f} TFLOP/s "
+              f"(CTA-pair tiles {pair * 1e3:7.1f} us {flops / pair / 1e9:7.1f}) | "
               f"torch.matmul {lib * 1e3:8.1f} us {flops / lib / 1e9:7.1f} TFLOP/s", flush=True)
 
 

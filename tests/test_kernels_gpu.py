@@ -41,6 +41,60 @@ def test_gemm_matches_fp32(m: int, n: int, k: int, a_mn: bool, b_mn: bool) -> No
     assert _rel(d, ref) < 1e-5, _rel(d, ref)
 
 
+@pytest.mark.parametrize("m,n,k,a_mn,b_mn,epi", [
+    (1024, 768, 256, False, False, "plain"), (300, 520, 192, False, False, "gelu"), (8192, 2304, 768, False, False, "plain"),
+    (777, 512, 320, False, True, "gelu_bwd"), (640, 1024, 448, False, True, "plain"), (3072, 768, 8192, True, True, "wgrad"),
+    (2304, 768, 1000, True, True, "wgrad_fast"), (600, 256, 4096, True, True, "wgrad")])
+def test_gemm_cta_pair_matches_single_cta_and_fp32(m: int, n: int, k: int, a_mn: bool, b_mn: bool, epi: str) -> None:
+    """256-row tiles on CTA pairs (tcgen05.mma.cta_group::2) against the single-CTA kernel and fp32 torch,
+    for the forward, data-gradient and weight-gradient layouts and their epilogues (split-K included)."""
+    ops = _ops()
+    ext = ops.extension()
+    dev = torch.device("cuda")
+    torch.manual_seed(1)
+    a = torch.randn((k, m) if a_mn else (m, k), device=dev).bfloat16()
+    b = (torch.randn((k, n) if b_mn else (n, k), device=dev) * 0.05).bfloat16()
+    bias = torch.randn(n, device=dev) if epi == "gelu" else None
+    pre = torch.randn(m, n, device=dev).bfloat16() if epi == "gelu_bwd" else None
+    c0 = torch.randn(m, n, device=dev)
+    outs = []
+    try:
+        ops.set_deterministic_reductions(epi != "wgrad_fast")
+        for mode in (0, 1):
+            ext.set_gemm_pair(mode)
+            if epi == "gelu":
+                aux = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+                y = ops.gemm(a, b, bias=bias, aux=aux, epilogue=ops.EPI_GELU)
+                outs.append((y, aux))
+            elif epi == "gelu_bwd":
+                outs.append((ops.gemm(a, b, b_mn_major=True, aux=pre, epilogue=ops.EPI_GELU_BWD), None))
+            elif epi.startswith("wgrad"):
+                d = c0.clone()
+                ops.gemm(a, b, out=d, a_mn_major=True, b_mn_major=True, beta=1.0)
+                outs.append((d, None))
+            else:
+                outs.append((ops.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn), None))
+        torch.cuda.synchronize()
+    finally:
+        ext.set_gemm_pair(0)
+        ops.set_deterministic_reductions(True)
+    if epi == "gelu":
+        ref, ref_pre = ops.reference_gemm(a, b, bias=bias, epilogue=ops.EPI_GELU)
+    elif epi == "gelu_bwd":
+        ref, ref_pre = ops.reference_gemm(a, b, b_mn_major=True, aux=pre, epilogue=ops.EPI_GELU_BWD)
+    elif epi.startswith("wgrad"):
+        ref, ref_pre = ops.reference_gemm(a, b, a_mn_major=True, b_mn_major=True, c=c0, beta=1.0)
+    else:
+        ref, ref_pre = ops.reference_gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn)
+    tol = 1e-5 if epi.startswith("wgrad") else 1e-2
+    for y, aux in outs:
+        assert _rel(y, ref) < tol, (epi, _rel(y, ref))
+        if aux is not None:
+            assert _rel(aux, ref_pre) < 1e-2
+    if epi != "wgrad_fast":  # same tile sums in the same order: equal bits
+        assert torch.equal(outs[0][0], outs[1][0]) or _rel(outs[0][0], outs[1][0]) < 1e-6
+
+
 def test_gemm_epilogues() -> None:
     ops = _ops()
     dev = torch.device("cuda")
