@@ -274,11 +274,11 @@ __device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc,
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
       : "memory");
 }
-// Arrive on `bar` (same offset) in both CTAs of the pair once the pair's issued MMAs complete.
+// Arrive on `bar` (same offset) in both CTAs of the pair once the pair's issued MMAs complete: one
+// commit to this CTA's barrier and one to the partner's (addressed through the cluster window).
 __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-                   smem_u32(bar)),
-               "h"((uint16_t)3)
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_in_cta(bar, 1))
                : "memory");
 }
 
