@@ -31,7 +31,8 @@ import torch
 
 from ._ext import extension
 
-__all__ = ["HAS_FUSED_TENSOR_PARALLEL", "all_gather_linear", "bucket_all_reduce", "nvls_available", "can_fuse_sequence_parallel",
+__all__ = ["HAS_FUSED_TENSOR_PARALLEL", "all_gather_linear", "bucket_all_reduce", "can_fuse_all_reduce",
+           "column_linear_reduced_grad", "linear_all_reduce", "nvls_available", "can_fuse_sequence_parallel",
            "fsdp_all_gather", "fsdp_reduce_scatter_adamw", "linear_reduce_scatter"]
 
 HAS_FUSED_TENSOR_PARALLEL = True
@@ -320,6 +321,141 @@ class _LinearReduceScatter(torch.autograd.Function):
                 value = value.to(weight.dtype)
             dw = deliver_grad(weight, compute=wgrad if value is None else None, value=value)
         return dx.view(b, s, kr), dw, None, None
+
+
+def _sum_over_group(st: _TensorParallelSites, owner: Any, kind: str, rows: int, cols: int,
+                    produce: Any) -> torch.Tensor:
+    """``produce(out)`` writes this rank's fp32 partial ``[rows, cols]`` straight into a peer-mapped
+    buffer (the GEMM's TMA-store epilogue); the two-shot in-kernel NVLink all-reduce then sums it in
+    place across the group.  Returns the sum (a view of the buffer, valid until the next call of
+    this site)."""
+    key = (owner, kind)
+    buf = st.local.get(key)
+    if buf is None or buf.numel() != rows * cols:
+        buf = st.workspace.allocate(rows * cols, torch.float32)
+        st.local[key] = buf
+    out = buf.view(rows, cols)
+    produce(out)
+    bucket_all_reduce(st.workspace, buf, 0, rows * cols, 1.0, wide=True)
+    _note("gemm_all_reduce", st, out)
+    return out
+
+
+class _LinearAllReduce(torch.autograd.Function):
+    """Row-parallel ``out = AllReduce(X W_r^T)`` (tensor parallelism without sequence parallelism).
+
+    Forward: the GEMM writes its fp32 partial product into peer-mapped memory and the in-kernel
+    all-reduce sums it (reference: the ``reduce_from_group`` all-reduce after the row-parallel
+    GEMM, ``autograd/collectives.py:192``, ``tensor_parallel.py:456``).  Backward: the output
+    gradient is the same on every rank, so the input and weight gradients are local GEMMs.
+    """
+
+    @staticmethod
+    def forward(ctx: Any, x: torch.Tensor, weight: torch.Tensor, workspace: Any, owner: Any) -> torch.Tensor:
+        from .linear import compute_weight, gemm
+
+        st = _sites(workspace)
+        lead, k = x.shape[:-1], x.shape[-1]
+        x2 = x.reshape(-1, k).contiguous()
+        w = compute_weight(weight, x.dtype)
+        n = w.shape[0]
+        summed = _sum_over_group(st, owner, "ar.out", x2.shape[0], n, lambda out: gemm(x2, w, out=out))
+        ctx.save_for_backward(x2, w)
+        ctx.weight = weight
+        return summed.to(x.dtype).view(*lead, n)
+
+    @staticmethod
+    def backward(ctx: Any, dy: torch.Tensor) -> tuple[Any, ...]:
+        from .grads import deliver_grad
+        from .linear import gemm
+
+        x2, w = ctx.saved_tensors
+        weight = ctx.weight
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        dx = gemm(dy2, w, b_mn_major=True).view(*dy.shape[:-1], w.shape[1]) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            dw = deliver_grad(weight, compute=lambda out, beta: gemm(dy2, x2, out=out, a_mn_major=True, b_mn_major=True,
+                                                                      beta=beta),
+                              value=None if getattr(weight, "main_grad", None) is not None else
+                              gemm(dy2, x2, out_dtype=weight.dtype, a_mn_major=True, b_mn_major=True))
+        return dx, dw, None, None
+
+
+class _ColumnLinearReducedGrad(torch.autograd.Function):
+    """Column-parallel ``Y = act(X W_r^T + b_r)`` whose input gradient is all-reduced in-kernel.
+
+    Forward: a local GEMM (GELU in its epilogue).  Backward: the input-gradient GEMM writes its fp32
+    partial into peer-mapped memory and the in-kernel all-reduce sums it (reference: the
+    ``copy_to_group`` adjoint, ``autograd/collectives.py:180``).
+    """
+
+    @staticmethod
+    def forward(ctx: Any, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, workspace: Any, owner: Any,
+                gelu: bool) -> torch.Tensor:
+        from .linear import EPI_GELU, compute_weight, gemm
+
+        lead, k = x.shape[:-1], x.shape[-1]
+        x2 = x.reshape(-1, k).contiguous()
+        w = compute_weight(weight, x.dtype)
+        y = torch.empty(x2.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+        pre = None
+        if gelu:
+            pre = torch.empty_like(y)
+            gemm(x2, w, out=y, bias=bias, aux=pre, epilogue=EPI_GELU)
+        else:
+            gemm(x2, w, out=y, bias=bias)
+        ctx.save_for_backward(x2, w, pre)
+        ctx.weight, ctx.bias, ctx.st, ctx.owner = weight, bias, _sites(workspace), owner
+        return y.view(*lead, w.shape[0])
+
+    @staticmethod
+    def backward(ctx: Any, dy: torch.Tensor) -> tuple[Any, ...]:
+        from .grads import deliver_grad
+        from .linear import _column_sum, gelu_backward, gemm
+
+        x2, w, pre = ctx.saved_tensors
+        weight, bias = ctx.weight, ctx.bias
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        g = gelu_backward(dy2, pre) if pre is not None else dy2
+        dx = None
+        if ctx.needs_input_grad[0]:
+            summed = _sum_over_group(ctx.st, ctx.owner, "ar.dx", g.shape[0], w.shape[1],
+                                     lambda out: gemm(g, w, out=out, b_mn_major=True))
+            dx = summed.to(dy.dtype).view(*dy.shape[:-1], w.shape[1])
+        dw = db = None
+        if ctx.needs_input_grad[1]:
+            dw = deliver_grad(weight, compute=lambda out, beta: gemm(g, x2, out=out, a_mn_major=True, b_mn_major=True,
+                                                                      beta=beta),
+                              value=None if getattr(weight, "main_grad", None) is not None else
+                              gemm(g, x2, out_dtype=weight.dtype, a_mn_major=True, b_mn_major=True))
+        if bias is not None and ctx.needs_input_grad[2]:
+            db = deliver_grad(bias, compute=lambda out, beta: _column_sum(g, out, beta),
+                              value=None if getattr(bias, "main_grad", None) is not None else _column_sum(g).to(bias.dtype))
+        return dx, dw, db, None, None, None
+
+
+def can_fuse_all_reduce(x: torch.Tensor, group: Any, *, features: tuple[int, ...]) -> bool:
+    """Whether the in-kernel all-reduce covers this tensor-parallel call: bf16 on CUDA, 2..8 ranks, 16-byte rows."""
+    return x.is_cuda and x.dtype == torch.bfloat16 and 2 <= group.size <= 8 and all(f % 8 == 0 for f in features)
+
+
+def linear_all_reduce(x: torch.Tensor, weight: torch.Tensor, workspace: Any, group: Any, *,
+                      owner: Any = None) -> torch.Tensor | None:
+    """Row-parallel linear (no sequence parallelism) with its output summed in-kernel; ``None`` when not applicable."""
+    if not can_fuse_all_reduce(x, group, features=(x.shape[-1], weight.shape[0])):
+        return None
+    return _LinearAllReduce.apply(x, weight, workspace, owner if owner is not None else id(weight))
+
+
+def column_linear_reduced_grad(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, workspace: Any, group: Any,
+                               *, activation: str | None = None, owner: Any = None) -> torch.Tensor | None:
+    """Column-parallel linear (no sequence parallelism) whose input gradient is summed in-kernel; ``None``
+    when not applicable."""
+    if activation not in (None, "gelu") or not can_fuse_all_reduce(x, group, features=(x.shape[-1], weight.shape[0])):
+        return None
+    return _ColumnLinearReducedGrad.apply(x, weight, bias, workspace, owner if owner is not None else id(weight),
+                                          activation == "gelu")
 
 
 def all_gather_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, workspace: Any, group: Any, *,

@@ -174,12 +174,15 @@ def describe_parallel_plan(config: ExperimentConfig, context: DistributedContext
             add(PlanStep("forward", "row-parallel GEMM output to sequence shards", "tensor",
                          "reduce-scatter in the tcgen05 GEMM epilogue" if fused_tp else f"{library} reduce-scatter"))
         else:
-            add(PlanStep("forward", "row-parallel GEMM partial sums", "tensor", f"{library} all-reduce"))
+            add(PlanStep("forward", "row-parallel GEMM partial sums", "tensor",
+                         "fp32 partials written by the GEMM into peer memory, summed by the in-kernel NVLink all-reduce"
+                         if fused_tp else f"{library} all-reduce"))
         add(PlanStep("forward", "vocab-parallel cross-entropy statistics (max, sum-exp, target logit)", "tensor",
                      f"{library} all-reduce of 3 floats per token; no logits are gathered"))
         add(PlanStep("backward", "column-parallel input gradients", "tensor",
                      ("reduce-scatter in the data-gradient GEMM epilogue" if fused_tp else f"{library} reduce-scatter")
-                     if sp else f"{library} all-reduce"))
+                     if sp else ("fp32 partials written by the data-gradient GEMM into peer memory, summed by the in-kernel "
+                                 "NVLink all-reduce" if fused_tp else f"{library} all-reduce")))
     if independent:
         algorithm = config.tensor_parallel.context_parallel_algorithm
         add(PlanStep("forward", "attention keys / values" if algorithm != "ulysses" else "attention sequence <-> head re-shard",

@@ -176,6 +176,14 @@ class ColumnParallelLinear(nn.Module):
                     return out
             x = gather_from_sequence_parallel_region(x, self.group, dim=SEQUENCE_DIM)
         else:
+            workspace = _fused_comm(self.group, x)
+            if workspace is not None:
+                from ..ops.comm import column_linear_reduced_grad
+
+                out = column_linear_reduced_grad(x, self.weight, self.bias, workspace, self.group, activation=self.activation,
+                                                 owner=id(self))
+                if out is not None:
+                    return gather_from_group(out, self.group, dim=-1) if self.gather_output else out
             x = copy_to_group(x, self.group)
         out = ops.linear(x, self.weight, self.bias, activation=self.activation)
         if self.gather_output:
@@ -249,6 +257,14 @@ class RowParallelLinear(nn.Module):
                 from ..ops.comm import linear_reduce_scatter
 
                 out = linear_reduce_scatter(x, self.weight, workspace, self.group, owner=id(self))
+                if out is not None:
+                    return out if self.bias is None else out + self.bias.to(out.dtype)
+        if not self.sequence_parallel:
+            workspace = _fused_comm(self.group, x)
+            if workspace is not None:
+                from ..ops.comm import linear_all_reduce
+
+                out = linear_all_reduce(x, self.weight, workspace, self.group, owner=id(self))
                 if out is not None:
                     return out if self.bias is None else out + self.bias.to(out.dtype)
         partial = ops.linear(x, self.weight, fused_bias)

@@ -338,14 +338,16 @@ def ddp_cuda_worker(rank: int, world: int, fused: bool, steps: int, overlap: boo
         ctx.shutdown()
 
 
-def tp_fused_collectives_worker(rank: int, world: int) -> dict[str, Any]:
-    """Column- and row-parallel SP linears with the fused collective kernels against the NCCL path."""
+def tp_fused_collectives_worker(rank: int, world: int, sp: bool = True) -> dict[str, Any]:
+    """Column- and row-parallel linears with the fused collective kernels against the NCCL path:
+    with sequence parallelism (all-gather GEMM, GEMM reduce-scatter) or without it (in-kernel
+    all-reduces of the row output and of the column input gradient)."""
     from hybrid_training.parallel.tensor_parallel import ColumnParallelLinear, RowParallelLinear
 
     cfg = ExperimentConfig.from_dict({
         "name": "tp-fused", "backend": "nccl", "device": "cuda", "timeout_seconds": 120.0,
-        "topology": {"tensor_parallel_size": world, "sequence_parallel_mode": "tensor_group"},
-        "tensor_parallel": {"sequence_parallel": True, "fused_collectives": True},
+        "topology": {"tensor_parallel_size": world, "sequence_parallel_mode": "tensor_group" if sp else "disabled"},
+        "tensor_parallel": {"sequence_parallel": sp, "fused_collectives": True},
         "mixed_precision": {"enabled": True, "param_dtype": "bfloat16"},
         "model": {"kind": "transformer", "hidden_size": 256, "num_layers": 1, "num_heads": 4, "vocab_size": 512,
                   "max_sequence_length": 128 * world}})
@@ -354,13 +356,14 @@ def tp_fused_collectives_worker(rank: int, world: int) -> dict[str, Any]:
         group = ctx.group("tensor")
         dev = ctx.device
         b, r, k, n = 2, 128, 256, 512
-        col = ColumnParallelLinear(k, n, group, bias=True, sequence_parallel=True, activation="gelu", init_seed=3, device=dev)
-        row = RowParallelLinear(n, k, group, bias=True, sequence_parallel=True, init_seed=4, device=dev)
+        col = ColumnParallelLinear(k, n, group, bias=True, sequence_parallel=sp, activation="gelu", init_seed=3, device=dev)
+        row = RowParallelLinear(n, k, group, bias=True, sequence_parallel=sp, init_seed=4, device=dev)
         gen = torch.Generator(device="cpu").manual_seed(7)
         x_full = torch.randn(b, r * world, k, generator=gen)
         g_full = torch.randn(b, r * world, k, generator=gen)
-        x_shard = x_full[:, rank * r:(rank + 1) * r].to(dev).bfloat16()
-        g_shard = g_full[:, rank * r:(rank + 1) * r].to(dev).bfloat16()
+        # with SP every rank holds its sequence chunk; without it the whole (replicated) sequence
+        x_shard = (x_full[:, rank * r:(rank + 1) * r] if sp else x_full).to(dev).bfloat16()
+        g_shard = (g_full[:, rank * r:(rank + 1) * r] if sp else g_full).to(dev).bfloat16()
         results = {}
         for fused in (True, False):
             ctx.fused_tensor_collectives = fused

@@ -68,9 +68,12 @@ def test_ddp_optimizer_update_overlapped_with_the_backward_matches_the_step_afte
             assert abs(a - b) < 1e-2 * max(1.0, abs(b)), (over[0].value["losses"], base[0].value["losses"])
 
 
-def test_fused_tensor_parallel_collectives_match_nccl_path() -> None:
-    """All-gather fused into the column GEMM's loads, reduce-scatter fused into the row GEMM's epilogue."""
-    results = launch_workers(W.tp_fused_collectives_worker, 2, timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
+@pytest.mark.parametrize("sp", [True, False])
+def test_fused_tensor_parallel_collectives_match_nccl_path(sp: bool) -> None:
+    """SP: all-gather fused into the column GEMM's loads, reduce-scatter fused into the row GEMM's epilogue.
+    No SP: the row output and the column input gradient summed by the in-kernel all-reduce."""
+    results = launch_workers(W.tp_fused_collectives_worker, 2, args=(sp,), timeout_seconds=300,
+                             extra_env={"NCCL_NVLS_ENABLE": "0"})
     for r in results:
         assert r.value["error_word"] == 0
         for key, err in r.value["errors"].items():
