@@ -69,13 +69,23 @@ def _padded(t: torch.Tensor) -> torch.Tensor:
     return torch.zeros(t.shape[0], cols, dtype=t.dtype, device=t.device)[:, : t.shape[1]].copy_(t)
 
 
-def bench_gemm(only: str | None, iters: int) -> None:
+def bench_gemm(only: str | None, iters: int, extra: list[str] | None = None) -> None:
+    """``extra`` adds shapes written ``M,N,K[,a_mn,b_mn,f32]`` (0/1 flags), e.g. ``32768,768,3072``."""
     from . import gemm
 
     dev = torch.device("cuda")
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    for name, (m, n, k, amn, bmn, f32) in GEMM_SHAPES.items():
-        if only and name != only:
+    shapes = dict(GEMM_SHAPES)
+    for spec in extra or []:
+        v = [int(t) for t in spec.split(",")]
+        v += [0] * (6 - len(v))
+        shapes[spec] = (v[0], v[1], v[2], bool(v[3]), bool(v[4]), bool(v[5]))
+        only = only if only is not None else "__extra__"
+    for name, (m, n, k, amn, bmn, f32) in shapes.items():
+        if only == "__extra__":
+            if name in GEMM_SHAPES:
+                continue
+        elif only and name != only:
             continue
         a = _padded(torch.randn((k, m) if amn else (m, k), device=dev).bfloat16())
         b = _padded(torch.randn((k, n) if bmn else (n, k), device=dev).bfloat16())
@@ -338,6 +348,7 @@ def main(argv: list[str] | None = None) -> None:
     g = sub.add_parser("gemm")
     g.add_argument("--only", choices=list(GEMM_SHAPES))
     g.add_argument("--iters", type=int, default=20)
+    g.add_argument("--shape", action="append", default=[], help="extra shape M,N,K[,a_mn,b_mn,f32]; only these run")
     a = sub.add_parser("attention")
     a.add_argument("--shape", choices=list(ATTN_SHAPES), default="gpt2")
     a.add_argument("--once", action="store_true")
@@ -356,7 +367,7 @@ def main(argv: list[str] | None = None) -> None:
     f.add_argument("--numel", type=int, default=50_597_888)
     args = p.parse_args(argv)
     if args.what == "gemm":
-        bench_gemm(args.only, args.iters)
+        bench_gemm(args.only, args.iters, args.shape)
     elif args.what == "attention":
         bench_attention(args.shape, args.once, args.fast)
     elif args.what == "norm":
