@@ -19,7 +19,8 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 def test_native_all_gather_context_parallel_attention_matches_the_whole_sequence() -> None:
     results = launch_workers(W.gathered_attention_worker, 2, timeout_seconds=300, extra_env={"NCCL_NVLS_ENABLE": "0"})
     for r in results:
-        assert r["out"] < 1e-2 and r["dq"] < 1e-2 and r["dkv"] < 2e-2, r
+        v = r.value
+        assert v["out"] < 1e-2 and v["dq"] < 1e-2 and v["dkv"] < 2e-2, v
 
 
 def test_in_kernel_bucket_all_reduce_matches_nccl() -> None:
