@@ -179,14 +179,36 @@ class FusedAdamW(torch.optim.Optimizer):
             self._hyper[2:3].copy_(self._grad_scale_device.reshape(1))
 
     @torch.no_grad()
-    def launch_step(self) -> None:
-        """Device half of a step (CUDA): one fused kernel over the flat buffers; no host synchronisation."""
+    def launch_step(self, deferred: tuple[int, int, Any] | None = None) -> None:
+        """Device half of a step (CUDA): one fused kernel over the flat buffers; no host synchronisation.
+
+        ``deferred = (start, numel, wait)``: the gradients in ``[start, start + numel)`` of the flat
+        buffer are still being reduced; every other element is updated first, then ``wait()`` makes
+        the stream wait for that reduction and the range is updated last, so the update of the rest
+        overlaps the last reduction.
+        """
         group = self.param_groups[0]
         beta1, beta2 = group["betas"]
         self._collect_autograd_grads()
         self.stage_hyper_parameters()
-        ops.adamw_flat(self._param_flat, self._grad_flat, self._exp_avg, self._exp_avg_sq, self._compute_flat, self._hyper,
-                       beta1=beta1, beta2=beta2, eps=group["eps"], weight_decay=group["weight_decay"])
+
+        def update(lo: int, hi: int) -> None:
+            if hi <= lo:
+                return
+            copy = None if self._compute_flat is None else self._compute_flat[lo:hi]
+            ops.adamw_flat(self._param_flat[lo:hi], self._grad_flat[lo:hi], self._exp_avg[lo:hi], self._exp_avg_sq[lo:hi], copy,
+                           self._hyper, beta1=beta1, beta2=beta2, eps=group["eps"], weight_decay=group["weight_decay"])
+
+        if deferred is None:
+            update(0, self._param_flat.numel())
+        else:
+            start, numel, wait = deferred
+            total = self._param_flat.numel()
+            end = min(total, start + -(-numel // _ALIGN) * _ALIGN)
+            update(0, start)
+            update(end, total)
+            wait()
+            update(start, end)
         if self._compute_flat is not None:
             for p in self._params:
                 p.compute_copy_version = p._version

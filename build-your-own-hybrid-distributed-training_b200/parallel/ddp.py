@@ -328,13 +328,20 @@ class DistributedDataParallel(nn.Module):
         self._statistics.buckets_reduced += 1
         self._statistics.bytes_reduced += bucket.num_bytes()
 
-    def finish_gradient_synchronization(self) -> None:
-        """Wait for every bucket and expose the averaged gradients as ``param.grad`` views."""
+    def finish_gradient_synchronization(self, *, defer_last: bool = False) -> tuple[int, int, Any] | None:
+        """Wait for every bucket and expose the averaged gradients as ``param.grad`` views.
+
+        ``defer_last`` (in-kernel all-reduce only): leave the last bucket's reduction running and
+        return ``(start, numel, wait)`` for it -- its range of the flat gradient buffer and a callable
+        that makes the current stream wait for it -- so that work that does not read that range (the
+        optimizer update of every other bucket) overlaps the last reduction.  ``None`` when nothing
+        was deferred.
+        """
         if not self._backward_in_progress:
-            return
+            return None
         if not self._require_backward_grad_sync:
             self._backward_in_progress = False
-            return
+            return None
         missing: list[str] = []
         for bucket in self._buckets:
             if bucket.pending == 0:
@@ -367,8 +374,13 @@ class DistributedDataParallel(nn.Module):
                                                  f"bucket {bucket.layout.index} never became ready", rank=self._group.global_rank,
                                                  expected="all buckets ready", observed=f"{bucket.pending} parameters pending",
                                                  resolution="the bucket counters are inconsistent (an internal error)"))
+        deferred = None
+        tail = self._buckets[-1] if self._buckets else None
+        if (defer_last and tail is not None and isinstance(tail.work, _FusedLaunch)
+                and all(p.dtype == tail.buffer.dtype for p in tail.parameters)):  # exposing a cast would read it
+            deferred = (tail.start, tail.layout.total_numel, tail.work.wait)
         for bucket in self._buckets:
-            if bucket.work is not None:
+            if bucket.work is not None and not (deferred is not None and bucket is tail):
                 bucket.work.wait()
         for bucket in self._buckets:
             for pos, p in enumerate(bucket.parameters):
@@ -378,6 +390,7 @@ class DistributedDataParallel(nn.Module):
         self._next_bucket = 0
         self._backward_in_progress = False
         self._statistics.steps += 1
+        return deferred
 
     def check_collective_status(self) -> None:
         """Raise :class:`KernelError` if an in-kernel bucket all-reduce gave up waiting for a peer.

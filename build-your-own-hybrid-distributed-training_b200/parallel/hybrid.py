@@ -289,14 +289,22 @@ class HybridModel(nn.Module):
             return self._fsdp.no_sync()
         return nullcontext()
 
-    def finish_backward(self) -> None:
-        """Complete every gradient reduction for the step (DDP wait, SP partial sums, FSDP free)."""
+    def finish_backward(self, *, defer_last: bool = False) -> tuple[int, int, Any] | None:
+        """Complete every gradient reduction for the step (DDP wait, SP partial sums, FSDP free).
+
+        ``defer_last``: with DDP's in-kernel all-reduce and no sequence-parallel partial sums, leave
+        the last bucket's reduction running and return ``(start, numel, wait)`` for it (see
+        :meth:`DistributedDataParallel.finish_gradient_synchronization`).
+        """
         if self._ddp is not None:
-            self._ddp.finish_gradient_synchronization()
+            deferred = self._ddp.finish_gradient_synchronization(defer_last=defer_last and self._sp_group is None)
+            if deferred is not None:
+                return deferred
         if self._sp_group is not None and self._fsdp is None:
             all_reduce_sequence_parallel_gradients(self._inner_model, self._sp_group, recorder=self._recorder)
         if self._fsdp is not None:
             self._fsdp.finish_backward()
+        return None
 
     def optimizer_parameters(self) -> list[nn.Parameter]:
         return [p for p in self.wrapped.parameters() if p.requires_grad]

@@ -120,6 +120,7 @@ class TrainingEngine:
         self.scaler = GradScaler(cfg.mixed_precision.scaler, ctx.group("world"), ctx.device, recorder=self.recorder)
         self._fsdp_fused_update = self._enable_fsdp_fused_update()
         self._overlap = self._enable_overlapped_step()
+        self._ddp_flat_base = self._ddp_flat_offset()
         self.state = TrainingState()
         self._transformer = cfg.model.kind == "transformer"
         self._fused_loss = self._transformer and cfg.model.fused_loss
@@ -181,6 +182,19 @@ class TrainingEngine:
         return OverlappedAdamW(inner, group_bytes=int(cfg.ddp.bucket_cap_mb * (1 << 20)))
 
     overlapped_step = property(lambda self: self._overlap)
+
+    def _ddp_flat_offset(self) -> int | None:
+        """Index in the fused optimizer's flat buffers of DDP's flat gradient buffer start, or ``None``
+        when the two do not share storage (then no bucket's update can be deferred)."""
+        ddp = self.model.ddp
+        inner = self.optimizer.inner
+        if (ddp is None or self.context.device.type != "cuda" or not isinstance(inner, FusedAdamW)
+                or not inner.flat_parameters.is_cuda or self.optimizer.offloaded):
+            return None
+        buf, flat = ddp.flat_gradient_buffer, inner.flat_gradients
+        if buf.untyped_storage().data_ptr() != flat.untyped_storage().data_ptr():
+            return None
+        return int(buf.storage_offset() - flat.storage_offset())
 
     # -- data ----------------------------------------------------------------------------------------------
     def _build_data(self) -> None:
@@ -259,13 +273,19 @@ class TrainingEngine:
                 with trace_range(f"step/backward {i}"), armed:
                     self.scaler.scale(loss).backward()
             total = loss.detach() if total is None else total + loss.detach()
+        t = self.config.training
+        # Plain fused AdamW after DDP's in-kernel all-reduce: update every other bucket while the
+        # last one (reduced only after the backward pass) is still on the wire.
+        split = (self._overlap is None and not self._fsdp_fused_update and self._ddp_flat_base is not None
+                 and not self.scaler.enabled and not (t.max_grad_norm > 0 or t.collect_metrics))
         with trace_range("step/finish_backward"):
-            self.model.finish_backward()
+            deferred = self.model.finish_backward(defer_last=split)
+        if deferred is not None:
+            deferred = (deferred[0] + self._ddp_flat_base, deferred[1], deferred[2])
         params = self.model.optimizer_parameters()
         if self.scaler.enabled:
             self.scaler.unscale_(params)
         norm = None
-        t = self.config.training
         if t.max_grad_norm > 0 or t.collect_metrics:
             norm = self.optimizer.clip_grad_norm(t.max_grad_norm)
         if self._fsdp_fused_update:
@@ -275,7 +295,7 @@ class TrainingEngine:
             self._overlap.finish(ddp.communication_stream if ddp is not None else None)
         elif isinstance(inner, FusedAdamW) and inner.flat_parameters.is_cuda and not self.scaler.enabled:
             with trace_range("step/adamw"):
-                inner.launch_step()
+                inner.launch_step(deferred)
         elif self.scaler.enabled:
             self.scaler.step(self.optimizer, params, already_unscaled=True)
         else:
