@@ -228,10 +228,9 @@ class CheckpointManifest:
 
     def summary(self) -> str:
         by = {c: len(self.tensors_by_category(c)) for c in ("model", "optimizer", "buffer")}
-        lines = [f"checkpoint format {self.format_version} written by {self.created_by or '?'}",
-                 f"  step               : {self.step}", f"  writer world size  : {self.writer_world_size}",
-                 f"  topology           : {self.topology}", f"  complete           : {self.complete}",
-                 f"  model tensors      : {by['model']}", f"  optimizer tensors  : {by['optimizer']}",
-                 f"  buffer tensors     : {by['buffer']}", f"  total elements     : {sum(r.numel for r in self.tensors.values())}",
-                 f"  payload files      : {len(self.files)}"]
+        rows = [("saved at step", self.step), ("ranks that wrote it", self.writer_world_size), ("grid", self.topology),
+                ("finished", self.complete), ("model tensors", by["model"]), ("optimizer tensors", by["optimizer"]),
+                ("buffers", by["buffer"]), ("elements in all", sum(r.numel for r in self.tensors.values())),
+                ("rank files", len(self.files))]
+        lines = [f"format v{self.format_version}, by {self.created_by or 'unknown'}"] + [f"  {k:<20} {v}" for k, v in rows]
         return "\n".join(lines)

@@ -293,7 +293,7 @@ def _warn_on_config_drift(saved: Any, current: ExperimentConfig) -> None:
 
     walk(norm(saved), norm(current.to_dict()), "")
     if diffs:
-        _LOG.warning("configuration differs from the checkpoint (%d field(s)); resuming anyway:\n  %s", len(diffs), "\n  ".join(diffs[:12]))
+        _LOG.warning("resuming with %d setting(s) changed since the save:\n  %s", len(diffs), "\n  ".join(diffs[:12]))
 
 
 def inspect_checkpoint(directory: str | Path, *, verify: bool = True) -> dict[str, Any]:

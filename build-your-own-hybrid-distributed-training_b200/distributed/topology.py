@@ -43,7 +43,7 @@ class RankCoordinates:
 
     def __getitem__(self, dimension: str) -> int:
         if dimension not in DIMENSIONS:
-            raise KeyError(f"unknown dimension {dimension!r}; expected one of {DIMENSIONS}")
+            raise KeyError(f"{dimension!r} is not a grid dimension (the grid has {', '.join(DIMENSIONS)})")
         return int(getattr(self, dimension))
 
     def label(self) -> str:

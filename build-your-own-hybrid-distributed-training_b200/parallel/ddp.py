@@ -360,7 +360,7 @@ class DistributedDataParallel(nn.Module):
                 "ddp.finish_gradient_synchronization", "parameters without a gradient leave their buckets incomplete, so those "
                 "buckets would never be reduced", rank=self._group.global_rank,
                 world_size=self._group.size, expected="a gradient for each trainable parameter",
-                observed=f"{len(missing)} without gradients: {missing[:8]}",
+                observed=f"no gradient for {len(missing)}, e.g. {missing[:8]}",
                 resolution="set DDPConfig(find_unused_parameters=True), or stop marking unused parameters trainable"))
         self._statistics.unused_parameters = tuple(missing)
         self._draining = True
@@ -371,7 +371,7 @@ class DistributedDataParallel(nn.Module):
         for bucket in self._buckets:
             if not bucket.launched:
                 raise ShardingError(format_error("ddp.finish_gradient_synchronization",
-                                                 f"bucket {bucket.layout.index} never became ready", rank=self._group.global_rank,
+                                                 f"bucket {bucket.layout.index} still waits for gradients after the backward pass", rank=self._group.global_rank,
                                                  expected="all buckets ready", observed=f"{bucket.pending} parameters pending",
                                                  resolution="the bucket counters are inconsistent (an internal error)"))
         deferred = None

@@ -85,7 +85,7 @@ def estimate_training_memory(
     if shard_group_size < 1:
         raise ValueError(f"the shard group has at least one rank; got {shard_group_size}")
     if optimizer not in OPTIMIZER_STATE_SLOTS:
-        raise ValueError(f"unknown optimizer {optimizer!r}; expected one of {sorted(OPTIMIZER_STATE_SLOTS)}")
+        raise ValueError(f"no state-size rule for optimizer {optimizer!r} (known: {', '.join(sorted(OPTIMIZER_STATE_SLOTS))})")
     unit = total_parameters if largest_unit_parameters is None else largest_unit_parameters
     local = -(-total_parameters // shard_group_size)
     gathered_params = gathered_grads = 0

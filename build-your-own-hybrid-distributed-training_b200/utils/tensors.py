@@ -179,7 +179,7 @@ def split_tensor_along_dim(tensor: torch.Tensor, dim: int, num_parts: int, *, co
     dim %= tensor.dim()
     size = tensor.shape[dim]
     if size % num_parts:
-        raise _err("split_tensor_along_dim", f"dimension {dim} of size {size} is not divisible by {num_parts}",
+        raise _err("split_tensor_along_dim", f"{num_parts} equal parts do not tile dimension {dim} (size {size})",
                    f"{size} % {num_parts} == 0", size % num_parts, "pick a parallel size that divides the dimension")
     parts = torch.chunk(tensor, num_parts, dim=dim) if size else tuple(tensor for _ in range(num_parts))
     return tuple(p.contiguous() for p in parts) if contiguous else tuple(parts)

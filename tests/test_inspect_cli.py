@@ -34,7 +34,7 @@ def checkpoint(tmp_path_factory: pytest.TempPathFactory) -> Path:
 def test_summary_and_json(checkpoint: Path, capsys: pytest.CaptureFixture[str]) -> None:
     assert _console_main([str(checkpoint)]) == 0
     text = capsys.readouterr().out
-    assert "writer world size  : 2" in text and "files verified         2 / 2" in text
+    assert "ranks that wrote it  2" in text and "files verified         2 / 2" in text
     assert _console_main([str(checkpoint), "--json"]) == 0
     summary = json.loads(capsys.readouterr().out)
     assert summary["writer_world_size"] == 2 and summary["verification"]["files_verified"] == 2
