@@ -49,6 +49,8 @@ __device__ __forceinline__ MS block_merge(MS v, float* sm, float* ss) {
 }
 
 __device__ __forceinline__ MS row_stats(const __nv_bfloat16* __restrict__ row, int V) {
+  // Online (max, sum) per thread: the running sum is rescaled only when a vector raises the
+  // running maximum, so the common case costs one exponential per element.
   MS acc{-INFINITY, 0.f};
   const int nv = V / 8;
   for (int i = threadIdx.x; i < nv; i += blockDim.x) {
@@ -61,10 +63,15 @@ __device__ __forceinline__ MS row_stats(const __nv_bfloat16* __restrict__ row, i
       x[j] = bf2f(p[j]);
       m = fmaxf(m, x[j]);
     }
+    if (m > acc.m) {
+      acc.s = acc.m == -INFINITY ? 0.f : acc.s * __expf(acc.m - m);
+      acc.m = m;
+    }
+    if (acc.m == -INFINITY) continue;  // every logit so far is -inf: nothing to add
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s += __expf(x[j] - m);
-    acc = merge(acc, MS{m, s});
+    for (int j = 0; j < 8; ++j) s += __expf(x[j] - acc.m);
+    acc.s += s;
   }
   for (int c = nv * 8 + threadIdx.x; c < V; c += blockDim.x) acc = merge(acc, MS{bf2f(row[c]), 1.f});
   return acc;

@@ -419,10 +419,14 @@ class TensorParallelFeedForward(nn.Module):
         self._activation = None if activation in ("gelu", "swiglu") else _activation_fn(activation)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if self.activation_name == "gelu" and self.fc1.group.is_trivial and x.is_cuda:
+        # The fused paths read fc1's and fc2's weights directly instead of calling them, so they are
+        # taken only when both are the plain layers: a layer wrapped as its own FSDP unit gathers its
+        # parameters when it is called, and holds a placeholder until then.
+        plain = type(self.fc1) in (ColumnParallelLinear, _GateUpParallelLinear) and type(self.fc2) is RowParallelLinear
+        if plain and self.activation_name == "gelu" and self.fc1.group.is_trivial and x.is_cuda:
             # Width-1 group: both linears and the GELU as one fused op (GELU' in fc2's dgrad epilogue).
             return ops.gelu_mlp(x, self.fc1.weight, self.fc1.bias, self.fc2.weight, self.fc2.bias)
-        if (self.activation_name == "swiglu" and self.fc1.group.is_trivial and x.is_cuda
+        if (plain and self.activation_name == "swiglu" and self.fc1.group.is_trivial and x.is_cuda
                 and ops.swiglu_mlp_supported(self.fc1.output_features_per_partition // 2)):
             # Width-1 group: SwiGLU in fc1's epilogue (gate and up rows in one tile) and its
             # gradient in fc2's data-gradient epilogue.
