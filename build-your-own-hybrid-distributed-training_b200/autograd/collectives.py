@@ -16,8 +16,10 @@ These are the adjoints of ``src/hybrid_training/autograd/collectives.py:166-420`
 The sequence-parallel gather's adjoint is a *reduce-scatter*, not a slice:
 every rank's column-parallel layer consumed the full gathered sequence, so the
 gradient of each position is the sum of all ranks' contributions.  The fused
-kernels in :mod:`hybrid_training.ops.comm_gemm` implement the same adjoints
-with the collective inside the GEMM.
+paths in :mod:`hybrid_training.ops.comm` implement the same adjoints with the
+collective inside the GEMM (all-gather in its operand loads, reduce-scatter in
+its epilogue) or in an NVLink all-reduce kernel that reads the GEMM's output
+from peer memory.
 """
 
 from __future__ import annotations
